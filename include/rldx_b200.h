@@ -1,0 +1,273 @@
+/*
+ * rldx_b200.h — C ABI of the B200 (sm_100a) MSAT inference library (librldx_b200.so).
+ *
+ * Plain pointers and sizes only.  All tensors are device pointers unless a function says
+ * otherwise; bf16 tensors are row-major with the leading dimension given in elements.
+ * `stream` is a cudaStream_t passed as void* (NULL = legacy default stream).
+ * Every function returns RLDX_OK (0) or a negative RLDX_ERR_* code; rldx_last_error() gives
+ * the message of the last failure on the calling thread.  Kernels never spin forever: a wait
+ * that runs out records a device error code that rldx_get_device_error() reports.
+ *
+ * The library has no CPU fallback: without an sm_100 device every compute call fails.
+ */
+#ifndef RLDX_B200_H_
+#define RLDX_B200_H_
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define RLDX_OK 0
+#define RLDX_ERR_ARG (-1)         /* bad shape, pointer, alignment or enum value        */
+#define RLDX_ERR_CUDA (-2)        /* a CUDA runtime / driver call failed                 */
+#define RLDX_ERR_DEVICE (-3)      /* a kernel recorded a device-side error (timeout)     */
+#define RLDX_ERR_UNSUPPORTED (-4) /* configuration outside what the kernels implement    */
+#define RLDX_ERR_STATE (-5)       /* call not valid in the object's current state        */
+
+/* ABI version of this header (major * 100 + minor). */
+int rldx_version(void);
+
+/* Message of the last failed call on this thread ("" if none). */
+const char* rldx_last_error(void);
+
+/* Reads and clears the device-side error word (0 = none).  Synchronizes the device. */
+int rldx_get_device_error(unsigned int* code);
+
+/* 1 if the current device is an sm_100 part the kernels were built for, else 0. */
+int rldx_device_supported(void);
+
+/* ------------------------------------------------------------------------------------------
+ * Grouped GEMM with fused epilogue:  out = epilogue(A[M,K] * B[N,K]^T).
+ * Replaces the cuBLAS nn.Linear / torch.bmm calls of every MSAT block and encoder
+ * (rldx/model/modules/action_model/blocks.py:314-351, 684-689;
+ *  rldx/model/modules/embodiment_conditioned_mlp.py:72-82) and the Triton SwiGLU epilogue
+ * ds::grouped_swiglu (rldx/inference/action_model/double_stream/engine/ops/op_grouped_swiglu.py:12-39).
+ * ------------------------------------------------------------------------------------------ */
+#define RLDX_EPI_STORE 0  /* out = act(bias(acc)) [+ add]                                       */
+#define RLDX_EPI_SWIGLU 1 /* B rows interleaved [32 gate | 32 up] per 64: out = silu(g) * u     */
+#define RLDX_EPI_QKV 2    /* per-head RMSNorm + RoPE of q/k into [B,H,L,64], v into [B,H,64,Lp] */
+#define RLDX_EPI_EULER 3  /* out = out + dt * act(bias(acc))                                     */
+
+#define RLDX_BIAS_NONE 0
+#define RLDX_BIAS_FUSED 1      /* bf16(acc + b)          (nn.Linear)                         */
+#define RLDX_BIAS_POST_ROUND 2 /* bf16(bf16(acc) + b)    (torch.bmm(x, W) + b)               */
+
+#define RLDX_ACT_NONE 0
+#define RLDX_ACT_RELU 1
+#define RLDX_ACT_SILU 2  /* bf16(x * sigmoid(x)) in one rounding (F.silu)                    */
+#define RLDX_ACT_SWISH 3 /* bf16(x * bf16(sigmoid(x)))             (x * torch.sigmoid(x))    */
+
+typedef struct {
+  const void* a; /* [M, K] bf16, row stride lda elements (lda*2 % 16 == 0, 16-byte aligned) */
+  int64_t lda;
+  const void* b; /* [N, K] bf16 (row stride ldb), or [cats, N, K] with cat_ids              */
+  int64_t ldb;
+  int64_t b_cat_stride;   /* elements between category slabs                              */
+  const int64_t* cat_ids; /* device [M / rows_per_cat] category ids, or NULL               */
+  int rows_per_cat;       /* rows sharing one category (<= 128)                            */
+  int num_cats;           /* number of category slabs in b                                 */
+  int M, N, K;
+  const void* bias; /* [N] bf16 or [cats, N] with cat_ids (stride bias_cat_stride)         */
+  int bias_mode;
+  int64_t bias_cat_stride;
+  int act;
+  const void* add; /* optional bf16 added after the activation (residual / positions)      */
+  int64_t ld_add;
+  int add_row_mod; /* add row = (row % rows_in) % add_row_mod when > 0, else the row itself  */
+  void* out;
+  int64_t ldo;
+  int col_off;
+  int epilogue;
+  int rows_in, rows_out, row_skip; /* batched row remap (0 = identity), see RLDX_EPI_*       */
+  float dt;                        /* RLDX_EPI_EULER step                                    */
+  /* RLDX_EPI_QKV */
+  const void* q_norm_w; /* [64] bf16 */
+  const void* k_norm_w; /* [64] bf16 */
+  const float* rope_cos; /* [L, 32] fp32 */
+  const float* rope_sin; /* [L, 32] fp32 */
+  void* q;               /* [B, H, L, 64] bf16 */
+  void* k;               /* [B, H, L, 64] bf16 */
+  void* vt;              /* [B, H, 64, Lp] bf16 */
+  int L, Lp, H, tok_off;
+  float eps;
+  int tile_n; /* 0 = choose automatically, else 64/128/192/256 */
+} rldx_gemm_desc;
+
+/* Runs up to 4 independent problems in one launch. */
+int rldx_gemm(const rldx_gemm_desc* problems, int nproblems, void* stream);
+
+/* ------------------------------------------------------------------------------------------
+ * Joint-stream attention (non-causal, head_dim 64, scale 1/8) over [seg0 | seg1 | seg2].
+ * Replaces the F.scaled_dot_product_attention of ds::fused_attention_3way
+ * (rldx/inference/action_model/double_stream/engine/ops/op_fused_attention_3way.py:13-116) and
+ * rldx/model/modules/action_model/blocks.py:866-869 (split of the output back into streams).
+ *   q, k  [B, H, L, 64] bf16;  vt [B, H, 64, Lp] bf16 (Lp >= L, Lp % 8 == 0)
+ *   key_mask [B, L] uint8 (1 = attend) or NULL
+ *   out[s] [B * seg_len[s], H*64] bf16, nseg in 1..3, sum(seg_len) == L
+ * ------------------------------------------------------------------------------------------ */
+int rldx_joint_attention(const void* q, const void* k, const void* vt, int B, int H, int L, int Lp,
+                         const uint8_t* key_mask, void* const* out, const int* seg_len, int nseg,
+                         void* stream);
+
+/* ------------------------------------------------------------------------------------------
+ * LayerNorm without affine (eps) over rows of width D (D % 8 == 0, D <= 4096), optionally
+ * followed by y * scale1p + shift (AdaLN-zero output projection, both bf16 [D]).
+ * Replaces nn.LayerNorm(elementwise_affine=False) (rldx/model/modules/norms.py:35-36), the LN of
+ * ds::vl_epilogue_ln (rldx/inference/action_model/double_stream/engine/ops/op_vl_epilogue_ln.py:13-38)
+ * and MSAT._output_projection (rldx/model/modules/action_model/msat.py:771-781).
+ * ------------------------------------------------------------------------------------------ */
+int rldx_layernorm(const void* in, int64_t ld_in, void* out, int64_t ld_out, int rows, int D,
+                   float eps, const void* scale1p, const void* shift, void* stream);
+
+/* ------------------------------------------------------------------------------------------
+ * Qwen3-style per-head RMSNorm + rotate-half RoPE on x [T, H, 128] -> y (may alias x).
+ *   pos [T] int32 rows of cos/sin [P, 128] bf16 tables; w [128] bf16.
+ * Replaces the QK-norm + RoPE stage of fused_llm_attention
+ * (rldx/inference/backbone/llm/engine/kernels/fused_llm_attention.py:100) and
+ * modeling_qwen3_vl.py:357-401 (rldx/model/modules/backbone).
+ * ------------------------------------------------------------------------------------------ */
+int rldx_qk_rmsnorm_rope(const void* x, void* y, const void* w, const int32_t* pos,
+                         const void* cos_table, const void* sin_table, int64_t tokens, int heads,
+                         int head_dim, float eps, void* stream);
+
+/* ------------------------------------------------------------------------------------------
+ * SwiGLU activation out[t,i] = silu(gate[t,i]) * up[t,i]  (H % 8 == 0).
+ * Replaces ds::grouped_swiglu's activation
+ * (rldx/inference/action_model/double_stream/engine/kernels/grouped_swiglu.py:108) and
+ * SwiGLUFFN.forward (rldx/model/modules/action_model/ops.py:157-161).
+ * ------------------------------------------------------------------------------------------ */
+int rldx_swiglu(const void* gate, const void* up, int64_t ld_in, void* out, int64_t ld_out,
+                int64_t rows, int H, void* stream);
+
+/* ------------------------------------------------------------------------------------------
+ * MSAT control step (all-modality action head): state encoder, physics history encoder, then
+ * num_steps flow-matching Euler steps of [action encoder + physics future encoder + depth
+ * ExpandedDoubleStreamBlocks over [VL | SA | P] + output projections + action / physics
+ * decoders + Euler updates], captured once as a single CUDA graph.
+ * Replaces CustomExpandedActionHeadChain.__init__/forward
+ * (rldx/inference/action_model/engine/custom_expanded_action_model_chain.py:19-213) and
+ * GraphSafeActionModel.forward (rldx/inference/action_model/model/graph_safe_action_model.py:170-312);
+ * semantics of RLDXActionModel.get_action_with_features (rldx/model/core/rldx.py:490-735)
+ * without RTC.
+ * ------------------------------------------------------------------------------------------ */
+typedef struct rldx_msat rldx_msat;
+
+#define RLDX_ROPE_SA_ONLY 0
+#define RLDX_ROPE_VL_SA 1
+
+typedef struct {
+  int batch;           /* observations per call                                          */
+  int n_vl;            /* cognition (VL) tokens per observation                          */
+  int n_state;         /* state tokens (1)                                               */
+  int horizon;         /* action tokens                                                  */
+  int physics_hist;    /* physics history tokens                                         */
+  int physics_fut;     /* physics future tokens (== horizon)                             */
+  int dim;             /* stream width: sa_dim == vl_dim == p_dim == heads * head_dim    */
+  int heads;
+  int head_dim;        /* 64                                                             */
+  int depth;           /* ExpandedDoubleStreamBlocks                                     */
+  int mlp_hidden;      /* SwiGLU hidden of the SA and P streams                          */
+  int vl_mlp_hidden;   /* SwiGLU hidden of the VL stream                                 */
+  int out_dim;         /* MSAT output_dim (= action decoder input)                       */
+  int action_dim;
+  int state_dim;
+  int dec_hidden;      /* action / state encoder hidden size                             */
+  int physics_dim;
+  int num_embodiments;
+  int num_steps;       /* Euler steps (t = i / num_steps, dt = 1 / num_steps)            */
+  int rope_mode;       /* RLDX_ROPE_*                                                    */
+  int rope_cos_only;   /* 1: RoPE buffers were cast to a real dtype (bf16 module) -> cos  */
+  float rope_theta;
+  int rope_max_seq;    /* RoPE table length (action_model_max_seq_len)                   */
+  int temb_channels;   /* Timesteps(num_channels) (256)                                  */
+  int use_graph;       /* 1: capture the whole control step as one CUDA graph            */
+} rldx_msat_config;
+
+typedef struct {
+  const void* w; /* nn.Linear weight [out, in] bf16 */
+  const void* b; /* [out] bf16 */
+} rldx_linear;
+
+typedef struct {
+  const void* W; /* CategorySpecificLinear.W [cats, in, out] bf16 */
+  const void* b; /* [cats, out] bf16 */
+} rldx_cat_linear;
+
+typedef struct {
+  rldx_linear qkv, proj, w12, w3; /* {sa,vl,p}_qkv / _proj / _mlp.w12 / _mlp.w3        */
+  const void* q_norm;             /* q_norm_{sa,vl,p}.weight [head_dim] bf16            */
+  const void* k_norm;
+} rldx_stream_weights;
+
+typedef struct {
+  rldx_stream_weights vl, sa, p;
+} rldx_block_weights;
+
+typedef struct {
+  const rldx_block_weights* blocks; /* [depth] (host array of device pointers)       */
+  rldx_linear temb_lin1, temb_lin2;  /* timestep_encoder.timestep_embedder.linear_1/2  */
+  rldx_linear time_token_proj;       /* w == NULL: identity                            */
+  rldx_linear proj_out_1, proj_out_2;
+  rldx_linear proj_out_phys_1, proj_out_phys_2;
+  rldx_cat_linear state_l1, state_l2;      /* state_encoder.layer1/2                    */
+  rldx_cat_linear act_w1, act_w2, act_w3;  /* action_encoder.W1/W2/W3                   */
+  rldx_cat_linear dec_l1, dec_l2;          /* action_decoder.layer1/2                   */
+  const void* pos_emb;                     /* position_embedding.weight [max, dim]      */
+  rldx_linear phc_w1, phc_w2, phc_w3;      /* physics.physics_cond_encoder.W1/W2/W3     */
+  rldx_linear phf_w1, phf_w2, phf_w3;      /* physics.physics_fut_encoder.W1/W2/W3      */
+  rldx_linear phd_l1, phd_l2;              /* physics.physics_decoder.net[0] / net[2]   */
+} rldx_msat_weights;
+
+typedef struct {
+  const void* vl;            /* [B, n_vl, dim] bf16                                     */
+  const void* state;         /* [B, n_state, state_dim] bf16                            */
+  const int64_t* emb_id;     /* [B] int64                                               */
+  const void* init_noise;    /* [B, horizon, action_dim] bf16                           */
+  const void* physics_hist;  /* [B, physics_hist, physics_dim] bf16                     */
+  const void* physics_noise; /* [B, physics_fut, physics_dim] bf16                      */
+  void* actions;             /* out: [B, horizon, action_dim] bf16                      */
+} rldx_msat_io;
+
+/* Copies and re-lays out the weights into a device arena owned by the handle, precomputes the
+ * step-constant tables (timestep embeddings, time tokens, AdaLN scale/shift, sinusoids, RoPE)
+ * and plans every launch.  Must be called outside stream capture with the device current. */
+int rldx_msat_create(const rldx_msat_config* cfg, const rldx_msat_weights* w, rldx_msat** out);
+int rldx_msat_destroy(rldx_msat* h);
+
+/* One control step on `stream`; io holds device pointers.  Asynchronous.  The first call
+ * captures the graph (when cfg.use_graph), so it must not itself run under stream capture. */
+int rldx_msat_step(rldx_msat* h, const rldx_msat_io* io, void* stream);
+
+/* One control step with io in host memory (pinned for full speed): host->device copies, the
+ * step, device->host copy of the actions, stream synchronize. */
+int rldx_msat_step_host(rldx_msat* h, const rldx_msat_io* io, void* stream);
+
+/* Number of kernel launches one control step performs (graph nodes when captured). */
+int rldx_msat_launch_count(const rldx_msat* h);
+
+typedef struct {
+  int kind;     /* 0 GEMM, 1 joint attention, 2 layernorm, 3 row copy                       */
+  int grid;     /* CTAs launched                                                            */
+  float ms;     /* device time between CUDA events recorded around the launch               */
+  double bytes; /* algorithmic HBM bytes: every operand read once, every result written once */
+  double flops; /* algorithmic FLOPs (2*M*N*K per GEMM problem, 4*L*L*64 per attention head) */
+} rldx_op_profile;
+
+/* Runs one control step eagerly (no graph, no programmatic overlap) with a CUDA event pair
+ * around every launch; fills up to max_ops entries, sets *n_ops and synchronizes `stream`. */
+int rldx_msat_profile(rldx_msat* h, const rldx_msat_io* io, rldx_op_profile* ops, int max_ops,
+                      int* n_ops, void* stream);
+
+/* Copies an intermediate buffer of the last control step into dst (device or host memory,
+ * dst_bytes large enough) on `stream`: 0 X_vl, 1 X_sa, 2 X_p (streams after the last block of
+ * the last Euler step), 3 the action state.  With dst == NULL only *rows / *cols are set. */
+int rldx_msat_read_buffer(const rldx_msat* h, int which, void* dst, int64_t dst_bytes,
+                          int64_t* rows, int64_t* cols, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* RLDX_B200_H_ */

@@ -1,0 +1,33 @@
+// Host-side helpers shared by the C-ABI entry points and the MSAT runtime.
+#pragma once
+#include <string>
+
+#include "../../include/rldx_b200.h"
+#include "kernels.cuh"
+
+namespace rldx {
+
+// Records the message returned by rldx_last_error() and returns `code`.
+int set_error(int code, const std::string& msg);
+int cuda_fail(cudaError_t e, const char* what);
+
+// Makes sure the current device is sm_100 and kernel attributes are set (once per device).
+int ensure_device();
+
+// 2D / 3D bf16 tensor maps with 128-byte swizzle; box inner extent is 64 elements (128 bytes).
+bool make_tmap_2d(CUtensorMap* m, const void* base, uint64_t inner, uint64_t rows,
+                  uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_rows,
+                  std::string* err);
+bool make_tmap_3d(CUtensorMap* m, const void* base, uint64_t d0, uint64_t d1, uint64_t d2,
+                  uint64_t stride1_bytes, uint64_t stride2_bytes, uint32_t b0, uint32_t b1,
+                  uint32_t b2, std::string* err);
+
+// Validates one GEMM description and fills the device problem (tile choice included).
+bool build_gemm_problem(const rldx_gemm_desc& d, GemmProblem* p, std::string* err);
+// Packs up to kMaxProblems problems into one launch; returns the grid size in *tiles.
+bool build_gemm_params(const rldx_gemm_desc* d, int n, GemmParams* params, int* tiles,
+                       std::string* err);
+
+int sm_count();
+
+}  // namespace rldx

@@ -1,0 +1,80 @@
+// Launch parameters and host launchers of every kernel in the library.
+#pragma once
+#include "gemm.cuh"
+
+namespace rldx {
+
+// ---- joint attention (attention.cu) ----
+struct AttnParams {
+  CUtensorMap tq;  // [B*H, L, 64], box (64, 128, 1)
+  CUtensorMap tk;  // [B*H, L, 64], box (64, 64, 1)
+  CUtensorMap tv;  // [B*H, 64, Lp] (V transposed), box (64 keys, 64 dims, 1)
+  int L, H, B;
+  const unsigned char* key_mask;  // [B, L] (1 = visible) or null
+  __nv_bfloat16* seg_out[3];      // per-stream outputs [B * seg_len, H*64]
+  int seg_len[3];
+  int nseg;
+  float scale_log2;  // log2(e) / sqrt(head_dim)
+};
+size_t attention_smem_bytes();
+cudaError_t attention_prepare_device();
+cudaError_t launch_attention(const AttnParams& p, cudaStream_t stream, bool pdl);
+
+// ---- row kernels (rownorm.cu) ----
+struct LnSegment {
+  const __nv_bfloat16* in;
+  __nv_bfloat16* out;
+  const __nv_bfloat16* scale1p;  // optional [D]: (1 + scale), bf16
+  const __nv_bfloat16* shift;    // optional [D]
+  int rows, ld_in, ld_out, row_begin;
+};
+constexpr int kMaxLnSegments = 4;
+struct LnParams {
+  LnSegment seg[kMaxLnSegments];
+  int nseg;
+  int D;
+  int total_rows;
+  float eps;
+};
+cudaError_t launch_ln(const LnParams& p, cudaStream_t stream, bool pdl);
+
+// Row copy: row i -> group g = i / group_rows, r = i % group_rows (group_rows 0: g = 0, r = i);
+// src + g*src_group_pitch + r*src_pitch -> dst + g*dst_group_pitch + r*dst_pitch.
+struct CopyRegion {
+  const uint8_t* src;
+  uint8_t* dst;
+  long long src_pitch, dst_pitch;
+  long long src_group_pitch, dst_group_pitch;
+  int group_rows;
+  int rows, bytes;  // bytes % 16 == 0
+};
+constexpr int kMaxCopyRegions = 8;
+struct CopyParams {
+  CopyRegion r[kMaxCopyRegions];
+  int n;
+};
+cudaError_t launch_copy(const CopyParams& p, int blocks, cudaStream_t stream, bool pdl);
+
+cudaError_t launch_qk_rmsnorm_rope(const __nv_bfloat16* x, __nv_bfloat16* y, const __nv_bfloat16* w,
+                                   const int* pos, const __nv_bfloat16* cos_t,
+                                   const __nv_bfloat16* sin_t, long long nrows, int heads,
+                                   float eps, cudaStream_t stream);
+cudaError_t launch_swiglu(const __nv_bfloat16* gate, const __nv_bfloat16* up, __nv_bfloat16* out,
+                          long long rows, int H, long long ld_in, long long ld_out, int sms,
+                          cudaStream_t stream);
+
+// ---- bind-time helpers (relayout.cu) ----
+// dst[i, :] = src[idx[i], :] for rows of `cols` bf16 (row gather).
+cudaError_t launch_gather_rows(const __nv_bfloat16* src, long long ld_src, __nv_bfloat16* dst,
+                               long long ld_dst, const int* idx, int rows, int cols,
+                               cudaStream_t stream);
+// dst[c, n, k] = src[c, k, n] (per-category transpose), zero-padding k in [K, Kp).
+cudaError_t launch_transpose_cat(const __nv_bfloat16* src, __nv_bfloat16* dst, int cats, int K,
+                                 int N, int Kp, cudaStream_t stream);
+// y = silu(x) (mode 0) or y = 1 + x (mode 1), bf16 rounding once.
+cudaError_t launch_elementwise(const __nv_bfloat16* x, __nv_bfloat16* y, long long n, int mode,
+                               cudaStream_t stream);
+
+cudaError_t gemm_prepare_device();
+
+}  // namespace rldx

@@ -1,0 +1,7 @@
+// Single translation unit of librldx_b200.so: every kernel and the C ABI.
+#include "gemm.cu"
+#include "attention.cu"
+#include "rownorm.cu"
+#include "relayout.cu"
+#include "capi.cu"
+#include "msat.cu"

@@ -1,0 +1,196 @@
+"""Torch-facing wrappers of the per-op C-ABI entry points (device tensors in, device tensors out).
+
+Each wrapper validates dtype/device/contiguity on the host, passes raw pointers to
+librldx_b200.so on the current CUDA stream and raises RldxError on any failure.  They are what
+the unit tests and the op-level drop-ins call; the control-step path runs inside the native
+runtime (chain.py) instead.
+"""
+
+from __future__ import annotations
+
+import ctypes as C
+from typing import Optional, Sequence
+
+import torch
+
+from . import _lib
+from ._lib import GemmDesc, check, load
+
+
+def _p(t: Optional[torch.Tensor]):
+    return None if t is None else C.c_void_p(t.data_ptr())
+
+
+def _stream():
+    return C.c_void_p(torch.cuda.current_stream().cuda_stream)
+
+
+def _need(t: torch.Tensor, name: str, dtype=torch.bfloat16):
+    if not isinstance(t, torch.Tensor):
+        raise TypeError(f"{name} must be a tensor")
+    if not t.is_cuda:
+        raise ValueError(f"{name} must be a CUDA tensor (no CPU path exists)")
+    if t.dtype != dtype:
+        raise TypeError(f"{name} must be {dtype}, got {t.dtype}")
+
+
+def _row_major(t: torch.Tensor, name: str) -> int:
+    if t.dim() != 2 or t.stride(1) != 1:
+        raise ValueError(f"{name} must be a 2-D row-major view")
+    return t.stride(0)
+
+
+def gemm_desc(
+    x: torch.Tensor,
+    weight: torch.Tensor,
+    out: torch.Tensor,
+    bias: Optional[torch.Tensor] = None,
+    *,
+    bias_mode: int = _lib.BIAS_FUSED,
+    act: int = _lib.ACT_NONE,
+    add: Optional[torch.Tensor] = None,
+    add_row_mod: int = 0,
+    epilogue: int = _lib.EPI_STORE,
+    rows_in: int = 0,
+    rows_out: int = 0,
+    row_skip: int = 0,
+    dt: float = 0.0,
+    cat_ids: Optional[torch.Tensor] = None,
+    rows_per_cat: int = 0,
+    col_off: int = 0,
+    tile_n: int = 0,
+) -> GemmDesc:
+    """Describes out = epilogue(x @ weight^T).  weight is [N, K] or [cats, N, K] (with cat_ids)."""
+    _need(x, "x")
+    _need(weight, "weight")
+    _need(out, "out")
+    lda = _row_major(x, "x")
+    M, K = x.shape
+    d = GemmDesc()
+    d.a, d.lda, d.M, d.K = x.data_ptr(), lda, M, K
+    d.b = weight.data_ptr()
+    if cat_ids is not None:
+        if weight.dim() != 3 or not weight.is_contiguous():
+            raise ValueError("category weight must be a contiguous [cats, N, K] tensor")
+        _need(cat_ids, "cat_ids", torch.int64)
+        d.cat_ids, d.rows_per_cat, d.num_cats = cat_ids.data_ptr(), rows_per_cat, weight.shape[0]
+        d.N, d.ldb, d.b_cat_stride = weight.shape[1], weight.shape[2], weight.shape[1] * weight.shape[2]
+        if bias is not None:
+            d.bias_cat_stride = bias.shape[-1]
+    else:
+        d.ldb = _row_major(weight, "weight")
+        d.N = weight.shape[0]
+    if bias is not None:
+        _need(bias, "bias")
+        d.bias, d.bias_mode = bias.data_ptr(), bias_mode
+    d.act = act
+    if add is not None:
+        _need(add, "add")
+        d.add, d.ld_add, d.add_row_mod = add.data_ptr(), _row_major(add, "add"), add_row_mod
+    d.out, d.ldo, d.col_off = out.data_ptr(), _row_major(out, "out"), col_off
+    d.epilogue, d.rows_in, d.rows_out, d.row_skip, d.dt = epilogue, rows_in, rows_out, row_skip, dt
+    d.eps = 1e-6
+    d.tile_n = tile_n
+    return d
+
+
+def gemm(descs: Sequence[GemmDesc]) -> None:
+    """Runs 1..4 GEMM problems in one grouped launch on the current stream."""
+    arr = (GemmDesc * len(descs))(*descs)
+    check(load().rldx_gemm(arr, len(descs), _stream()))
+
+
+def linear(x, weight, bias=None, *, act=_lib.ACT_NONE, bias_mode=_lib.BIAS_FUSED, add=None,
+           out=None, tile_n=0) -> torch.Tensor:
+    """nn.Linear (+activation, +residual) through the tcgen05 GEMM."""
+    if out is None:
+        out = torch.empty(x.shape[0], weight.shape[0], dtype=torch.bfloat16, device=x.device)
+    gemm([gemm_desc(x, weight, out, bias, bias_mode=bias_mode, act=act, add=add, tile_n=tile_n)])
+    return out
+
+
+def qkv_desc(x, weight, bias, q_norm, k_norm, rope_cos, rope_sin, q, k, vt, *, tok_off: int,
+             rows_per_batch: int, tile_n: int = 0) -> GemmDesc:
+    """QKV projection of one stream with fused per-head RMSNorm + RoPE, scattered into the joint
+    attention layout q, k [B, H, L, 64] and vt [B, H, 64, Lp]."""
+    B, H, L, hd = q.shape
+    if hd != 64:
+        raise ValueError("head_dim must be 64")
+    d = gemm_desc(x, weight, q.view(-1, 64), bias, epilogue=_lib.EPI_QKV, rows_in=rows_per_batch,
+                  rows_out=rows_per_batch, tile_n=tile_n)
+    _need(q_norm, "q_norm")
+    _need(k_norm, "k_norm")
+    _need(rope_cos, "rope_cos", torch.float32)
+    _need(rope_sin, "rope_sin", torch.float32)
+    d.q_norm_w, d.k_norm_w = q_norm.data_ptr(), k_norm.data_ptr()
+    d.rope_cos, d.rope_sin = rope_cos.data_ptr(), rope_sin.data_ptr()
+    d.q, d.k, d.vt = q.data_ptr(), k.data_ptr(), vt.data_ptr()
+    d.L, d.Lp, d.H, d.tok_off = L, vt.shape[-1], H, tok_off
+    return d
+
+
+def joint_attention(q, k, vt, seg_lens: Sequence[int], key_mask=None, outs=None):
+    """Non-causal joint attention over concatenated segments; returns one output per segment
+    as [B * seg_len, H * 64]."""
+    for t, n in ((q, "q"), (k, "k"), (vt, "vt")):
+        _need(t, n)
+        if not t.is_contiguous():
+            raise ValueError(f"{n} must be contiguous")
+    B, H, L, _ = q.shape
+    Lp = vt.shape[-1]
+    if outs is None:
+        outs = [torch.empty(B * n, H * 64, dtype=torch.bfloat16, device=q.device) for n in seg_lens]
+    ptrs = (C.c_void_p * len(outs))(*[o.data_ptr() for o in outs])
+    lens = (C.c_int * len(seg_lens))(*seg_lens)
+    if key_mask is not None:
+        _need(key_mask, "key_mask", torch.uint8)
+    check(load().rldx_joint_attention(_p(q), _p(k), _p(vt), B, H, L, Lp, _p(key_mask), ptrs, lens,
+                                      len(seg_lens), _stream()))
+    return outs
+
+
+def layernorm(x, eps: float = 1e-6, scale1p=None, shift=None, out=None):
+    """LayerNorm without affine (optionally * scale1p + shift) over the last dim of [rows, D]."""
+    _need(x, "x")
+    ld = _row_major(x, "x")
+    if out is None:
+        out = torch.empty_like(x)
+    check(load().rldx_layernorm(_p(x), ld, _p(out), _row_major(out, "out"), x.shape[0], x.shape[1],
+                                eps, _p(scale1p), _p(shift), _stream()))
+    return out
+
+
+def qk_rmsnorm_rope(x, weight, pos, cos_table, sin_table, eps: float = 1e-6, out=None):
+    """Qwen3-style per-head RMSNorm + rotate-half RoPE on [T, H, 128]."""
+    _need(x, "x")
+    _need(pos, "pos", torch.int32)
+    if not x.is_contiguous() or x.dim() != 3:
+        raise ValueError("x must be contiguous [T, H, head_dim]")
+    if out is None:
+        out = torch.empty_like(x)
+    T, Hh, hd = x.shape
+    check(load().rldx_qk_rmsnorm_rope(_p(x), _p(out), _p(weight), _p(pos), _p(cos_table),
+                                      _p(sin_table), T, Hh, hd, eps, _stream()))
+    return out
+
+
+def swiglu(gate, up, out=None):
+    """silu(gate) * up for [rows, H] views (gate / up may be halves of one [rows, 2H] tensor)."""
+    _need(gate, "gate")
+    _need(up, "up")
+    ld_g, ld_u = _row_major(gate, "gate"), _row_major(up, "up")
+    if ld_g != ld_u:
+        raise ValueError("gate and up must share a row stride")
+    rows, H = gate.shape
+    if out is None:
+        out = torch.empty(rows, H, dtype=torch.bfloat16, device=gate.device)
+    check(load().rldx_swiglu(_p(gate), _p(up), ld_g, _p(out), _row_major(out, "out"), rows, H,
+                             _stream()))
+    return out
+
+
+def device_error() -> int:
+    """Reads and clears the device-side error word (synchronizes)."""
+    v = C.c_uint(0)
+    check(load().rldx_get_device_error(C.byref(v)))
+    return int(v.value)

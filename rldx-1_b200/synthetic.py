@@ -1,0 +1,112 @@
+"""Seeded random-init action-head weights laid out like the reference module tree.
+
+The benchmark and smoke paths have no checkpoint (none is shipped and there is no network),
+so they bind B200ExpandedActionHeadChain to this namespace tree: the same attribute names and
+tensor shapes as RLDXActionModel's inference sub-modules (rldx/model/core/rldx.py:43-106 with
+use_physics=True), bf16 tensors created directly on the GPU.  Linear / category weights and
+biases ~ N(0, std), QK-RMSNorm scales ~ 1 + N(0, std).
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass
+from types import SimpleNamespace as NS
+
+import torch
+from torch import nn
+
+
+@dataclass
+class HeadDims:
+    """full MSAT action decoder, 16 blocks, hidden 1536, 24 x 64 heads."""
+
+    n_vl: int = 512
+    n_state: int = 1
+    horizon: int = 16
+    physics_hist: int = 16
+    physics_fut: int = 16
+    dim: int = 1536
+    heads: int = 24
+    depth: int = 16
+    mlp_hidden: int = 4096
+    vl_mlp_hidden: int = 4096
+    out_dim: int = 1024
+    action_dim: int = 32
+    state_dim: int = 64
+    dec_hidden: int = 1024
+    physics_dim: int = 37
+    num_embodiments: int = 36
+    num_steps: int = 4
+    rope_theta: float = 10000.0
+    rope_max_seq: int = 1024
+    pos_emb_len: int = 1024
+
+    @property
+    def tokens(self) -> int:
+        return self.n_vl + 1 + self.n_state + self.horizon + self.physics_hist + self.physics_fut
+
+
+def random_action_head(d: HeadDims, seed: int = 0, device="cuda", std: float = 0.02,
+                       cos_only_rope: bool = True) -> NS:
+    g = torch.Generator(device=device).manual_seed(seed)
+    bf = torch.bfloat16
+
+    def rnd(*shape, mean=0.0):
+        return (torch.randn(*shape, generator=g, device=device) * std + mean).to(bf)
+
+    def lin(i, o):
+        return NS(weight=rnd(o, i), bias=rnd(o))
+
+    def cat(i, o):
+        return NS(W=rnd(d.num_embodiments, i, o), b=rnd(d.num_embodiments, o))
+
+    blocks = []
+    for _ in range(d.depth):
+        b = NS(num_heads=d.heads)
+        for s, hid in (("sa", d.mlp_hidden), ("vl", d.vl_mlp_hidden), ("p", d.mlp_hidden)):
+            setattr(b, f"{s}_qkv", lin(d.dim, 3 * d.dim))
+            setattr(b, f"{s}_proj", lin(d.dim, d.dim))
+            setattr(b, f"{s}_mlp", NS(w12=lin(d.dim, 2 * hid), w3=lin(hid, d.dim)))
+            setattr(b, f"q_norm_{s}", NS(weight=rnd(64, mean=1.0)))
+            setattr(b, f"k_norm_{s}", NS(weight=rnd(64, mean=1.0)))
+        blocks.append(b)
+    rope_table = torch.zeros(d.rope_max_seq, 8, dtype=bf if cos_only_rope else torch.complex64, device=device)
+    msat = NS(
+        double_blocks=blocks, single_blocks=[], temb_type="input_token",
+        positional_embeddings="rope_sa_only", time_token_proj=nn.Identity(),
+        timestep_encoder=NS(timestep_embedder=NS(linear_1=lin(256, d.dim), linear_2=lin(d.dim, d.dim))),
+        rope_embedder=NS(freqs_cis_0=rope_table, theta=d.rope_theta),
+        proj_out_1=lin(d.dim, 2 * d.dim), proj_out_2=lin(d.dim, d.out_dim),
+        proj_out_physics_1=lin(d.dim, 2 * d.dim), proj_out_physics_2=lin(d.dim, d.out_dim))
+
+    def enc():
+        return NS(W1=lin(d.physics_dim, d.dim), W2=lin(2 * d.dim, d.dim), W3=lin(d.dim, d.dim))
+
+    return NS(
+        model=msat,
+        state_encoder=NS(layer1=cat(d.state_dim, d.dec_hidden), layer2=cat(d.dec_hidden, d.dim)),
+        action_encoder=NS(W1=cat(d.action_dim, d.dim), W2=cat(2 * d.dim, d.dim), W3=cat(d.dim, d.dim)),
+        action_decoder=NS(layer1=cat(d.out_dim, d.dec_hidden), layer2=cat(d.dec_hidden, d.action_dim)),
+        position_embedding=NS(weight=rnd(d.pos_emb_len, d.dim)),
+        physics=NS(physics_cond_encoder=enc(), physics_fut_encoder=enc(),
+                   physics_decoder=NS(net=[lin(d.out_dim, d.dim), None, lin(d.dim, d.physics_dim)]),
+                   physics_hist_len=d.physics_hist, physics_fut_len=d.physics_fut,
+                   physics_dim=d.physics_dim),
+        vlln=nn.Identity(), num_inference_timesteps=d.num_steps, action_horizon=d.horizon)
+
+
+def random_inputs(d: HeadDims, batch: int, seed: int = 42, device="cuda", pin: bool = False) -> dict:
+    """BASELINE config 2 inputs: vl ~ N(0,1), state * 0.01, physics ~ N(0,1), noise ~ N(0,1)."""
+    g = torch.Generator(device="cpu").manual_seed(seed)
+    bf = torch.bfloat16
+    t = {
+        "vl": torch.randn(batch, d.n_vl, d.dim, generator=g).to(bf),
+        "state": (torch.randn(batch, d.n_state, d.state_dim, generator=g) * 0.01).to(bf),
+        "embodiment_id": torch.zeros(batch, dtype=torch.int64),
+        "init_noise": torch.randn(batch, d.horizon, d.action_dim, generator=g).to(bf),
+        "physics_hist": torch.randn(batch, d.physics_hist, d.physics_dim, generator=g).to(bf),
+        "physics_noise": torch.randn(batch, d.physics_fut, d.physics_dim, generator=g).to(bf),
+    }
+    if device == "cpu":
+        return {k: (v.pin_memory() if pin else v) for k, v in t.items()}
+    return {k: v.to(device) for k, v in t.items()}

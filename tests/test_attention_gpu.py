@@ -1,0 +1,55 @@
+"""tcgen05 joint attention vs a plain PyTorch fp32 softmax attention of the same inputs."""
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+import rldx_b200  # noqa: E402,F401
+from rldx_b200 import ops  # noqa: E402
+
+BF = torch.bfloat16
+
+
+def run_case(cuda, B, H, segs, mask=False, seed=0):
+    L = sum(segs)
+    Lp = (L + 7) // 8 * 8
+    g = torch.Generator(device=cuda).manual_seed(seed)
+    q = torch.randn(B, H, L, 64, device=cuda, generator=g).to(BF)
+    k = torch.randn(B, H, L, 64, device=cuda, generator=g).to(BF)
+    v = torch.randn(B, H, L, 64, device=cuda, generator=g).to(BF)
+    vt = torch.zeros(B, H, 64, Lp, dtype=BF, device=cuda)
+    vt[..., :L] = v.transpose(-1, -2)
+    key_mask = None
+    bias = torch.zeros(B, 1, 1, L, device=cuda)
+    if mask:
+        key_mask = (torch.rand(B, L, device=cuda, generator=g) > 0.3).to(torch.uint8)
+        key_mask[:, segs[0]:] = 1  # the action stream is always visible (blocks.py:852)
+        bias = torch.where(key_mask.bool(), 0.0, float("-inf"))[:, None, None, :]
+    outs = ops.joint_attention(q, k, vt, segs, key_mask=key_mask)
+    torch.cuda.synchronize()
+    s = (q.float() @ k.float().transpose(-1, -2)) / 8.0 + bias
+    ref = torch.softmax(s, dim=-1) @ v.float()  # [B, H, L, 64]
+    ref = ref.permute(0, 2, 1, 3).reshape(B, L, H * 64)
+    off = 0
+    for o, n in zip(outs, segs):
+        exp = ref[:, off:off + n].reshape(B * n, H * 64)
+        err = (o.float() - exp).abs().max().item()
+        assert err < 2e-2, f"segment at {off}: max err {err}"
+        off += n
+    assert ops.device_error() == 0
+
+
+@pytest.mark.parametrize("segs", [[1], [5], [64], [65], [127, 1], [128], [129], [256, 16, 16],
+                                  [512, 18, 32], [1000, 48]])
+def test_joint_attention_lengths(cuda, segs):
+    run_case(cuda, 1, 2, segs, seed=len(segs) + sum(segs))
+
+
+@pytest.mark.parametrize("B,H", [(2, 3), (3, 24)])
+def test_joint_attention_batched(cuda, B, H):
+    run_case(cuda, B, H, [200, 18, 32], seed=B * 100 + H)
+
+
+def test_joint_attention_key_mask(cuda):
+    run_case(cuda, 2, 4, [96, 18, 32], mask=True, seed=7)

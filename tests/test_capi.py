@@ -1,0 +1,46 @@
+"""C-ABI surface (CPU only): the library loads and exports every function that
+include/rldx_b200.h declares, and the ctypes mirrors match the header's structs."""
+
+import ctypes as C
+import re
+from pathlib import Path
+
+import rldx_b200  # noqa: F401
+from rldx_b200 import _lib
+
+HEADER = Path(__file__).resolve().parents[1] / "include" / "rldx_b200.h"
+
+
+def declared_functions():
+    text = HEADER.read_text()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"^\s*(?:const\s+)?\w+\*?\s+\*?(rldx_\w+)\s*\(", text, flags=re.M)))
+
+
+def test_every_declared_symbol_is_exported(lib):
+    names = declared_functions()
+    assert len(names) >= 14
+    for n in names:
+        assert hasattr(lib, n), f"{n} declared in rldx_b200.h but not exported"
+        assert n in _lib.SIGNATURES, f"{n} has no ctypes signature"
+
+
+def test_version_and_error_string(lib):
+    assert lib.rldx_version() == 100
+    assert isinstance(lib.rldx_last_error(), bytes)
+
+
+def test_struct_layouts_match_header():
+    # sizes of the C structs as laid out by the C compiler on this ABI (x86-64 / aarch64 LP64)
+    assert C.sizeof(_lib.GemmDesc) == 248
+    assert C.sizeof(_lib.MsatConfig) == 25 * 4
+    assert C.sizeof(_lib.MsatIO) == 7 * 8
+    assert C.sizeof(_lib.BlockWeights) == 3 * (4 * 16 + 16)
+
+
+def test_null_arguments_are_rejected_without_a_device(lib):
+    # argument validation happens before any device work
+    assert lib.rldx_get_device_error(None) == _lib.RLDX_ERR_ARG
+    assert lib.rldx_msat_step(None, None, None) == _lib.RLDX_ERR_ARG
+    assert lib.rldx_msat_create(None, None, None) == _lib.RLDX_ERR_ARG
+    assert lib.rldx_msat_destroy(None) == _lib.RLDX_OK

@@ -1,0 +1,188 @@
+"""tcgen05 grouped GEMM vs a plain PyTorch fp32 reference of the same op (same bf16 rounding
+points), across tile widths, ragged M/N/K, every epilogue and the category-weight path."""
+
+import pytest
+import torch
+import torch.nn.functional as F
+
+pytestmark = pytest.mark.gpu
+
+import rldx_b200  # noqa: E402,F401
+from rldx_b200 import _lib, ops  # noqa: E402
+
+BF = torch.bfloat16
+
+
+def r(x):
+    return x.to(BF).float()
+
+
+def ref_finish(acc, b, bias_mode, act):
+    if bias_mode == _lib.BIAS_FUSED:
+        y = r(acc + b.float())
+    elif bias_mode == _lib.BIAS_POST_ROUND:
+        y = r(r(acc) + b.float())
+    else:
+        y = r(acc)
+    if act == _lib.ACT_RELU:
+        y = torch.relu(y)
+    elif act == _lib.ACT_SILU:
+        y = r(F.silu(y))
+    elif act == _lib.ACT_SWISH:
+        y = r(y * r(torch.sigmoid(y)))
+    return y
+
+
+def close(out, ref, tol=2e-2):
+    out = out.float()
+    scale = ref.abs().max().clamp_min(1e-3)
+    err = (out - ref).abs().max()
+    assert err <= tol * scale, f"max err {err.item():.4g} vs scale {scale.item():.4g}"
+    # bf16 rounding of an fp32 sum in another order: almost every element is exact or 1 ulp off
+    bad = ((out - ref).abs() > 2 ** -7 * ref.abs() + 1e-3 * scale).float().mean()
+    assert bad < 0.01, f"{bad.item():.3%} elements beyond 1 ulp"
+
+
+SHAPES = [(1, 64, 64), (18, 4608, 1536), (32, 1536, 4096), (128, 128, 64), (200, 300, 136),
+          (512, 4608, 1536), (17, 37, 1024), (300, 1000, 40)]
+
+
+@pytest.mark.parametrize("M,N,K", SHAPES)
+@pytest.mark.parametrize("tile_n", [0, 64, 128, 256])
+def test_linear_fused_bias(cuda, M, N, K, tile_n):
+    g = torch.Generator(device=cuda).manual_seed(M * 7 + N + K)
+    x = torch.randn(M, K, device=cuda, generator=g).to(BF)
+    w = (torch.randn(N, K, device=cuda, generator=g) * 0.05).to(BF)
+    b = (torch.randn(N, device=cuda, generator=g) * 0.1).to(BF)
+    out = ops.linear(x, w, b, tile_n=tile_n)
+    torch.cuda.synchronize()
+    ref = ref_finish(x.float() @ w.float().t(), b, _lib.BIAS_FUSED, _lib.ACT_NONE)
+    close(out, ref)
+    assert ops.device_error() == 0
+
+
+@pytest.mark.parametrize("act", [_lib.ACT_RELU, _lib.ACT_SILU, _lib.ACT_SWISH])
+@pytest.mark.parametrize("bias_mode", [_lib.BIAS_NONE, _lib.BIAS_FUSED, _lib.BIAS_POST_ROUND])
+def test_activation_and_bias_modes(cuda, act, bias_mode):
+    g = torch.Generator(device=cuda).manual_seed(act * 10 + bias_mode)
+    M, N, K = 48, 320, 256
+    x = torch.randn(M, K, device=cuda, generator=g).to(BF)
+    w = (torch.randn(N, K, device=cuda, generator=g) * 0.1).to(BF)
+    b = (torch.randn(N, device=cuda, generator=g) * 0.5).to(BF)
+    out = ops.linear(x, w, b if bias_mode else None, act=act, bias_mode=bias_mode)
+    torch.cuda.synchronize()
+    close(out, ref_finish(x.float() @ w.float().t(), b, bias_mode, act))
+
+
+def test_residual_add_in_place(cuda):
+    g = torch.Generator(device=cuda).manual_seed(3)
+    M, N, K = 530, 1536, 1536
+    x = torch.randn(M, K, device=cuda, generator=g).to(BF)
+    w = (torch.randn(N, K, device=cuda, generator=g) * 0.03).to(BF)
+    b = (torch.randn(N, device=cuda, generator=g) * 0.1).to(BF)
+    res = torch.randn(M, N, device=cuda, generator=g).to(BF)
+    expect = r(ref_finish(x.float() @ w.float().t(), b, _lib.BIAS_FUSED, 0) + res.float())
+    ops.linear(x, w, b, add=res, out=res)  # residual updated in place, like the MSAT blocks
+    torch.cuda.synchronize()
+    close(res, expect)
+
+
+def test_swiglu_epilogue(cuda):
+    """w12 rows interleaved in groups of [32 gate | 32 up]: out = silu(g) * u."""
+    g = torch.Generator(device=cuda).manual_seed(5)
+    M, D, Hd = 70, 512, 384
+    x = torch.randn(M, D, device=cuda, generator=g).to(BF)
+    w12 = (torch.randn(2 * Hd, D, device=cuda, generator=g) * 0.05).to(BF)
+    b12 = (torch.randn(2 * Hd, device=cuda, generator=g) * 0.1).to(BF)
+    idx = torch.cat([torch.cat([torch.arange(gi * 32, gi * 32 + 32), Hd + torch.arange(gi * 32, gi * 32 + 32)])
+                     for gi in range(Hd // 32)]).to(cuda)
+    out = torch.empty(M, Hd, dtype=BF, device=cuda)
+    ops.gemm([ops.gemm_desc(x, w12[idx].contiguous(), out, b12[idx].contiguous(), epilogue=_lib.EPI_SWIGLU)])
+    torch.cuda.synchronize()
+    y = r(x.float() @ w12.float().t() + b12.float())
+    x1, x2 = y.chunk(2, dim=-1)
+    close(out, r(r(F.silu(x1)) * x2))
+
+
+def test_category_weights_and_euler(cuda):
+    """Per-batch category slabs (CategorySpecificLinear) + Euler update with row remap."""
+    g = torch.Generator(device=cuda).manual_seed(9)
+    cats, B, rows, K, N = 5, 3, 18, 1024, 32
+    x = torch.randn(B * rows, K, device=cuda, generator=g).to(BF)
+    W = (torch.randn(cats, K, N, device=cuda, generator=g) * 0.05).to(BF)  # reference layout
+    bb = (torch.randn(cats, N, device=cuda, generator=g) * 0.1).to(BF)
+    ids = torch.tensor([4, 0, 2], device=cuda, dtype=torch.int64)
+    state = torch.randn(B * 16, N, device=cuda, generator=g).to(BF)
+    expect = state.float().clone()
+    Wt = W.transpose(1, 2).contiguous()  # [cats, N, K]
+    d = ops.gemm_desc(x, Wt, state, bb, bias_mode=_lib.BIAS_POST_ROUND, cat_ids=ids, rows_per_cat=rows,
+                      epilogue=_lib.EPI_EULER, rows_in=rows, rows_out=16, row_skip=2, dt=0.25)
+    ops.gemm([d])
+    torch.cuda.synchronize()
+    for bi in range(B):
+        c = int(ids[bi])
+        v = r(r(x[bi * rows:(bi + 1) * rows].float() @ W[c].float()) + bb[c].float())
+        v = v[2:]
+        expect[bi * 16:(bi + 1) * 16] = r(expect[bi * 16:(bi + 1) * 16] + r(0.25 * v))
+    close(state, expect)
+
+
+def test_grouped_three_streams(cuda):
+    """Three independent problems of very different shape in one launch."""
+    g = torch.Generator(device=cuda).manual_seed(11)
+    descs, refs, outs = [], [], []
+    for M in (512, 18, 32):
+        x = torch.randn(M, 1536, device=cuda, generator=g).to(BF)
+        w = (torch.randn(1536, 1536, device=cuda, generator=g) * 0.03).to(BF)
+        b = (torch.randn(1536, device=cuda, generator=g) * 0.1).to(BF)
+        o = torch.empty(M, 1536, dtype=BF, device=cuda)
+        descs.append(ops.gemm_desc(x, w, o, b))
+        refs.append(ref_finish(x.float() @ w.float().t(), b, _lib.BIAS_FUSED, 0))
+        outs.append(o)
+    ops.gemm(descs)
+    torch.cuda.synchronize()
+    for o, ref in zip(outs, refs):
+        close(o, ref)
+
+
+def test_qkv_epilogue_rmsnorm_rope_layout(cuda):
+    """QKV + per-head RMSNorm (weight then cast) + interleaved RoPE, scattered into q/k
+    [B, H, L, 64] and v^T [B, H, 64, Lp] at the stream's token offset."""
+    g = torch.Generator(device=cuda).manual_seed(13)
+    B, H, D, n, L, tok_off = 2, 4, 256, 18, 50, 20
+    Lp = 56
+    x = torch.randn(B * n, D, device=cuda, generator=g).to(BF)
+    w = (torch.randn(3 * H * 64, D, device=cuda, generator=g) * 0.05).to(BF)
+    b = (torch.randn(3 * H * 64, device=cuda, generator=g) * 0.1).to(BF)
+    qn = (1 + 0.1 * torch.randn(64, device=cuda, generator=g)).to(BF)
+    kn = (1 + 0.1 * torch.randn(64, device=cuda, generator=g)).to(BF)
+    ang = torch.rand(L, 32, device=cuda, generator=g) * 6.28
+    cos, sin = torch.cos(ang).contiguous(), torch.sin(ang).contiguous()
+    q = torch.zeros(B, H, L, 64, dtype=BF, device=cuda)
+    k = torch.zeros_like(q)
+    vt = torch.zeros(B, H, 64, Lp, dtype=BF, device=cuda)
+    ops.gemm([ops.qkv_desc(x, w, b, qn, kn, cos, sin, q, k, vt, tok_off=tok_off, rows_per_batch=n)])
+    torch.cuda.synchronize()
+    y = r(x.float() @ w.float().t() + b.float()).view(B, n, 3, H, 64).permute(2, 0, 3, 1, 4)
+
+    def norm_rope(t, wn):
+        tn = r(wn.float() * (t * torch.rsqrt(t.pow(2).mean(-1, keepdim=True) + 1e-6)))
+        c = cos[tok_off:tok_off + n][None, None]
+        s = sin[tok_off:tok_off + n][None, None]
+        a, bb = tn[..., 0::2], tn[..., 1::2]
+        outr = torch.stack([a * c - bb * s, a * s + bb * c], dim=-1).flatten(-2)
+        return r(outr)
+
+    close(q[:, :, tok_off:tok_off + n], norm_rope(y[0], qn))
+    close(k[:, :, tok_off:tok_off + n], norm_rope(y[1], kn))
+    close(vt[..., tok_off:tok_off + n], y[2].transpose(-1, -2))
+    assert q[:, :, :tok_off].abs().sum() == 0 and vt[..., tok_off + n:].abs().sum() == 0
+
+
+def test_bad_arguments_raise(cuda):
+    x = torch.randn(16, 60, device=cuda).to(BF)  # K not a multiple of 8
+    w = torch.randn(64, 60, device=cuda).to(BF)
+    with pytest.raises(_lib.RldxError):
+        ops.linear(x, w)
+    with pytest.raises(ValueError):
+        ops.linear(x.cpu(), w)
