@@ -130,12 +130,13 @@ def test_category_weights_and_euler(cuda):
 def test_grouped_three_streams(cuda):
     """Three independent problems of very different shape in one launch."""
     g = torch.Generator(device=cuda).manual_seed(11)
-    descs, refs, outs = [], [], []
+    descs, refs, outs, keep = [], [], [], []
     for M in (512, 18, 32):
         x = torch.randn(M, 1536, device=cuda, generator=g).to(BF)
         w = (torch.randn(1536, 1536, device=cuda, generator=g) * 0.03).to(BF)
         b = (torch.randn(1536, device=cuda, generator=g) * 0.1).to(BF)
         o = torch.empty(M, 1536, dtype=BF, device=cuda)
+        keep += [x, w, b]  # descriptors hold raw pointers: keep the tensors alive
         descs.append(ops.gemm_desc(x, w, o, b))
         refs.append(ref_finish(x.float() @ w.float().t(), b, _lib.BIAS_FUSED, 0))
         outs.append(o)
