@@ -95,8 +95,22 @@ typedef struct {
   int tile_n; /* 0 = choose automatically, else 64/128/192/256 */
 } rldx_gemm_desc;
 
-/* Runs up to 4 independent problems in one launch. */
+/* Runs up to 4 independent problems in one persistent launch (no K split). */
 int rldx_gemm(const rldx_gemm_desc* problems, int nproblems, void* stream);
+
+/* Bytes of workspace with which rldx_gemm_ws may split long K loops of these problems across
+ * SMs (0 = the plan would not split).  Same validation as rldx_gemm; launches nothing. */
+int rldx_gemm_workspace_size(const rldx_gemm_desc* problems, int nproblems, uint64_t* bytes);
+
+/* rldx_gemm with a device workspace: problems whose K loop would leave SMs idle are split,
+ * each split writes an fp32 partial tile, and the last split of a tile to finish adds the
+ * partials in split order (the result does not depend on which finishes last) and runs the
+ * epilogue.  The workspace must be 16-byte aligned and ZERO-FILLED before its first use; its
+ * first bytes hold per-tile arrival counters that every call leaves at zero again.  Calls that
+ * share one workspace must be ordered on one stream.  A workspace smaller than
+ * rldx_gemm_workspace_size() (or NULL) runs the problems unsplit. */
+int rldx_gemm_ws(const rldx_gemm_desc* problems, int nproblems, void* workspace,
+                 uint64_t workspace_bytes, void* stream);
 
 /* ------------------------------------------------------------------------------------------
  * Joint-stream attention (non-causal, head_dim 64, scale 1/8) over [seg0 | seg1 | seg2].

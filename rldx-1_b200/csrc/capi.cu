@@ -1,6 +1,12 @@
 // C-ABI entry points of the per-op kernels, error reporting and the host helpers that turn
 // plain pointers and sizes into TMA descriptors and launch parameters.
+#include <algorithm>
 #include <cmath>
+#include <cstdlib>
+#include <functional>
+#include <map>
+#include <queue>
+#include <vector>
 #include <cstdio>
 #include <cstring>
 #include <mutex>
@@ -134,7 +140,213 @@ bool make_tmap_3d(CUtensorMap* m, const void* base, uint64_t d0, uint64_t d1, ui
   return true;
 }
 
-bool build_gemm_problem(const rldx_gemm_desc& d, GemmProblem* p, std::string* err) {
+namespace {
+
+bool make_tmap_4d(CUtensorMap* m, const void* base, const cuuint64_t (&dims)[4],
+                  const cuuint64_t (&strides)[3], const cuuint32_t (&box)[4], std::string* err) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) {
+    *err = "cuTensorMapEncodeTiled unavailable";
+    return false;
+  }
+  cuuint32_t es[4] = {1, 1, 1, 1};
+  CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(base), dims, strides,
+                  box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    *err = "cuTensorMapEncodeTiled(4d) failed with code " + std::to_string(static_cast<int>(r));
+    return false;
+  }
+  return true;
+}
+
+// ---- GEMM planning ----------------------------------------------------------------------------
+// Cost model of one work unit on one SM, in nanoseconds, from measurements of this kernel's
+// building blocks on B200: a TMA ring sustains ~114 GB/s of shared-memory fill per SM, the
+// tensor core ~11.3 TFLOP/s per SM (dense bf16, M = 128 whatever the live rows), a unit pays a
+// fixed pipeline fill + epilogue tail, and a K-split unit also writes its fp32 partial tile and
+// (for the last one) reads all partials of the tile back from L2.
+constexpr double kFillBytesPerNs = 114.0;
+constexpr double kMmaFlopsPerNs = 11300.0;
+constexpr double kChunkNs = 20.0;
+constexpr double kUnitNs = 1500.0;
+constexpr int kSlotTargetBytes = 48 * 1024;
+constexpr int kMinSplitChunks = 4;
+constexpr int kMaxSplit = 8;
+constexpr size_t kCounterBytes = ((kMaxUnits * 4 + 255) / 256) * 256;
+
+struct ProbShape {
+  int M, N, K, m_step, tiles_m, a_rows, live_rows, nchunks, kdim3, cat;
+};
+
+double chunk_ns(const ProbShape& s, int bn) {
+  const double fill = (s.a_rows + bn) * 128.0 / kFillBytesPerNs;
+  const double mma = 128.0 * bn * 64.0 * 2.0 / kMmaFlopsPerNs;
+  return std::max(fill, mma) + kChunkNs;
+}
+
+double unit_ns(const ProbShape& s, int bn, int chunks, int nsplit) {
+  double t = chunks * chunk_ns(s, bn) + kUnitNs;
+  if (nsplit > 1) t += s.live_rows * bn * 4.0 * 2.0 / kFillBytesPerNs;
+  return t;
+}
+
+// Units of one problem for a (bn, nsplit) choice, appended as costs.
+void unit_costs(const ProbShape& s, int bn, int nsplit, std::vector<double>* out) {
+  const int tiles = s.tiles_m * ((s.N + bn - 1) / bn);
+  const int per = (s.nchunks + nsplit - 1) / nsplit;
+  for (int t = 0; t < tiles; ++t)
+    for (int k = 0; k < nsplit; ++k) {
+      const int c = std::min(per, s.nchunks - k * per);
+      out->push_back(unit_ns(s, bn, c, nsplit));
+    }
+}
+
+// Makespan of the longest-processing-time-first assignment of `costs` to `ncta` CTAs.
+double lpt_makespan(std::vector<double> costs, int nsm) {
+  if (costs.empty()) return 0.0;
+  std::sort(costs.begin(), costs.end(), std::greater<double>());
+  const int ncta = std::min<int>(nsm, static_cast<int>(costs.size()));
+  std::priority_queue<double, std::vector<double>, std::greater<double>> loads;
+  for (int i = 0; i < ncta; ++i) loads.push(0.0);
+  double mk = 0.0;
+  for (double c : costs) {
+    double l = loads.top() + c;
+    loads.pop();
+    loads.push(l);
+    mk = std::max(mk, l);
+  }
+  return mk;
+}
+
+int normalize_split(int nchunks, int nsplit) {
+  const int per = (nchunks + nsplit - 1) / nsplit;
+  return (nchunks + per - 1) / per;  // no empty trailing split
+}
+
+// Tile width (from 64/128/256) and K-split count of every problem of one launch: for each
+// tile-width combination, splits are added greedily while they shorten the modelled makespan;
+// the best combination wins.  Results are cached per shape set (an MSAT control step repeats
+// a handful of shape sets hundreds of times).
+void choose_tiles_uncached(const ProbShape* sh, const int* fixed_bn, int n, int nsm,
+                           bool can_split, int* best_bn, int* best_split) {
+  double best_mk = 1e300;
+  int cand[kMaxProblems][3], ncand[kMaxProblems];
+  for (int i = 0; i < n; ++i) {
+    if (fixed_bn[i]) {
+      cand[i][0] = fixed_bn[i];
+      ncand[i] = 1;
+      continue;
+    }
+    const int nmax = std::max(64, round_up(sh[i].N, 64));
+    int k = 0;
+    for (int bn : {64, 128, 256}) {
+      if (bn > nmax) continue;
+      if (sh[i].tiles_m >= 2 && bn == 64 && nmax > 64) continue;  // A re-reads: keep tiles wide
+      cand[i][k++] = bn;
+    }
+    ncand[i] = k;
+  }
+  int idx[kMaxProblems] = {0, 0, 0, 0};
+  std::vector<double> c;
+  while (true) {
+    int bn[kMaxProblems], sp[kMaxProblems];
+    for (int i = 0; i < n; ++i) {
+      bn[i] = cand[i][idx[i]];
+      sp[i] = 1;
+    }
+    auto eval = [&]() {
+      c.clear();
+      int units = 0;
+      for (int i = 0; i < n; ++i) {
+        unit_costs(sh[i], bn[i], sp[i], &c);
+        units += sh[i].tiles_m * ((sh[i].N + bn[i] - 1) / bn[i]) * sp[i];
+      }
+      if (units > kMaxUnits) return 1e299;
+      return lpt_makespan(c, nsm);
+    };
+    double mk = eval();
+    if (can_split) {
+      for (int iter = 0; iter < 16; ++iter) {
+        int bi = -1, bs = 0;
+        double bm = mk;
+        for (int i = 0; i < n; ++i) {
+          const int maxs = std::min(kMaxSplit, std::max(1, sh[i].nchunks / kMinSplitChunks));
+          int ns = sp[i];
+          do {
+            ns = normalize_split(sh[i].nchunks, ns + 1);
+          } while (ns == sp[i] && ns < maxs);
+          if (ns <= sp[i] || ns > maxs) continue;
+          const int old = sp[i];
+          sp[i] = ns;
+          const double m = eval();
+          sp[i] = old;
+          if (m < bm * 0.99) {
+            bm = m;
+            bi = i;
+            bs = ns;
+          }
+        }
+        if (bi < 0) break;
+        sp[bi] = bs;
+        mk = bm;
+      }
+    }
+    if (mk < best_mk) {
+      best_mk = mk;
+      for (int i = 0; i < n; ++i) {
+        best_bn[i] = bn[i];
+        best_split[i] = sp[i];
+      }
+    }
+    int i = 0;
+    for (; i < n; ++i) {
+      if (++idx[i] < ncand[i]) break;
+      idx[i] = 0;
+    }
+    if (i == n) break;
+  }
+}
+
+void choose_tiles(const ProbShape* sh, const int* fixed_bn, int n, int nsm, bool can_split,
+                  int* best_bn, int* best_split) {
+  std::vector<int> key = {n, nsm, can_split ? 1 : 0};
+  for (int i = 0; i < n; ++i) {
+    const ProbShape& s = sh[i];
+    key.insert(key.end(), {s.M, s.N, s.K, s.m_step, s.a_rows, s.cat, fixed_bn[i]});
+  }
+  static std::mutex mu;
+  static std::map<std::vector<int>, std::vector<int>> cache;
+  {
+    std::lock_guard<std::mutex> lk(mu);
+    auto it = cache.find(key);
+    if (it != cache.end()) {
+      for (int i = 0; i < n; ++i) {
+        best_bn[i] = it->second[2 * i];
+        best_split[i] = it->second[2 * i + 1];
+      }
+      return;
+    }
+  }
+  choose_tiles_uncached(sh, fixed_bn, n, nsm, can_split, best_bn, best_split);
+  std::vector<int> v;
+  for (int i = 0; i < n; ++i) v.insert(v.end(), {best_bn[i], best_split[i]});
+  std::lock_guard<std::mutex> lk(mu);
+  cache[key] = v;
+}
+
+bool split_disabled() {
+  static int v = [] {
+    const char* e = std::getenv("RLDX_GEMM_SPLIT");
+    return (e && e[0] == '0') ? 1 : 0;
+  }();
+  return v != 0;
+}
+
+}  // namespace
+
+// Validates one GEMM description and fills the shape-only fields of the device problem.
+bool validate_gemm_problem(const rldx_gemm_desc& d, GemmProblem* p, std::string* err) {
   std::memset(p, 0, sizeof(*p));
   if (!d.a || !d.b || !d.out) return (*err = "gemm: null a/b/out"), false;
   if (d.M <= 0 || d.N <= 0 || d.K <= 0) return (*err = "gemm: M, N, K must be positive"), false;
@@ -148,6 +360,8 @@ bool build_gemm_problem(const rldx_gemm_desc& d, GemmProblem* p, std::string* er
     return (*err = "gemm: bad bias_mode / act"), false;
   if (d.bias_mode != RLDX_BIAS_NONE && !d.bias) return (*err = "gemm: bias_mode needs bias"), false;
   if (d.ldo <= 0) return (*err = "gemm: ldo must be positive"), false;
+  if (d.tile_n != 0 && (d.tile_n < 64 || d.tile_n > 256 || d.tile_n % 64 != 0))
+    return (*err = "gemm: tile_n must be 64..256, x64"), false;
 
   int m_step, tiles_m;
   if (d.cat_ids) {
@@ -162,21 +376,6 @@ bool build_gemm_problem(const rldx_gemm_desc& d, GemmProblem* p, std::string* er
     m_step = 128;
     tiles_m = (d.M + 127) / 128;
   }
-  const int a_rows = std::min(128, round_up(std::min(m_step, d.M), 8));
-
-  int bn = d.tile_n;
-  if (bn == 0) {
-    const int t256 = tiles_m * ((d.N + 255) / 256);
-    const int t128 = tiles_m * ((d.N + 127) / 128);
-    if (d.N >= 256 && t256 >= 96)
-      bn = 256;
-    else if (d.N >= 128 && t128 >= 96)
-      bn = 128;
-    else
-      bn = 64;
-  }
-  if (bn < 64 || bn > 256 || bn % 64 != 0) return (*err = "gemm: tile_n must be 64..256, x64"), false;
-
   if (d.epilogue == RLDX_EPI_SWIGLU && d.N % 64 != 0)
     return (*err = "gemm: SwiGLU needs N % 64 == 0 (interleaved 32 gate + 32 up)"), false;
   if (d.epilogue == RLDX_EPI_QKV) {
@@ -186,6 +385,9 @@ bool build_gemm_problem(const rldx_gemm_desc& d, GemmProblem* p, std::string* er
     if (d.L <= 0 || d.Lp < d.L || d.Lp % 8 != 0) return (*err = "gemm: QKV needs Lp >= L, Lp % 8 == 0"), false;
     if (d.rows_in <= 0 || d.tok_off < 0 || d.tok_off + d.rows_in > d.L)
       return (*err = "gemm: QKV rows_in/tok_off outside L"), false;
+    if (!aligned16(d.q) || !aligned16(d.k) || !aligned16(d.q_norm_w) || !aligned16(d.k_norm_w) ||
+        !aligned16(d.rope_cos) || !aligned16(d.rope_sin))
+      return (*err = "gemm: QKV buffers must be 16-byte aligned"), false;
   }
   if (d.rows_in < 0 || (d.rows_in > 0 && d.rows_out <= 0))
     return (*err = "gemm: bad rows_in / rows_out"), false;
@@ -193,23 +395,12 @@ bool build_gemm_problem(const rldx_gemm_desc& d, GemmProblem* p, std::string* er
   p->M = d.M;
   p->N = d.N;
   p->K = d.K;
-  p->bn = bn;
-  p->a_rows = a_rows;
   p->m_step = m_step;
   p->tiles_m = tiles_m;
-  p->tiles_n = (d.N + bn - 1) / bn;
+  p->a_rows = std::min(128, round_up(std::min(m_step, d.M), 8));
+  p->nchunks = (d.K + 63) / 64;
+  p->kdim3 = (d.K % 64 == 0) ? 1 : 0;
   p->cat_ids = reinterpret_cast<const long long*>(d.cat_ids);
-
-  if (!make_tmap_2d(&p->ta, d.a, d.K, d.M, static_cast<uint64_t>(d.lda) * 2, 64, a_rows, err))
-    return false;
-  if (d.cat_ids) {
-    if (!make_tmap_3d(&p->tb, d.b, d.K, d.N, d.num_cats, static_cast<uint64_t>(d.ldb) * 2,
-                      static_cast<uint64_t>(d.b_cat_stride) * 2, 64, bn, 1, err))
-      return false;
-  } else {
-    if (!make_tmap_2d(&p->tb, d.b, d.K, d.N, static_cast<uint64_t>(d.ldb) * 2, 64, bn, err))
-      return false;
-  }
 
   GemmEpilogue& e = p->ep;
   e.mode = d.epilogue;
@@ -242,22 +433,163 @@ bool build_gemm_problem(const rldx_gemm_desc& d, GemmProblem* p, std::string* er
   return true;
 }
 
-bool build_gemm_params(const rldx_gemm_desc* d, int n, GemmParams* params, int* tiles,
-                       std::string* err) {
+bool build_gemm_params(const rldx_gemm_desc* d, int n, void* ws, size_t ws_bytes,
+                       GemmParams* params, size_t* ws_needed, std::string* err) {
   if (n <= 0 || n > kMaxProblems) return (*err = "gemm: 1..4 problems per launch"), false;
   std::memset(params, 0, sizeof(*params));
-  int total = 0, bn_max = 64;
+  const int nsm = std::min(sm_count(), kMaxCtas);
+  for (int i = 1; i < n; ++i)
+    if (d[i].epilogue != d[0].epilogue)
+      return (*err = "gemm: every problem of one launch must use the same epilogue"), false;
+  ProbShape sh[kMaxProblems];
   for (int i = 0; i < n; ++i) {
-    if (!build_gemm_problem(d[i], &params->p[i], err)) return false;
-    params->p[i].tile_begin = total;
-    total += params->p[i].tiles_m * params->p[i].tiles_n;
-    bn_max = std::max(bn_max, params->p[i].bn);
+    GemmProblem& p = params->p[i];
+    if (!validate_gemm_problem(d[i], &p, err)) return false;
+    ProbShape& s = sh[i];
+    s.M = p.M;
+    s.N = p.N;
+    s.K = p.K;
+    s.m_step = p.m_step;
+    s.tiles_m = p.tiles_m;
+    s.a_rows = p.a_rows;
+    s.live_rows = std::min(p.m_step, p.M);
+    s.nchunks = p.nchunks;
+    s.kdim3 = p.kdim3;
+    s.cat = d[i].cat_ids ? 1 : 0;
+  }
+
+  // ---- tile width and K splits: minimise the modelled LPT makespan ----
+  const bool can_split = (ws != nullptr || ws_needed != nullptr) && !split_disabled();
+  int fixed_bn[kMaxProblems], best_bn[kMaxProblems], best_split[kMaxProblems];
+  for (int i = 0; i < n; ++i) fixed_bn[i] = d[i].tile_n;
+  choose_tiles(sh, fixed_bn, n, nsm, can_split, best_bn, best_split);
+
+  // ---- workspace layout: [tile counters][fp32 partial tiles] ----
+  size_t need = 0;
+  for (int pass = 0; pass < 2; ++pass) {
+    size_t off_f = 0;
+    int cnt = 0;
+    bool any = false;
+    for (int i = 0; i < n; ++i) {
+      GemmProblem& p = params->p[i];
+      p.bn = best_bn[i];
+      p.tiles_n = (p.N + p.bn - 1) / p.bn;
+      p.nsplit = best_split[i];
+      p.split_chunks = (p.nchunks + p.nsplit - 1) / p.nsplit;
+      p.ws_off = 0;
+      p.cnt_off = 0;
+      if (p.nsplit > 1) {
+        any = true;
+        p.ws_off = static_cast<long long>(off_f);
+        p.cnt_off = cnt;
+        off_f += static_cast<size_t>(p.tiles_m) * p.tiles_n * p.nsplit * 128 * p.bn;
+        cnt += p.tiles_m * p.tiles_n;
+      }
+    }
+    need = any ? kCounterBytes + off_f * 4 : 0;
+    if (ws_needed) *ws_needed = std::max(*ws_needed, need);
+    if (!any || (ws != nullptr && need <= ws_bytes)) break;
+    for (int i = 0; i < n; ++i) best_split[i] = 1;  // no (or too small a) workspace
+  }
+  params->ws = reinterpret_cast<float*>(static_cast<uint8_t*>(ws) + kCounterBytes);
+  params->counters = static_cast<unsigned int*>(ws);
+  if (!ws) {
+    params->ws = nullptr;
+    params->counters = nullptr;
+  }
+
+  // ---- ring slot: ksub chunks of every problem must fit one slot ----
+  int slot = 0;
+  for (int i = 0; i < n; ++i) {
+    GemmProblem& p = params->p[i];
+    const int per_chunk = (p.a_rows + p.bn) * 128;
+    p.ksub = p.kdim3 ? std::max(1, std::min({kSlotTargetBytes / per_chunk, 8, p.split_chunks})) : 1;
+    slot = std::max(slot, p.ksub * per_chunk);
+  }
+  params->slot_bytes = slot;
+  const int budget = 227 * 1024 - 1024 - kRingSlack - 256;
+  params->stages = std::min(kMaxStages, budget / slot);
+  if (params->stages < 2) return (*err = "gemm: ring does not fit shared memory"), false;
+
+  // ---- tensor maps ----
+  for (int i = 0; i < n; ++i) {
+    GemmProblem& p = params->p[i];
+    const rldx_gemm_desc& q = d[i];
+    if (p.kdim3) {
+      if (!make_tmap_3d(&p.ta, q.a, 64, p.M, p.nchunks, static_cast<uint64_t>(q.lda) * 2, 128, 64,
+                        p.a_rows, p.ksub, err))
+        return false;
+      if (q.cat_ids) {
+        const cuuint64_t dims[4] = {64, static_cast<cuuint64_t>(p.N), static_cast<cuuint64_t>(p.nchunks),
+                                    static_cast<cuuint64_t>(q.num_cats)};
+        const cuuint64_t strides[3] = {static_cast<cuuint64_t>(q.ldb) * 2, 128,
+                                       static_cast<cuuint64_t>(q.b_cat_stride) * 2};
+        const cuuint32_t box[4] = {64, static_cast<cuuint32_t>(p.bn), static_cast<cuuint32_t>(p.ksub), 1};
+        if (!make_tmap_4d(&p.tb, q.b, dims, strides, box, err)) return false;
+      } else if (!make_tmap_3d(&p.tb, q.b, 64, p.N, p.nchunks, static_cast<uint64_t>(q.ldb) * 2, 128,
+                               64, p.bn, p.ksub, err)) {
+        return false;
+      }
+    } else {
+      if (!make_tmap_2d(&p.ta, q.a, q.K, p.M, static_cast<uint64_t>(q.lda) * 2, 64, p.a_rows, err))
+        return false;
+      if (q.cat_ids) {
+        if (!make_tmap_3d(&p.tb, q.b, q.K, p.N, q.num_cats, static_cast<uint64_t>(q.ldb) * 2,
+                          static_cast<uint64_t>(q.b_cat_stride) * 2, 64, p.bn, 1, err))
+          return false;
+      } else if (!make_tmap_2d(&p.tb, q.b, q.K, p.N, static_cast<uint64_t>(q.ldb) * 2, 64, p.bn, err)) {
+        return false;
+      }
+    }
+  }
+
+  // ---- units and the LPT schedule ----
+  int total = 0;
+  for (int i = 0; i < n; ++i) {
+    GemmProblem& p = params->p[i];
+    p.unit_begin = total;
+    total += p.tiles_m * p.tiles_n * p.nsplit;
   }
   params->nprob = n;
-  params->stage_bytes = kATileBytes + bn_max * 128;
-  const int budget = 227 * 1024 - 1024 - 512;
-  params->stages = std::min(kMaxStages, budget / params->stage_bytes);
-  *tiles = total;
+  params->nunits = total;
+  params->ncta = std::min(nsm, total);
+  if (total > kMaxUnits) {
+    params->explicit_sched = 0;
+    return true;
+  }
+  params->explicit_sched = 1;
+  struct U {
+    double cost;
+    int id;
+  };
+  std::vector<U> us;
+  us.reserve(total);
+  for (int i = 0; i < n; ++i) {
+    const GemmProblem& p = params->p[i];
+    for (int local = 0; local < p.tiles_m * p.tiles_n * p.nsplit; ++local) {
+      const int ks = local % p.nsplit;
+      const int c = std::min(p.split_chunks, p.nchunks - ks * p.split_chunks);
+      us.push_back({unit_ns(sh[i], p.bn, c, p.nsplit), p.unit_begin + local});
+    }
+  }
+  std::stable_sort(us.begin(), us.end(), [](const U& a, const U& b) { return a.cost > b.cost; });
+  using Load = std::pair<double, int>;
+  std::priority_queue<Load, std::vector<Load>, std::greater<Load>> loads;
+  for (int c = 0; c < params->ncta; ++c) loads.push({0.0, c});
+  std::vector<std::vector<int>> lists(params->ncta);
+  for (const U& u : us) {
+    Load l = loads.top();
+    loads.pop();
+    lists[l.second].push_back(u.id);
+    l.first += u.cost;
+    loads.push(l);
+  }
+  int off = 0;
+  for (int c = 0; c < params->ncta; ++c) {
+    params->cta_begin[c] = static_cast<unsigned short>(off);
+    for (int id : lists[c]) params->sched[off++] = static_cast<unsigned short>(id);
+  }
+  params->cta_begin[params->ncta] = static_cast<unsigned short>(off);
   return true;
 }
 
@@ -294,12 +626,40 @@ int rldx_gemm(const rldx_gemm_desc* problems, int nproblems, void* stream) {
   int rc = ensure_device();
   if (rc != RLDX_OK) return rc;
   if (!problems) return set_error(RLDX_ERR_ARG, "gemm: null problems");
-  GemmParams params;
-  int tiles = 0;
+  static thread_local GemmParams params;
   std::string err;
-  if (!build_gemm_params(problems, nproblems, &params, &tiles, &err))
+  if (!build_gemm_params(problems, nproblems, nullptr, 0, &params, nullptr, &err))
     return set_error(RLDX_ERR_ARG, err);
-  cudaError_t e = launch_gemm(params, tiles, static_cast<cudaStream_t>(stream), false);
+  cudaError_t e = launch_gemm(params, static_cast<cudaStream_t>(stream), false);
+  if (e != cudaSuccess) return cuda_fail(e, "gemm launch");
+  return RLDX_OK;
+}
+
+int rldx_gemm_workspace_size(const rldx_gemm_desc* problems, int nproblems, uint64_t* bytes) {
+  int rc = ensure_device();
+  if (rc != RLDX_OK) return rc;
+  if (!problems || !bytes) return set_error(RLDX_ERR_ARG, "gemm_workspace_size: null argument");
+  static thread_local GemmParams params;
+  std::string err;
+  size_t need = 0;
+  if (!build_gemm_params(problems, nproblems, nullptr, 0, &params, &need, &err))
+    return set_error(RLDX_ERR_ARG, err);
+  *bytes = need;
+  return RLDX_OK;
+}
+
+int rldx_gemm_ws(const rldx_gemm_desc* problems, int nproblems, void* workspace,
+                 uint64_t workspace_bytes, void* stream) {
+  int rc = ensure_device();
+  if (rc != RLDX_OK) return rc;
+  if (!problems) return set_error(RLDX_ERR_ARG, "gemm: null problems");
+  if (workspace && !aligned16(workspace)) return set_error(RLDX_ERR_ARG, "gemm: workspace must be 16-byte aligned");
+  static thread_local GemmParams params;
+  std::string err;
+  if (!build_gemm_params(problems, nproblems, workspace, workspace ? workspace_bytes : 0, &params,
+                         nullptr, &err))
+    return set_error(RLDX_ERR_ARG, err);
+  cudaError_t e = launch_gemm(params, static_cast<cudaStream_t>(stream), false);
   if (e != cudaSuccess) return cuda_fail(e, "gemm launch");
   return RLDX_OK;
 }

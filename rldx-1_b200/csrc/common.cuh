@@ -1,7 +1,7 @@
 // Shared device helpers for the sm_100a MSAT kernels: shared-memory mbarriers with bounded
 // waits, TMA tile loads, tcgen05 (TMEM alloc / MMA / commit / load) and the UMMA descriptors.
 //
-// Every wait on an mbarrier is bounded by a wall-clock limit read from %globaltimer.  A wait
+// Every wait on an mbarrier is bounded by a limit on the SM cycle counter.  A wait
 // that runs out records an error code in `g_rldx_err` (first error wins) and returns false;
 // callers then skip the rest of their work, release TMEM and return, so a lost arrival never
 // hangs the GPU.  The host reads and clears the code through rldx_get_device_error().
@@ -24,8 +24,9 @@ enum DeviceError : unsigned int {
   kErrTeardownTimeout = 0x300,
 };
 
-// Wall-clock bound of one mbarrier wait.  Healthy waits last microseconds.
-constexpr unsigned long long kWaitLimitNs = 2000000000ull;
+// Bound of one mbarrier wait in SM clock cycles (about 2 s at the B200's 1.9 GHz, 4 s at a
+// throttled 1 GHz).  Healthy waits last microseconds.
+constexpr long long kWaitLimitCycles = 4000000000ll;
 
 __device__ __forceinline__ void record_error(unsigned int code) {
   atomicCAS(&g_rldx_err, 0u, code);
@@ -33,12 +34,6 @@ __device__ __forceinline__ void record_error(unsigned int code) {
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
-}
-
-__device__ __forceinline__ unsigned long long globaltimer_ns() {
-  unsigned long long t;
-  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
-  return t;
 }
 
 // ---------------------------------------------------------------------------------------------
@@ -74,23 +69,30 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
-// Bounded wait for the phase of `bar` with the given parity to complete.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, unsigned int err_code,
-                                          unsigned long long limit_ns = kWaitLimitNs) {
-  if (mbar_try_wait(bar, parity)) return true;
-  const unsigned long long t0 = globaltimer_ns();
-  while (true) {
-    if (mbar_try_wait(bar, parity)) return true;
-    if (globaltimer_ns() - t0 > limit_ns) {
-      record_error(err_code);
-      return false;
-    }
-  }
-}
-
 // True once any kernel of the library has recorded an error: lets sibling warps give up early.
 __device__ __forceinline__ bool error_raised() {
   return *reinterpret_cast<volatile unsigned int*>(&g_rldx_err) != 0u;
+}
+
+// Bounded wait for the phase of `bar` with the given parity to complete.  The hot loop only
+// polls the barrier: reading %globaltimer or global memory on every poll delays the wake-up
+// after the phase completes by up to a microsecond, which serialises every producer/consumer
+// hand-off.  Every 256 polls it reads the SM cycle counter (the bound) and the shared error
+// word, so that sibling roles give up quickly once one of them has.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, unsigned int err_code,
+                                          long long limit_cycles = kWaitLimitCycles) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const long long t0 = clock64();
+  for (uint32_t n = 1;; ++n) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((n & 255u) == 0u) {
+      if (error_raised()) return false;  // a sibling role already gave up: do not wait it out
+      if (clock64() - t0 > limit_cycles) {
+        record_error(err_code);
+        return false;
+      }
+    }
+  }
 }
 
 // ---------------------------------------------------------------------------------------------
@@ -129,6 +131,21 @@ __device__ __forceinline__ void tma_load_3d(void* dst, const void* tmap, uint64_
       "l"(reinterpret_cast<uint64_t>(tmap)), "r"(c0), "r"(c1), "r"(c2), "r"(smem_u32(bar)),
       "l"(policy)
       : "memory");
+}
+
+__device__ __forceinline__ void tma_load_4d(void* dst, const void* tmap, uint64_t* bar, int c0,
+                                            int c1, int c2, int c3, uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::"
+      "cache_hint [%0], [%1, {%2, %3, %4, %5}], [%6], %7;" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(tmap)), "r"(c0), "r"(c1), "r"(c2), "r"(c3),
+      "r"(smem_u32(bar)), "l"(policy)
+      : "memory");
+}
+
+// Barrier over a subset of the CTA's warps (ids 1..15; id 0 is __syncthreads).
+__device__ __forceinline__ void named_bar_sync(int id, int nthreads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
 }
 
 // Generic-proxy shared-memory writes become visible to the async proxy (tensor core reads).
@@ -198,6 +215,19 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
   for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
 
+// 8 consecutive fp32 columns of one TMEM lane per thread.
+__device__ __forceinline__ void tmem_ld8(uint32_t taddr, float (&v)[8]) {
+  uint32_t r[8];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7])
+      : "r"(taddr)
+      : "memory");
+#pragma unroll
+  for (int i = 0; i < 8; ++i) v[i] = __uint_as_float(r[i]);
+}
+
 __device__ __forceinline__ void tmem_wait_ld() {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
@@ -230,8 +260,18 @@ __device__ __forceinline__ void griddep_launch() {
 // ---------------------------------------------------------------------------------------------
 // bf16 helpers (round-to-nearest-even, same as torch's .to(bfloat16))
 // ---------------------------------------------------------------------------------------------
+// Round to bf16 (nearest, ties to even) and back, on the fp32 bit pattern: integer ALU work
+// that pipelines well, instead of two conversions.  NaN stays a (quiet) NaN.
 __device__ __forceinline__ float bf16r(float x) {
-  return __bfloat162float(__float2bfloat16_rn(x));
+  const uint32_t u = __float_as_uint(x);
+  const uint32_t r = (u + 0x7fffu + ((u >> 16) & 1u)) & 0xffff0000u;
+  const bool nan = (u & 0x7fffffffu) > 0x7f800000u;
+  return __uint_as_float(nan ? ((u | 0x00400000u) & 0xffff0000u) : r);
+}
+
+// Packs two values that are already bf16-exact (e.g. results of bf16r) into a bf16x2 word.
+__device__ __forceinline__ uint32_t pack_exact_bf16x2(float lo, float hi) {
+  return __byte_perm(__float_as_uint(lo), __float_as_uint(hi), 0x7632);
 }
 
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {

@@ -1,4 +1,4 @@
-// Grouped tcgen05 GEMM with fused row epilogues (see gemm.cuh for the CTA layout).
+// Grouped persistent tcgen05 GEMM with fused row epilogues (see gemm.cuh for the CTA layout).
 //
 // Rounding follows the reference bf16 eager path step by step: nn.Linear rounds once after
 // the fused bias (cuBLASLt bias epilogue), CategorySpecificLinear (bmm + b) rounds the matmul
@@ -14,320 +14,597 @@
 
 namespace rldx {
 
-__device__ __forceinline__ float apply_act(float y, int act) {
-  if (act == kActRelu) return fmaxf(y, 0.0f);
-  if (act == kActSilu) return bf16r(y / (1.0f + expf(-y)));
-  if (act == kActSwish) {  // sigmoid rounded to bf16, then the product rounded
-    const float sg = bf16r(1.0f / (1.0f + expf(-y)));
-    return bf16r(y * sg);
+namespace {
+
+// Activation of one bias-finished bf16 value.  The exponential and the reciprocal use the fast
+// hardware paths (a couple of fp32 ulps); the result is rounded to bf16 like the reference.
+template <int kAct>
+__device__ __forceinline__ float act_fn(float y) {
+  if constexpr (kAct == kActRelu) {
+    return fmaxf(y, 0.0f);
+  } else if constexpr (kAct == kActSilu) {  // F.silu: one rounding
+    return bf16r(__fdividef(y, 1.0f + __expf(-y)));
+  } else if constexpr (kAct == kActSwish) {  // x * torch.sigmoid(x): sigmoid rounded, then product
+    return bf16r(y * bf16r(__fdividef(1.0f, 1.0f + __expf(-y))));
+  } else {
+    return y;
   }
-  return y;
 }
 
+// Bias epilogue without branches: an absent bias reads as zeros (bf16(acc + 0) = bf16(acc)),
+// the post-rounded form (torch.bmm then + b) rounds the product first.
 __device__ __forceinline__ float finish_acc(float acc, float b, int bias_mode) {
-  if (bias_mode == kBiasFused) return bf16r(acc + b);
-  if (bias_mode == kBiasPostRound) return bf16r(bf16r(acc) + b);
-  return bf16r(acc);
+  const float a = (bias_mode == kBiasPostRound) ? bf16r(acc) : acc;
+  return bf16r(a + b);
 }
 
-__device__ __forceinline__ void load_bf16x64(const __nv_bfloat16* src, bool vec_ok, int nvalid,
-                                             float (&dst)[64]) {
-  if (vec_ok && nvalid >= 64) {
-    const uint4* p = reinterpret_cast<const uint4*>(src);
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      uint4 u = p[i];
-      unpack_bf16x2(u.x, dst[8 * i + 0], dst[8 * i + 1]);
-      unpack_bf16x2(u.y, dst[8 * i + 2], dst[8 * i + 3]);
-      unpack_bf16x2(u.z, dst[8 * i + 4], dst[8 * i + 5]);
-      unpack_bf16x2(u.w, dst[8 * i + 6], dst[8 * i + 7]);
-    }
-  } else {
-#pragma unroll
-    for (int i = 0; i < 64; ++i) dst[i] = (i < nvalid) ? __bfloat162float(src[i]) : 0.0f;
-  }
+__device__ __forceinline__ bool al16(const void* p) {
+  return (reinterpret_cast<uintptr_t>(p) & 15u) == 0;
 }
 
-__device__ __forceinline__ void store_bf16x64(__nv_bfloat16* dst, bool vec_ok, int nvalid,
-                                              const float (&v)[64]) {
-  if (vec_ok && nvalid >= 64) {
-    uint4* p = reinterpret_cast<uint4*>(dst);
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      uint4 u;
-      u.x = pack_bf16x2(v[8 * i + 0], v[8 * i + 1]);
-      u.y = pack_bf16x2(v[8 * i + 2], v[8 * i + 3]);
-      u.z = pack_bf16x2(v[8 * i + 4], v[8 * i + 5]);
-      u.w = pack_bf16x2(v[8 * i + 6], v[8 * i + 7]);
-      p[i] = u;
-    }
-  } else {
-#pragma unroll
-    for (int i = 0; i < 64; ++i)
-      if (i < nvalid) dst[i] = __float2bfloat16_rn(v[i]);
-  }
+__device__ __forceinline__ float bf_lo(uint32_t u) { return __uint_as_float(u << 16); }
+__device__ __forceinline__ float bf_hi(uint32_t u) { return __uint_as_float(u & 0xffff0000u); }
+__device__ __forceinline__ float bf_at(const uint4& q, int i) {
+  const uint32_t w = (i < 2) ? q.x : (i < 4) ? q.y : (i < 6) ? q.z : q.w;
+  return (i & 1) ? bf_hi(w) : bf_lo(w);
 }
 
-// Epilogue of one 128 x BN tile; thread = accumulator row (TMEM lane).
-__device__ __forceinline__ void gemm_epilogue(const GemmProblem& pr, uint32_t tmem_acc, int tm,
-                                              int tn, int lane_grp, int lane) {
+// Output-row bookkeeping of one accumulator row (thread) of one M tile.
+struct RowCtx {
+  int row, r_local, bidx, t, out_row, cat;
+  bool live;  // row exists and is not dropped
+};
+
+__device__ __forceinline__ RowCtx row_ctx(const GemmProblem& pr, int tm, int r_local) {
   const GemmEpilogue& ep = pr.ep;
-  const int r_local = lane_grp * 32 + lane;
-  const int row = tm * pr.m_step + r_local;
-  const bool valid = (r_local < pr.m_step) && (row < pr.M);
-  int bidx = 0, t = row;
+  RowCtx c;
+  c.r_local = r_local;
+  c.row = tm * pr.m_step + r_local;
+  c.bidx = 0;
+  c.t = c.row;
   if (ep.rows_in > 0) {
-    bidx = row / ep.rows_in;
-    t = row - bidx * ep.rows_in;
+    c.bidx = c.row / ep.rows_in;
+    c.t = c.row - c.bidx * ep.rows_in;
   }
-  const bool dropped = (ep.rows_in > 0) && (t < ep.row_skip);
-  const int out_row = (ep.rows_in > 0) ? bidx * ep.rows_out + t - ep.row_skip : row;
-  int cat = 0;
-  if (pr.cat_ids != nullptr) cat = static_cast<int>(pr.cat_ids[tm]);
-  const __nv_bfloat16* bias =
-      ep.bias ? ep.bias + static_cast<size_t>(cat) * ep.bias_cat_stride : nullptr;
-  const uint32_t tbase = tmem_acc + (static_cast<uint32_t>(lane_grp * 32) << 16);
+  const bool dropped = (ep.rows_in > 0) && (c.t < ep.row_skip);
+  c.out_row = (ep.rows_in > 0) ? c.bidx * ep.rows_out + c.t - ep.row_skip : c.row;
+  c.live = (r_local < pr.m_step) && (c.row < pr.M) && !dropped;
+  c.cat = pr.cat_ids ? static_cast<int>(pr.cat_ids[tm]) : 0;
+  return c;
+}
 
-  for (int c = 0; c < pr.bn / 64; ++c) {
-    float lo[32], hi[32];
-    tmem_ld32(tbase + c * 64, lo);
-    tmem_ld32(tbase + c * 64 + 32, hi);
+// Accumulator sources of the epilogue: 8 fp32 columns of this thread's row.
+//   TmemSrc  the unit's own TMEM accumulator (tcgen05.ld: every lane of the warp calls it).
+//   PartSrc  the sum, in split order, of a K-split tile's fp32 partials in the workspace.
+struct TmemSrc {
+  uint32_t taddr;
+  __device__ __forceinline__ void get8(int col, bool /*live*/, float (&v)[8]) const {
+    __syncwarp();
+    tmem_ld8(taddr + static_cast<uint32_t>(col), v);
     tmem_wait_ld();
-    const int n0 = tn * pr.bn + c * 64;
-    if (!valid || dropped || n0 >= pr.N) continue;
-    const int nvalid = min(64, pr.N - n0);
-    float v[64];
-#pragma unroll
-    for (int i = 0; i < 32; ++i) {
-      v[i] = lo[i];
-      v[32 + i] = hi[i];
-    }
-    float bv[64];
-    if (bias) {
-      load_bf16x64(bias + n0, (n0 % 8) == 0, nvalid, bv);
-    } else {
-#pragma unroll
-      for (int i = 0; i < 64; ++i) bv[i] = 0.0f;
-    }
+  }
+};
 
-    if (ep.mode == kEpiStore || ep.mode == kEpiEuler) {
+struct PartSrc {
+  const float* row0;  // split 0, this thread's row, column 0
+  size_t split_stride;
+  int nsplit;
+  __device__ __forceinline__ void get8(int col, bool live, float (&v)[8]) const {
 #pragma unroll
-      for (int i = 0; i < 64; ++i) v[i] = apply_act(finish_acc(v[i], bv[i], ep.bias_mode), ep.act);
-      if (ep.add) {
-        const int arow = ep.add_row_mod > 0 ? (t % ep.add_row_mod) : row;
-        float av[64];
-        const __nv_bfloat16* ap = ep.add + static_cast<size_t>(arow) * ep.ld_add + n0;
-        load_bf16x64(ap, (ep.ld_add % 8 == 0) && (n0 % 8 == 0), nvalid, av);
+    for (int i = 0; i < 8; ++i) v[i] = 0.0f;
+    if (!live) return;
+#pragma unroll 1
+    for (int s = 0; s < nsplit; ++s) {
+      const float4* p = reinterpret_cast<const float4*>(row0 + s * split_stride + col);
+      const float4 a = __ldcg(p), b = __ldcg(p + 1);
+      v[0] += a.x; v[1] += a.y; v[2] += a.z; v[3] += a.w;
+      v[4] += b.x; v[5] += b.y; v[6] += b.z; v[7] += b.w;
+    }
+  }
+};
+
+// 8 bf16 at p (n of them valid; one 16-byte load when full and aligned), or zeros when !on.
+__device__ __forceinline__ uint4 load8q(const __nv_bfloat16* p, bool on, int n) {
+  if (!on) return make_uint4(0, 0, 0, 0);
+  if (n >= 8 && al16(p)) return *reinterpret_cast<const uint4*>(p);
+  uint16_t h[8];
 #pragma unroll
-        for (int i = 0; i < 64; ++i) v[i] = bf16r(v[i] + av[i]);
+  for (int i = 0; i < 8; ++i) h[i] = (i < n) ? __bfloat16_as_ushort(p[i]) : 0;
+  return make_uint4(h[0] | (static_cast<uint32_t>(h[1]) << 16), h[2] | (static_cast<uint32_t>(h[3]) << 16),
+                    h[4] | (static_cast<uint32_t>(h[5]) << 16), h[6] | (static_cast<uint32_t>(h[7]) << 16));
+}
+
+// 8 bf16-exact values to p (n of them valid).
+__device__ __forceinline__ void store8q(__nv_bfloat16* p, int n, const float (&y)[8]) {
+  if (n >= 8 && al16(p)) {
+    uint4 u;
+    u.x = pack_exact_bf16x2(y[0], y[1]);
+    u.y = pack_exact_bf16x2(y[2], y[3]);
+    u.z = pack_exact_bf16x2(y[4], y[5]);
+    u.w = pack_exact_bf16x2(y[6], y[7]);
+    *reinterpret_cast<uint4*>(p) = u;
+    return;
+  }
+#pragma unroll
+  for (int i = 0; i < 8; ++i)
+    if (i < n) p[i] = __ushort_as_bfloat16(static_cast<unsigned short>(__float_as_uint(y[i]) >> 16));
+}
+
+// Epilogue of one unit by one of the two epilogue warp sets (`set` 0/1: both sets hold the
+// same 32 rows of a TMEM lane quadrant and split the columns).  The loop bodies are small
+// (8 columns per iteration) so the code stays resident in the instruction caches.
+template <int kMode, int kAct, class Src>
+__device__ __forceinline__ void unit_epilogue(const GemmProblem& pr, const RowCtx& rc, int n_base,
+                                              int set, const Src& src) {
+  const GemmEpilogue& ep = pr.ep;
+  const int bn = pr.bn;
+  const __nv_bfloat16* bias_row =
+      ep.bias ? ep.bias + static_cast<size_t>(rc.cat) * ep.bias_cat_stride : nullptr;
+  const int bias_mode = ep.bias_mode;
+
+  if constexpr (kMode == kEpiStore || kMode == kEpiEuler) {
+    __nv_bfloat16* orow = ep.out + static_cast<size_t>(rc.out_row) * ep.ldo + ep.col_off;
+    const __nv_bfloat16* arow = nullptr;
+    if (ep.add) {
+      const int r = ep.add_row_mod > 0 ? (rc.t % ep.add_row_mod) : rc.row;
+      arow = ep.add + static_cast<size_t>(r) * ep.ld_add;
+    }
+    const float dt = ep.dt;
+    // set s takes the 32-column blocks s, s+2, s+4, ...; the operand loads of the next group
+    // are issued before the current group is computed (one group of software pipelining)
+    auto next_col = [](int col) { return col + ((col % 32 == 24) ? 40 : 8); };
+    auto fetch = [&](int col, uint4& bq, uint4& aq, uint4& xq) {
+      const int n0 = n_base + col;
+      const int n = pr.N - n0;
+      const bool on = rc.live && n > 0 && col < bn;
+      bq = load8q(bias_row + n0, on && bias_row, n);
+      aq = load8q(arow + n0, on && arow, n);
+      xq = load8q(orow + n0, on && kMode == kEpiEuler, n);
+    };
+    uint4 nb, na, nx;
+    fetch(set * 32, nb, na, nx);
+#pragma unroll 1
+    for (int col = set * 32; col < bn; col = next_col(col)) {
+      const int n0 = n_base + col;
+      const int n = pr.N - n0;  // valid columns from n0 (uniform over the warp)
+      const bool on = rc.live && n > 0;
+      const uint4 bq = nb, aq = na, xq = nx;
+      fetch(next_col(col), nb, na, nx);
+      float v[8];
+      src.get8(col, rc.live, v);
+      if (!on) continue;
+      float y[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        float t = act_fn<kAct>(finish_acc(v[i], bf_at(bq, i), bias_mode));
+        t = bf16r(t + bf_at(aq, i));  // an absent add reads as zeros: exact no-op
+        if constexpr (kMode == kEpiEuler) t = bf16r(bf_at(xq, i) + bf16r(dt * t));
+        y[i] = t;
       }
-      __nv_bfloat16* op = ep.out + static_cast<size_t>(out_row) * ep.ldo + ep.col_off + n0;
-      const bool vec_ok = (ep.ldo % 8 == 0) && ((ep.col_off + n0) % 8 == 0);
-      if (ep.mode == kEpiEuler) {
-        float xv[64];
-        load_bf16x64(op, vec_ok, nvalid, xv);
+      store8q(orow + n0, n, y);
+    }
+  } else if constexpr (kMode == kEpiSwiGLU) {
+    // every 64 columns: [0,32) gate, [32,64) up of hidden units n0/2 .. n0/2+31 (N % 64 == 0);
+    // set s takes hidden units 16s .. 16s+15 of each chunk
+    __nv_bfloat16* orow = ep.out + static_cast<size_t>(rc.out_row) * ep.ldo + ep.col_off;
+#pragma unroll 1
+    for (int c = 0; c < bn; c += 64) {
+      const int n0 = n_base + c;
+      const bool on = rc.live && n0 < pr.N;
+#pragma unroll 1
+      for (int j = 2 * set; j < 2 * set + 2; ++j) {
+        const uint4 bg = load8q(bias_row + n0 + 8 * j, on && bias_row, 8);
+        const uint4 bu = load8q(bias_row + n0 + 32 + 8 * j, on && bias_row, 8);
+        float g[8], u[8];
+        src.get8(c + 8 * j, rc.live, g);
+        src.get8(c + 32 + 8 * j, rc.live, u);
+        if (!on) continue;
+        float h[8];
 #pragma unroll
-        for (int i = 0; i < 64; ++i) v[i] = bf16r(xv[i] + bf16r(ep.dt * v[i]));
-      }
-      store_bf16x64(op, vec_ok, nvalid, v);
-    } else if (ep.mode == kEpiSwiGLU) {
-      // columns [0,32) gate, [32,64) up of hidden units n0/2 .. n0/2+31
-      float h[64];
-#pragma unroll
-      for (int i = 0; i < 32; ++i) {
-        const float g = finish_acc(v[i], bv[i], ep.bias_mode);
-        const float u = finish_acc(v[32 + i], bv[32 + i], ep.bias_mode);
-        const float sg = bf16r(g / (1.0f + expf(-g)));
-        h[i] = bf16r(sg * u);
-        h[32 + i] = 0.0f;
-      }
-      const int hcol = n0 / 2;
-      __nv_bfloat16* op = ep.out + static_cast<size_t>(out_row) * ep.ldo + ep.col_off + hcol;
-      const bool vec_ok = (ep.ldo % 8 == 0) && ((ep.col_off + hcol) % 8 == 0);
-      if (vec_ok) {
-        uint4* p = reinterpret_cast<uint4*>(op);
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          uint4 u;
-          u.x = pack_bf16x2(h[8 * i + 0], h[8 * i + 1]);
-          u.y = pack_bf16x2(h[8 * i + 2], h[8 * i + 3]);
-          u.z = pack_bf16x2(h[8 * i + 4], h[8 * i + 5]);
-          u.w = pack_bf16x2(h[8 * i + 6], h[8 * i + 7]);
-          p[i] = u;
+        for (int i = 0; i < 8; ++i) {
+          const float a = finish_acc(g[i], bf_at(bg, i), bias_mode);
+          const float b = finish_acc(u[i], bf_at(bu, i), bias_mode);
+          h[i] = bf16r(act_fn<kActSilu>(a) * b);
         }
-      } else {
-        for (int i = 0; i < 32; ++i) op[i] = __float2bfloat16_rn(h[i]);
+        store8q(orow + n0 / 2 + 8 * j, 8, h);
       }
-    } else {  // kEpiQKV: chunk = one head of q, k or v
-      const int inner = ep.H * 64;
+    }
+  } else {  // kEpiQKV: every 64 columns = one head of q, k or v; set s takes heads s, s+2, ...
+    const int inner = ep.H * 64;
+    const int tok = ep.tok_off + rc.t;
+#pragma unroll 1
+    for (int c = 64 * set; c < bn; c += 128) {
+      const int n0 = n_base + c;
+      if (n0 >= pr.N) break;  // uniform over the warp
       const int part = n0 / inner;
       const int head = (n0 - part * inner) / 64;
-      const int tok = ep.tok_off + t;
-      const size_t bh = static_cast<size_t>(bidx) * ep.H + head;
-#pragma unroll
-      for (int i = 0; i < 64; ++i) v[i] = finish_acc(v[i], bv[i], kBiasFused);
+      const size_t bh = static_cast<size_t>(rc.bidx) * ep.H + head;
+      const __nv_bfloat16* hb = bias_row ? bias_row + n0 : nullptr;
       if (part < 2) {
-        float ss = 0.0f;
-#pragma unroll
-        for (int i = 0; i < 64; ++i) ss += v[i] * v[i];
-        const float rstd = rsqrtf(ss * (1.0f / 64.0f) + ep.eps);
         const __nv_bfloat16* w = (part == 0) ? ep.qn_w : ep.kn_w;
-        float wv[64];
-        load_bf16x64(w, true, 64, wv);
+        const float4* cp = reinterpret_cast<const float4*>(ep.rope_cos + static_cast<size_t>(tok) * 32);
+        const float4* sp = reinterpret_cast<const float4*>(ep.rope_sin + static_cast<size_t>(tok) * 32);
+        const float4 z4 = make_float4(0.f, 0.f, 0.f, 0.f);
+        // operands of pass 2's first group: in flight during pass 1
+        uint4 nw = load8q(w, rc.live, 8);
+        float4 nc = rc.live ? cp[0] : z4, ns = rc.live ? sp[0] : z4;
+        float ss = 0.0f;
+        uint4 nb = load8q(hb, rc.live && hb, 8);
+#pragma unroll 1
+        for (int g = 0; g < 64; g += 8) {  // pass 1: sum of squares of the finished head
+          const uint4 bq = nb;
+          nb = load8q(hb + ((g + 8) & 63), rc.live && hb, 8);  // wraps to pass 2's first group
+          float v[8];
+          src.get8(c + g, rc.live, v);
 #pragma unroll
-        for (int i = 0; i < 64; ++i) v[i] = bf16r(wv[i] * (v[i] * rstd));
-        const float* cs = ep.rope_cos + static_cast<size_t>(tok) * 32;
-        const float* sn = ep.rope_sin + static_cast<size_t>(tok) * 32;
-#pragma unroll
-        for (int p = 0; p < 32; ++p) {
-          const float c0 = cs[p], s0 = sn[p];
-          const float a = v[2 * p], b = v[2 * p + 1];
-          v[2 * p] = bf16r(a * c0 - b * s0);
-          v[2 * p + 1] = bf16r(a * s0 + b * c0);
+          for (int i = 0; i < 8; ++i) {
+            const float y = finish_acc(v[i], bf_at(bq, i), kBiasFused);
+            ss += y * y;
+          }
         }
+        const float rstd = rsqrtf(ss * (1.0f / 64.0f) + ep.eps);
         __nv_bfloat16* dst = ((part == 0) ? ep.q : ep.k) + (bh * ep.L + tok) * 64;
-        store_bf16x64(dst, true, 64, v);
+#pragma unroll 1
+        for (int g = 0; g < 64; g += 8) {  // pass 2: RMSNorm (weight then cast) + pair RoPE
+          const uint4 bq = nb, wq = nw;
+          const float4 c4 = nc, s4 = ns;
+          const bool more = rc.live && g + 8 < 64;
+          nb = load8q(hb + g + 8, more && hb, 8);
+          nw = load8q(w + g + 8, more, 8);
+          nc = more ? cp[g / 8 + 1] : z4;
+          ns = more ? sp[g / 8 + 1] : z4;
+          float v[8];
+          src.get8(c + g, rc.live, v);
+          if (!rc.live) continue;
+          const float cc[4] = {c4.x, c4.y, c4.z, c4.w};
+          const float sv[4] = {s4.x, s4.y, s4.z, s4.w};
+          float y[8];
+#pragma unroll
+          for (int p = 0; p < 4; ++p) {
+            const float x0 = finish_acc(v[2 * p], bf_at(bq, 2 * p), kBiasFused);
+            const float x1 = finish_acc(v[2 * p + 1], bf_at(bq, 2 * p + 1), kBiasFused);
+            const float a = bf16r(bf_at(wq, 2 * p) * (x0 * rstd));
+            const float b = bf16r(bf_at(wq, 2 * p + 1) * (x1 * rstd));
+            y[2 * p] = bf16r(a * cc[p] - b * sv[p]);
+            y[2 * p + 1] = bf16r(a * sv[p] + b * cc[p]);
+          }
+          store8q(dst + g, 8, y);
+        }
       } else {
         __nv_bfloat16* dst = ep.vt + bh * 64 * ep.Lp + tok;
+#pragma unroll 1
+        for (int g = 0; g < 64; g += 8) {
+          const uint4 bq = load8q(hb + g, rc.live && hb, 8);
+          float v[8];
+          src.get8(c + g, rc.live, v);
+          if (!rc.live) continue;
 #pragma unroll
-        for (int d = 0; d < 64; ++d) dst[static_cast<size_t>(d) * ep.Lp] = __float2bfloat16_rn(v[d]);
+          for (int i = 0; i < 8; ++i) {
+            const float y = finish_acc(v[i], bf_at(bq, i), kBiasFused);
+            dst[static_cast<size_t>(g + i) * ep.Lp] =
+                __ushort_as_bfloat16(static_cast<unsigned short>(__float_as_uint(y) >> 16));
+          }
+        }
       }
     }
   }
 }
 
+// Dispatch of the activation (uniform per problem) outside the per-element loops.
+template <int kMode, class Src>
+__device__ __forceinline__ void unit_epilogue_act(const GemmProblem& pr, const RowCtx& rc,
+                                                  int n_base, int set, const Src& src) {
+  if constexpr (kMode == kEpiStore || kMode == kEpiEuler) {
+    switch (pr.ep.act) {
+      case kActRelu:
+        unit_epilogue<kMode, kActRelu>(pr, rc, n_base, set, src);
+        return;
+      case kActSilu:
+        unit_epilogue<kMode, kActSilu>(pr, rc, n_base, set, src);
+        return;
+      case kActSwish:
+        unit_epilogue<kMode, kActSwish>(pr, rc, n_base, set, src);
+        return;
+      default:
+        unit_epilogue<kMode, kActNone>(pr, rc, n_base, set, src);
+        return;
+    }
+  } else {
+    unit_epilogue<kMode, kActNone>(pr, rc, n_base, set, src);
+  }
+}
+
+// Unit `i` of this CTA's list (host LPT schedule or plain striding).
+__device__ __forceinline__ int cta_units(const GemmParams& P, int& first) {
+  const int cta = blockIdx.x;
+  if (P.explicit_sched) {
+    first = P.cta_begin[cta];
+    return P.cta_begin[cta + 1] - first;
+  }
+  first = 0;
+  return (P.nunits - cta + P.ncta - 1) / P.ncta;
+}
+
+__device__ __forceinline__ int unit_id(const GemmParams& P, int first, int i) {
+  return P.explicit_sched ? static_cast<int>(P.sched[first + i]) : blockIdx.x + i * P.ncta;
+}
+
+struct UnitInfo {
+  int pi, tile, tm, tn, ks, c_begin, c_end, nslots;
+};
+
+__device__ __forceinline__ UnitInfo decode_unit(const GemmParams& P, int u) {
+  UnitInfo d;
+  d.pi = 0;
+#pragma unroll
+  for (int i = 1; i < kMaxProblems; ++i)
+    if (i < P.nprob && u >= P.p[i].unit_begin) d.pi = i;
+  const GemmProblem& pr = P.p[d.pi];
+  const int local = u - pr.unit_begin;
+  d.ks = local % pr.nsplit;
+  d.tile = local / pr.nsplit;
+  d.tm = d.tile % pr.tiles_m;
+  d.tn = d.tile / pr.tiles_m;
+  d.c_begin = d.ks * pr.split_chunks;
+  d.c_end = min(pr.nchunks, d.c_begin + pr.split_chunks);
+  d.nslots = (d.c_end - d.c_begin + pr.ksub - 1) / pr.ksub;
+  return d;
+}
+
+}  // namespace
+
+template <int kMode>
 __global__ void __launch_bounds__(kGemmThreads, 1) gemm_bf16_kernel(const __grid_constant__ GemmParams P) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
   const int S = P.stages;
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + S * P.stage_bytes);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + S * P.slot_bytes + kRingSlack);
   uint64_t* empty = full + kMaxStages;
-  uint64_t* accum = empty + kMaxStages;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accum + 1);
+  uint64_t* acc_full = empty + kMaxStages;
+  uint64_t* acc_empty = acc_full + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
+  uint32_t* bcast = tmem_slot + 1;
 
-  const int bid = blockIdx.x;
-  int pi = 0;
-#pragma unroll
-  for (int i = 1; i < kMaxProblems; ++i)
-    if (i < P.nprob && bid >= P.p[i].tile_begin) pi = i;
-  const GemmProblem& pr = P.p[pi];
-  const int local = bid - pr.tile_begin;
-  const int tm = local % pr.tiles_m;
-  const int tn = local / pr.tiles_m;
-  const int nk = (pr.K + 63) / 64;
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
+  int first = 0;
+  const int nunits = cta_units(P, first);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
-      mbar_init(&full[s], 1);
+      mbar_init(&full[s], 2);  // A producer + B producer
       mbar_init(&empty[s], 1);
     }
-    mbar_init(accum, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&acc_full[i], 1);
+      mbar_init(&acc_empty[i], kEpiWarps);  // one arrival per epilogue warp
+    }
     fence_mbar_init();
   }
   if (warp == 0 && lane == 0) {
-    tma_prefetch_desc(&pr.ta);
-    tma_prefetch_desc(&pr.tb);
+    for (int i = 0; i < P.nprob; ++i) tma_prefetch_desc(&P.p[i].ta);
   }
-  if (warp == 1) tmem_alloc(tmem_slot, 256);
+  if (warp == 2 && lane == 0) {
+    for (int i = 0; i < P.nprob; ++i) tma_prefetch_desc(&P.p[i].tb);
+  }
+  if (warp == 1) tmem_alloc(tmem_slot, 2 * kAccCols);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  const uint32_t tmem_acc = *tmem_slot;
+  const uint32_t tmem_base = *tmem_slot;
+  // TMEM is held from here on: only now may dependent grids be scheduled next to this CTA.
   if (threadIdx.x == 0) griddep_launch();
 
-  if (warp == 0) {
+  if (warp == 0 || warp == 2) {
+    // ---------------- TMA producers: warp 0 = A (activations), warp 2 = B (weights) ----------
     if (lane == 0) {
-      const uint32_t a_bytes = static_cast<uint32_t>(pr.a_rows) * 128u;
-      const uint32_t b_bytes = static_cast<uint32_t>(pr.bn) * 128u;
-      const uint64_t pol_a = l2_policy_evict_last();
-      const uint64_t pol_b = (pr.tiles_m == 1) ? l2_policy_evict_first() : l2_policy_evict_last();
-      const int a_row0 = tm * pr.m_step;
-      const int n0 = tn * pr.bn;
-      const int cat = pr.cat_ids ? static_cast<int>(pr.cat_ids[tm]) : 0;
-      const int npre = min(S, nk);
-      // Weight tiles do not depend on the previous kernel: issue them first.
-      for (int kb = 0; kb < npre; ++kb) {
-        uint8_t* st = smem + kb * P.stage_bytes;
-        mbar_arrive_expect_tx(&full[kb], a_bytes + b_bytes);
-        if (pr.cat_ids)
-          tma_load_3d(st + kATileBytes, &pr.tb, &full[kb], kb * 64, n0, cat, pol_b);
-        else
-          tma_load_2d(st + kATileBytes, &pr.tb, &full[kb], kb * 64, n0, pol_b);
-      }
-      griddep_wait();
-      for (int kb = 0; kb < npre; ++kb)
-        tma_load_2d(smem + kb * P.stage_bytes, &pr.ta, &full[kb], kb * 64, a_row0, pol_a);
-      for (int kb = npre; kb < nk; ++kb) {
-        const int s = kb % S;
-        const uint32_t ph = static_cast<uint32_t>(kb / S) & 1u;
-        if (!mbar_wait(&empty[s], ph ^ 1u, kErrGemmTimeout + 1)) break;
-        uint8_t* st = smem + s * P.stage_bytes;
-        mbar_arrive_expect_tx(&full[s], a_bytes + b_bytes);
-        if (pr.cat_ids)
-          tma_load_3d(st + kATileBytes, &pr.tb, &full[s], kb * 64, n0, cat, pol_b);
-        else
-          tma_load_2d(st + kATileBytes, &pr.tb, &full[s], kb * 64, n0, pol_b);
-        tma_load_2d(st, &pr.ta, &full[s], kb * 64, a_row0, pol_a);
+      const bool is_a = (warp == 0);
+      if (is_a) griddep_wait();  // activations come from the previous kernel; weights do not
+      const uint64_t pol_keep = l2_policy_evict_last();
+      const uint64_t pol_once = l2_policy_evict_first();
+      int it = 0;
+      bool ok = true;
+      for (int i = 0; ok && i < nunits; ++i) {
+        const UnitInfo u = decode_unit(P, unit_id(P, first, i));
+        const GemmProblem& pr = P.p[u.pi];
+        const uint32_t a_sub = static_cast<uint32_t>(pr.a_rows) * 128u;
+        const uint32_t b_sub = static_cast<uint32_t>(pr.bn) * 128u;
+        const uint32_t bytes = (is_a ? a_sub : b_sub) * static_cast<uint32_t>(pr.ksub);
+        const int a_row0 = u.tm * pr.m_step;
+        const int n0 = u.tn * pr.bn;
+        const int cat = pr.cat_ids ? static_cast<int>(pr.cat_ids[u.tm]) : 0;
+        const uint64_t pol = is_a ? pol_keep : ((pr.tiles_m == 1 && !pr.cat_ids) ? pol_once : pol_keep);
+        for (int sl = 0; sl < u.nslots; ++sl, ++it) {
+          const int s = it % S;
+          const uint32_t ph = static_cast<uint32_t>(it / S) & 1u;
+          if (!mbar_wait(&empty[s], ph ^ 1u, kErrGemmTimeout + 1)) {
+            ok = false;
+            break;
+          }
+          uint8_t* slot = smem + s * P.slot_bytes;
+          const int chunk = u.c_begin + sl * pr.ksub;
+          mbar_arrive_expect_tx(&full[s], bytes);
+          if (is_a) {
+            if (pr.kdim3)
+              tma_load_3d(slot, &pr.ta, &full[s], 0, a_row0, chunk, pol);
+            else
+              tma_load_2d(slot, &pr.ta, &full[s], chunk * 64, a_row0, pol);
+          } else {
+            uint8_t* dst = slot + a_sub * pr.ksub;
+            if (pr.kdim3) {
+              if (pr.cat_ids)
+                tma_load_4d(dst, &pr.tb, &full[s], 0, n0, chunk, cat, pol);
+              else
+                tma_load_3d(dst, &pr.tb, &full[s], 0, n0, chunk, pol);
+            } else {
+              if (pr.cat_ids)
+                tma_load_3d(dst, &pr.tb, &full[s], chunk * 64, n0, cat, pol);
+              else
+                tma_load_2d(dst, &pr.tb, &full[s], chunk * 64, n0, pol);
+            }
+          }
+        }
       }
     }
   } else if (warp == 1) {
+    // ---------------- MMA issuer ----------------
     if (lane == 0) {
-      const uint32_t idesc = umma_idesc_bf16(128, pr.bn);
-      for (int kb = 0; kb < nk; ++kb) {
-        const int s = kb % S;
-        const uint32_t ph = static_cast<uint32_t>(kb / S) & 1u;
-        if (!mbar_wait(&full[s], ph, kErrGemmTimeout + 2)) break;
+      int it = 0;
+      bool ok = true;
+      for (int j = 0; ok && j < nunits; ++j) {
+        const UnitInfo u = decode_unit(P, unit_id(P, first, j));
+        const GemmProblem& pr = P.p[u.pi];
+        const int ab = j & 1;
+        if (!mbar_wait(&acc_empty[ab], (static_cast<uint32_t>(j >> 1) & 1u) ^ 1u, kErrGemmTimeout + 2))
+          break;
         tc_fence_after();
-        const uint32_t a_addr = smem_u32(smem + s * P.stage_bytes);
-        const uint32_t b_addr = a_addr + kATileBytes;
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(ab * kAccCols);
+        const uint32_t idesc = umma_idesc_bf16(128, pr.bn);
+        const uint32_t a_sub = static_cast<uint32_t>(pr.a_rows) * 128u;
+        const uint32_t b_sub = static_cast<uint32_t>(pr.bn) * 128u;
+        for (int sl = 0; sl < u.nslots; ++sl, ++it) {
+          const int s = it % S;
+          const uint32_t ph = static_cast<uint32_t>(it / S) & 1u;
+          if (!mbar_wait(&full[s], ph, kErrGemmTimeout + 2)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(smem + s * P.slot_bytes);
+          const uint32_t b_addr = a_addr + a_sub * static_cast<uint32_t>(pr.ksub);
+          const int nsub = min(pr.ksub, u.c_end - (u.c_begin + sl * pr.ksub));
+          for (int sub = 0; sub < nsub; ++sub) {
 #pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          umma_f16(tmem_acc, umma_desc_sw128(a_addr + 32 * k), umma_desc_sw128(b_addr + 32 * k),
-                   idesc, (kb | k) != 0 ? 1u : 0u);
+            for (int k = 0; k < 4; ++k) {
+              umma_f16(d_tmem, umma_desc_sw128(a_addr + sub * a_sub + 32 * k),
+                       umma_desc_sw128(b_addr + sub * b_sub + 32 * k), idesc,
+                       (sl | sub | k) != 0 ? 1u : 0u);
+            }
+          }
+          umma_commit(&empty[s]);
         }
-        umma_commit(&empty[s]);
+        if (!ok) break;
+        umma_commit(&acc_full[ab]);
       }
-      umma_commit(accum);
     }
   } else {
+    // ---------------- epilogue warps 3..10 ----------------
     griddep_wait();
-    if (mbar_wait(accum, 0, kErrGemmTimeout + 3)) {
+    const int quad = warp & 3;           // TMEM lane quadrant this warp may read
+    const int set = (warp - 3) >> 2;     // column half of the unit (0 or 1)
+    const int r_local = quad * 32 + lane;
+    const uint32_t lane_off = static_cast<uint32_t>(quad * 32) << 16;
+    // After a failed wait the warps keep walking the unit list (every wait then returns at
+    // once) so that all of them still meet at the named barriers of the K-split units.
+    bool ok = true;
+    for (int j = 0; j < nunits; ++j) {
+      const UnitInfo u = decode_unit(P, unit_id(P, first, j));
+      const GemmProblem& pr = P.p[u.pi];
+      const int ab = j & 1;
+      if (ok && !mbar_wait(&acc_full[ab], static_cast<uint32_t>(j >> 1) & 1u, kErrGemmTimeout + 3))
+        ok = false;
       tc_fence_after();
-      gemm_epilogue(pr, tmem_acc, tm, tn, warp & 3, lane);
+      const uint32_t tacc = tmem_base + lane_off + static_cast<uint32_t>(ab * kAccCols);
+      const RowCtx rc = row_ctx(pr, u.tm, r_local);
+      const int n_base = u.tn * pr.bn;
+      auto release = [&]() {
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&acc_empty[ab]);
+      };
+
+      if (pr.nsplit == 1) {
+        if (!ok) continue;
+        unit_epilogue_act<kMode>(pr, rc, n_base, set, TmemSrc{tacc});
+        release();
+        continue;
+      }
+
+      // K split: write this unit's fp32 partial tile, count arrivals, the last one reduces.
+      const size_t split_stride = static_cast<size_t>(128) * pr.bn;
+      float* row0 = P.ws + pr.ws_off + static_cast<size_t>(u.tile) * pr.nsplit * split_stride +
+                    static_cast<size_t>(r_local) * pr.bn;
+      if (ok) {
+        const TmemSrc src{tacc};
+#pragma unroll 1
+        for (int col = set * 32; col < pr.bn; col += (col % 32 == 24) ? 40 : 8) {
+          float v[8];
+          src.get8(col, rc.live, v);
+          if (rc.live && n_base + col < pr.N) {
+            float4* dst = reinterpret_cast<float4*>(row0 + u.ks * split_stride + col);
+            dst[0] = make_float4(v[0], v[1], v[2], v[3]);
+            dst[1] = make_float4(v[4], v[5], v[6], v[7]);
+          }
+        }
+        release();
+      }
+      __threadfence();
+      named_bar_sync(1, kEpiWarps * 32);
+      if (threadIdx.x == kEpiWarp0 * 32) {
+        unsigned int* cnt = P.counters + pr.cnt_off + u.tile;
+        const unsigned int prev = atomicAdd(cnt, 1u);
+        const bool last = (prev == static_cast<unsigned int>(pr.nsplit - 1));
+        if (last) *cnt = 0u;  // every split of this tile has arrived: ready for the next launch
+        *bcast = last ? 1u : 0u;
+      }
+      named_bar_sync(1, kEpiWarps * 32);
+      const bool last = (*reinterpret_cast<volatile uint32_t*>(bcast) != 0u);
+      named_bar_sync(1, kEpiWarps * 32);  // bcast is rewritten by the next split unit
+      if (!last || !ok) continue;
+      __threadfence();
+      unit_epilogue_act<kMode>(pr, rc, n_base, set, PartSrc{row0, split_stride, pr.nsplit});
     }
   }
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem_acc, 256);
+    tmem_dealloc(tmem_base, 2 * kAccCols);
   }
 }
 
-size_t gemm_smem_bytes(int stages, int stage_bytes) {
-  return 1024 + static_cast<size_t>(stages) * stage_bytes + (2 * kMaxStages + 2) * 8;
+// At least 116 KB so that two CTAs never share an SM: a second CTA would only wait in
+// tcgen05.alloc for the first one's 512 TMEM columns.
+size_t gemm_smem_bytes(int stages, int slot_bytes) {
+  const size_t need = 1024 + static_cast<size_t>(stages) * slot_bytes + kRingSlack + 256;
+  return need < 116 * 1024 ? 116 * 1024 : need;
 }
 
 cudaError_t gemm_prepare_device() {
-  return cudaFuncSetAttribute(gemm_bf16_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                              227 * 1024);
+  cudaError_t e = cudaSuccess;
+  auto set = [&](const void* fn) {
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+  };
+  set(reinterpret_cast<const void*>(gemm_bf16_kernel<kEpiStore>));
+  set(reinterpret_cast<const void*>(gemm_bf16_kernel<kEpiSwiGLU>));
+  set(reinterpret_cast<const void*>(gemm_bf16_kernel<kEpiQKV>));
+  set(reinterpret_cast<const void*>(gemm_bf16_kernel<kEpiEuler>));
+  return e;
 }
 
-cudaError_t launch_gemm(const GemmParams& params, int total_tiles, cudaStream_t stream, bool pdl) {
+cudaError_t launch_gemm(const GemmParams& params, cudaStream_t stream, bool pdl) {
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(total_tiles, 1, 1);
+  cfg.gridDim = dim3(params.ncta, 1, 1);
   cfg.blockDim = dim3(kGemmThreads, 1, 1);
-  cfg.dynamicSmemBytes = gemm_smem_bytes(params.stages, params.stage_bytes);
+  cfg.dynamicSmemBytes = gemm_smem_bytes(params.stages, params.slot_bytes);
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = pdl ? 1 : 0;
-  return cudaLaunchKernelEx(&cfg, gemm_bf16_kernel, params);
+  switch (params.p[0].ep.mode) {  // every problem of a launch shares the epilogue mode
+    case kEpiSwiGLU:
+      return cudaLaunchKernelEx(&cfg, gemm_bf16_kernel<kEpiSwiGLU>, params);
+    case kEpiQKV:
+      return cudaLaunchKernelEx(&cfg, gemm_bf16_kernel<kEpiQKV>, params);
+    case kEpiEuler:
+      return cudaLaunchKernelEx(&cfg, gemm_bf16_kernel<kEpiEuler>, params);
+    default:
+      return cudaLaunchKernelEx(&cfg, gemm_bf16_kernel<kEpiStore>, params);
+  }
 }
 
 }  // namespace rldx

@@ -1,16 +1,29 @@
 // Grouped bf16 GEMM for sm_100a: up to kMaxProblems independent problems (the cognition /
-// action / physics streams of one MSAT projection) share one launch.  Each CTA owns one
-// 128 x BN output tile of one problem and runs the full K loop:
+// action / physics streams of one MSAT projection) share one persistent launch.
 //
-//   warp 0      TMA producer: B (weight) tiles are issued before griddepcontrol.wait, so a
-//               programmatic-dependent launch streams weights while the previous kernel drains;
-//               A (activation) tiles after it.
-//   warp 1      TMEM allocator + single-thread tcgen05.mma issuer (M=128, N=BN, K=16 steps).
-//   warps 2..5  epilogue: tcgen05.ld of the fp32 accumulator (thread = output row) and the
-//               fused row epilogue (bias / activation / residual / SwiGLU / QK-RMSNorm+RoPE /
-//               Euler update), written straight to global memory.
+// Work unit = (problem, 128-row M tile, BN-column N tile, K split).  The host orders the units
+// longest-first and deals them to at most one CTA per SM (LPT schedule, kept in the launch
+// parameters), so the weight-streaming work of all streams is spread evenly over the SMs.
+// Roles inside a CTA (352 threads):
 //
-// Operands are K-major in 128-byte-swizzled shared-memory tiles (64 bf16 of K per row).
+//   warp 0      TMA producer of A (activations), after griddepcontrol.wait.
+//   warp 2      TMA producer of B (weights).  Weights never depend on the previous kernel, so
+//               this warp starts streaming them as soon as the CTA is resident, overlapping the
+//               tail of the previous kernel under programmatic dependent launch.
+//   warp 1      TMEM allocator + single-thread tcgen05.mma issuer (M=128, N=BN, K=16 steps)
+//               into one of two TMEM accumulators (2 x 256 columns), so the epilogue of one
+//               unit overlaps the main loop of the next.
+//   warps 3..10 epilogue: two warps per TMEM lane quadrant (thread = output row) split the
+//               unit's columns; tcgen05.ld of 8 fp32 columns at a time and the fused row
+//               epilogue (bias / activation / residual / SwiGLU / QK-RMSNorm+RoPE / Euler
+//               update), written straight to global memory.  K-split units write fp32
+//               partial tiles to a workspace; the last of a tile's units to finish (arrival
+//               counter) adds the partials in split order and runs the epilogue, so results do
+//               not depend on which CTA finishes last.
+//
+// Operands are K-major in 128-byte-swizzled shared-memory tiles (64 bf16 of K per row).  When
+// K is a multiple of 64 the tensor maps view each operand as [K/64][rows][64], so one TMA box
+// brings `ksub` consecutive 64-wide K chunks (one instruction per operand per ring slot).
 // C = A[M,K] * B[N,K]^T, the nn.Linear convention, so weights are used in place.
 #pragma once
 #include "common.cuh"
@@ -19,8 +32,13 @@ namespace rldx {
 
 constexpr int kMaxProblems = 4;
 constexpr int kMaxStages = 8;
-constexpr int kGemmThreads = 192;
-constexpr int kATileBytes = 128 * 128;  // 128 rows x 128 bytes
+constexpr int kEpiWarp0 = 3;         // first epilogue warp
+constexpr int kEpiWarps = 8;         // two warps per TMEM lane quadrant, splitting the columns
+constexpr int kGemmThreads = (kEpiWarp0 + kEpiWarps) * 32;
+constexpr int kMaxUnits = 1536;     // explicit schedule capacity; larger launches stride units
+constexpr int kMaxCtas = 160;       // >= SM count of the part
+constexpr int kRingSlack = 16384;   // the MMA reads 128 A rows from every A sub-tile
+constexpr int kAccCols = 256;       // TMEM columns per accumulator (two accumulators)
 
 enum EpiMode : int {
   kEpiStore = 0,   // y = act(bias(acc)) (+ add) -> out
@@ -55,13 +73,21 @@ struct GemmEpilogue {
 };
 
 struct __align__(64) GemmProblem {
-  CUtensorMap ta;  // A [M, K] (2D), box (64, a_rows)
-  CUtensorMap tb;  // B [N, K] (2D) or [categories, N, K] (3D), box (64, bn[, 1])
+  CUtensorMap ta;  // A: [K/64][M][64] (kdim3) or [M][K] (2D)
+  CUtensorMap tb;  // B: [K/64][N][64] / [cats][K/64][N][64] (kdim3) or [N][K] / [cats][N][K]
   int M, N, K;
   int bn;          // tile N (64..256, multiple of 64)
-  int a_rows;      // A box rows (8..128)
+  int a_rows;      // A box rows (8..128, multiple of 8)
   int m_step;      // output rows owned by one M tile (<= 128)
-  int tiles_m, tiles_n, tile_begin;
+  int tiles_m, tiles_n;
+  int nchunks;     // ceil(K / 64)
+  int ksub;        // 64-wide K chunks per TMA box (1 unless kdim3)
+  int kdim3;       // 1: chunked tensor maps (K % 64 == 0)
+  int nsplit;      // K splits per output tile
+  int split_chunks;  // chunks per split (the last split may hold fewer)
+  int unit_begin;  // first unit id of this problem
+  long long ws_off;  // float offset of this problem's partial tiles in the workspace
+  int cnt_off;     // offset of this problem's tile counters
   const long long* cat_ids;  // non-null: M tile index = batch element, B slab = cat_ids[tile]
   GemmEpilogue ep;
 };
@@ -70,10 +96,17 @@ struct GemmParams {
   GemmProblem p[kMaxProblems];
   int nprob;
   int stages;
-  int stage_bytes;  // kATileBytes + bn_max * 128
+  int slot_bytes;
+  int nunits;
+  int ncta;
+  int explicit_sched;       // 1: sched/cta_begin hold the unit list; 0: unit = cta + i * ncta
+  float* ws;                // K-split partial tiles (fp32)
+  unsigned int* counters;   // one arrival counter per split tile; zero between launches
+  unsigned short cta_begin[kMaxCtas + 1];
+  unsigned short sched[kMaxUnits];
 };
 
-size_t gemm_smem_bytes(int stages, int stage_bytes);
-cudaError_t launch_gemm(const GemmParams& params, int total_tiles, cudaStream_t stream, bool pdl);
+size_t gemm_smem_bytes(int stages, int slot_bytes);
+cudaError_t launch_gemm(const GemmParams& params, cudaStream_t stream, bool pdl);
 
 }  // namespace rldx

@@ -22,11 +22,15 @@ bool make_tmap_3d(CUtensorMap* m, const void* base, uint64_t d0, uint64_t d1, ui
                   uint64_t stride1_bytes, uint64_t stride2_bytes, uint32_t b0, uint32_t b1,
                   uint32_t b2, std::string* err);
 
-// Validates one GEMM description and fills the device problem (tile choice included).
-bool build_gemm_problem(const rldx_gemm_desc& d, GemmProblem* p, std::string* err);
-// Packs up to kMaxProblems problems into one launch; returns the grid size in *tiles.
-bool build_gemm_params(const rldx_gemm_desc* d, int n, GemmParams* params, int* tiles,
-                       std::string* err);
+// Validates one GEMM description and fills the shape-only fields of the device problem.
+bool validate_gemm_problem(const rldx_gemm_desc& d, GemmProblem* p, std::string* err);
+// Plans up to kMaxProblems problems as one persistent launch: tile widths and K splits from a
+// cost model, ring sizing, tensor maps and the longest-first unit schedule.  K splits need a
+// workspace (`ws`, `ws_bytes`: tile counters that start at zero, then fp32 partial tiles);
+// with ws == nullptr no problem is split.  *ws_needed (optional) receives the workspace bytes
+// the plan would use if a workspace were given.
+bool build_gemm_params(const rldx_gemm_desc* d, int n, void* ws, size_t ws_bytes,
+                       GemmParams* params, size_t* ws_needed, std::string* err);
 
 int sm_count();
 

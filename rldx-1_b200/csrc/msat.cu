@@ -55,6 +55,14 @@ float bf_round(float f) {
   return r;
 }
 
+// K-split GEMMs in the control step: off by default (measured slower at batch 1 on B200, where
+// the last split's reduction pass costs more than the idle SMs it recovers); RLDX_MSAT_SPLIT_K=1
+// turns them on.
+bool split_k_enabled() {
+  const char* e = std::getenv("RLDX_MSAT_SPLIT_K");
+  return e && e[0] == '1';
+}
+
 struct Fail : std::runtime_error {
   int code;
   Fail(int c, const std::string& m) : std::runtime_error(m), code(c) {}
@@ -124,6 +132,11 @@ struct rldx_msat {
   std::vector<bf16*> act_cat, phf_cat;
 
   std::vector<Op> ops;
+  // K-split workspace shared by every GEMM launch of the step (launches are stream-ordered):
+  // tile arrival counters (zero between launches) followed by fp32 partial tiles.
+  void* gemm_ws = nullptr;
+  size_t gemm_ws_bytes = 0, ws_need = 0;
+  bool sizing = false;
   cudaStream_t stream = nullptr;
   cudaGraph_t graph = nullptr;
   cudaGraphExec_t exec = nullptr;
@@ -252,8 +265,12 @@ struct rldx_msat {
     std::memset(&o, 0, sizeof(o));
     o.kind = Op::kGemm;
     std::string err;
-    if (!build_gemm_params(v.data(), static_cast<int>(v.size()), &o.g, &o.grid, &err))
+    size_t need = 0;
+    if (!build_gemm_params(v.data(), static_cast<int>(v.size()), sizing ? nullptr : gemm_ws,
+                           sizing ? 0 : gemm_ws_bytes, &o.g, sizing ? &need : nullptr, &err))
       throw Fail(RLDX_ERR_ARG, err);
+    ws_need = std::max(ws_need, need);
+    o.grid = o.g.ncta;
     for (const rldx_gemm_desc& d : v) {
       const double M = d.M, N = d.N, K = d.K;
       const double slabs = d.cat_ids ? static_cast<double>(d.M / d.rows_per_cat) : 1.0;
@@ -307,7 +324,7 @@ struct rldx_msat {
       cudaError_t e = cudaSuccess;
       switch (o.kind) {
         case Op::kGemm:
-          e = launch_gemm(o.g, o.grid, st, p);
+          e = launch_gemm(o.g, st, p);
           break;
         case Op::kAttn:
           e = launch_attention(o.a, st, p);
@@ -473,6 +490,16 @@ void rldx_msat::create(const rldx_msat_config& cfg, const rldx_msat_weights& w) 
   pdec_h = alloc<bf16>(static_cast<size_t>(B) * np * D);
 
   precompute(w);
+  if (split_k_enabled()) {
+    sizing = true;  // first pass: workspace the K-split plans want
+    plan();
+    sizing = false;
+    ops.clear();
+    if (ws_need > 0) {
+      gemm_ws = alloc<uint8_t>(ws_need);  // zero-filled: the tile counters start at zero
+      gemm_ws_bytes = ws_need;
+    }
+  }
   plan();
 
   // Warm-up run (loads every kernel), then capture.
@@ -557,10 +584,10 @@ void rldx_msat::precompute(const rldx_msat_weights& w) {
   std::string err;
   auto run = [&](std::initializer_list<rldx_gemm_desc> ds) {
     std::vector<rldx_gemm_desc> v(ds);
-    GemmParams gp;
-    int tiles = 0;
-    if (!build_gemm_params(v.data(), static_cast<int>(v.size()), &gp, &tiles, &err)) throw Fail(RLDX_ERR_ARG, err);
-    ck(launch_gemm(gp, tiles, stream, false), "bind gemm");
+    static GemmParams gp;
+    if (!build_gemm_params(v.data(), static_cast<int>(v.size()), nullptr, 0, &gp, nullptr, &err))
+      throw Fail(RLDX_ERR_ARG, err);
+    ck(launch_gemm(gp, stream, false), "bind gemm");
     ck(cudaStreamSynchronize(stream), "bind gemm sync");
   };
   {

@@ -94,10 +94,24 @@ def gemm_desc(
     return d
 
 
-def gemm(descs: Sequence[GemmDesc]) -> None:
-    """Runs 1..4 GEMM problems in one grouped launch on the current stream."""
+def gemm(descs: Sequence[GemmDesc], workspace: torch.Tensor = None) -> None:
+    """Runs 1..4 GEMM problems in one grouped launch on the current stream.  With `workspace`
+    (a zero-filled device byte tensor, at least gemm_workspace_size(descs) long) long K loops
+    may be split across SMs; calls sharing a workspace must stay on one stream."""
     arr = (GemmDesc * len(descs))(*descs)
-    check(load().rldx_gemm(arr, len(descs), _stream()))
+    if workspace is None:
+        check(load().rldx_gemm(arr, len(descs), _stream()))
+        return
+    _need(workspace, "workspace", torch.uint8)
+    check(load().rldx_gemm_ws(arr, len(descs), workspace.data_ptr(), workspace.numel(), _stream()))
+
+
+def gemm_workspace_size(descs: Sequence[GemmDesc]) -> int:
+    """Workspace bytes with which gemm(descs, workspace) would split K (0: no split)."""
+    arr = (GemmDesc * len(descs))(*descs)
+    n = C.c_uint64(0)
+    check(load().rldx_gemm_workspace_size(arr, len(descs), C.byref(n)))
+    return int(n.value)
 
 
 def linear(x, weight, bias=None, *, act=_lib.ACT_NONE, bias_mode=_lib.BIAS_FUSED, add=None,

@@ -187,3 +187,105 @@ def test_bad_arguments_raise(cuda):
         ops.linear(x, w)
     with pytest.raises(ValueError):
         ops.linear(x.cpu(), w)
+
+
+# Arrival counters sit in the first bytes of the workspace (one uint32 per split tile, the
+# region rounded up to 256 bytes for up to 1536 units).
+COUNTER_BYTES = 6144
+
+
+def _block_like(cuda, seed, hidden=4096):
+    """The four projections of one MSAT block for [VL 512 | SA 18 | P 32] at width 1536."""
+    g = torch.Generator(device=cuda).manual_seed(seed)
+    keep, cases = [], []
+    for M in (512, 18, 32):
+        x = torch.randn(M, hidden, device=cuda, generator=g).to(BF)
+        w = (torch.randn(1536, hidden, device=cuda, generator=g) * 0.02).to(BF)
+        b = (torch.randn(1536, device=cuda, generator=g) * 0.1).to(BF)
+        res = torch.randn(M, 1536, device=cuda, generator=g).to(BF)
+        keep += [x, w, b, res]
+        cases.append((x, w, b, res))
+    return keep, cases
+
+
+@pytest.mark.parametrize("hidden", [1536, 4096])
+def test_split_k_workspace_matches_reference_and_is_deterministic(cuda, hidden):
+    """Grouped long-K GEMM (w3-like, residual epilogue) through the K-split path: close to the
+    fp32 reference, bit-identical across calls, counters back at zero."""
+    keep, cases = _block_like(cuda, 21 + hidden, hidden)
+    outs = [torch.empty(x.shape[0], 1536, dtype=BF, device=cuda) for x, *_ in cases]
+    descs = [ops.gemm_desc(x, w, o, b, add=res) for (x, w, b, res), o in zip(cases, outs)]
+    need = ops.gemm_workspace_size(descs)
+    assert need > COUNTER_BYTES, "the planner should split K for these shapes"
+    ws = torch.zeros(need, dtype=torch.uint8, device=cuda)
+    ops.gemm(descs, workspace=ws)
+    torch.cuda.synchronize()
+    first = [o.clone() for o in outs]
+    assert int(ws[:COUNTER_BYTES].count_nonzero()) == 0
+    ops.gemm(descs, workspace=ws)
+    torch.cuda.synchronize()
+    for o, f in zip(outs, first):
+        assert torch.equal(o, f)
+    for (x, w, b, res), o in zip(cases, outs):
+        ref = r(ref_finish(x.float() @ w.float().t(), b, _lib.BIAS_FUSED, 0) + res.float())
+        close(o, ref)
+    assert int(ws[:COUNTER_BYTES].count_nonzero()) == 0
+    assert ops.device_error() == 0
+
+
+def test_split_k_swiglu_and_qkv_epilogues(cuda):
+    """The K-split reduction feeds the SwiGLU and QKV epilogues like the unsplit path."""
+    g = torch.Generator(device=cuda).manual_seed(31)
+    M, K, hid = 18, 1536, 4096
+    x = torch.randn(M, K, device=cuda, generator=g).to(BF)
+    w12 = (torch.randn(2 * hid, K, device=cuda, generator=g) * 0.03).to(BF)
+    b12 = (torch.randn(2 * hid, device=cuda, generator=g) * 0.1).to(BF)
+    idx = torch.arange(2 * hid, device=cuda).view(2, hid // 32, 32).permute(1, 0, 2).reshape(-1)
+    w12i, b12i = w12[idx].contiguous(), b12[idx].contiguous()
+    h_ws = torch.empty(M, hid, dtype=BF, device=cuda)
+    h_plain = torch.empty_like(h_ws)
+    d_ws = [ops.gemm_desc(x, w12i, h_ws, b12i, epilogue=_lib.EPI_SWIGLU)]
+    ws = torch.zeros(max(ops.gemm_workspace_size(d_ws), 16), dtype=torch.uint8, device=cuda)
+    ops.gemm(d_ws, workspace=ws)
+    ops.gemm([ops.gemm_desc(x, w12i, h_plain, b12i, epilogue=_lib.EPI_SWIGLU)])
+    torch.cuda.synchronize()
+    y = r(x.float() @ w12.float().t() + b12.float())
+    x1, x2 = y.chunk(2, dim=-1)
+    close(h_ws, r(r(F.silu(x1)) * x2))
+    close(h_ws, h_plain.float())
+
+    H, n, L, tok_off, Lp = 24, 18, 40, 10, 40
+    wq = (torch.randn(3 * H * 64, K, device=cuda, generator=g) * 0.03).to(BF)
+    bq = (torch.randn(3 * H * 64, device=cuda, generator=g) * 0.1).to(BF)
+    qn = (1 + 0.1 * torch.randn(64, device=cuda, generator=g)).to(BF)
+    kn = (1 + 0.1 * torch.randn(64, device=cuda, generator=g)).to(BF)
+    ang = torch.rand(L, 32, device=cuda, generator=g) * 6.28
+    cos, sin = torch.cos(ang).contiguous(), torch.sin(ang).contiguous()
+    res = []
+    for use_ws in (True, False):
+        q = torch.zeros(1, H, L, 64, dtype=BF, device=cuda)
+        k = torch.zeros_like(q)
+        vt = torch.zeros(1, H, 64, Lp, dtype=BF, device=cuda)
+        d = [ops.qkv_desc(x, wq, bq, qn, kn, cos, sin, q, k, vt, tok_off=tok_off, rows_per_batch=n)]
+        if use_ws:
+            ws = torch.zeros(max(ops.gemm_workspace_size(d), 16), dtype=torch.uint8, device=cuda)
+            ops.gemm(d, workspace=ws)
+        else:
+            ops.gemm(d)
+        torch.cuda.synchronize()
+        res.append((q, k, vt))
+    for a, b in zip(res[0], res[1]):
+        close(a, b.float())
+    assert ops.device_error() == 0
+
+
+def test_workspace_too_small_runs_unsplit(cuda):
+    g = torch.Generator(device=cuda).manual_seed(5)
+    x = torch.randn(32, 4096, device=cuda, generator=g).to(BF)
+    w = (torch.randn(1536, 4096, device=cuda, generator=g) * 0.02).to(BF)
+    out = torch.empty(32, 1536, dtype=BF, device=cuda)
+    d = [ops.gemm_desc(x, w, out)]
+    ws = torch.zeros(64, dtype=torch.uint8, device=cuda)
+    ops.gemm(d, workspace=ws)
+    torch.cuda.synchronize()
+    close(out, r(x.float() @ w.float().t()))
