@@ -112,6 +112,15 @@ int rldx_gemm_workspace_size(const rldx_gemm_desc* problems, int nproblems, uint
 int rldx_gemm_ws(const rldx_gemm_desc* problems, int nproblems, void* workspace,
                  uint64_t workspace_bytes, void* stream);
 
+/* rldx_gemm_ws without a caller workspace: the K-split partials and arrival counters live in
+ * an 8 MiB static device array of the library.  For callers that cannot allocate device
+ * memory when they run a GEMM (allocator-free serving paths, C-ABI hosts without a CUDA
+ * allocator).  No counterpart in the reference.  Allocates nothing.  The first call on a
+ * device sets the scratch up (address lookup and a synchronous zero-fill): make it before any
+ * stream capture.  Plans needing more than 8 MiB of workspace fail with RLDX_ERR_UNSUPPORTED.
+ * One scratch per device: calls that overlap on the GPU race, so order them on one stream. */
+int rldx_gemm_static_ws(const rldx_gemm_desc* problems, int nproblems, void* stream);
+
 /* ------------------------------------------------------------------------------------------
  * Joint-stream attention (non-causal, head_dim 64, scale 1/8) over [seg0 | seg1 | seg2].
  * Replaces the F.scaled_dot_product_attention of ds::fused_attention_3way

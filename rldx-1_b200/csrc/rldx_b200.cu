@@ -4,4 +4,5 @@
 #include "rownorm.cu"
 #include "relayout.cu"
 #include "capi.cu"
+#include "static_ws.cu"
 #include "msat.cu"
