@@ -334,7 +334,11 @@ def run_b200(args, rank, world, local):
         "roofline": {"bound": "hbm", "kernel": "gemm_bf16_kernel (grouped tcgen05 GEMM, all launches of a step)",
                      "achieved": achieved, "peak": hbm_peak, "unit": "GB/s", "frac": achieved / hbm_peak,
                      "peak_source": peak_kind,
-                     "traffic": traffic.get("bytes_per_launch") if traffic else None,
+                     # ncu DRAM bytes of a captured launch, scaled by its ratio to the algorithmic
+                     # bytes onto the average launch of the step (one capture, not every launch)
+                     "traffic": (traffic["dram_bytes"] / traffic["algorithmic_bytes"] * g_bytes / len(gem))
+                                if traffic else None,
+                     "traffic_source": traffic.get("capture") if traffic else None,
                      "bytes_per_launch": g_bytes / len(gem), "avg_launch_us": g_ms / len(gem) * 1e3,
                      "tensor_tflops": tflops, "tensor_frac": tflops / tc_peak},
         "breakdown_ms": {k: {"launches": v[0], "ms": round(v[1], 4)} for k, v in by_kind.items()},

@@ -1,7 +1,6 @@
 """B200-native (sm_100a) MSAT real-time inference: the all-modality action head of RLDX-1.
 
   rldx_b200.chain.B200ExpandedActionHeadChain   drop-in for CustomExpandedActionHeadChain
-  rldx_b200.serve.install                       drop-in for apply_optimization's action head
   rldx_b200.ops                                 per-kernel wrappers (tests, op-level use)
   rldx_b200.replicas                            data-parallel replicas (one process per GPU)
 

@@ -262,10 +262,10 @@ class B200ExpandedActionHeadChain(nn.Module):
         return out
 
     def __del__(self):
-        h = getattr(self, "_handle", None)
+        # plain dict access: nn.Module.__setattr__ may be unusable during interpreter shutdown
+        h = self.__dict__.pop("_handle", None)
         if h:
             try:
                 _lib.load().rldx_msat_destroy(h)
             except Exception:  # noqa: BLE001
                 pass
-            self._handle = None
