@@ -10,10 +10,12 @@
 // One CTA = one (128-query tile, head, batch element).  Q, K come as [B*H, L, 64] and V as
 // V^T [B*H, 64, Lp] (written by the QKV GEMM epilogue), so every tcgen05 operand is K-major:
 //   S_j  = Q K_j^T          (M=128, N=64 keys, K=64 dims)   -> TMEM, double buffered
-//   O_j  = P_j V_j          (M=128, N=64 dims, K=64 keys)   -> TMEM, double buffered
-// The four softmax warps own one query row per thread: row max / sum need no shuffles, P_j is
-// written to shared memory in the 128-byte-swizzled K-major layout the next MMA reads, and the
-// per-tile O_j is folded into a register accumulator with the online-softmax rescale.
+//   O   += P_j V_j          (M=128, N=64 dims, K=64 keys)   -> one TMEM accumulator
+// The four softmax warps own one query row per thread, so row max / sum need no shuffles.
+// P_j goes to shared memory in the 128-byte-swizzled K-major layout the PV MMA reads.  The
+// running max is rescaled lazily: exponentials use a reference max that only moves when a
+// row's max grows by more than 2^8 (P then stays <= 256, exact in the final O / l); only then
+// is that row of O read from TMEM, scaled and written back, after the previous PV MMA landed.
 #include "kernels.cuh"
 
 namespace rldx {
@@ -23,6 +25,8 @@ constexpr int kKvStages = 3;
 constexpr int kQBytes = 128 * 128;
 constexpr int kKvTileBytes = 64 * 128;
 constexpr int kPBytes = 128 * 128;
+constexpr float kRescaleLog2 = 8.0f;  // lazy-rescale threshold (log2 units)
+constexpr uint32_t kOCol = 128;       // TMEM column of the O accumulator (S buffers at 0, 64)
 
 __global__ void __launch_bounds__(kAttnThreads, 1) joint_attention_kernel(const __grid_constant__ AttnParams P) {
   extern __shared__ uint8_t smem_raw[];
@@ -40,9 +44,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1) joint_attention_kernel(const 
   uint64_t* s_empty = s_full + 2;
   uint64_t* p_full = s_empty + 2;
   uint64_t* p_empty = p_full + 2;
-  uint64_t* o_full = p_empty + 2;
-  uint64_t* o_empty = o_full + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_empty + 2);
+  uint64_t* o_done = p_empty + 2;  // one phase per PV MMA
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_done + 1);
 
   const int q0 = blockIdx.x * 128;
   const int head = blockIdx.y;
@@ -64,9 +67,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1) joint_attention_kernel(const 
       mbar_init(&s_empty[i], 4);
       mbar_init(&p_full[i], 4);
       mbar_init(&p_empty[i], 1);
-      mbar_init(&o_full[i], 1);
-      mbar_init(&o_empty[i], 4);
     }
+    mbar_init(o_done, 1);
     fence_mbar_init();
   }
   if (warp == 0 && lane == 0) {
@@ -126,140 +128,153 @@ __global__ void __launch_bounds__(kAttnThreads, 1) joint_attention_kernel(const 
           if (!ok) break;
         }
         const int pb = j & 1;
-        const uint32_t ph = static_cast<uint32_t>(j >> 1) & 1u;
-        if (!mbar_wait(&p_full[pb], ph, kErrAttnTimeout + 2)) break;
-        if (!mbar_wait(&o_empty[pb], ph ^ 1u, kErrAttnTimeout + 2)) break;
+        if (!mbar_wait(&p_full[pb], static_cast<uint32_t>(j >> 1) & 1u, kErrAttnTimeout + 2)) break;
         tc_fence_after();
         const int s = j % kKvStages;
         const uint32_t p_addr = smem_u32(sP + pb * kPBytes);
         const uint32_t v_addr = smem_u32(sV + s * kKvTileBytes);
 #pragma unroll
         for (int k = 0; k < 4; ++k)
-          umma_f16(tmem + 128 + pb * 64, umma_desc_sw128(p_addr + 32 * k),
-                   umma_desc_sw128(v_addr + 32 * k), idesc, k != 0 ? 1u : 0u);
-        umma_commit(&o_full[pb]);
+          umma_f16(tmem + kOCol, umma_desc_sw128(p_addr + 32 * k), umma_desc_sw128(v_addr + 32 * k),
+                   idesc, (j | k) != 0 ? 1u : 0u);
+        umma_commit(o_done);
         umma_commit(&kv_empty[s]);
         umma_commit(&p_empty[pb]);
       }
     }
   } else {
-    // ---------------- softmax / output warps ----------------
+    // ---------------- softmax warps ----------------
     griddep_wait();
-    const int lane_grp = warp & 3;
-    const int r = lane_grp * 32 + lane;
+    const int quad = warp & 3;
+    const int r = quad * 32 + lane;
     const int qrow = q0 + r;
-    const uint32_t lane_off = static_cast<uint32_t>(lane_grp * 32) << 16;
+    const uint32_t lane_off = static_cast<uint32_t>(quad * 32) << 16;
     const unsigned char* kmask = P.key_mask ? P.key_mask + static_cast<size_t>(b) * L : nullptr;
-    float m_run = -INFINITY, l_run = 0.0f, alpha_pend = 0.0f;
-    float acc[64];
-#pragma unroll
-    for (int i = 0; i < 64; ++i) acc[i] = 0.0f;
+    const float scale = P.scale_log2;
+    float m_ref = -INFINITY;  // reference max of the exponentials (log2 units)
+    float l_run = 0.0f;
     bool ok = true;
-
-    auto consume_o = [&](int i, float alpha) -> bool {
-      const int ob = i & 1;
-      if (!mbar_wait(&o_full[ob], static_cast<uint32_t>(i >> 1) & 1u, kErrAttnTimeout + 3))
-        return false;
-      tc_fence_after();
-      float lo[32], hi[32];
-      tmem_ld32(tmem + lane_off + 128 + ob * 64, lo);
-      tmem_ld32(tmem + lane_off + 128 + ob * 64 + 32, hi);
-      tmem_wait_ld();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&o_empty[ob]);
-#pragma unroll
-      for (int c = 0; c < 32; ++c) {
-        acc[c] = acc[c] * alpha + lo[c];
-        acc[32 + c] = acc[32 + c] * alpha + hi[c];
-      }
-      return true;
-    };
 
     for (int j = 0; j < nkv; ++j) {
       const int sb = j & 1;
       const uint32_t ph = static_cast<uint32_t>(j >> 1) & 1u;
-      if (!mbar_wait(&s_full[sb], ph, kErrAttnTimeout + 3)) { ok = false; break; }
+      // every exit is warp-uniform: the warp-collective TMEM loads / stores and the vote below
+      // need all 32 lanes
+      ok = mbar_wait(&s_full[sb], ph, kErrAttnTimeout + 3);
+      if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
       tc_fence_after();
-      float s[64];
-      {
-        float lo[32], hi[32];
-        tmem_ld32(tmem + lane_off + sb * 64, lo);
-        tmem_ld32(tmem + lane_off + sb * 64 + 32, hi);
-        tmem_wait_ld();
-#pragma unroll
-        for (int c = 0; c < 32; ++c) {
-          s[c] = lo[c];
-          s[32 + c] = hi[c];
-        }
-      }
+      float sv[64];
+      tmem_ld32(tmem + lane_off + sb * 64, *reinterpret_cast<float(*)[32]>(&sv[0]));
+      tmem_ld32(tmem + lane_off + sb * 64 + 32, *reinterpret_cast<float(*)[32]>(&sv[32]));
+      tmem_wait_ld();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&s_empty[sb]);
 
-      float mx = -INFINITY;
+      // scale, mask, row max (four independent chains); the key mask, when there is one, is
+      // read as 64 bytes once per tile, so the per-element work stays branch-free
+      const int kbase = j * 64;
+      const int nvis = L - kbase;  // keys of this tile inside the sequence
+      float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+      if (kmask == nullptr) {
+#pragma unroll
+        for (int c = 0; c < 64; ++c) {
+          sv[c] = (c < nvis) ? sv[c] * scale : -INFINITY;
+          mx4[c & 3] = fmaxf(mx4[c & 3], sv[c]);
+        }
+      } else {
+        uint32_t mbits[2] = {0u, 0u};  // bit c: key kbase + c visible
+#pragma unroll 1
+        for (int c = 0; c < 64; ++c)
+          if (c < nvis && kmask[kbase + c] != 0) mbits[c >> 5] |= 1u << (c & 31);
+#pragma unroll
+        for (int c = 0; c < 64; ++c) {
+          sv[c] = ((mbits[c >> 5] >> (c & 31)) & 1u) ? sv[c] * scale : -INFINITY;
+          mx4[c & 3] = fmaxf(mx4[c & 3], sv[c]);
+        }
+      }
+      const float mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3]));
+
+      // lazy rescale of O and l when this row's max outgrows the reference by 2^8
+      const bool grow = mx > m_ref + kRescaleLog2;
+      float alpha = 1.0f;
+      if (grow) {
+        alpha = (m_ref == -INFINITY) ? 0.0f : exp2f(m_ref - mx);
+        m_ref = mx;
+        l_run *= alpha;
+      }
+      if (j > 0 && __any_sync(0xffffffffu, grow)) {
+        // O holds PV_0..PV_{j-1}: wait for the last one, scale the rows that moved
+        ok = mbar_wait(o_done, static_cast<uint32_t>(j - 1) & 1u, kErrAttnTimeout + 3);
+        if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
+        tc_fence_after();
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          float o[32];
+          tmem_ld32(tmem + lane_off + kOCol + 32 * h, o);
+          tmem_wait_ld();
+#pragma unroll
+          for (int c = 0; c < 32; ++c) o[c] *= alpha;
+          tmem_st32(tmem + lane_off + kOCol + 32 * h, o);
+        }
+        tmem_wait_st();
+      }
+      const float m_use = (m_ref == -INFINITY) ? 0.0f : m_ref;
+      float ps4[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
       for (int c = 0; c < 64; ++c) {
-        const int key = j * 64 + c;
-        bool vis = key < L;
-        if (vis && kmask) vis = kmask[key] != 0;
-        s[c] = vis ? s[c] * P.scale_log2 : -INFINITY;
-        mx = fmaxf(mx, s[c]);
+        sv[c] = exp2f(sv[c] - m_use);
+        ps4[c & 3] += sv[c];
       }
-      const float m_new = fmaxf(m_run, mx);
-      const float m_use = (m_new == -INFINITY) ? 0.0f : m_new;
-      const float alpha = exp2f(m_run - m_use);
-      float psum = 0.0f;
-#pragma unroll
-      for (int c = 0; c < 64; ++c) {
-        s[c] = exp2f(s[c] - m_use);
-        psum += s[c];
-      }
-      l_run = l_run * alpha + psum;
-      m_run = m_new;
+      l_run += (ps4[0] + ps4[1]) + (ps4[2] + ps4[3]);
 
       // P_j -> shared memory (K-major, 128-byte swizzle: chunk c of row r at (c ^ (r & 7)) * 16)
-      if (!mbar_wait(&p_empty[sb], ph ^ 1u, kErrAttnTimeout + 3)) { ok = false; break; }
+      ok = mbar_wait(&p_empty[sb], ph ^ 1u, kErrAttnTimeout + 3);
+      if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
       uint8_t* prow = sP + sb * kPBytes + r * 128;
 #pragma unroll
       for (int cc = 0; cc < 8; ++cc) {
         uint4 u;
-        u.x = pack_bf16x2(s[8 * cc + 0], s[8 * cc + 1]);
-        u.y = pack_bf16x2(s[8 * cc + 2], s[8 * cc + 3]);
-        u.z = pack_bf16x2(s[8 * cc + 4], s[8 * cc + 5]);
-        u.w = pack_bf16x2(s[8 * cc + 6], s[8 * cc + 7]);
+        u.x = pack_bf16x2(sv[8 * cc + 0], sv[8 * cc + 1]);
+        u.y = pack_bf16x2(sv[8 * cc + 2], sv[8 * cc + 3]);
+        u.z = pack_bf16x2(sv[8 * cc + 4], sv[8 * cc + 5]);
+        u.w = pack_bf16x2(sv[8 * cc + 6], sv[8 * cc + 7]);
         *reinterpret_cast<uint4*>(prow + ((cc ^ (r & 7)) << 4)) = u;
       }
       fence_proxy_async_smem();
+      tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&p_full[sb]);
-
-      if (j >= 1) {
-        if (!consume_o(j - 1, alpha_pend)) { ok = false; break; }
-      }
-      alpha_pend = alpha;
     }
-    if (ok && nkv > 0) ok = consume_o(nkv - 1, alpha_pend);
 
-    if (ok && qrow < L) {
-      int seg = 0, off = 0;
-      while (seg + 1 < P.nseg && qrow >= off + P.seg_len[seg]) {
-        off += P.seg_len[seg];
-        ++seg;
-      }
-      const float inv_l = 1.0f / l_run;
-      __nv_bfloat16* dst = P.seg_out[seg] +
-                           (static_cast<size_t>(b) * P.seg_len[seg] + (qrow - off)) * (P.H * 64) +
-                           head * 64;
-      uint4* d4 = reinterpret_cast<uint4*>(dst);
+    // O = (sum of PV) / l after the last PV MMA
+    if (ok && nkv > 0) ok = mbar_wait(o_done, static_cast<uint32_t>(nkv - 1) & 1u, kErrAttnTimeout + 3);
+    if (__all_sync(0xffffffffu, ok) && nkv > 0) {
+      tc_fence_after();
+      float o[64];
+      tmem_ld32(tmem + lane_off + kOCol, *reinterpret_cast<float(*)[32]>(&o[0]));
+      tmem_ld32(tmem + lane_off + kOCol + 32, *reinterpret_cast<float(*)[32]>(&o[32]));
+      tmem_wait_ld();
+      if (qrow < L) {
+        int seg = 0, off = 0;
+        while (seg + 1 < P.nseg && qrow >= off + P.seg_len[seg]) {
+          off += P.seg_len[seg];
+          ++seg;
+        }
+        const float inv_l = 1.0f / l_run;
+        __nv_bfloat16* dst = P.seg_out[seg] +
+                             (static_cast<size_t>(b) * P.seg_len[seg] + (qrow - off)) * (P.H * 64) +
+                             head * 64;
+        uint4* d4 = reinterpret_cast<uint4*>(dst);
 #pragma unroll
-      for (int cc = 0; cc < 8; ++cc) {
-        uint4 u;
-        u.x = pack_bf16x2(acc[8 * cc + 0] * inv_l, acc[8 * cc + 1] * inv_l);
-        u.y = pack_bf16x2(acc[8 * cc + 2] * inv_l, acc[8 * cc + 3] * inv_l);
-        u.z = pack_bf16x2(acc[8 * cc + 4] * inv_l, acc[8 * cc + 5] * inv_l);
-        u.w = pack_bf16x2(acc[8 * cc + 6] * inv_l, acc[8 * cc + 7] * inv_l);
-        d4[cc] = u;
+        for (int cc = 0; cc < 8; ++cc) {
+          uint4 u;
+          u.x = pack_bf16x2(o[8 * cc + 0] * inv_l, o[8 * cc + 1] * inv_l);
+          u.y = pack_bf16x2(o[8 * cc + 2] * inv_l, o[8 * cc + 3] * inv_l);
+          u.z = pack_bf16x2(o[8 * cc + 4] * inv_l, o[8 * cc + 5] * inv_l);
+          u.w = pack_bf16x2(o[8 * cc + 6] * inv_l, o[8 * cc + 7] * inv_l);
+          d4[cc] = u;
+        }
       }
     }
   }
