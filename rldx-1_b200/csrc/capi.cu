@@ -287,8 +287,38 @@ void choose_tiles_uncached(const ProbShape* sh, const int* fixed_bn, int n, int 
             bs = ns;
           }
         }
+        // group move: every problem one split further at once (identical problems only gain
+        // together, since the longest unit of any one of them bounds the makespan)
+        int gsp[kMaxProblems];
+        bool gmove = false;
+        for (int i = 0; i < n; ++i) {
+          const int maxs = std::min(kMaxSplit, std::max(1, sh[i].nchunks / kMinSplitChunks));
+          int ns = sp[i];
+          do {
+            ns = normalize_split(sh[i].nchunks, ns + 1);
+          } while (ns == sp[i] && ns < maxs);
+          gsp[i] = (ns > sp[i] && ns <= maxs) ? ns : sp[i];
+          gmove = gmove || gsp[i] != sp[i];
+        }
+        if (gmove) {
+          int old[kMaxProblems];
+          for (int i = 0; i < n; ++i) {
+            old[i] = sp[i];
+            sp[i] = gsp[i];
+          }
+          const double m = eval();
+          for (int i = 0; i < n; ++i) sp[i] = old[i];
+          if (m < bm * 0.99) {
+            bm = m;
+            bi = n;  // marks the group move
+          }
+        }
         if (bi < 0) break;
-        sp[bi] = bs;
+        if (bi == n) {
+          for (int i = 0; i < n; ++i) sp[i] = gsp[i];
+        } else {
+          sp[bi] = bs;
+        }
         mk = bm;
       }
     }

@@ -88,17 +88,30 @@ struct TmemSrc {
 struct PartSrc {
   const float* row0;  // split 0, this thread's row, column 0
   size_t split_stride;
-  int nsplit;
+  int nsplit;  // <= kMaxSplitLoads issue their loads together; more are added in a second round
+  static constexpr int kMaxSplitLoads = 2;
   __device__ __forceinline__ void get8(int col, bool live, float (&v)[8]) const {
 #pragma unroll
     for (int i = 0; i < 8; ++i) v[i] = 0.0f;
     if (!live) return;
 #pragma unroll 1
-    for (int s = 0; s < nsplit; ++s) {
-      const float4* p = reinterpret_cast<const float4*>(row0 + s * split_stride + col);
-      const float4 a = __ldcg(p), b = __ldcg(p + 1);
-      v[0] += a.x; v[1] += a.y; v[2] += a.z; v[3] += a.w;
-      v[4] += b.x; v[5] += b.y; v[6] += b.z; v[7] += b.w;
+    for (int s0 = 0; s0 < nsplit; s0 += kMaxSplitLoads) {
+      float4 a[kMaxSplitLoads], b[kMaxSplitLoads];
+#pragma unroll
+      for (int t = 0; t < kMaxSplitLoads; ++t) {  // all loads in flight before the first add
+        if (s0 + t < nsplit) {
+          const float4* p = reinterpret_cast<const float4*>(row0 + (s0 + t) * split_stride + col);
+          a[t] = __ldcg(p);
+          b[t] = __ldcg(p + 1);
+        }
+      }
+#pragma unroll
+      for (int t = 0; t < kMaxSplitLoads; ++t) {  // added in split order
+        if (s0 + t < nsplit) {
+          v[0] += a[t].x; v[1] += a[t].y; v[2] += a[t].z; v[3] += a[t].w;
+          v[4] += b[t].x; v[5] += b[t].y; v[6] += b[t].z; v[7] += b[t].w;
+        }
+      }
     }
   }
 };
@@ -353,7 +366,9 @@ __device__ __forceinline__ UnitInfo decode_unit(const GemmParams& P, int u) {
 
 }  // namespace
 
-template <int kMode>
+// kSplit: whether any problem of the launch is split along K.  Launches without splits use the
+// instantiation without the reduction code, which keeps the hot loops compact.
+template <int kMode, bool kSplit>
 __global__ void __launch_bounds__(kGemmThreads, 1) gemm_bf16_kernel(const __grid_constant__ GemmParams P) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -514,12 +529,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_bf16_kernel(const __grid
         if (lane == 0) mbar_arrive(&acc_empty[ab]);
       };
 
-      if (pr.nsplit == 1) {
+      if (!kSplit || pr.nsplit == 1) {
         if (!ok) continue;
         unit_epilogue_act<kMode>(pr, rc, n_base, set, TmemSrc{tacc});
         release();
         continue;
       }
+      if constexpr (kSplit) {
 
       // K split: write this unit's fp32 partial tile, count arrivals, the last one reduces.
       const size_t split_stride = static_cast<size_t>(128) * pr.bn;
@@ -554,6 +570,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_bf16_kernel(const __grid
       if (!last || !ok) continue;
       __threadfence();
       unit_epilogue_act<kMode>(pr, rc, n_base, set, PartSrc{row0, split_stride, pr.nsplit});
+      }
     }
   }
   tc_fence_before();
@@ -577,10 +594,14 @@ cudaError_t gemm_prepare_device() {
     if (e == cudaSuccess)
       e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
   };
-  set(reinterpret_cast<const void*>(gemm_bf16_kernel<kEpiStore>));
-  set(reinterpret_cast<const void*>(gemm_bf16_kernel<kEpiSwiGLU>));
-  set(reinterpret_cast<const void*>(gemm_bf16_kernel<kEpiQKV>));
-  set(reinterpret_cast<const void*>(gemm_bf16_kernel<kEpiEuler>));
+  set(reinterpret_cast<const void*>(gemm_bf16_kernel<kEpiStore, false>));
+  set(reinterpret_cast<const void*>(gemm_bf16_kernel<kEpiSwiGLU, false>));
+  set(reinterpret_cast<const void*>(gemm_bf16_kernel<kEpiQKV, false>));
+  set(reinterpret_cast<const void*>(gemm_bf16_kernel<kEpiEuler, false>));
+  set(reinterpret_cast<const void*>(gemm_bf16_kernel<kEpiStore, true>));
+  set(reinterpret_cast<const void*>(gemm_bf16_kernel<kEpiSwiGLU, true>));
+  set(reinterpret_cast<const void*>(gemm_bf16_kernel<kEpiQKV, true>));
+  set(reinterpret_cast<const void*>(gemm_bf16_kernel<kEpiEuler, true>));
   return e;
 }
 
@@ -595,15 +616,21 @@ cudaError_t launch_gemm(const GemmParams& params, cudaStream_t stream, bool pdl)
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = pdl ? 1 : 0;
+  bool split = false;
+  for (int i = 0; i < params.nprob; ++i) split = split || params.p[i].nsplit > 1;
   switch (params.p[0].ep.mode) {  // every problem of a launch shares the epilogue mode
     case kEpiSwiGLU:
-      return cudaLaunchKernelEx(&cfg, gemm_bf16_kernel<kEpiSwiGLU>, params);
+      return split ? cudaLaunchKernelEx(&cfg, gemm_bf16_kernel<kEpiSwiGLU, true>, params)
+                   : cudaLaunchKernelEx(&cfg, gemm_bf16_kernel<kEpiSwiGLU, false>, params);
     case kEpiQKV:
-      return cudaLaunchKernelEx(&cfg, gemm_bf16_kernel<kEpiQKV>, params);
+      return split ? cudaLaunchKernelEx(&cfg, gemm_bf16_kernel<kEpiQKV, true>, params)
+                   : cudaLaunchKernelEx(&cfg, gemm_bf16_kernel<kEpiQKV, false>, params);
     case kEpiEuler:
-      return cudaLaunchKernelEx(&cfg, gemm_bf16_kernel<kEpiEuler>, params);
+      return split ? cudaLaunchKernelEx(&cfg, gemm_bf16_kernel<kEpiEuler, true>, params)
+                   : cudaLaunchKernelEx(&cfg, gemm_bf16_kernel<kEpiEuler, false>, params);
     default:
-      return cudaLaunchKernelEx(&cfg, gemm_bf16_kernel<kEpiStore>, params);
+      return split ? cudaLaunchKernelEx(&cfg, gemm_bf16_kernel<kEpiStore, true>, params)
+                   : cudaLaunchKernelEx(&cfg, gemm_bf16_kernel<kEpiStore, false>, params);
   }
 }
 

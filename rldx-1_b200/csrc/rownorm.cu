@@ -13,10 +13,12 @@
 
 namespace rldx {
 
-// One warp per row; D <= 32 * 8 * kLnMaxVec.
-constexpr int kLnMaxVec = 16;
-
+// One warp per row; D <= 32 * 8 * kVec.  Instantiated for rows up to 1536 (6 vectors per
+// lane, few registers, so the CTAs fit next to a running GEMM and start the moment it
+// completes) and up to 4096.
+template <int kVec>
 __global__ void __launch_bounds__(256) ln_rows_kernel(const __grid_constant__ LnParams P) {
+  constexpr int kLnMaxVec = kVec;
   griddep_wait();
   griddep_launch();
   const int warp_global = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
@@ -108,7 +110,8 @@ cudaError_t launch_ln(const LnParams& p, cudaStream_t stream, bool pdl) {
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = pdl ? 1 : 0;
-  return cudaLaunchKernelEx(&cfg, ln_rows_kernel, p);
+  if (p.D <= 32 * 8 * 6) return cudaLaunchKernelEx(&cfg, ln_rows_kernel<6>, p);
+  return cudaLaunchKernelEx(&cfg, ln_rows_kernel<16>, p);
 }
 
 // ---------------------------------------------------------------------------------------------
