@@ -89,7 +89,7 @@ struct PartSrc {
   const float* row0;  // split 0, this thread's row, column 0
   size_t split_stride;
   int nsplit;  // <= kMaxSplitLoads issue their loads together; more are added in a second round
-  static constexpr int kMaxSplitLoads = 2;
+  static constexpr int kMaxSplitLoads = 1;
   __device__ __forceinline__ void get8(int col, bool live, float (&v)[8]) const {
 #pragma unroll
     for (int i = 0; i < 8; ++i) v[i] = 0.0f;
@@ -143,8 +143,8 @@ __device__ __forceinline__ void store8q(__nv_bfloat16* p, int n, const float (&y
     if (i < n) p[i] = __ushort_as_bfloat16(static_cast<unsigned short>(__float_as_uint(y[i]) >> 16));
 }
 
-// Epilogue of one unit by one of the two epilogue warp sets (`set` 0/1: both sets hold the
-// same 32 rows of a TMEM lane quadrant and split the columns).  The loop bodies are small
+// Epilogue of one unit by one of the kEpiSets epilogue warp sets (every set holds the same 32
+// rows of a TMEM lane quadrant; the sets split the columns).  The loop bodies are small
 // (8 columns per iteration) so the code stays resident in the instruction caches.
 template <int kMode, int kAct, class Src>
 __device__ __forceinline__ void unit_epilogue(const GemmProblem& pr, const RowCtx& rc, int n_base,
@@ -163,9 +163,9 @@ __device__ __forceinline__ void unit_epilogue(const GemmProblem& pr, const RowCt
       arow = ep.add + static_cast<size_t>(r) * ep.ld_add;
     }
     const float dt = ep.dt;
-    // set s takes the 32-column blocks s, s+2, s+4, ...; the operand loads of the next group
+    // set s takes the 8-column groups s, s + kEpiSets, ...; the operand loads of the next group
     // are issued before the current group is computed (one group of software pipelining)
-    auto next_col = [](int col) { return col + ((col % 32 == 24) ? 40 : 8); };
+    auto next_col = [](int col) { return col + 8 * kEpiSets; };
     auto fetch = [&](int col, uint4& bq, uint4& aq, uint4& xq) {
       const int n0 = n_base + col;
       const int n = pr.N - n0;
@@ -175,9 +175,9 @@ __device__ __forceinline__ void unit_epilogue(const GemmProblem& pr, const RowCt
       xq = load8q(orow + n0, on && kMode == kEpiEuler, n);
     };
     uint4 nb, na, nx;
-    fetch(set * 32, nb, na, nx);
+    fetch(set * 8, nb, na, nx);
 #pragma unroll 1
-    for (int col = set * 32; col < bn; col = next_col(col)) {
+    for (int col = set * 8; col < bn; col = next_col(col)) {
       const int n0 = n_base + col;
       const int n = pr.N - n0;  // valid columns from n0 (uniform over the warp)
       const bool on = rc.live && n > 0;
@@ -198,14 +198,14 @@ __device__ __forceinline__ void unit_epilogue(const GemmProblem& pr, const RowCt
     }
   } else if constexpr (kMode == kEpiSwiGLU) {
     // every 64 columns: [0,32) gate, [32,64) up of hidden units n0/2 .. n0/2+31 (N % 64 == 0);
-    // set s takes hidden units 16s .. 16s+15 of each chunk
+    // set s takes the 8-unit groups j = s, s + kEpiSets, ... (j < 4) of each chunk
     __nv_bfloat16* orow = ep.out + static_cast<size_t>(rc.out_row) * ep.ldo + ep.col_off;
 #pragma unroll 1
     for (int c = 0; c < bn; c += 64) {
       const int n0 = n_base + c;
       const bool on = rc.live && n0 < pr.N;
 #pragma unroll 1
-      for (int j = 2 * set; j < 2 * set + 2; ++j) {
+      for (int j = set; j < 4; j += kEpiSets) {
         const uint4 bg = load8q(bias_row + n0 + 8 * j, on && bias_row, 8);
         const uint4 bu = load8q(bias_row + n0 + 32 + 8 * j, on && bias_row, 8);
         float g[8], u[8];
@@ -222,11 +222,11 @@ __device__ __forceinline__ void unit_epilogue(const GemmProblem& pr, const RowCt
         store8q(orow + n0 / 2 + 8 * j, 8, h);
       }
     }
-  } else {  // kEpiQKV: every 64 columns = one head of q, k or v; set s takes heads s, s+2, ...
+  } else {  // kEpiQKV: every 64 columns = one head of q, k or v; set s takes heads s, s+kEpiSets, ...
     const int inner = ep.H * 64;
     const int tok = ep.tok_off + rc.t;
 #pragma unroll 1
-    for (int c = 64 * set; c < bn; c += 128) {
+    for (int c = 64 * set; c < bn; c += 64 * kEpiSets) {
       const int n0 = n_base + c;
       if (n0 >= pr.N) break;  // uniform over the warp
       const int part = n0 / inner;
@@ -504,10 +504,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_bf16_kernel(const __grid
       }
     }
   } else {
-    // ---------------- epilogue warps 3..10 ----------------
+    // ---------------- epilogue warps ----------------
     griddep_wait();
     const int quad = warp & 3;           // TMEM lane quadrant this warp may read
-    const int set = (warp - 3) >> 2;     // column half of the unit (0 or 1)
+    const int set = (warp - kEpiWarp0) >> 2;  // column share of the unit (0 .. kEpiSets-1)
     const int r_local = quad * 32 + lane;
     const uint32_t lane_off = static_cast<uint32_t>(quad * 32) << 16;
     // After a failed wait the warps keep walking the unit list (every wait then returns at
@@ -544,7 +544,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_bf16_kernel(const __grid
       if (ok) {
         const TmemSrc src{tacc};
 #pragma unroll 1
-        for (int col = set * 32; col < pr.bn; col += (col % 32 == 24) ? 40 : 8) {
+        for (int col = set * 8; col < pr.bn; col += 8 * kEpiSets) {
           float v[8];
           src.get8(col, rc.live, v);
           if (rc.live && n_base + col < pr.N) {

@@ -4,7 +4,7 @@
 // Work unit = (problem, 128-row M tile, BN-column N tile, K split).  The host orders the units
 // longest-first and deals them to at most one CTA per SM (LPT schedule, kept in the launch
 // parameters), so the weight-streaming work of all streams is spread evenly over the SMs.
-// Roles inside a CTA (352 threads):
+// Roles inside a CTA (3 + kEpiWarps warps):
 //
 //   warp 0      TMA producer of A (activations), after griddepcontrol.wait.
 //   warp 2      TMA producer of B (weights).  Weights never depend on the previous kernel, so
@@ -13,8 +13,8 @@
 //   warp 1      TMEM allocator + single-thread tcgen05.mma issuer (M=128, N=BN, K=16 steps)
 //               into one of two TMEM accumulators (2 x 256 columns), so the epilogue of one
 //               unit overlaps the main loop of the next.
-//   warps 3..10 epilogue: two warps per TMEM lane quadrant (thread = output row) split the
-//               unit's columns; tcgen05.ld of 8 fp32 columns at a time and the fused row
+//   warps 3..    epilogue: kEpiSets warps per TMEM lane quadrant (thread = output row) split
+//               the unit's columns; tcgen05.ld of 8 fp32 columns at a time and the fused row
 //               epilogue (bias / activation / residual / SwiGLU / QK-RMSNorm+RoPE / Euler
 //               update), written straight to global memory.  K-split units write fp32
 //               partial tiles to a workspace; the last of a tile's units to finish (arrival
@@ -33,7 +33,11 @@ namespace rldx {
 constexpr int kMaxProblems = 4;
 constexpr int kMaxStages = 8;
 constexpr int kEpiWarp0 = 3;         // first epilogue warp
-constexpr int kEpiWarps = 8;         // two warps per TMEM lane quadrant, splitting the columns
+#ifndef RLDX_GEMM_EPI_WARPS
+#define RLDX_GEMM_EPI_WARPS 16
+#endif
+constexpr int kEpiWarps = RLDX_GEMM_EPI_WARPS;  // kEpiSets warps per TMEM lane quadrant
+constexpr int kEpiSets = kEpiWarps / 4;         // ... splitting the columns of a unit
 constexpr int kGemmThreads = (kEpiWarp0 + kEpiWarps) * 32;
 constexpr int kMaxUnits = 1536;     // explicit schedule capacity; larger launches stride units
 constexpr int kMaxCtas = 160;       // >= SM count of the part
