@@ -298,13 +298,9 @@ __device__ __forceinline__ void griddep_launch() {
 // ---------------------------------------------------------------------------------------------
 // bf16 helpers (round-to-nearest-even, same as torch's .to(bfloat16))
 // ---------------------------------------------------------------------------------------------
-// Round to bf16 (nearest, ties to even) and back, on the fp32 bit pattern: integer ALU work
-// that pipelines well, instead of two conversions.  NaN stays a (quiet) NaN.
+// Round to bf16 (nearest, ties to even) and back: one conversion instruction each way.
 __device__ __forceinline__ float bf16r(float x) {
-  const uint32_t u = __float_as_uint(x);
-  const uint32_t r = (u + 0x7fffu + ((u >> 16) & 1u)) & 0xffff0000u;
-  const bool nan = (u & 0x7fffffffu) > 0x7f800000u;
-  return __uint_as_float(nan ? ((u | 0x00400000u) & 0xffff0000u) : r);
+  return __bfloat162float(__float2bfloat16_rn(x));
 }
 
 // Packs two values that are already bf16-exact (e.g. results of bf16r) into a bf16x2 word.

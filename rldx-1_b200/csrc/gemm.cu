@@ -85,33 +85,31 @@ struct TmemSrc {
   }
 };
 
+// Partial tiles are stored column-major, [split][column][128 rows] per tile, so that the 32
+// rows of a warp read and write 128 contiguous bytes per column.
 struct PartSrc {
-  const float* row0;  // split 0, this thread's row, column 0
-  size_t split_stride;
-  int nsplit;  // <= kMaxSplitLoads issue their loads together; more are added in a second round
-  static constexpr int kMaxSplitLoads = 1;
+  const float* col0;  // split 0, column 0, this thread's row
+  size_t split_stride;  // floats between splits (= 128 * BN)
+  int nsplit;
+  static constexpr int kSplitsInFlight = 4;  // splits whose loads are issued before adding
   __device__ __forceinline__ void get8(int col, bool live, float (&v)[8]) const {
 #pragma unroll
     for (int i = 0; i < 8; ++i) v[i] = 0.0f;
     if (!live) return;
+    const float* base = col0 + static_cast<size_t>(col) * 128;
 #pragma unroll 1
-    for (int s0 = 0; s0 < nsplit; s0 += kMaxSplitLoads) {
-      float4 a[kMaxSplitLoads], b[kMaxSplitLoads];
+    for (int s0 = 0; s0 < nsplit; s0 += kSplitsInFlight) {
+      float a[kSplitsInFlight][8];
 #pragma unroll
-      for (int t = 0; t < kMaxSplitLoads; ++t) {  // all loads in flight before the first add
-        if (s0 + t < nsplit) {
-          const float4* p = reinterpret_cast<const float4*>(row0 + (s0 + t) * split_stride + col);
-          a[t] = __ldcg(p);
-          b[t] = __ldcg(p + 1);
-        }
-      }
+      for (int t = 0; t < kSplitsInFlight; ++t)
 #pragma unroll
-      for (int t = 0; t < kMaxSplitLoads; ++t) {  // added in split order
-        if (s0 + t < nsplit) {
-          v[0] += a[t].x; v[1] += a[t].y; v[2] += a[t].z; v[3] += a[t].w;
-          v[4] += b[t].x; v[5] += b[t].y; v[6] += b[t].z; v[7] += b[t].w;
-        }
-      }
+        for (int i = 0; i < 8; ++i)
+          a[t][i] = (s0 + t < nsplit) ? __ldcg(base + (s0 + t) * split_stride + i * 128) : 0.0f;
+#pragma unroll
+      for (int t = 0; t < kSplitsInFlight; ++t)  // added in split order
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+          if (s0 + t < nsplit) v[i] += a[t][i];
     }
   }
 };
@@ -539,8 +537,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_bf16_kernel(const __grid
 
       // K split: write this unit's fp32 partial tile, count arrivals, the last one reduces.
       const size_t split_stride = static_cast<size_t>(128) * pr.bn;
-      float* row0 = P.ws + pr.ws_off + static_cast<size_t>(u.tile) * pr.nsplit * split_stride +
-                    static_cast<size_t>(r_local) * pr.bn;
+      float* col0 = P.ws + pr.ws_off + static_cast<size_t>(u.tile) * pr.nsplit * split_stride +
+                    static_cast<size_t>(r_local);
       if (ok) {
         const TmemSrc src{tacc};
 #pragma unroll 1
@@ -548,9 +546,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_bf16_kernel(const __grid
           float v[8];
           src.get8(col, rc.live, v);
           if (rc.live && n_base + col < pr.N) {
-            float4* dst = reinterpret_cast<float4*>(row0 + u.ks * split_stride + col);
-            dst[0] = make_float4(v[0], v[1], v[2], v[3]);
-            dst[1] = make_float4(v[4], v[5], v[6], v[7]);
+            float* dst = col0 + u.ks * split_stride + static_cast<size_t>(col) * 128;
+#pragma unroll
+            for (int i = 0; i < 8; ++i) dst[i * 128] = v[i];
           }
         }
         release();
@@ -569,7 +567,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_bf16_kernel(const __grid
       named_bar_sync(1, kEpiWarps * 32);  // bcast is rewritten by the next split unit
       if (!last || !ok) continue;
       __threadfence();
-      unit_epilogue_act<kMode>(pr, rc, n_base, set, PartSrc{row0, split_stride, pr.nsplit});
+      unit_epilogue_act<kMode>(pr, rc, n_base, set, PartSrc{col0, split_stride, pr.nsplit});
       }
     }
   }
