@@ -164,8 +164,8 @@ bool make_tmap_4d(CUtensorMap* m, const void* base, const cuuint64_t (&dims)[4],
 // Cost model of one work unit on one SM, in nanoseconds, from measurements of this kernel's
 // building blocks on B200: a TMA ring sustains ~114 GB/s of shared-memory fill per SM, the
 // tensor core ~11.3 TFLOP/s per SM (dense bf16, M = 128 whatever the live rows), a unit pays a
-// fixed pipeline fill + epilogue tail, and a K-split unit also writes its fp32 partial tile and
-// (for the last one) reads all partials of the tile back from L2.
+// fixed pipeline fill, an epilogue proportional to its columns, and a K-split unit also writes
+// its fp32 partial tile and (for the last one) reads all partials of the tile back from L2.
 constexpr double kFillBytesPerNs = 114.0;
 constexpr double kMmaFlopsPerNs = 11300.0;
 constexpr double kChunkNs = 20.0;
@@ -176,8 +176,14 @@ constexpr int kMaxSplit = 8;
 constexpr size_t kCounterBytes = ((kMaxUnits * 4 + 255) / 256) * 256;
 
 struct ProbShape {
-  int M, N, K, m_step, tiles_m, a_rows, live_rows, nchunks, kdim3, cat;
+  int M, N, K, m_step, tiles_m, a_rows, live_rows, nchunks, kdim3, cat, epi;
 };
+
+// Epilogue time per output column of a unit (ns), by epilogue mode, measured on B200 for the
+// 16-warp epilogue: per-head RMSNorm + RoPE and SwiGLU cost about twice the plain store.
+double epi_ns_per_col(int epi) {
+  return (epi == RLDX_EPI_QKV || epi == RLDX_EPI_SWIGLU) ? 26.0 : 15.0;
+}
 
 double chunk_ns(const ProbShape& s, int bn) {
   const double fill = (s.a_rows + bn) * 128.0 / kFillBytesPerNs;
@@ -186,7 +192,7 @@ double chunk_ns(const ProbShape& s, int bn) {
 }
 
 double unit_ns(const ProbShape& s, int bn, int chunks, int nsplit) {
-  double t = chunks * chunk_ns(s, bn) + kUnitNs;
+  double t = chunks * chunk_ns(s, bn) + kUnitNs + bn * epi_ns_per_col(s.epi);
   if (nsplit > 1) t += s.live_rows * bn * 4.0 * 2.0 / kFillBytesPerNs;
   return t;
 }
@@ -343,7 +349,7 @@ void choose_tiles(const ProbShape* sh, const int* fixed_bn, int n, int nsm, bool
   std::vector<int> key = {n, nsm, can_split ? 1 : 0};
   for (int i = 0; i < n; ++i) {
     const ProbShape& s = sh[i];
-    key.insert(key.end(), {s.M, s.N, s.K, s.m_step, s.a_rows, s.cat, fixed_bn[i]});
+    key.insert(key.end(), {s.M, s.N, s.K, s.m_step, s.a_rows, s.cat, s.epi, fixed_bn[i]});
   }
   static std::mutex mu;
   static std::map<std::vector<int>, std::vector<int>> cache;
@@ -486,6 +492,7 @@ bool build_gemm_params(const rldx_gemm_desc* d, int n, void* ws, size_t ws_bytes
     s.nchunks = p.nchunks;
     s.kdim3 = p.kdim3;
     s.cat = d[i].cat_ids ? 1 : 0;
+    s.epi = d[i].epilogue;
   }
 
   // ---- tile width and K splits: minimise the modelled LPT makespan ----

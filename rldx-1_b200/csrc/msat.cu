@@ -55,12 +55,12 @@ float bf_round(float f) {
   return r;
 }
 
-// K-split GEMMs in the control step: off by default (measured slower at batch 1 on B200, where
-// the last split's reduction pass costs more than the idle SMs it recovers); RLDX_MSAT_SPLIT_K=1
-// turns them on.
+// K-split GEMMs in the control step: on by default (the planner splits where its cost model
+// says idle SMs outweigh the partial-tile traffic, chiefly the K = 4096 MLP down-projection);
+// RLDX_MSAT_SPLIT_K=0 turns them off.
 bool split_k_enabled() {
   const char* e = std::getenv("RLDX_MSAT_SPLIT_K");
-  return e && e[0] == '1';
+  return !(e && e[0] == '0');
 }
 
 struct Fail : std::runtime_error {
