@@ -17,7 +17,7 @@ namespace rldx {
 // lane, few registers, so the CTAs fit next to a running GEMM and start the moment it
 // completes) and up to 4096.
 template <int kVec>
-__global__ void __launch_bounds__(256) ln_rows_kernel(const __grid_constant__ LnParams P) {
+__global__ void __launch_bounds__(128) ln_rows_kernel(const __grid_constant__ LnParams P) {
   constexpr int kLnMaxVec = kVec;
   griddep_wait();
   griddep_launch();
@@ -101,7 +101,9 @@ __global__ void __launch_bounds__(256) ln_rows_kernel(const __grid_constant__ Ln
 
 cudaError_t launch_ln(const LnParams& p, cudaStream_t stream, bool pdl) {
   cudaLaunchConfig_t cfg = {};
-  const int warps_per_block = 8;
+  // 4 warps (rows) per CTA: small enough in registers to sit next to a 608-thread GEMM CTA and
+  // start the moment it completes
+  const int warps_per_block = 4;
   cfg.gridDim = dim3((p.total_rows + warps_per_block - 1) / warps_per_block, 1, 1);
   cfg.blockDim = dim3(32 * warps_per_block, 1, 1);
   cfg.stream = stream;
