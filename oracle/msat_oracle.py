@@ -17,9 +17,15 @@ same module tree and parameter names, so a reference state_dict loads into it un
                                from its published definition: get_timestep_embedding with
                                flip_sin_to_cos=True, downscale_freq_shift=1; Linear-SiLU-Linear)
   SwiGLUFFN                    rldx/model/modules/action_model/ops.py:137-161
+  DoubleStreamBlock            rldx/model/modules/action_model/blocks.py:257-609
   ExpandedDoubleStreamBlock    rldx/model/modules/action_model/blocks.py:612-891 (input_token
                                temb => identity modulation, blocks.py:737-760)
-  MSAT._forward_physics        rldx/model/modules/action_model/msat.py:558-781 (0 single blocks)
+  SingleStreamBlock            rldx/model/modules/action_model/blocks.py:42-254
+  ExpandedSingleStreamBlock    rldx/model/modules/action_model/blocks.py:894-1089
+  MSAT._forward_inner          rldx/model/modules/action_model/msat.py:291-556 (standard path:
+                               DoubleStreamBlocks [VL | SA] -> SingleStreamBlocks [VL_proj | SA])
+  MSAT._forward_physics        rldx/model/modules/action_model/msat.py:558-781 (ExpandedDouble
+                               [VL | SA | P] -> ExpandedSingle [VL_proj + SA | P])
   CategorySpecificLinear/MLP   rldx/model/modules/embodiment_conditioned_mlp.py:62-164
   MultiEmbodimentActionEncoder rldx/model/modules/embodiment_conditioned_mlp.py:180-227
   SinusoidalPositionalEncoding rldx/model/modules/embodiment_conditioned_mlp.py:29-59
@@ -52,10 +58,13 @@ class MsatHeadConfig:
     horizon: int = 16
     physics_hist: int = 16
     physics_fut: int = 16
-    dim: int = 1536  # sa_dim == vl_dim == p_dim == heads * head_dim
+    dim: int = 1536  # sa_dim == p_dim == heads * head_dim
     heads: int = 24
     head_dim: int = 64
-    depth: int = 16
+    depth: int = 16  # double-stream blocks
+    depth_single: int = 0  # single-stream blocks after them
+    use_physics: bool = True
+    vl_dim: Optional[int] = None  # width of the VL stream in the double blocks (None: dim)
     mlp_ratio: float = 4.0
     vl_mlp_ratio: Optional[float] = None
     out_dim: int = 1024  # MSAT output_dim == hidden_size
@@ -75,9 +84,21 @@ class MsatHeadConfig:
         return int(2 / 3 * int(self.dim * self.mlp_ratio))
 
     @property
+    def vl_width(self) -> int:
+        return self.vl_dim if self.vl_dim is not None else self.dim
+
+    @property
     def vl_mlp_hidden(self) -> int:
         r = self.vl_mlp_ratio if self.vl_mlp_ratio is not None else self.mlp_ratio
-        return int(2 / 3 * int(self.dim * r))
+        return int(2 / 3 * int(self.vl_width * r))
+
+    @property
+    def single_expanded(self) -> int:  # SwiGLU width of a single-stream block (w12 out / 2)
+        return int(self.dim * self.mlp_ratio)
+
+    @property
+    def single_mlp_hidden(self) -> int:  # mlp_proj output width of a single-stream block
+        return int(2 / 3 * self.single_expanded)
 
 
 # ----------------------------------------------------------------------------------------------
@@ -202,19 +223,25 @@ def _merge_heads(x):
 class ExpandedDoubleStreamBlock(nn.Module):
     """3-way joint block [VL | SA | P]; identity modulation (temb_type='input_token')."""
 
-    def __init__(self, dim: int, heads: int, head_dim: int, mlp_hidden: int, vl_mlp_hidden: int):
+    streams = ("sa", "vl", "p")
+
+    def __init__(self, dim: int, heads: int, head_dim: int, mlp_hidden: int, vl_mlp_hidden: int,
+                 vl_dim: Optional[int] = None):
         super().__init__()
         self.num_heads = heads
         inner = heads * head_dim
-        for s, hid in (("sa", mlp_hidden), ("vl", vl_mlp_hidden), ("p", mlp_hidden)):
-            setattr(self, f"{s}_norm1", _ln(dim))
+        vl_dim = vl_dim if vl_dim is not None else dim
+        widths = {"sa": (dim, mlp_hidden), "vl": (vl_dim, vl_mlp_hidden), "p": (dim, mlp_hidden)}
+        for s in self.streams:
+            w, hid = widths[s]
+            setattr(self, f"{s}_norm1", _ln(w))
             setattr(self, f"{s}_norm2_attn", nn.Identity())
-            setattr(self, f"{s}_norm2_mlp", _ln(dim))
+            setattr(self, f"{s}_norm2_mlp", _ln(w))
             setattr(self, f"{s}_norm3_mlp", nn.Identity())
-            setattr(self, f"{s}_qkv", nn.Linear(dim, 3 * inner))
-            setattr(self, f"{s}_proj", nn.Linear(inner, dim))
-            setattr(self, f"{s}_mlp", SwiGLUFFN(dim, hid))
-        for s in ("sa", "vl", "p"):
+            setattr(self, f"{s}_qkv", nn.Linear(w, 3 * inner))
+            setattr(self, f"{s}_proj", nn.Linear(inner, w))
+            setattr(self, f"{s}_mlp", SwiGLUFFN(w, hid))
+        for s in self.streams:
             setattr(self, f"q_norm_{s}", RMSNorm(head_dim))
             setattr(self, f"k_norm_{s}", RMSNorm(head_dim))
 
@@ -245,8 +272,104 @@ class ExpandedDoubleStreamBlock(nn.Module):
         return res["sa"], res["vl"], res["p"]
 
 
+class DoubleStreamBlock(ExpandedDoubleStreamBlock):
+    """2-way joint block [VL | SA] (blocks.py:257-609); same per-stream structure."""
+
+    streams = ("sa", "vl")
+
+    def forward(self, sa, vl, pe, attn_mask=None):
+        H = self.num_heads
+        qs, ks, vs = [], [], []
+        for s, x in (("vl", vl), ("sa", sa)):
+            y = getattr(self, f"{s}_norm1")(x)
+            q, k, v = [_split_heads(t, H) for t in getattr(self, f"{s}_qkv")(y).chunk(3, dim=-1)]
+            B, _, N, Dh = q.shape
+            q = getattr(self, f"q_norm_{s}")(q.reshape(B * H, N, Dh)).reshape(B, H, N, Dh)
+            k = getattr(self, f"k_norm_{s}")(k.reshape(B * H, N, Dh)).reshape(B, H, N, Dh)
+            qs.append(q)
+            ks.append(k)
+            vs.append(v)
+        q, k, v = torch.cat(qs, 2), torch.cat(ks, 2), torch.cat(vs, 2)
+        if pe is not None:
+            q, k = apply_rotary_emb(q, k, pe)
+        o = F.scaled_dot_product_attention(q, k, v, attn_mask=attn_mask)
+        n_vl = vl.shape[1]
+        outs = {"vl": _merge_heads(o[:, :, :n_vl]), "sa": _merge_heads(o[:, :, n_vl:])}
+        res = {}
+        for s, x in (("sa", sa), ("vl", vl)):
+            x = x + getattr(self, f"{s}_proj")(outs[s])
+            x = x + getattr(self, f"{s}_mlp")(getattr(self, f"{s}_norm2_mlp")(x))
+            res[s] = x
+        return res["sa"], res["vl"]
+
+
+class SingleStreamBlock(nn.Module):
+    """Flux-style single block over [VL_proj | time | SA] (blocks.py:42-254) with SwiGLU,
+    RMS QK-norm, LayerNorm pre-norm, no post-norm and identity modulation (input_token):
+    x + linear2(cat[attn, mlp_proj(silu(x1) * x2)]) with linear1 = [qkv | x1 | x2]."""
+
+    prefixes = ("",)
+
+    def __init__(self, dim: int, heads: int, head_dim: int, mlp_ratio: float):
+        super().__init__()
+        self.num_heads = heads
+        self.inner_dim = heads * head_dim
+        self.expanded = int(dim * mlp_ratio)
+        self.mlp_hidden = int(2 / 3 * self.expanded)
+        for pre in self.prefixes:
+            setattr(self, f"{pre}linear1", nn.Linear(dim, 3 * self.inner_dim + 2 * self.expanded))
+            setattr(self, f"{pre}linear2", nn.Linear(self.inner_dim + self.mlp_hidden, dim))
+            setattr(self, f"{pre}mlp_proj", nn.Linear(self.expanded, self.mlp_hidden))
+            setattr(self, f"{pre}q_norm", RMSNorm(head_dim))
+            setattr(self, f"{pre}k_norm", RMSNorm(head_dim))
+            setattr(self, f"{pre}pre_norm", _ln(dim))
+            setattr(self, f"{pre}post_norm", nn.Identity())
+
+    def _in(self, pre, x):
+        H = self.num_heads
+        y = getattr(self, f"{pre}pre_norm")(x)
+        qkv, mlp = torch.split(getattr(self, f"{pre}linear1")(y), [3 * self.inner_dim, 2 * self.expanded], dim=-1)
+        q, k, v = [_split_heads(t, H) for t in qkv.chunk(3, dim=-1)]
+        B, _, N, Dh = q.shape
+        q = getattr(self, f"{pre}q_norm")(q.reshape(B * H, N, Dh)).reshape(B, H, N, Dh)
+        k = getattr(self, f"{pre}k_norm")(k.reshape(B * H, N, Dh)).reshape(B, H, N, Dh)
+        return q, k, v, mlp
+
+    def _out(self, pre, x, attn, mlp):
+        x1, x2 = mlp.chunk(2, dim=-1)
+        m = getattr(self, f"{pre}mlp_proj")(F.silu(x1) * x2)
+        o = getattr(self, f"{pre}linear2")(torch.cat([attn, m], dim=-1))
+        return x + getattr(self, f"{pre}post_norm")(o)
+
+    def forward(self, x, pe, attn_mask=None):
+        q, k, v, mlp = self._in("", x)
+        if pe is not None:
+            q, k = apply_rotary_emb(q, k, pe)
+        o = F.scaled_dot_product_attention(q, k, v, attn_mask=attn_mask)
+        return self._out("", x, _merge_heads(o), mlp)
+
+
+class ExpandedSingleStreamBlock(SingleStreamBlock):
+    """Single block with the physics stream beside it: joint attention [VL_proj + SA | P], the
+    P stream with its own p_* weights (blocks.py:894-1089)."""
+
+    prefixes = ("", "p_")
+
+    def forward(self, x, pe, attn_mask=None, p=None):
+        xq, xk, xv, xm = self._in("", x)
+        pq, pk, pv, pm = self._in("p_", p)
+        q, k, v = torch.cat([xq, pq], 2), torch.cat([xk, pk], 2), torch.cat([xv, pv], 2)
+        if pe is not None:
+            q, k = apply_rotary_emb(q, k, pe)
+        o = F.scaled_dot_product_attention(q, k, v, attn_mask=attn_mask)
+        n_x = x.shape[1]
+        return (self._out("", x, _merge_heads(o[:, :, :n_x]), xm),
+                self._out("p_", p, _merge_heads(o[:, :, n_x:]), pm))
+
+
 class MSAT(nn.Module):
-    """MSAT with physics stream, `depth` ExpandedDoubleStreamBlocks and no single blocks."""
+    """MSAT: physics path (ExpandedDoubleStreamBlocks [VL | SA | P], then ExpandedSingleStream
+    blocks) or standard path (DoubleStreamBlocks [VL | SA], then SingleStreamBlocks)."""
 
     def __init__(self, cfg: MsatHeadConfig):
         super().__init__()
@@ -269,14 +392,21 @@ class MSAT(nn.Module):
         else:
             raise ValueError(cfg.positional_embeddings)
         self.rope_embedder = RoPEEmbedder1D(hd, axes, cfg.rope_theta, cfg.max_seq_len)
-        self.vl_proj_to_sa = nn.Identity()
+        self.use_physics = cfg.use_physics
+        self.vl_dim = cfg.vl_width
+        self.vl_proj_to_sa = (nn.Linear(cfg.vl_width, cfg.dim) if cfg.vl_width != cfg.dim
+                              else nn.Identity())
+        dbl = ExpandedDoubleStreamBlock if cfg.use_physics else DoubleStreamBlock
         self.double_blocks = nn.ModuleList(
-            ExpandedDoubleStreamBlock(cfg.dim, cfg.heads, hd, cfg.mlp_hidden, cfg.vl_mlp_hidden)
+            dbl(cfg.dim, cfg.heads, hd, cfg.mlp_hidden, cfg.vl_mlp_hidden, cfg.vl_width)
             for _ in range(cfg.depth))
-        self.single_blocks = nn.ModuleList()
-        self.norm_out_physics = _ln(cfg.dim)
-        self.proj_out_physics_1 = nn.Linear(inner, 2 * cfg.dim)
-        self.proj_out_physics_2 = nn.Linear(cfg.dim, cfg.out_dim)
+        sgl = ExpandedSingleStreamBlock if cfg.use_physics else SingleStreamBlock
+        self.single_blocks = nn.ModuleList(
+            sgl(cfg.dim, cfg.heads, hd, cfg.mlp_ratio) for _ in range(cfg.depth_single))
+        if cfg.use_physics:
+            self.norm_out_physics = _ln(cfg.dim)
+            self.proj_out_physics_1 = nn.Linear(inner, 2 * cfg.dim)
+            self.proj_out_physics_2 = nn.Linear(cfg.dim, cfg.out_dim)
         self.norm_out = _ln(cfg.dim)
         self.proj_out_1 = nn.Linear(inner, 2 * cfg.dim)
         self.proj_out_2 = nn.Linear(cfg.dim, cfg.out_dim)
@@ -296,8 +426,63 @@ class MSAT(nn.Module):
         ids[:, p0:, 1] = torch.arange(n_p)
         return ids
 
-    def forward(self, hidden_states, encoder_hidden_states, timestep, physics_embs,
+    def position_ids_standard(self, B: int, n_vl: int, n_sa: int) -> torch.Tensor:
+        """Position ids of the double blocks over [VL | SA(time, state, actions)]
+        (msat.py:369-420): time (0, 0), S/A (0, 1..) — rope_vl_sa: VL (j, 0), S/A (0, 2..)."""
+        ids = torch.zeros(B, n_vl + n_sa, 2, dtype=torch.long)
+        if self.cfg.positional_embeddings == "rope_vl_sa":
+            ids[:, :n_vl, 0] = torch.arange(n_vl)
+            start = 2
+        else:
+            start = 1
+        ids[:, n_vl + 1:, 1] = torch.arange(start, start + n_sa - 1)
+        return ids
+
+    def position_ids_single(self, B: int, n_vl: int, n_sa_pure: int, n_p: int = 0) -> torch.Tensor:
+        """Position ids of the single blocks over [VL_proj | time | S/A (| P)]
+        (msat.py:460-505, 676-709): time (0, 0), S/A (0, 2..) in both RoPE modes, VL (j, 0) under
+        rope_vl_sa, P (1, 0..)."""
+        n_x = n_vl + 1 + n_sa_pure
+        ids = torch.zeros(B, n_x + n_p, 2, dtype=torch.long)
+        if self.cfg.positional_embeddings == "rope_vl_sa":
+            ids[:, :n_vl, 0] = torch.arange(n_vl)
+        ids[:, n_vl + 1:n_x, 1] = torch.arange(2, 2 + n_sa_pure)
+        if n_p:
+            ids[:, n_x:, 0] = 1
+            ids[:, n_x:, 1] = torch.arange(n_p)
+        return ids
+
+    def forward_standard(self, hidden_states, encoder_hidden_states, timestep, return_hidden=False):
+        """Standard path without physics (msat.py:363-556)."""
+        temb = self.timestep_encoder(timestep)
+        time_token = self.time_token_proj(temb).unsqueeze(1)
+        sa = torch.cat([time_token, hidden_states], dim=1)
+        vl = encoder_hidden_states
+        B = sa.shape[0]
+        pe = self.rope_embedder(self.position_ids_standard(B, vl.shape[1], sa.shape[1]))
+        hidden = []
+        for blk in self.double_blocks:
+            sa, vl = blk(sa, vl, pe)
+            if return_hidden:
+                hidden.append((sa, vl))
+        time_token, sa = sa[:, :self.num_temb_tokens], sa[:, self.num_temb_tokens:]
+        if len(self.single_blocks):
+            x = torch.cat([self.vl_proj_to_sa(vl), time_token, sa], dim=1)
+            pe_s = self.rope_embedder(self.position_ids_single(B, vl.shape[1], sa.shape[1]))
+            for blk in self.single_blocks:
+                x = blk(x, pe_s)
+                if return_hidden:
+                    hidden.append((x,))
+            sa = x[:, -sa.shape[1]:]
+        shift, scale = self.proj_out_1(F.silu(temb)).chunk(2, dim=1)
+        a = self.proj_out_2(self.norm_out(sa) * (1 + scale[:, None]) + shift[:, None])
+        out = {"action": a}
+        return (out, hidden) if return_hidden else out
+
+    def forward(self, hidden_states, encoder_hidden_states, timestep, physics_embs=None,
                 encoder_attention_mask=None, physics_attention_mask=None, return_hidden=False):
+        if not self.use_physics:
+            return self.forward_standard(hidden_states, encoder_hidden_states, timestep, return_hidden)
         temb = self.timestep_encoder(timestep)
         time_token = self.time_token_proj(temb).unsqueeze(1)
         sa = torch.cat([time_token, hidden_states], dim=1)
@@ -319,7 +504,15 @@ class MSAT(nn.Module):
             sa, vl, p = blk(sa, vl, p, pe, attn_mask)
             if return_hidden:
                 hidden.append((sa, vl, p))
-        sa = sa[:, self.num_temb_tokens:]
+        time_token, sa = sa[:, :self.num_temb_tokens], sa[:, self.num_temb_tokens:]
+        if len(self.single_blocks):
+            x = torch.cat([self.vl_proj_to_sa(vl), time_token, sa], dim=1)
+            pe_s = self.rope_embedder(self.position_ids_single(B, vl.shape[1], sa.shape[1], p.shape[1]))
+            for blk in self.single_blocks:
+                x, p = blk(x, pe_s, None, p)
+                if return_hidden:
+                    hidden.append((x, p))
+            sa = x[:, -sa.shape[1]:]
         shift, scale = self.proj_out_1(F.silu(temb)).chunk(2, dim=1)
         a = self.proj_out_2(self.norm_out(sa) * (1 + scale[:, None]) + shift[:, None])
         pshift, pscale = self.proj_out_physics_1(F.silu(temb)).chunk(2, dim=1)
@@ -440,8 +633,10 @@ class ActionHead(nn.Module):
         self.action_decoder = CategorySpecificMLP(cfg.num_embodiments, cfg.out_dim, cfg.dec_hidden, cfg.action_dim)
         self.position_embedding = nn.Embedding(cfg.pos_emb_len, cfg.dim)
         self.vlln = nn.Identity()
-        self.physics = PhysicsHead(cfg.physics_dim, cfg.dim, cfg.out_dim, cfg.physics_hist, cfg.physics_fut)
-        self.use_physics = True
+        if cfg.use_physics:
+            self.physics = PhysicsHead(cfg.physics_dim, cfg.dim, cfg.out_dim, cfg.physics_hist,
+                                       cfg.physics_fut)
+        self.use_physics = cfg.use_physics
         self.action_horizon = cfg.horizon
         self.action_dim = cfg.action_dim
         self.num_inference_timesteps = cfg.num_steps
@@ -453,16 +648,16 @@ def init_weights(module: nn.Module, seed: int, std: float = 0.02) -> nn.Module:
     with torch.no_grad():
         for name, p in sorted(module.named_parameters(), key=lambda kv: kv[0]):
             noise = torch.randn(p.shape, generator=g, dtype=torch.float32) * std
-            if name.endswith("norm_sa.weight") or name.endswith("norm_vl.weight") or \
-                    name.endswith("norm_p.weight"):
+            if name.endswith(("norm_sa.weight", "norm_vl.weight", "norm_p.weight",
+                              "q_norm.weight", "k_norm.weight")):
                 noise = noise + 1.0
             p.copy_(noise.to(p.dtype))
     return module
 
 
 @torch.no_grad()
-def denoise(head: nn.Module, vl_embs, state, embodiment_id, init_noise, physics_hist, physics_noise,
-            num_steps: int, return_trace: bool = False):
+def denoise(head: nn.Module, vl_embs, state, embodiment_id, init_noise, physics_hist=None,
+            physics_noise=None, num_steps: int = 4, return_trace: bool = False):
     """Control step with vanilla_action_head_forward semantics (benchmark_action_model.py:50-123)."""
     msat = head.model
     dt = 1.0 / num_steps
@@ -472,6 +667,18 @@ def denoise(head: nn.Module, vl_embs, state, embodiment_id, init_noise, physics_
     state_features = head.state_encoder(state, embodiment_id)
     pos_embs = head.position_embedding(torch.arange(horizon)).unsqueeze(0)
     current = init_noise.clone()
+    if not head.use_physics:
+        trace = []
+        for t in range(num_steps):
+            timesteps = torch.tensor([t / float(num_steps)], dtype=vl.dtype).expand(B)
+            af = head.action_encoder(current, timesteps, embodiment_id) + pos_embs
+            sa = torch.cat([state_features, af], dim=1)
+            out, hidden = msat(sa, vl, timesteps, return_hidden=True)
+            pred = head.action_decoder(out["action"], embodiment_id)[:, -horizon:]
+            current = current + dt * pred
+            if return_trace:
+                trace.append({"hidden": hidden, "out": out, "actions": current})
+        return (current, trace) if return_trace else current
     phys = head.physics
     physics_hist_tok = phys.physics_cond_encoder(physics_hist)
     physics_fut = physics_noise.clone()
@@ -495,7 +702,7 @@ def make_inputs(cfg: MsatHeadConfig, batch: int, seed: int = 42, dtype=torch.flo
     """Seeded synthetic inputs with the shapes of BASELINE config 2 (vl ~ N(0,1), state * 0.01,
     physics ~ N(0,1), init noise ~ N(0,1) from seed + 1, like benchmark_action_model.py:225-241)."""
     g = torch.Generator().manual_seed(seed)
-    vl = torch.randn(batch, cfg.n_vl, cfg.dim, generator=g)
+    vl = torch.randn(batch, cfg.n_vl, cfg.vl_width, generator=g)
     state = torch.randn(batch, cfg.n_state, cfg.state_dim, generator=g) * 0.01
     physics_hist = torch.randn(batch, cfg.physics_hist, cfg.physics_dim, generator=g)
     g2 = torch.Generator().manual_seed(seed + 1)

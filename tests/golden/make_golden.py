@@ -84,17 +84,23 @@ SMALL = om.MsatHeadConfig(n_vl=24, n_state=1, horizon=8, physics_hist=4, physics
                           heads=2, head_dim=64, depth=2, mlp_ratio=3.0, out_dim=64, action_dim=16,
                           state_dim=16, dec_hidden=64, physics_dim=13, num_embodiments=3,
                           num_steps=4, max_seq_len=64, pos_emb_len=32)
+# standard topology (no physics): DoubleStreamBlocks [VL | SA] with a wider VL stream, then
+# SingleStreamBlocks over [VL_proj | time | SA] (the shape of the production no-add-on model)
+STD = om.MsatHeadConfig(**{**vars(SMALL), "use_physics": False, "depth_single": 2, "vl_dim": 256})
+# physics topology with ExpandedSingleStreamBlocks above the ExpandedDoubleStreamBlocks
+PHYS_SS = om.MsatHeadConfig(**{**vars(SMALL), "depth_single": 2, "vl_dim": 256})
 
 
 def reference_head(R, cfg: om.MsatHeadConfig):
     """Builds the reference action-head modules for `cfg` (rldx/model/core/rldx.py:43-106)."""
     msat = R.msat.MSAT(num_attention_heads=cfg.heads, attention_head_dim=cfg.head_dim,
-                       output_dim=cfg.out_dim, depth_multi_stream=cfg.depth, depth_single_stream=0,
-                       dropout=0.0, positional_embeddings=cfg.positional_embeddings,
-                       action_model_max_seq_len=cfg.max_seq_len, sa_dim=cfg.dim, vl_dim=cfg.dim,
+                       output_dim=cfg.out_dim, depth_multi_stream=cfg.depth,
+                       depth_single_stream=cfg.depth_single, dropout=0.0,
+                       positional_embeddings=cfg.positional_embeddings,
+                       action_model_max_seq_len=cfg.max_seq_len, sa_dim=cfg.dim, vl_dim=cfg.vl_width,
                        qk_norm="rms_norm", use_swiglu=True, mlp_ratio=cfg.mlp_ratio,
                        temb_type="input_token", pre_norm="layer_norm", rope_theta=cfg.rope_theta,
-                       use_physics=True, physics_dim=cfg.physics_dim)
+                       use_physics=cfg.use_physics, physics_dim=cfg.physics_dim if cfg.use_physics else 0)
     head = nn.Module()
     head.model = msat
     head.state_encoder = R.ecm.CategorySpecificMLP(cfg.num_embodiments, cfg.state_dim, cfg.dec_hidden, cfg.dim)
@@ -102,22 +108,28 @@ def reference_head(R, cfg: om.MsatHeadConfig):
     head.action_decoder = R.ecm.CategorySpecificMLP(cfg.num_embodiments, cfg.out_dim, cfg.dec_hidden, cfg.action_dim)
     head.position_embedding = nn.Embedding(cfg.pos_emb_len, cfg.dim)
     head.vlln = nn.Identity()
-    delta = list(range(-cfg.physics_hist + 1, 1)) + list(range(1, cfg.physics_fut + 1))
-    head.physics = R.physics_head.PhysicsHead(physics_dim=cfg.physics_dim, embed_dim=cfg.dim,
-                                              msat_output_dim=cfg.out_dim, physics_delta_indices=delta,
-                                              physics_use_flow_matching=True, physics_loss_weight=1.0,
-                                              action_horizon=cfg.horizon)
-    head.use_physics = True
+    if cfg.use_physics:
+        delta = list(range(-cfg.physics_hist + 1, 1)) + list(range(1, cfg.physics_fut + 1))
+        head.physics = R.physics_head.PhysicsHead(physics_dim=cfg.physics_dim, embed_dim=cfg.dim,
+                                                  msat_output_dim=cfg.out_dim, physics_delta_indices=delta,
+                                                  physics_use_flow_matching=True, physics_loss_weight=1.0,
+                                                  action_horizon=cfg.horizon)
+    head.use_physics = cfg.use_physics
     return head
 
 
 def run_reference_loop(R, head, cfg, inp):
+    common = dict(msat=head.model, state_encoder=head.state_encoder, action_encoder=head.action_encoder,
+                  action_decoder=head.action_decoder, position_embedding=head.position_embedding,
+                  vlln=head.vlln, n_vl=cfg.n_vl, n_sa_pure=cfg.n_state + cfg.horizon,
+                  action_horizon=cfg.horizon, action_dim=cfg.action_dim,
+                  num_inference_timesteps=cfg.num_steps, device="cpu", dtype=inp["vl"].dtype)
+    if not cfg.use_physics:
+        gs = R.gs.GraphSafeActionModel(**common)
+        with torch.no_grad():
+            return gs(inp["vl"], inp["state"], inp["embodiment_id"], init_noise=inp["init_noise"])
     gs = R.gs.GraphSafeActionModel(
-        msat=head.model, state_encoder=head.state_encoder, action_encoder=head.action_encoder,
-        action_decoder=head.action_decoder, position_embedding=head.position_embedding,
-        vlln=head.vlln, n_vl=cfg.n_vl, n_sa_pure=cfg.n_state + cfg.horizon,
-        action_horizon=cfg.horizon, action_dim=cfg.action_dim, num_inference_timesteps=cfg.num_steps,
-        device="cpu", dtype=inp["vl"].dtype, physics_cond_encoder=head.physics.physics_cond_encoder,
+        **common, physics_cond_encoder=head.physics.physics_cond_encoder,
         physics_fut_encoder=head.physics.physics_fut_encoder, physics_decoder=head.physics.physics_decoder,
         physics_hist_len=cfg.physics_hist, physics_fut_len=cfg.physics_fut, physics_dim=cfg.physics_dim)
     with torch.no_grad():
@@ -135,6 +147,13 @@ def run_vanilla_loop(head, cfg, inp):
         sf = head.state_encoder(inp["state"], inp["embodiment_id"])
         pos = head.position_embedding(torch.arange(cfg.horizon)).unsqueeze(0)
         cur = inp["init_noise"].clone()
+        if not cfg.use_physics:
+            for t in range(cfg.num_steps):
+                ts = torch.tensor([t / float(cfg.num_steps)], dtype=vl.dtype).expand(B)
+                af = head.action_encoder(cur, ts, inp["embodiment_id"]) + pos
+                mo = head.model(hidden_states=torch.cat([sf, af], 1), encoder_hidden_states=vl, timestep=ts)
+                cur = cur + dt * head.action_decoder(mo, inp["embodiment_id"])[:, -cfg.horizon:]
+            return cur
         phys = head.physics
         hist = phys.physics_cond_encoder(inp["physics_hist"])
         fut = inp["physics_noise"].clone()
@@ -153,9 +172,8 @@ def weight_checksum(module: nn.Module) -> float:
     return float(sum(p.detach().double().abs().sum() for p in module.parameters()))
 
 
-def head_fixture(R, dtype, batch: int) -> dict:
+def head_fixture(R, dtype, batch: int, cfg: om.MsatHeadConfig = SMALL) -> dict:
     """batch 1: the reference GraphSafeActionModel loop; batch > 1: the vanilla eager loop."""
-    cfg = SMALL
     ref = reference_head(R, cfg)
     om.init_weights(ref, seed=1234)
     orc = om.ActionHead(cfg)
@@ -175,10 +193,14 @@ def head_fixture(R, dtype, batch: int) -> dict:
         sf = ref.state_encoder(inp["state"], inp["embodiment_id"])
         af = ref.action_encoder(inp["init_noise"], t0, inp["embodiment_id"]) + \
             ref.position_embedding(torch.arange(cfg.horizon)).unsqueeze(0)
-        pe = torch.cat([ref.physics.physics_cond_encoder(inp["physics_hist"]),
-                        ref.physics.physics_fut_encoder(inp["physics_noise"], t0)], dim=1)
-        msat_out = ref.model(hidden_states=torch.cat([sf, af], 1), encoder_hidden_states=inp["vl"],
-                             timestep=t0, physics_embs=pe)
+        if cfg.use_physics:
+            pe = torch.cat([ref.physics.physics_cond_encoder(inp["physics_hist"]),
+                            ref.physics.physics_fut_encoder(inp["physics_noise"], t0)], dim=1)
+            msat_out = ref.model(hidden_states=torch.cat([sf, af], 1), encoder_hidden_states=inp["vl"],
+                                 timestep=t0, physics_embs=pe)
+        else:
+            msat_out = {"action": ref.model(hidden_states=torch.cat([sf, af], 1),
+                                            encoder_hidden_states=inp["vl"], timestep=t0)}
     return {"config": vars(cfg), "seed": 1234, "weight_abs_sum": weight_checksum(ref),
             "dtype": str(dtype), "batch": batch, "loop": "graph_safe" if batch == 1 else "vanilla",
             "inputs": inp, "actions": actions,
@@ -216,6 +238,10 @@ def main():
     torch.save(head_fixture(R, torch.float32, 2), HERE / "head_small_b2_fp32.pt")
     torch.save(head_fixture(R, torch.bfloat16, 2), HERE / "head_small_b2_bf16.pt")
     torch.save(c1_block_fixture(R), HERE / "c1_block_fp32.pt")
+    for tag, cfg in (("std", STD), ("physss", PHYS_SS)):
+        for dtype, dn in ((torch.float32, "fp32"), (torch.bfloat16, "bf16")):
+            for batch in (1, 2):
+                torch.save(head_fixture(R, dtype, batch, cfg), HERE / f"head_{tag}_b{batch}_{dn}.pt")
     for f in sorted(HERE.glob("*.pt")):
         print(f.name, f.stat().st_size)
 

@@ -1,7 +1,9 @@
 """Pins the CPU oracle against golden vectors produced by the reference implementation itself
 (tests/golden/make_golden.py): the reference's GraphSafeActionModel loop (batch 1), its eager
 loop around the reference modules (batch 2) and one reference ExpandedDoubleStreamBlock at
-BASELINE config 1 shapes."""
+BASELINE config 1 shapes.  Three topologies: "small" (physics, double blocks only, config 2's
+form), "std" (no physics: DoubleStreamBlocks with a wider VL stream + SingleStreamBlocks, the
+production no-add-on form) and "physss" (physics with ExpandedSingleStreamBlocks on top)."""
 
 from pathlib import Path
 
@@ -17,8 +19,11 @@ def _load(name):
     return torch.load(GOLD / name, weights_only=False)
 
 
-@pytest.mark.parametrize("name", ["head_small_b1_fp32.pt", "head_small_b2_fp32.pt",
-                                  "head_small_b1_bf16.pt", "head_small_b2_bf16.pt"])
+HEADS = [f"head_{tag}_b{b}_{dt}.pt" for tag in ("small", "std", "physss") for b in (1, 2)
+         for dt in ("fp32", "bf16")]
+
+
+@pytest.mark.parametrize("name", HEADS)
 def test_oracle_matches_reference_head(name):
     fx = _load(name)
     cfg = om.MsatHeadConfig(**fx["config"])
@@ -30,8 +35,9 @@ def test_oracle_matches_reference_head(name):
     assert wsum == pytest.approx(fx["weight_abs_sum"], rel=1e-9)
     assert (not head.model.rope_embedder.freqs_cis_0.is_complex()) == fx["cos_only_rope"]
     inp = fx["inputs"]
+    phys = (inp["physics_hist"], inp["physics_noise"]) if cfg.use_physics else (None, None)
     out = om.denoise(head, inp["vl"], inp["state"], inp["embodiment_id"], inp["init_noise"],
-                     inp["physics_hist"], inp["physics_noise"], cfg.num_steps)
+                     *phys, cfg.num_steps)
     ref = fx["actions"]
     if dtype == torch.float32:
         torch.testing.assert_close(out, ref, rtol=1e-5, atol=1e-5)
@@ -39,7 +45,8 @@ def test_oracle_matches_reference_head(name):
         assert torch.equal(out, ref), (out.float() - ref.float()).abs().max()
 
 
-@pytest.mark.parametrize("name", ["head_small_b2_fp32.pt", "head_small_b2_bf16.pt"])
+@pytest.mark.parametrize("name", [f"head_{tag}_b2_{dt}.pt" for tag in ("small", "std", "physss")
+                                  for dt in ("fp32", "bf16")])
 def test_oracle_msat_forward_matches_reference(name):
     fx = _load(name)
     cfg = om.MsatHeadConfig(**fx["config"])
@@ -53,10 +60,13 @@ def test_oracle_msat_forward_matches_reference(name):
         sf = head.state_encoder(inp["state"], inp["embodiment_id"])
         af = head.action_encoder(inp["init_noise"], t0, inp["embodiment_id"]) + \
             head.position_embedding(torch.arange(cfg.horizon)).unsqueeze(0)
-        pe = torch.cat([head.physics.physics_cond_encoder(inp["physics_hist"]),
-                        head.physics.physics_fut_encoder(inp["physics_noise"], t0)], dim=1)
-        out = head.model(torch.cat([sf, af], 1), inp["vl"], t0, pe)
-    for k in ("action", "physics"):
+        if cfg.use_physics:
+            pe = torch.cat([head.physics.physics_cond_encoder(inp["physics_hist"]),
+                            head.physics.physics_fut_encoder(inp["physics_noise"], t0)], dim=1)
+            out = head.model(torch.cat([sf, af], 1), inp["vl"], t0, pe)
+        else:
+            out = head.model(torch.cat([sf, af], 1), inp["vl"], t0)
+    for k in fx["msat_step0"]:
         if "bf16" in name:
             assert torch.equal(out[k], fx["msat_step0"][k])
         else:
