@@ -185,12 +185,12 @@ typedef struct {
   int n_vl;            /* cognition (VL) tokens per observation                          */
   int n_state;         /* state tokens (1)                                               */
   int horizon;         /* action tokens                                                  */
-  int physics_hist;    /* physics history tokens                                         */
-  int physics_fut;     /* physics future tokens (== horizon)                             */
-  int dim;             /* stream width: sa_dim == vl_dim == p_dim == heads * head_dim    */
+  int physics_hist;    /* physics history tokens (ignored on the standard path)          */
+  int physics_fut;     /* physics future tokens (== horizon; ignored on the standard path) */
+  int dim;             /* sa_dim == p_dim == heads * head_dim (single-block width)       */
   int heads;
   int head_dim;        /* 64                                                             */
-  int depth;           /* ExpandedDoubleStreamBlocks                                     */
+  int depth;           /* double-stream blocks (Expanded... with physics)                */
   int mlp_hidden;      /* SwiGLU hidden of the SA and P streams                          */
   int vl_mlp_hidden;   /* SwiGLU hidden of the VL stream                                 */
   int out_dim;         /* MSAT output_dim (= action decoder input)                       */
@@ -206,6 +206,13 @@ typedef struct {
   int rope_max_seq;    /* RoPE table length (action_model_max_seq_len)                   */
   int temb_channels;   /* Timesteps(num_channels) (256)                                  */
   int use_graph;       /* 1: capture the whole control step as one CUDA graph            */
+  /* Topology (a zero-filled tail gives the all-modality form above: physics, double blocks) */
+  int standard_path;   /* 1: no physics stream: DoubleStreamBlocks [VL | SA], then
+                          SingleStreamBlocks [VL_proj | time | SA] (msat.py:363-556)       */
+  int vl_dim;          /* VL stream width in the double blocks (0: dim)                  */
+  int depth_single;    /* single-stream blocks after the double ones (Expanded... with P) */
+  int single_expanded; /* SingleStreamBlock SwiGLU width: int(dim * mlp_ratio)            */
+  int single_mlp_hidden; /* SingleStreamBlock mlp_proj output: int(2/3 * single_expanded) */
 } rldx_msat_config;
 
 typedef struct {
@@ -228,6 +235,19 @@ typedef struct {
   rldx_stream_weights vl, sa, p;
 } rldx_block_weights;
 
+/* SingleStreamBlock (blocks.py:42-254) / ExpandedSingleStreamBlock (blocks.py:894-1089):
+ * linear1 [3*inner + 2*expanded, dim] = [q | k | v | SwiGLU gate | SwiGLU up],
+ * mlp_proj [mlp_hidden, expanded], linear2 [dim, inner + mlp_hidden]; p_* for the physics
+ * stream of the expanded block (NULL on the standard path). */
+typedef struct {
+  rldx_linear linear1, linear2, mlp_proj;
+  const void* q_norm; /* [head_dim] bf16 */
+  const void* k_norm;
+  rldx_linear p_linear1, p_linear2, p_mlp_proj;
+  const void* p_q_norm;
+  const void* p_k_norm;
+} rldx_single_block_weights;
+
 typedef struct {
   const rldx_block_weights* blocks; /* [depth] (host array of device pointers)       */
   rldx_linear temb_lin1, temb_lin2;  /* timestep_encoder.timestep_embedder.linear_1/2  */
@@ -241,15 +261,17 @@ typedef struct {
   rldx_linear phc_w1, phc_w2, phc_w3;      /* physics.physics_cond_encoder.W1/W2/W3     */
   rldx_linear phf_w1, phf_w2, phf_w3;      /* physics.physics_fut_encoder.W1/W2/W3      */
   rldx_linear phd_l1, phd_l2;              /* physics.physics_decoder.net[0] / net[2]   */
+  const rldx_single_block_weights* single_blocks; /* [depth_single] (host array)         */
+  rldx_linear vl_proj_to_sa;               /* w == NULL: identity (vl_dim == dim)       */
 } rldx_msat_weights;
 
 typedef struct {
-  const void* vl;            /* [B, n_vl, dim] bf16                                     */
+  const void* vl;            /* [B, n_vl, vl_dim] bf16                                  */
   const void* state;         /* [B, n_state, state_dim] bf16                            */
   const int64_t* emb_id;     /* [B] int64                                               */
   const void* init_noise;    /* [B, horizon, action_dim] bf16                           */
-  const void* physics_hist;  /* [B, physics_hist, physics_dim] bf16                     */
-  const void* physics_noise; /* [B, physics_fut, physics_dim] bf16                      */
+  const void* physics_hist;  /* [B, physics_hist, physics_dim] bf16 (NULL: standard)   */
+  const void* physics_noise; /* [B, physics_fut, physics_dim] bf16 (NULL: standard)    */
   void* actions;             /* out: [B, horizon, action_dim] bf16                      */
 } rldx_msat_io;
 
@@ -284,8 +306,10 @@ int rldx_msat_profile(rldx_msat* h, const rldx_msat_io* io, rldx_op_profile* ops
                       int* n_ops, void* stream);
 
 /* Copies an intermediate buffer of the last control step into dst (device or host memory,
- * dst_bytes large enough) on `stream`: 0 X_vl, 1 X_sa, 2 X_p (streams after the last block of
- * the last Euler step), 3 the action state.  With dst == NULL only *rows / *cols are set. */
+ * dst_bytes large enough) on `stream`: 0 X_vl ([B*n_vl, vl_dim]), 1 X_sa, 2 X_p (streams after
+ * the last block of the last Euler step; with single blocks, X_sa / X_p after the last single
+ * block and X_vl after the last double block unless vl_proj_to_sa is the identity), 3 the
+ * action state.  With dst == NULL only *rows / *cols are set. */
 int rldx_msat_read_buffer(const rldx_msat* h, int which, void* dst, int64_t dst_bytes,
                           int64_t* rows, int64_t* cols, void* stream);
 

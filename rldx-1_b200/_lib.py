@@ -58,6 +58,8 @@ class MsatConfig(C.Structure):
         ("physics_dim", C.c_int), ("num_embodiments", C.c_int), ("num_steps", C.c_int),
         ("rope_mode", C.c_int), ("rope_cos_only", C.c_int), ("rope_theta", C.c_float),
         ("rope_max_seq", C.c_int), ("temb_channels", C.c_int), ("use_graph", C.c_int),
+        ("standard_path", C.c_int), ("vl_dim", C.c_int), ("depth_single", C.c_int),
+        ("single_expanded", C.c_int), ("single_mlp_hidden", C.c_int),
     ]
 
 
@@ -78,6 +80,13 @@ class BlockWeights(C.Structure):
     _fields_ = [("vl", StreamWeights), ("sa", StreamWeights), ("p", StreamWeights)]
 
 
+class SingleBlockWeights(C.Structure):
+    _fields_ = [("linear1", Linear), ("linear2", Linear), ("mlp_proj", Linear),
+                ("q_norm", vp), ("k_norm", vp),
+                ("p_linear1", Linear), ("p_linear2", Linear), ("p_mlp_proj", Linear),
+                ("p_q_norm", vp), ("p_k_norm", vp)]
+
+
 class MsatWeights(C.Structure):
     _fields_ = [
         ("blocks", C.POINTER(BlockWeights)),
@@ -91,6 +100,7 @@ class MsatWeights(C.Structure):
         ("phc_w1", Linear), ("phc_w2", Linear), ("phc_w3", Linear),
         ("phf_w1", Linear), ("phf_w2", Linear), ("phf_w3", Linear),
         ("phd_l1", Linear), ("phd_l2", Linear),
+        ("single_blocks", C.POINTER(SingleBlockWeights)), ("vl_proj_to_sa", Linear),
     ]
 
 

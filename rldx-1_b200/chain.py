@@ -1,11 +1,21 @@
-"""Drop-in replacement for the reference's all-modality action-head chain.
+"""Drop-in replacements for the reference's action-head chains.
 
 `B200ExpandedActionHeadChain` has the constructor and forward signature of
-CustomExpandedActionHeadChain (rldx/inference/action_model/engine/custom_expanded_action_model_chain.py:19-213):
+CustomExpandedActionHeadChain (rldx/inference/action_model/engine/custom_expanded_action_model_chain.py:19-213),
+the all-modality head (ExpandedDoubleStreamBlocks over [VL | SA | P], then ExpandedSingleStreamBlocks
+over [VL_proj | SA | P] when the model has any):
 
     chain = B200ExpandedActionHeadChain(gs_action_model, device, dtype=torch.bfloat16)
     actions = chain(vl_embs, state, embodiment_id, init_noise=None, physics_hist=None,
                     physics_init_noise=None)
+
+`B200ActionHeadChain` has those of CustomActionHeadChain
+(rldx/inference/action_model/engine/custom_action_model_chain.py:23-170), the head without add-ons
+(DoubleStreamBlocks over [VL | SA] with a VL stream of its own width, vl_proj_to_sa, then
+SingleStreamBlocks over [VL_proj | SA]):
+
+    chain = B200ActionHeadChain(gs_action_model, device, dtype=torch.bfloat16)
+    actions = chain(vl_embs, state, embodiment_id, init_noise=None)
 
 It reads the weights by the reference's attribute names from a GraphSafeActionModel
 (rldx/inference/action_model/model/graph_safe_action_model.py:27-168) or from an action model
@@ -27,30 +37,52 @@ import torch
 from torch import nn
 
 from . import _lib
-from ._lib import BlockWeights, CatLinear, Linear, MsatConfig, MsatIO, MsatWeights, StreamWeights, check
+from ._lib import (BlockWeights, CatLinear, Linear, MsatConfig, MsatIO, MsatWeights,
+                   SingleBlockWeights, StreamWeights, check)
 
 
 def _parts(head: nn.Module):
-    """(msat, state_encoder, action_encoder, action_decoder, position_embedding, physics, vlln)"""
+    """(msat, state_encoder, action_encoder, action_decoder, position_embedding, physics, vlln);
+    physics is None for a head without the physics stream."""
     if hasattr(head, "gs_msat"):  # GraphSafeActionModel
         msat = head.gs_msat._msat if hasattr(head.gs_msat, "_msat") else head.gs_msat
-        physics = nn.Module()
-        physics.physics_cond_encoder = head.physics_cond_encoder
-        physics.physics_fut_encoder = head.physics_fut_encoder
-        physics.physics_decoder = head.physics_decoder
-        physics.physics_hist_len = head.physics_hist_len
-        physics.physics_fut_len = head.physics_fut_len
-        physics.physics_dim = head.physics_dim
+        physics = None
+        if getattr(head, "physics_cond_encoder", None) is not None:
+            physics = nn.Module()
+            physics.physics_cond_encoder = head.physics_cond_encoder
+            physics.physics_fut_encoder = head.physics_fut_encoder
+            physics.physics_decoder = head.physics_decoder
+            physics.physics_hist_len = head.physics_hist_len
+            physics.physics_fut_len = head.physics_fut_len
+            physics.physics_dim = head.physics_dim
     else:
         msat = head.model
-        physics = head.physics
+        physics = getattr(head, "physics", None)
+    if not getattr(msat, "use_physics", physics is not None):
+        physics = None
     return (msat, head.state_encoder, head.action_encoder, head.action_decoder,
             head.position_embedding, physics, getattr(head, "vlln", nn.Identity()))
 
 
-class B200ExpandedActionHeadChain(nn.Module):
-    """All-modality action head (state encoder, physics history encoder, num_steps x
-    [action / physics encoders + MSAT + decoders + Euler]) on librldx_b200."""
+def _check_single_block(blk: nn.Module, prefix: str) -> None:
+    """The runtime implements the SingleStreamBlock form the heads are built with: LayerNorm
+    without affine as pre_norm, no post_norm, SwiGLU with mlp_proj (blocks.py:42-254)."""
+    pre = getattr(blk, f"{prefix}pre_norm")
+    if not isinstance(pre, nn.LayerNorm) or pre.weight is not None:
+        raise NotImplementedError("single blocks: only a LayerNorm without affine as pre_norm is bound")
+    if not isinstance(getattr(blk, f"{prefix}post_norm", nn.Identity()), nn.Identity):
+        raise NotImplementedError("single blocks: post_norm must be the identity")
+    if getattr(blk, f"{prefix}mlp_proj", None) is None:
+        raise NotImplementedError("single blocks: the SwiGLU form with mlp_proj is the one bound")
+    if getattr(blk, f"{prefix}linear1").bias is None or getattr(blk, f"{prefix}linear2").bias is None:
+        raise NotImplementedError("single blocks: linear1 / linear2 without bias are not bound")
+
+
+class _B200HeadChain(nn.Module):
+    """State encoder (+ physics history encoder), then num_steps x [action (+ physics) encoders
+    + MSAT + decoders + Euler], as one native control step on librldx_b200."""
+
+    _physics = True
 
     def __init__(self, gs_action_model: nn.Module, device=None, dtype=torch.bfloat16, *,
                  num_inference_timesteps: Optional[int] = None, use_graph: bool = True):
@@ -59,10 +91,15 @@ class B200ExpandedActionHeadChain(nn.Module):
             raise ValueError("the B200 chain computes in bfloat16 only")
         parts = _parts(gs_action_model)
         self._msat, self._state_enc, self._act_enc, self._act_dec, self._pos, self._phys, vlln = parts
+        if (self._phys is not None) != self._physics:
+            raise ValueError(f"{type(self).__name__} needs a head {'with' if self._physics else 'without'} "
+                             "the physics stream")
         if not isinstance(vlln, nn.Identity):
             raise NotImplementedError("use_vlln=True (LayerNorm on backbone features) is not bound")
-        if len(getattr(self._msat, "single_blocks", [])) != 0:
-            raise NotImplementedError("ExpandedSingleStreamBlocks are not bound (depth_single_stream must be 0)")
+        for blk in getattr(self._msat, "single_blocks", []):
+            _check_single_block(blk, "")
+            if self._physics:
+                _check_single_block(blk, "p_")
         if getattr(self._msat, "temb_type", "input_token") != "input_token":
             raise NotImplementedError("only temb_type='input_token' is supported")
         self.device = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
@@ -110,7 +147,14 @@ class B200ExpandedActionHeadChain(nn.Module):
         c.action_dim = self._act_dec.layer2.W.shape[2]
         c.state_dim = self._state_enc.layer1.W.shape[1]
         c.dec_hidden = self._state_enc.layer1.W.shape[2]
-        c.physics_dim = self._phys.physics_cond_encoder.W1.weight.shape[1]
+        c.physics_dim = self._phys.physics_cond_encoder.W1.weight.shape[1] if self._physics else 0
+        c.standard_path = 0 if self._physics else 1
+        c.vl_dim = blk.vl_qkv.weight.shape[1]
+        singles = list(getattr(msat, "single_blocks", []))
+        c.depth_single = len(singles)
+        if singles:
+            c.single_expanded = singles[0].mlp_proj.weight.shape[1]
+            c.single_mlp_hidden = singles[0].mlp_proj.weight.shape[0]
         c.num_embodiments = self._state_enc.layer1.W.shape[0]
         c.num_steps = self.num_inference_timesteps
         c.rope_mode = _lib.ROPE_SA_ONLY if mode == "rope_sa_only" else _lib.ROPE_VL_SA
@@ -130,7 +174,7 @@ class B200ExpandedActionHeadChain(nn.Module):
         w = MsatWeights()
         blocks = (BlockWeights * len(msat.double_blocks))()
         for i, blk in enumerate(msat.double_blocks):
-            for s in ("vl", "sa", "p"):
+            for s in (("vl", "sa", "p") if self._physics else ("vl", "sa")):
                 sw = StreamWeights()
                 sw.qkv = self._lin(getattr(blk, f"{s}_qkv"))
                 sw.proj = self._lin(getattr(blk, f"{s}_proj"))
@@ -142,16 +186,33 @@ class B200ExpandedActionHeadChain(nn.Module):
                 setattr(blocks[i], s, sw)
         self._keep.append(blocks)
         w.blocks = C.cast(blocks, C.POINTER(BlockWeights))
+        singles = list(getattr(msat, "single_blocks", []))
+        if singles:
+            sb = (SingleBlockWeights * len(singles))()
+            for i, blk in enumerate(singles):
+                for pre in (("", "p_") if self._physics else ("",)):
+                    setattr(sb[i], f"{pre}linear1", self._lin(getattr(blk, f"{pre}linear1")))
+                    setattr(sb[i], f"{pre}linear2", self._lin(getattr(blk, f"{pre}linear2")))
+                    setattr(sb[i], f"{pre}mlp_proj", self._lin(getattr(blk, f"{pre}mlp_proj")))
+                    setattr(sb[i], f"{pre}q_norm", self._bf16(getattr(blk, f"{pre}q_norm").weight))
+                    setattr(sb[i], f"{pre}k_norm", self._bf16(getattr(blk, f"{pre}k_norm").weight))
+            self._keep.append(sb)
+            w.single_blocks = C.cast(sb, C.POINTER(SingleBlockWeights))
+            if not isinstance(msat.vl_proj_to_sa, nn.Identity):
+                w.vl_proj_to_sa = self._lin(msat.vl_proj_to_sa)
         te = msat.timestep_encoder.timestep_embedder
         w.temb_lin1, w.temb_lin2 = self._lin(te.linear_1), self._lin(te.linear_2)
         w.proj_out_1, w.proj_out_2 = self._lin(msat.proj_out_1), self._lin(msat.proj_out_2)
-        w.proj_out_phys_1 = self._lin(msat.proj_out_physics_1)
-        w.proj_out_phys_2 = self._lin(msat.proj_out_physics_2)
+        if self._physics:
+            w.proj_out_phys_1 = self._lin(msat.proj_out_physics_1)
+            w.proj_out_phys_2 = self._lin(msat.proj_out_physics_2)
         w.state_l1, w.state_l2 = self._cat(self._state_enc.layer1), self._cat(self._state_enc.layer2)
         ae = self._act_enc
         w.act_w1, w.act_w2, w.act_w3 = self._cat(ae.W1), self._cat(ae.W2), self._cat(ae.W3)
         w.dec_l1, w.dec_l2 = self._cat(self._act_dec.layer1), self._cat(self._act_dec.layer2)
         w.pos_emb = self._bf16(self._pos.weight)
+        if not self._physics:
+            return w
         pc, pf, pd = (self._phys.physics_cond_encoder, self._phys.physics_fut_encoder,
                       self._phys.physics_decoder)
         w.phc_w1, w.phc_w2, w.phc_w3 = self._lin(pc.W1), self._lin(pc.W2), self._lin(pc.W3)
@@ -179,18 +240,13 @@ class B200ExpandedActionHeadChain(nn.Module):
         return int(_lib.load().rldx_msat_launch_count(self._handle)) if self._handle else 0
 
     # ------------------------------------------------------------------ forward
-    def forward(self, vl_embs, state, embodiment_id, init_noise=None, physics_hist=None,
-                physics_init_noise=None, prefix_actions=None):
-        if prefix_actions is not None:
-            raise NotImplementedError("RTC prefix inpainting is not bound yet")
-        if physics_hist is None:
-            raise ValueError("physics_hist is required by the all-modality chain")
+    def _step(self, vl_embs, state, embodiment_id, init_noise, physics_hist, physics_init_noise):
         B, n_vl, _ = vl_embs.shape
         if state.dim() == 2:
             state = state.unsqueeze(1)
         horizon = self.action_horizon or (init_noise.shape[1] if init_noise is not None else 16)
-        hist = physics_hist.shape[1]
-        fut = physics_init_noise.shape[1] if physics_init_noise is not None else horizon
+        hist = physics_hist.shape[1] if self._physics else 0
+        fut = (physics_init_noise.shape[1] if physics_init_noise is not None else horizon) if self._physics else 0
         shapes = (B, n_vl, state.shape[1], horizon, hist, fut)
         if self._handle is None:
             self.bind(*shapes)
@@ -209,20 +265,25 @@ class B200ExpandedActionHeadChain(nn.Module):
         ids = _in(embodiment_id.reshape(-1), torch.int64)
         if init_noise is None:
             init_noise = torch.randn(B, horizon, self.action_dim, dtype=bf, device=dev)
-        if physics_init_noise is None:
-            physics_init_noise = torch.randn(B, fut, self._cfg.physics_dim, dtype=bf, device=dev)
-        noise, ph, pn = _in(init_noise), _in(physics_hist), _in(physics_init_noise)
+        noise = _in(init_noise)
+        ph_ptr = pn_ptr = None
+        if self._physics:
+            if physics_init_noise is None:
+                physics_init_noise = torch.randn(B, fut, self._cfg.physics_dim, dtype=bf, device=dev)
+            ph, pn = _in(physics_hist), _in(physics_init_noise)
+            ph_ptr, pn_ptr = ph.data_ptr(), pn.data_ptr()
         out = torch.empty(B, horizon, self.action_dim, dtype=bf, device=dev)
-        io = MsatIO(vl.data_ptr(), st.data_ptr(), ids.data_ptr(), noise.data_ptr(), ph.data_ptr(),
-                    pn.data_ptr(), out.data_ptr())
+        io = MsatIO(vl.data_ptr(), st.data_ptr(), ids.data_ptr(), noise.data_ptr(), ph_ptr,
+                    pn_ptr, out.data_ptr())
         stream = torch.cuda.current_stream(dev)
         check(_lib.load().rldx_msat_step(self._handle, C.byref(io), C.c_void_p(stream.cuda_stream)))
         return out
 
     def _io(self, inp: dict, out: torch.Tensor) -> MsatIO:
+        ph = inp["physics_hist"].data_ptr() if self._physics else None
+        pn = inp["physics_noise"].data_ptr() if self._physics else None
         return MsatIO(inp["vl"].data_ptr(), inp["state"].data_ptr(), inp["embodiment_id"].data_ptr(),
-                      inp["init_noise"].data_ptr(), inp["physics_hist"].data_ptr(),
-                      inp["physics_noise"].data_ptr(), out.data_ptr())
+                      inp["init_noise"].data_ptr(), ph, pn, out.data_ptr())
 
     def forward_host(self, inp: dict, out: torch.Tensor) -> torch.Tensor:
         """One control step from (pinned) host tensors to a host tensor through
@@ -269,3 +330,29 @@ class B200ExpandedActionHeadChain(nn.Module):
                 _lib.load().rldx_msat_destroy(h)
             except Exception:  # noqa: BLE001
                 pass
+
+
+class B200ExpandedActionHeadChain(_B200HeadChain):
+    """All-modality head: CustomExpandedActionHeadChain.forward
+    (custom_expanded_action_model_chain.py:82-213)."""
+
+    _physics = True
+
+    def forward(self, vl_embs, state, embodiment_id, init_noise=None, physics_hist=None,
+                physics_init_noise=None, prefix_actions=None):
+        if prefix_actions is not None:
+            raise NotImplementedError("RTC prefix inpainting is not bound yet")
+        if physics_hist is None:
+            raise ValueError("physics_hist is required by the all-modality chain")
+        return self._step(vl_embs, state, embodiment_id, init_noise, physics_hist, physics_init_noise)
+
+
+class B200ActionHeadChain(_B200HeadChain):
+    """Head without add-ons: CustomActionHeadChain.forward (custom_action_model_chain.py:81-170)."""
+
+    _physics = False
+
+    def forward(self, vl_embs, state, embodiment_id, init_noise=None, prefix_actions=None, **kwargs):
+        if prefix_actions is not None:
+            raise NotImplementedError("RTC prefix inpainting is not bound yet")
+        return self._step(vl_embs, state, embodiment_id, init_noise, None, None)

@@ -262,9 +262,9 @@ __global__ void __launch_bounds__(kAttnThreads, 1) joint_attention_kernel(const 
           ++seg;
         }
         const float inv_l = 1.0f / l_run;
+        const int ld = P.seg_ld[seg] > 0 ? P.seg_ld[seg] : P.H * 64;
         __nv_bfloat16* dst = P.seg_out[seg] +
-                             (static_cast<size_t>(b) * P.seg_len[seg] + (qrow - off)) * (P.H * 64) +
-                             head * 64;
+                             (static_cast<size_t>(b) * P.seg_len[seg] + (qrow - off)) * ld + head * 64;
         uint4* d4 = reinterpret_cast<uint4*>(dst);
 #pragma unroll
         for (int cc = 0; cc < 8; ++cc) {

@@ -13,6 +13,7 @@ struct AttnParams {
   const unsigned char* key_mask;  // [B, L] (1 = visible) or null
   __nv_bfloat16* seg_out[3];      // per-stream outputs [B * seg_len, H*64]
   int seg_len[3];
+  int seg_ld[3];                  // row stride of seg_out[s] in elements (0: H*64)
   int nseg;
   float scale_log2;  // log2(e) / sqrt(head_dim)
 };
@@ -27,12 +28,13 @@ struct LnSegment {
   const __nv_bfloat16* scale1p;  // optional [D]: (1 + scale), bf16
   const __nv_bfloat16* shift;    // optional [D]
   int rows, ld_in, ld_out, row_begin;
+  int D;  // row width of this segment (0: LnParams::D)
 };
 constexpr int kMaxLnSegments = 4;
 struct LnParams {
   LnSegment seg[kMaxLnSegments];
   int nseg;
-  int D;
+  int D;  // widest segment (selects the kernel variant)
   int total_rows;
   float eps;
 };

@@ -2,7 +2,12 @@
 // table, plans the whole control step as a list of kernel launches over static buffers and
 // captures it as one CUDA graph.
 //
-// Reference call sequence (all-modality action head, no RTC):
+// Two topologies (no RTC):
+//   * all-modality (physics): ExpandedDoubleStreamBlocks over [VL | SA | P], then optional
+//     ExpandedSingleStreamBlocks over [VL_proj + SA | P] (msat.py:558-781);
+//   * standard (no add-ons): DoubleStreamBlocks over [VL | SA] with a VL stream of its own
+//     width, then SingleStreamBlocks over [VL_proj | time | SA] (msat.py:363-556).
+// Reference call sequence of the all-modality action head:
 //   rldx/inference/action_model/model/graph_safe_action_model.py:170-312   (loop structure)
 //   rldx/inference/action_model/engine/custom_expanded_action_model_chain.py:51-66 (baked temb,
 //       time tokens and positional embeddings)
@@ -107,12 +112,30 @@ struct rldx_msat {
   int device = 0;
   std::vector<void*> allocs;
   int B = 0, nvl = 0, nsa = 0, np = 0, L = 0, Lp = 0, D = 0, H = 0, hc = 0, S = 0;
+  bool standard = false;  // no physics stream
+  int Dv = 0;             // VL stream width in the double blocks
+  int nx = 0;             // single-block x stream tokens per observation: [VL_proj | time | S/A]
+  int E = 0, Mh = 0;      // single-block SwiGLU width and mlp_proj output width
 
   struct StreamW {
     bf16 *qkv_w, *qkv_b, *proj_w, *proj_b, *w12_w, *w12_b, *w3_w, *w3_b, *qn, *kn;
     int hidden;
   };
   std::vector<StreamW> wvl, wsa, wp;
+  struct SingleW {
+    bf16 *qkv_w, *qkv_b, *w12_w, *w12_b, *mp_w, *mp_b, *l2_w, *l2_b, *qn, *kn;
+  };
+  std::vector<SingleW> sgx, sgp;  // single blocks: x stream, physics stream (expanded form)
+  bf16 *vlp_w = nullptr, *vlp_b = nullptr;  // vl_proj_to_sa (null: identity)
+  float *rope_cos_s = nullptr, *rope_sin_s = nullptr;
+  // Single-block row groups [VL_proj | time, S/A | P].  The x stream is the first two groups:
+  // they share the x weights and run as two problems of one grouped GEMM, so the S/A rows stay
+  // in xsa and VL_proj is xvl itself when vl_proj_to_sa is the identity.  The joint sequence
+  // has the same length L as in the double blocks.
+  bf16* sx[3] = {};    // group rows (residual stream)
+  bf16* sln[3] = {};   // pre_norm output
+  bf16* sh[3] = {};    // silu(x1) * x2
+  bf16* scat[3] = {};  // [attention | mlp_proj] = linear2 input, row width inner + Mh
   bf16 *po2_w = nullptr, *po2_b = nullptr, *pp2_w = nullptr, *pp2_b = nullptr;
   bf16 *st1_W, *st1_b, *st2_W, *st2_b, *aw1_W, *aw1_b, *aw2_W, *aw2_b, *aw3_W, *aw3_b;
   bf16 *dl1_W, *dl1_b, *dl2_W, *dl2_b, *pos;
@@ -211,19 +234,42 @@ struct rldx_msat {
     release(didx);
   }
 
-  StreamW bind_stream(const rldx_stream_weights& s, int hidden) {
+  StreamW bind_stream(const rldx_stream_weights& s, int hidden, int width) {
     StreamW w{};
     const size_t inner = static_cast<size_t>(H) * 64;
     w.hidden = hidden;
-    w.qkv_w = copy_in(s.qkv.w, 3 * inner * D, "qkv.w");
+    w.qkv_w = copy_in(s.qkv.w, 3 * inner * width, "qkv.w");
     w.qkv_b = copy_in(s.qkv.b, 3 * inner, "qkv.b");
-    w.proj_w = copy_in(s.proj.w, static_cast<size_t>(D) * inner, "proj.w");
-    w.proj_b = copy_in(s.proj.b, D, "proj.b");
-    w12_interleave(s.w12, hidden, D, &w.w12_w, &w.w12_b);
-    w.w3_w = copy_in(s.w3.w, static_cast<size_t>(D) * hidden, "w3.w");
-    w.w3_b = copy_in(s.w3.b, D, "w3.b");
+    w.proj_w = copy_in(s.proj.w, static_cast<size_t>(width) * inner, "proj.w");
+    w.proj_b = copy_in(s.proj.b, width, "proj.b");
+    w12_interleave(s.w12, hidden, width, &w.w12_w, &w.w12_b);
+    w.w3_w = copy_in(s.w3.w, static_cast<size_t>(width) * hidden, "w3.w");
+    w.w3_b = copy_in(s.w3.b, width, "w3.b");
     w.qn = copy_in(s.q_norm, 64, "q_norm");
     w.kn = copy_in(s.k_norm, 64, "k_norm");
+    return w;
+  }
+
+  // SingleStreamBlock weights: linear1 = [q | k | v | gate | up] rows, split into the QKV part
+  // and the SwiGLU part (re-laid as [32 gate | 32 up] row groups); mlp_proj; linear2.
+  SingleW bind_single(const rldx_linear& l1, const rldx_linear& l2, const rldx_linear& mp,
+                      const void* qn, const void* kn) {
+    SingleW w{};
+    const size_t inner3 = static_cast<size_t>(3) * H * 64;
+    const size_t inner = static_cast<size_t>(H) * 64;
+    if (!l1.w || !l1.b) throw Fail(RLDX_ERR_ARG, "missing single block linear1");
+    w.qkv_w = copy_in(l1.w, inner3 * D, "linear1.w (qkv)");
+    w.qkv_b = copy_in(l1.b, inner3, "linear1.b (qkv)");
+    rldx_linear l12;
+    l12.w = static_cast<const uint16_t*>(l1.w) + inner3 * D;
+    l12.b = static_cast<const uint16_t*>(l1.b) + inner3;
+    w12_interleave(l12, E, D, &w.w12_w, &w.w12_b);
+    w.mp_w = copy_in(mp.w, static_cast<size_t>(Mh) * E, "mlp_proj.w");
+    w.mp_b = copy_in(mp.b, Mh, "mlp_proj.b");
+    w.l2_w = copy_in(l2.w, static_cast<size_t>(D) * (inner + Mh), "linear2.w");
+    w.l2_b = copy_in(l2.b, D, "linear2.b");
+    w.qn = copy_in(qn, 64, "q_norm");
+    w.kn = copy_in(kn, 64, "k_norm");
     return w;
   }
 
@@ -259,8 +305,8 @@ struct rldx_msat {
     return d;
   }
 
-  void push_gemm(std::initializer_list<rldx_gemm_desc> ds) {
-    std::vector<rldx_gemm_desc> v(ds);
+  void push_gemm(std::initializer_list<rldx_gemm_desc> ds) { push_gemm(std::vector<rldx_gemm_desc>(ds)); }
+  void push_gemm(const std::vector<rldx_gemm_desc>& v) {
     Op o;
     std::memset(&o, 0, sizeof(o));
     o.kind = Op::kGemm;
@@ -283,25 +329,83 @@ struct rldx_msat {
     ops.push_back(o);
   }
 
-  void push_ln(std::initializer_list<LnSegment> segs, const bf16* dummy = nullptr) {
-    (void)dummy;
+  void push_ln(const std::vector<LnSegment>& segs) {
     Op o;
     std::memset(&o, 0, sizeof(o));
     o.kind = Op::kLn;
-    int row = 0, n = 0;
+    int row = 0, n = 0, dmax = 0;
+    double elems = 0.0;
     for (const LnSegment& s : segs) {
       o.l.seg[n] = s;
       o.l.seg[n].row_begin = row;
+      const int w = s.D > 0 ? s.D : D;
+      o.l.seg[n].D = w;
+      dmax = std::max(dmax, w);
+      elems += static_cast<double>(s.rows) * w;
       row += s.rows;
       ++n;
     }
     o.l.nseg = n;
-    o.l.D = D;
+    o.l.D = dmax;
     o.l.total_rows = row;
     o.l.eps = 1e-6f;
     o.grid = (row + 7) / 8;
-    o.bytes = 4.0 * row * D;
-    o.flops = 8.0 * row * D;
+    o.bytes = 4.0 * elems;
+    o.flops = 8.0 * elems;
+    ops.push_back(o);
+  }
+
+  // QKV projection of one stream / row group with the fused RMS QK-norm + RoPE epilogue that
+  // scatters q, k (and v transposed) into the joint sequence at token offset tok_off.
+  rldx_gemm_desc qkv_desc(const bf16* a, int width, const bf16* w, const bf16* b, const bf16* qn,
+                          const bf16* kn, int rows, int tok_off, const float* rc, const float* rs) const {
+    const int inner = H * 64;
+    rldx_gemm_desc d = lin(a, width, w, b, B * rows, 3 * inner, width, q, inner);
+    d.epilogue = RLDX_EPI_QKV;
+    d.q_norm_w = qn;
+    d.k_norm_w = kn;
+    d.rope_cos = rc;
+    d.rope_sin = rs;
+    d.q = q;
+    d.k = k;
+    d.vt = vt;
+    d.L = L;
+    d.Lp = Lp;
+    d.H = H;
+    d.tok_off = tok_off;
+    d.rows_in = rows;
+    d.rows_out = rows;
+    return d;
+  }
+
+  // Joint attention over the L tokens of each observation; query rows of segment i go to
+  // outs[i] (row stride lds[i], or H*64 when lds is null).
+  void push_attn(bf16* const* outs, const int* lens, const int* lds, int nseg) {
+    Op o;
+    std::memset(&o, 0, sizeof(o));
+    o.kind = Op::kAttn;
+    AttnParams& a = o.a;
+    a.L = L;
+    a.H = H;
+    a.B = B;
+    a.key_mask = nullptr;
+    for (int i = 0; i < nseg; ++i) {
+      a.seg_out[i] = outs[i];
+      a.seg_len[i] = lens[i];
+      a.seg_ld[i] = lds ? lds[i] : 0;
+    }
+    a.nseg = nseg;
+    a.scale_log2 = 1.4426950408889634f / 8.0f;
+    std::string err;
+    const uint64_t bh = static_cast<uint64_t>(B) * H;
+    o.grid = ((L + 127) / 128) * H * B;
+    o.bytes = 2.0 * 4.0 * static_cast<double>(bh) * L * 64;
+    o.flops = 4.0 * static_cast<double>(bh) * L * L * 64;
+    if (!make_tmap_3d(&a.tq, q, 64, L, bh, 128, static_cast<uint64_t>(L) * 128, 64, 128, 1, &err) ||
+        !make_tmap_3d(&a.tk, k, 64, L, bh, 128, static_cast<uint64_t>(L) * 128, 64, 64, 1, &err) ||
+        !make_tmap_3d(&a.tv, vt, L, 64, bh, static_cast<uint64_t>(Lp) * 2, static_cast<uint64_t>(Lp) * 128, 64, 64, 1,
+                      &err))
+      throw Fail(RLDX_ERR_ARG, err);
     ops.push_back(o);
   }
 
@@ -342,7 +446,7 @@ struct rldx_msat {
   }
 
   void copy_inputs(const rldx_msat_io* io, cudaStream_t st) {
-    ck(cudaMemcpyAsync(vl_in, io->vl, static_cast<size_t>(B) * nvl * D * 2, cudaMemcpyDefault, st), "vl");
+    ck(cudaMemcpyAsync(vl_in, io->vl, static_cast<size_t>(B) * nvl * Dv * 2, cudaMemcpyDefault, st), "vl");
     ck(cudaMemcpy2DAsync(state_in, sdp * 2, io->state, c.state_dim * 2, c.state_dim * 2,
                          static_cast<size_t>(B) * c.n_state, cudaMemcpyDefault, st),
        "state");
@@ -350,6 +454,7 @@ struct rldx_msat {
     ck(cudaMemcpyAsync(x, io->init_noise, static_cast<size_t>(B) * c.horizon * c.action_dim * 2,
                        cudaMemcpyDefault, st),
        "noise");
+    if (standard) return;
     ck(cudaMemcpy2DAsync(phys_hist_in, hc * 2, io->physics_hist, c.physics_dim * 2, c.physics_dim * 2,
                          static_cast<size_t>(B) * c.physics_hist, cudaMemcpyDefault, st),
        "physics_hist");
@@ -375,15 +480,27 @@ void rldx_msat::create(const rldx_msat_config& cfg, const rldx_msat_weights& w) 
   if (c.dim != c.heads * c.head_dim) throw Fail(RLDX_ERR_UNSUPPORTED, "dim must equal heads * head_dim");
   if (c.batch <= 0 || c.n_vl <= 0 || c.horizon <= 0 || c.depth <= 0 || c.num_steps <= 0)
     throw Fail(RLDX_ERR_ARG, "batch, n_vl, horizon, depth, num_steps must be positive");
-  if (c.physics_fut != c.horizon) throw Fail(RLDX_ERR_UNSUPPORTED, "physics_fut must equal horizon");
+  standard = c.standard_path != 0;
+  Dv = c.vl_dim > 0 ? c.vl_dim : c.dim;
+  if (!standard && c.physics_fut != c.horizon) throw Fail(RLDX_ERR_UNSUPPORTED, "physics_fut must equal horizon");
   if (c.n_state <= 0 || 1 + c.n_state + c.horizon > 128 || c.horizon > 128 ||
-      c.physics_hist + c.physics_fut > 128)
+      (!standard && c.physics_hist + c.physics_fut > 128))
     throw Fail(RLDX_ERR_UNSUPPORTED, "per-observation action / physics streams must fit 128 rows");
-  if (c.dim % 64 || c.mlp_hidden % 32 || c.vl_mlp_hidden % 32 || c.out_dim % 8 || c.dec_hidden % 8)
-    throw Fail(RLDX_ERR_UNSUPPORTED, "dims must be multiples of 64 (dim) / 32 (hidden) / 8");
-  if (c.dim > 4096) throw Fail(RLDX_ERR_UNSUPPORTED, "dim > 4096");
-  if (c.physics_dim <= 0 || c.physics_hist <= 0) throw Fail(RLDX_ERR_UNSUPPORTED, "physics stream required");
+  if (c.dim % 64 || Dv % 64 || c.mlp_hidden % 32 || c.vl_mlp_hidden % 32 || c.out_dim % 8 || c.dec_hidden % 8)
+    throw Fail(RLDX_ERR_UNSUPPORTED, "dims must be multiples of 64 (dim, vl_dim) / 32 (hidden) / 8");
+  if (c.dim > 4096 || Dv > 4096) throw Fail(RLDX_ERR_UNSUPPORTED, "dim / vl_dim > 4096");
+  if (!standard && (c.physics_dim <= 0 || c.physics_hist <= 0))
+    throw Fail(RLDX_ERR_UNSUPPORTED, "the all-modality path needs the physics stream");
+  if (c.depth_single < 0) throw Fail(RLDX_ERR_ARG, "depth_single must be >= 0");
+  if (c.depth_single > 0) {
+    if (!w.single_blocks) throw Fail(RLDX_ERR_ARG, "missing single block weights");
+    if (c.single_expanded <= 0 || c.single_expanded % 32 || c.single_mlp_hidden <= 0 ||
+        c.single_mlp_hidden % 8)
+      throw Fail(RLDX_ERR_UNSUPPORTED, "single-block widths must be multiples of 32 (SwiGLU) / 8");
+    if (Dv != c.dim && !w.vl_proj_to_sa.w) throw Fail(RLDX_ERR_ARG, "missing vl_proj_to_sa");
+  }
   if (!w.blocks) throw Fail(RLDX_ERR_ARG, "missing block weights");
+  if (standard) c.physics_hist = c.physics_fut = c.physics_dim = 0;  // no physics buffers
   if (w.time_token_proj.w) throw Fail(RLDX_ERR_UNSUPPORTED, "time_token_proj must be identity (inner == sa_dim)");
   ck(cudaGetDevice(&device), "cudaGetDevice");
   const char* env = getenv("RLDX_PDL");
@@ -394,9 +511,12 @@ void rldx_msat::create(const rldx_msat_config& cfg, const rldx_msat_weights& w) 
   H = c.heads;
   nvl = c.n_vl;
   nsa = 1 + c.n_state + c.horizon;
-  np = c.physics_hist + c.physics_fut;
+  np = standard ? 0 : c.physics_hist + c.physics_fut;
   L = nvl + nsa + np;
   Lp = (L + 7) / 8 * 8;
+  nx = nvl + nsa;
+  E = c.single_expanded;
+  Mh = c.single_mlp_hidden;
   S = c.num_steps;
   hc = (c.physics_dim + 7) / 8 * 8;
   sdp = (c.state_dim + 7) / 8 * 8;
@@ -407,14 +527,25 @@ void rldx_msat::create(const rldx_msat_config& cfg, const rldx_msat_weights& w) 
   // ---- weights ----
   for (int i = 0; i < c.depth; ++i) {
     const rldx_block_weights& bw = w.blocks[i];
-    wvl.push_back(bind_stream(bw.vl, c.vl_mlp_hidden));
-    wsa.push_back(bind_stream(bw.sa, c.mlp_hidden));
-    wp.push_back(bind_stream(bw.p, c.mlp_hidden));
+    wvl.push_back(bind_stream(bw.vl, c.vl_mlp_hidden, Dv));
+    wsa.push_back(bind_stream(bw.sa, c.mlp_hidden, D));
+    if (!standard) wp.push_back(bind_stream(bw.p, c.mlp_hidden, D));
+  }
+  for (int i = 0; i < c.depth_single; ++i) {
+    const rldx_single_block_weights& sw = w.single_blocks[i];
+    sgx.push_back(bind_single(sw.linear1, sw.linear2, sw.mlp_proj, sw.q_norm, sw.k_norm));
+    if (!standard) sgp.push_back(bind_single(sw.p_linear1, sw.p_linear2, sw.p_mlp_proj, sw.p_q_norm, sw.p_k_norm));
+  }
+  if (c.depth_single > 0 && Dv != D) {
+    vlp_w = copy_in(w.vl_proj_to_sa.w, static_cast<size_t>(D) * Dv, "vl_proj_to_sa.w");
+    vlp_b = copy_in(w.vl_proj_to_sa.b, D, "vl_proj_to_sa.b");
   }
   po2_w = copy_in(w.proj_out_2.w, static_cast<size_t>(c.out_dim) * D, "proj_out_2.w");
   po2_b = copy_in(w.proj_out_2.b, c.out_dim, "proj_out_2.b");
-  pp2_w = copy_in(w.proj_out_phys_2.w, static_cast<size_t>(c.out_dim) * D, "proj_out_physics_2.w");
-  pp2_b = copy_in(w.proj_out_phys_2.b, c.out_dim, "proj_out_physics_2.b");
+  if (!standard) {
+    pp2_w = copy_in(w.proj_out_phys_2.w, static_cast<size_t>(c.out_dim) * D, "proj_out_physics_2.w");
+    pp2_b = copy_in(w.proj_out_phys_2.b, c.out_dim, "proj_out_physics_2.b");
+  }
   const int cats = c.num_embodiments;
   st1_W = cat_weight(w.state_l1.W, c.state_dim, c.dec_hidden, sdp, "state_encoder.layer1.W");
   st1_b = copy_in(w.state_l1.b, static_cast<size_t>(cats) * c.dec_hidden, "state_encoder.layer1.b");
@@ -431,6 +562,7 @@ void rldx_msat::create(const rldx_msat_config& cfg, const rldx_msat_weights& w) 
   dl2_W = cat_weight(w.dec_l2.W, c.dec_hidden, c.action_dim, c.dec_hidden, "action_decoder.layer2.W");
   dl2_b = copy_in(w.dec_l2.b, static_cast<size_t>(cats) * c.action_dim, "action_decoder.layer2.b");
   pos = copy_in(w.pos_emb, static_cast<size_t>(c.horizon) * D, "position_embedding");
+  if (!standard) {
   phc1_w = copy_pad(w.phc_w1.w, D, c.physics_dim, hc, "physics_cond_encoder.W1");
   phc1_b = copy_in(w.phc_w1.b, D, "physics_cond_encoder.W1.b");
   phc2_w = copy_in(w.phc_w2.w, static_cast<size_t>(D) * 2 * D, "physics_cond_encoder.W2");
@@ -447,19 +579,32 @@ void rldx_msat::create(const rldx_msat_config& cfg, const rldx_msat_weights& w) 
   phd1_b = copy_in(w.phd_l1.b, D, "physics_decoder.net.0.b");
   phd2_w = copy_in(w.phd_l2.w, static_cast<size_t>(c.physics_dim) * D, "physics_decoder.net.2");
   phd2_b = copy_in(w.phd_l2.b, c.physics_dim, "physics_decoder.net.2.b");
+  }
 
   // ---- activations ----
   const size_t inner = static_cast<size_t>(H) * 64;
-  vl_in = alloc<bf16>(static_cast<size_t>(B) * nvl * D);
-  xvl = alloc<bf16>(static_cast<size_t>(B) * nvl * D);
+  vl_in = alloc<bf16>(static_cast<size_t>(B) * nvl * Dv);
+  xvl = alloc<bf16>(static_cast<size_t>(B) * nvl * Dv);
   xsa = alloc<bf16>(static_cast<size_t>(B) * nsa * D);
   xp = alloc<bf16>(static_cast<size_t>(B) * np * D);
-  lnvl = alloc<bf16>(static_cast<size_t>(B) * nvl * D);
+  lnvl = alloc<bf16>(static_cast<size_t>(B) * nvl * Dv);
   lnsa = alloc<bf16>(static_cast<size_t>(B) * nsa * D);
   lnp = alloc<bf16>(static_cast<size_t>(B) * np * D);
   q = alloc<bf16>(static_cast<size_t>(B) * H * L * 64);
   k = alloc<bf16>(static_cast<size_t>(B) * H * L * 64);
   vt = alloc<bf16>(static_cast<size_t>(B) * H * 64 * Lp);
+  if (c.depth_single > 0) {
+    const int grows[3] = {nvl, nsa, np};
+    sx[0] = (Dv != D) ? alloc<bf16>(static_cast<size_t>(B) * nvl * D) : xvl;
+    sx[1] = xsa;
+    sx[2] = xp;
+    for (int g = 0; g < 3; ++g) {
+      const size_t r = static_cast<size_t>(B) * grows[g];
+      sln[g] = (g == 0) ? alloc<bf16>(r * D) : (g == 1 ? lnsa : lnp);
+      sh[g] = alloc<bf16>(r * E);
+      scat[g] = alloc<bf16>(r * (inner + Mh));
+    }
+  }
   ovl = alloc<bf16>(static_cast<size_t>(B) * nvl * inner);
   osa = alloc<bf16>(static_cast<size_t>(B) * nsa * inner);
   op = alloc<bf16>(static_cast<size_t>(B) * np * inner);
@@ -526,46 +671,55 @@ void rldx_msat::create(const rldx_msat_config& cfg, const rldx_msat_weights& w) 
 }
 
 void rldx_msat::precompute(const rldx_msat_weights& w) {
-  // ---- RoPE tables over the joint sequence [VL | SA | P] (msat.py:583-631, ops.py:11-25) ----
+  // ---- RoPE tables over the joint sequence [VL | time, S/A | P]: position ids of the double
+  //      blocks (msat.py:583-631 with physics, msat.py:369-420 without) and of the single
+  //      blocks (msat.py:460-505, 676-709), angles as ops.py:11-25 ----
   const int axes0 = (c.rope_mode == RLDX_ROPE_SA_ONLY) ? 16 : 48;
   const int axes1 = 64 - axes0;
-  std::vector<float> hc_cos(static_cast<size_t>(L) * 32), hc_sin(static_cast<size_t>(L) * 32);
   auto freq = [&](int dim, int i) {
     const float ex = static_cast<float>(2 * i) / static_cast<float>(dim);
     return 1.0f / powf(c.rope_theta, ex);
   };
-  for (int t = 0; t < L; ++t) {
-    int id0 = 0, id1 = 0;
-    if (t < nvl) {
-      if (c.rope_mode == RLDX_ROPE_VL_SA) id0 = t;
-    } else if (t < nvl + nsa) {
-      const int j = t - nvl;  // 0 = time token
-      if (j > 0) id1 = (c.rope_mode == RLDX_ROPE_SA_ONLY) ? j : j + 1;
-    } else {
-      id0 = 1;
-      id1 = t - nvl - nsa;
-    }
-    if (id0 >= c.rope_max_seq || id1 >= c.rope_max_seq) throw Fail(RLDX_ERR_ARG, "RoPE position beyond rope_max_seq");
-    for (int p = 0; p < 32; ++p) {
-      float ang;
-      if (p < axes0 / 2)
-        ang = static_cast<float>(id0) * freq(axes0, p);
-      else
-        ang = static_cast<float>(id1) * freq(axes1, p - axes0 / 2);
-      float cs = static_cast<float>(std::cos(static_cast<double>(ang)));
-      float sn = static_cast<float>(std::sin(static_cast<double>(ang)));
-      if (c.rope_cos_only) {
-        cs = bf_round(cs);
-        sn = 0.0f;
+  // S/A ids (after the time token at 0) start at 1 in the double blocks under rope_sa_only and
+  // at 2 otherwise; the single blocks start them at 2 in both modes.
+  auto table = [&](int sa_start, float** dcos, float** dsin) {
+    std::vector<float> hc_cos(static_cast<size_t>(L) * 32), hc_sin(static_cast<size_t>(L) * 32);
+    for (int t = 0; t < L; ++t) {
+      int id0 = 0, id1 = 0;
+      if (t < nvl) {
+        if (c.rope_mode == RLDX_ROPE_VL_SA) id0 = t;
+      } else if (t < nvl + nsa) {
+        const int j = t - nvl;  // 0 = time token
+        if (j > 0) id1 = sa_start + j - 1;
+      } else {
+        id0 = 1;
+        id1 = t - nvl - nsa;
       }
-      hc_cos[static_cast<size_t>(t) * 32 + p] = cs;
-      hc_sin[static_cast<size_t>(t) * 32 + p] = sn;
+      if (id0 >= c.rope_max_seq || id1 >= c.rope_max_seq)
+        throw Fail(RLDX_ERR_ARG, "RoPE position beyond rope_max_seq");
+      for (int p = 0; p < 32; ++p) {
+        float ang;
+        if (p < axes0 / 2)
+          ang = static_cast<float>(id0) * freq(axes0, p);
+        else
+          ang = static_cast<float>(id1) * freq(axes1, p - axes0 / 2);
+        float cs = static_cast<float>(std::cos(static_cast<double>(ang)));
+        float sn = static_cast<float>(std::sin(static_cast<double>(ang)));
+        if (c.rope_cos_only) {
+          cs = bf_round(cs);
+          sn = 0.0f;
+        }
+        hc_cos[static_cast<size_t>(t) * 32 + p] = cs;
+        hc_sin[static_cast<size_t>(t) * 32 + p] = sn;
+      }
     }
-  }
-  rope_cos = alloc<float>(hc_cos.size());
-  rope_sin = alloc<float>(hc_sin.size());
-  ck(cudaMemcpy(rope_cos, hc_cos.data(), hc_cos.size() * 4, cudaMemcpyHostToDevice), "rope");
-  ck(cudaMemcpy(rope_sin, hc_sin.data(), hc_sin.size() * 4, cudaMemcpyHostToDevice), "rope");
+    *dcos = alloc<float>(hc_cos.size());
+    *dsin = alloc<float>(hc_sin.size());
+    ck(cudaMemcpy(*dcos, hc_cos.data(), hc_cos.size() * 4, cudaMemcpyHostToDevice), "rope");
+    ck(cudaMemcpy(*dsin, hc_sin.data(), hc_sin.size() * 4, cudaMemcpyHostToDevice), "rope");
+  };
+  table(c.rope_mode == RLDX_ROPE_SA_ONLY ? 1 : 2, &rope_cos, &rope_sin);
+  if (c.depth_single > 0) table(2, &rope_cos_s, &rope_sin_s);
 
   // ---- timestep embedding per Euler step (ops.py:123-133), baked like
   //      custom_expanded_action_model_chain.py:57-66 ----
@@ -619,7 +773,7 @@ void rldx_msat::precompute(const rldx_msat_weights& w) {
     ck(launch_elementwise(sc, *sc1p, static_cast<long long>(S) * D, 1, stream), "1+scale");
   };
   adaln(w.proj_out_1, &ada_sc1p, &ada_shift, "proj_out_1");
-  adaln(w.proj_out_phys_1, &pada_sc1p, &pada_shift, "proj_out_physics_1");
+  if (!standard) adaln(w.proj_out_phys_1, &pada_sc1p, &pada_shift, "proj_out_physics_1");
 
   // ---- sinusoids: action encoder / physics future encoder use t, the physics history
   //      encoder uses the token index (embodiment_conditioned_mlp.py:39-59, physics.py:19-25) ----
@@ -646,18 +800,24 @@ void rldx_msat::plan() {
   const int h = c.horizon;
   const int hist = c.physics_hist, fut = c.physics_fut;
   const float dt = 1.0f / static_cast<float>(S);
+  const int ns = standard ? 2 : 3;  // streams / row groups: VL, SA (, P)
 
   // ---- once per control step: state encoder, physics history encoder ----
   {
     rldx_gemm_desc s1 = catlin(state_in, sdp, st1_W, st1_b, B * c.n_state, c.dec_hidden, sdp, c.n_state, state_h, c.dec_hidden);
     s1.act = RLDX_ACT_RELU;
-    rldx_gemm_desc p1 = lin(phys_hist_in, hc, phc1_w, phc1_b, B * hist, D, hc, phc_cat, 2 * D);
-    push_gemm({s1, p1});
     rldx_gemm_desc s2 = catlin(state_h, c.dec_hidden, st2_W, st2_b, B * c.n_state, D, c.dec_hidden, c.n_state, state_feat, D);
-    rldx_gemm_desc p2 = lin(phc_cat, 2 * D, phc2_w, phc2_b, B * hist, D, 2 * D, phc_h, D);
-    p2.act = RLDX_ACT_SILU;
-    push_gemm({s2, p2});
-    push_gemm({lin(phc_h, D, phc3_w, phc3_b, B * hist, D, D, phist, D)});
+    if (standard) {
+      push_gemm({s1});
+      push_gemm({s2});
+    } else {
+      rldx_gemm_desc p1 = lin(phys_hist_in, hc, phc1_w, phc1_b, B * hist, D, hc, phc_cat, 2 * D);
+      push_gemm({s1, p1});
+      rldx_gemm_desc p2 = lin(phc_cat, 2 * D, phc2_w, phc2_b, B * hist, D, 2 * D, phc_h, D);
+      p2.act = RLDX_ACT_SILU;
+      push_gemm({s2, p2});
+      push_gemm({lin(phc_h, D, phc3_w, phc3_b, B * hist, D, D, phist, D)});
+    }
   }
 
   for (int s = 0; s < S; ++s) {
@@ -667,9 +827,9 @@ void rldx_msat::plan() {
       CopyRegion r{};
       r.src = reinterpret_cast<const uint8_t*>(vl_in);
       r.dst = reinterpret_cast<uint8_t*>(xvl);
-      r.src_pitch = r.dst_pitch = static_cast<long long>(D) * 2;
+      r.src_pitch = r.dst_pitch = static_cast<long long>(Dv) * 2;
       r.rows = B * nvl;
-      r.bytes = D * 2;
+      r.bytes = Dv * 2;
       rs.push_back(r);
       CopyRegion t{};
       t.src = reinterpret_cast<const uint8_t*>(time_tok + static_cast<size_t>(s) * inner);
@@ -689,28 +849,27 @@ void rldx_msat::plan() {
       st.rows = B * c.n_state;
       st.bytes = D * 2;
       rs.push_back(st);
-      CopyRegion ph{};
-      ph.src = reinterpret_cast<const uint8_t*>(phist);
-      ph.dst = reinterpret_cast<uint8_t*>(xp);
-      ph.src_pitch = ph.dst_pitch = static_cast<long long>(D) * 2;
-      ph.group_rows = hist;
-      ph.src_group_pitch = static_cast<long long>(hist) * D * 2;
-      ph.dst_group_pitch = static_cast<long long>(np) * D * 2;
-      ph.rows = B * hist;
-      ph.bytes = D * 2;
-      rs.push_back(ph);
+      if (!standard) {
+        CopyRegion ph{};
+        ph.src = reinterpret_cast<const uint8_t*>(phist);
+        ph.dst = reinterpret_cast<uint8_t*>(xp);
+        ph.src_pitch = ph.dst_pitch = static_cast<long long>(D) * 2;
+        ph.group_rows = hist;
+        ph.src_group_pitch = static_cast<long long>(hist) * D * 2;
+        ph.dst_group_pitch = static_cast<long long>(np) * D * 2;
+        ph.rows = B * hist;
+        ph.bytes = D * 2;
+        rs.push_back(ph);
+      }
       push_copy(rs);
     }
     // ---- action encoder + physics future encoder ----
     {
-      rldx_gemm_desc a1 = catlin(x, adp, aw1_W, aw1_b, B * h, D, adp, h, act_cat[s], 2 * D);
-      rldx_gemm_desc f1 = lin(phys_x, hc, phf1_w, phf1_b, B * fut, D, hc, phf_cat[s], 2 * D);
-      push_gemm({a1, f1});
+      std::vector<rldx_gemm_desc> g1, g2, g3;
+      g1.push_back(catlin(x, adp, aw1_W, aw1_b, B * h, D, adp, h, act_cat[s], 2 * D));
       rldx_gemm_desc a2 = catlin(act_cat[s], 2 * D, aw2_W, aw2_b, B * h, D, 2 * D, h, act_h, D);
       a2.act = RLDX_ACT_SWISH;
-      rldx_gemm_desc f2 = lin(phf_cat[s], 2 * D, phf2_w, phf2_b, B * fut, D, 2 * D, phf_h, D);
-      f2.act = RLDX_ACT_SILU;
-      push_gemm({a2, f2});
+      g2.push_back(a2);
       rldx_gemm_desc a3 = catlin(act_h, D, aw3_W, aw3_b, B * h, D, D, h, xsa, D);
       a3.add = pos;
       a3.ld_add = D;
@@ -718,128 +877,164 @@ void rldx_msat::plan() {
       a3.rows_in = h;
       a3.rows_out = nsa;
       a3.row_skip = -(1 + c.n_state);
-      rldx_gemm_desc f3 = lin(phf_h, D, phf3_w, phf3_b, B * fut, D, D, xp, D);
-      f3.rows_in = fut;
-      f3.rows_out = np;
-      f3.row_skip = -hist;
-      push_gemm({a3, f3});
+      g3.push_back(a3);
+      if (!standard) {
+        g1.push_back(lin(phys_x, hc, phf1_w, phf1_b, B * fut, D, hc, phf_cat[s], 2 * D));
+        rldx_gemm_desc f2 = lin(phf_cat[s], 2 * D, phf2_w, phf2_b, B * fut, D, 2 * D, phf_h, D);
+        f2.act = RLDX_ACT_SILU;
+        g2.push_back(f2);
+        rldx_gemm_desc f3 = lin(phf_h, D, phf3_w, phf3_b, B * fut, D, D, xp, D);
+        f3.rows_in = fut;
+        f3.rows_out = np;
+        f3.row_skip = -hist;
+        g3.push_back(f3);
+      }
+      push_gemm(g1);
+      push_gemm(g2);
+      push_gemm(g3);
     }
-    // ---- ExpandedDoubleStreamBlocks over [VL | SA | P] ----
+    // ---- (Expanded)DoubleStreamBlocks over [VL | SA (| P)] ----
     bf16* xs[3] = {xvl, xsa, xp};
     bf16* lns[3] = {lnvl, lnsa, lnp};
     bf16* os[3] = {ovl, osa, op};
     bf16* hs[3] = {hvl, hsa, hp};
     const int rows[3] = {nvl, nsa, np};
+    const int wd[3] = {Dv, D, D};
     const int toff[3] = {0, nvl, nvl + nsa};
     for (int blk = 0; blk < c.depth; ++blk) {
-      const StreamW* sw[3] = {&wvl[blk], &wsa[blk], &wp[blk]};
+      const StreamW* sw[3] = {&wvl[blk], &wsa[blk], standard ? nullptr : &wp[blk]};
       auto ln_all = [&]() {
-        push_ln({LnSegment{xvl, lnvl, nullptr, nullptr, B * nvl, D, D, 0},
-                 LnSegment{xsa, lnsa, nullptr, nullptr, B * nsa, D, D, 0},
-                 LnSegment{xp, lnp, nullptr, nullptr, B * np, D, D, 0}});
+        std::vector<LnSegment> v;
+        for (int i = 0; i < ns; ++i)
+          v.push_back(LnSegment{xs[i], lns[i], nullptr, nullptr, B * rows[i], wd[i], wd[i], 0, wd[i]});
+        push_ln(v);
       };
       ln_all();
       {
-        rldx_gemm_desc d[3];
-        for (int i = 0; i < 3; ++i) {
-          d[i] = lin(lns[i], D, sw[i]->qkv_w, sw[i]->qkv_b, B * rows[i], 3 * inner, D, q, inner);
-          d[i].epilogue = RLDX_EPI_QKV;
-          d[i].q_norm_w = sw[i]->qn;
-          d[i].k_norm_w = sw[i]->kn;
-          d[i].rope_cos = rope_cos;
-          d[i].rope_sin = rope_sin;
-          d[i].q = q;
-          d[i].k = k;
-          d[i].vt = vt;
-          d[i].L = L;
-          d[i].Lp = Lp;
-          d[i].H = H;
-          d[i].tok_off = toff[i];
-          d[i].rows_in = rows[i];
-          d[i].rows_out = rows[i];
-        }
-        push_gemm({d[0], d[1], d[2]});
+        std::vector<rldx_gemm_desc> d(ns);
+        for (int i = 0; i < ns; ++i)
+          d[i] = qkv_desc(lns[i], wd[i], sw[i]->qkv_w, sw[i]->qkv_b, sw[i]->qn, sw[i]->kn, rows[i], toff[i],
+                          rope_cos, rope_sin);
+        push_gemm(d);
       }
+      push_attn(os, rows, nullptr, ns);
       {
-        Op o;
-        std::memset(&o, 0, sizeof(o));
-        o.kind = Op::kAttn;
-        AttnParams& a = o.a;
-        a.L = L;
-        a.H = H;
-        a.B = B;
-        a.key_mask = nullptr;
-        for (int i = 0; i < 3; ++i) {
-          a.seg_out[i] = os[i];
-          a.seg_len[i] = rows[i];
-        }
-        a.nseg = 3;
-        a.scale_log2 = 1.4426950408889634f / 8.0f;
-        std::string err;
-        const uint64_t bh = static_cast<uint64_t>(B) * H;
-        o.grid = ((L + 127) / 128) * H * B;
-        o.bytes = 2.0 * 4.0 * static_cast<double>(bh) * L * 64;
-        o.flops = 4.0 * static_cast<double>(bh) * L * L * 64;
-        if (!make_tmap_3d(&a.tq, q, 64, L, bh, 128, static_cast<uint64_t>(L) * 128, 64, 128, 1, &err) ||
-            !make_tmap_3d(&a.tk, k, 64, L, bh, 128, static_cast<uint64_t>(L) * 128, 64, 64, 1, &err) ||
-            !make_tmap_3d(&a.tv, vt, L, 64, bh, static_cast<uint64_t>(Lp) * 2, static_cast<uint64_t>(Lp) * 128, 64, 64, 1, &err))
-          throw Fail(RLDX_ERR_ARG, err);
-        ops.push_back(o);
-      }
-      {
-        rldx_gemm_desc d[3];
-        for (int i = 0; i < 3; ++i) {
-          d[i] = lin(os[i], inner, sw[i]->proj_w, sw[i]->proj_b, B * rows[i], D, inner, xs[i], D);
+        std::vector<rldx_gemm_desc> d(ns);
+        for (int i = 0; i < ns; ++i) {
+          d[i] = lin(os[i], inner, sw[i]->proj_w, sw[i]->proj_b, B * rows[i], wd[i], inner, xs[i], wd[i]);
           d[i].add = xs[i];
-          d[i].ld_add = D;
+          d[i].ld_add = wd[i];
         }
-        push_gemm({d[0], d[1], d[2]});
+        push_gemm(d);
       }
       ln_all();
       {
-        rldx_gemm_desc d[3];
-        for (int i = 0; i < 3; ++i) {
+        std::vector<rldx_gemm_desc> d(ns);
+        for (int i = 0; i < ns; ++i) {
           const int hid = sw[i]->hidden;
-          d[i] = lin(lns[i], D, sw[i]->w12_w, sw[i]->w12_b, B * rows[i], 2 * hid, D, hs[i], hid);
+          d[i] = lin(lns[i], wd[i], sw[i]->w12_w, sw[i]->w12_b, B * rows[i], 2 * hid, wd[i], hs[i], hid);
           d[i].epilogue = RLDX_EPI_SWIGLU;
         }
-        push_gemm({d[0], d[1], d[2]});
+        push_gemm(d);
       }
       {
-        rldx_gemm_desc d[3];
-        for (int i = 0; i < 3; ++i) {
+        std::vector<rldx_gemm_desc> d(ns);
+        for (int i = 0; i < ns; ++i) {
           const int hid = sw[i]->hidden;
-          d[i] = lin(hs[i], hid, sw[i]->w3_w, sw[i]->w3_b, B * rows[i], D, hid, xs[i], D);
+          d[i] = lin(hs[i], hid, sw[i]->w3_w, sw[i]->w3_b, B * rows[i], wd[i], hid, xs[i], wd[i]);
           d[i].add = xs[i];
-          d[i].ld_add = D;
+          d[i].ld_add = wd[i];
         }
-        push_gemm({d[0], d[1], d[2]});
+        push_gemm(d);
+      }
+    }
+    // ---- (Expanded)SingleStreamBlocks over [VL_proj | time, S/A (| P)] ----
+    if (c.depth_single > 0) {
+      if (Dv != D) push_gemm({lin(xvl, Dv, vlp_w, vlp_b, B * nvl, D, Dv, sx[0], D)});
+      const int ld_cat = inner + Mh;
+      for (int blk = 0; blk < c.depth_single; ++blk) {
+        const SingleW* gw[3] = {&sgx[blk], &sgx[blk], standard ? nullptr : &sgp[blk]};
+        {
+          std::vector<LnSegment> v;
+          for (int g = 0; g < ns; ++g)
+            v.push_back(LnSegment{sx[g], sln[g], nullptr, nullptr, B * rows[g], D, D, 0, D});
+          push_ln(v);
+        }
+        {
+          std::vector<rldx_gemm_desc> d(ns);
+          for (int g = 0; g < ns; ++g)
+            d[g] = qkv_desc(sln[g], D, gw[g]->qkv_w, gw[g]->qkv_b, gw[g]->qn, gw[g]->kn, rows[g], toff[g],
+                            rope_cos_s, rope_sin_s);
+          push_gemm(d);
+        }
+        {
+          std::vector<rldx_gemm_desc> d(ns);
+          for (int g = 0; g < ns; ++g) {
+            d[g] = lin(sln[g], D, gw[g]->w12_w, gw[g]->w12_b, B * rows[g], 2 * E, D, sh[g], E);
+            d[g].epilogue = RLDX_EPI_SWIGLU;
+          }
+          push_gemm(d);
+        }
+        const int lds[3] = {ld_cat, ld_cat, ld_cat};
+        push_attn(scat, rows, lds, ns);
+        {
+          std::vector<rldx_gemm_desc> d(ns);
+          for (int g = 0; g < ns; ++g) {
+            d[g] = lin(sh[g], E, gw[g]->mp_w, gw[g]->mp_b, B * rows[g], Mh, E, scat[g], ld_cat);
+            d[g].col_off = inner;
+          }
+          push_gemm(d);
+        }
+        {
+          std::vector<rldx_gemm_desc> d(ns);
+          for (int g = 0; g < ns; ++g) {
+            d[g] = lin(scat[g], ld_cat, gw[g]->l2_w, gw[g]->l2_b, B * rows[g], D, ld_cat, sx[g], D);
+            d[g].add = sx[g];
+            d[g].ld_add = D;
+          }
+          push_gemm(d);
+        }
       }
     }
     // ---- output projections, decoders, Euler updates ----
-    push_ln({LnSegment{xsa, oln_sa, ada_sc1p + static_cast<size_t>(s) * D, ada_shift + static_cast<size_t>(s) * D, B * nsa, D, D, 0},
-             LnSegment{xp, oln_p, pada_sc1p + static_cast<size_t>(s) * D, pada_shift + static_cast<size_t>(s) * D, B * np, D, D, 0}});
-    push_gemm({lin(oln_sa, D, po2_w, po2_b, B * nsa, c.out_dim, D, oproj_sa, c.out_dim),
-               lin(oln_p, D, pp2_w, pp2_b, B * np, c.out_dim, D, oproj_p, c.out_dim)});
     {
+      std::vector<LnSegment> v;
+      v.push_back(LnSegment{xsa, oln_sa, ada_sc1p + static_cast<size_t>(s) * D, ada_shift + static_cast<size_t>(s) * D,
+                            B * nsa, D, D, 0, D});
+      if (!standard)
+        v.push_back(LnSegment{xp, oln_p, pada_sc1p + static_cast<size_t>(s) * D,
+                              pada_shift + static_cast<size_t>(s) * D, B * np, D, D, 0, D});
+      push_ln(v);
+    }
+    {
+      std::vector<rldx_gemm_desc> g1, g2, g3;
+      g1.push_back(lin(oln_sa, D, po2_w, po2_b, B * nsa, c.out_dim, D, oproj_sa, c.out_dim));
       rldx_gemm_desc d1 = catlin(oproj_sa, c.out_dim, dl1_W, dl1_b, B * nsa, c.dec_hidden, c.out_dim, nsa, dec_h, c.dec_hidden);
       d1.act = RLDX_ACT_RELU;
-      rldx_gemm_desc p1 = lin(oproj_p, c.out_dim, phd1_w, phd1_b, B * np, D, c.out_dim, pdec_h, D);
-      p1.act = RLDX_ACT_SILU;
-      push_gemm({d1, p1});
+      g2.push_back(d1);
       rldx_gemm_desc d2 = catlin(dec_h, c.dec_hidden, dl2_W, dl2_b, B * nsa, c.action_dim, c.dec_hidden, nsa, x, adp);
       d2.epilogue = RLDX_EPI_EULER;
       d2.dt = dt;
       d2.rows_in = nsa;
       d2.rows_out = h;
       d2.row_skip = nsa - h;
-      rldx_gemm_desc p2 = lin(pdec_h, D, phd2_w, phd2_b, B * np, c.physics_dim, D, phys_x, hc);
-      p2.epilogue = RLDX_EPI_EULER;
-      p2.dt = dt;
-      p2.rows_in = np;
-      p2.rows_out = fut;
-      p2.row_skip = hist;
-      push_gemm({d2, p2});
+      g3.push_back(d2);
+      if (!standard) {
+        g1.push_back(lin(oln_p, D, pp2_w, pp2_b, B * np, c.out_dim, D, oproj_p, c.out_dim));
+        rldx_gemm_desc p1 = lin(oproj_p, c.out_dim, phd1_w, phd1_b, B * np, D, c.out_dim, pdec_h, D);
+        p1.act = RLDX_ACT_SILU;
+        g2.push_back(p1);
+        rldx_gemm_desc p2 = lin(pdec_h, D, phd2_w, phd2_b, B * np, c.physics_dim, D, phys_x, hc);
+        p2.epilogue = RLDX_EPI_EULER;
+        p2.dt = dt;
+        p2.rows_in = np;
+        p2.rows_out = fut;
+        p2.row_skip = hist;
+        g3.push_back(p2);
+      }
+      push_gemm(g1);
+      push_gemm(g2);
+      push_gemm(g3);
     }
   }
 }
@@ -893,9 +1088,9 @@ int rldx_msat_destroy(rldx_msat* h) {
 
 static int msat_step_impl(rldx_msat* h, const rldx_msat_io* io, cudaStream_t st) {
   if (!h || !io) return set_error(RLDX_ERR_ARG, "msat_step: null argument");
-  if (!io->vl || !io->state || !io->emb_id || !io->init_noise || !io->physics_hist ||
-      !io->physics_noise || !io->actions)
-    return set_error(RLDX_ERR_ARG, "msat_step: every io pointer is required");
+  if (!io->vl || !io->state || !io->emb_id || !io->init_noise || !io->actions ||
+      (!h->standard && (!io->physics_hist || !io->physics_noise)))
+    return set_error(RLDX_ERR_ARG, "msat_step: every io pointer is required (physics ones on the all-modality path)");
   return guard([&] {
     h->copy_inputs(io, st);
     if (h->exec)
@@ -957,7 +1152,7 @@ int rldx_msat_read_buffer(const rldx_msat* h, int which, void* dst, int64_t dst_
     case 0:
       src = h->xvl;
       *rows = static_cast<int64_t>(h->B) * h->nvl;
-      *cols = h->D;
+      *cols = h->Dv;
       break;
     case 1:
       src = h->xsa;

@@ -30,7 +30,8 @@ __global__ void __launch_bounds__(128) ln_rows_kernel(const __grid_constant__ Ln
     if (i < P.nseg && warp_global >= P.seg[i].row_begin) si = i;
   const LnSegment& sg = P.seg[si];
   const int row = warp_global - sg.row_begin;
-  const int nvec = P.D / 8;
+  const int D = sg.D > 0 ? sg.D : P.D;
+  const int nvec = D / 8;
   const uint4* src = reinterpret_cast<const uint4*>(sg.in + static_cast<size_t>(row) * sg.ld_in);
   float x[kLnMaxVec][8];
   float sum = 0.0f;
@@ -49,7 +50,7 @@ __global__ void __launch_bounds__(128) ln_rows_kernel(const __grid_constant__ Ln
   }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
-  const float mean = sum / static_cast<float>(P.D);
+  const float mean = sum / static_cast<float>(D);
   float var = 0.0f;
 #pragma unroll
   for (int i = 0; i < kLnMaxVec; ++i) {
@@ -64,7 +65,7 @@ __global__ void __launch_bounds__(128) ln_rows_kernel(const __grid_constant__ Ln
   }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) var += __shfl_xor_sync(0xffffffffu, var, o);
-  const float rstd = rsqrtf(var / static_cast<float>(P.D) + P.eps);
+  const float rstd = rsqrtf(var / static_cast<float>(D) + P.eps);
   uint4* dst = reinterpret_cast<uint4*>(sg.out + static_cast<size_t>(row) * sg.ld_out);
   const uint4* sc = reinterpret_cast<const uint4*>(sg.scale1p);
   const uint4* sh = reinterpret_cast<const uint4*>(sg.shift);
