@@ -213,6 +213,9 @@ typedef struct {
   int depth_single;    /* single-stream blocks after the double ones (Expanded... with P) */
   int single_expanded; /* SingleStreamBlock SwiGLU width: int(dim * mlp_ratio)            */
   int single_mlp_hidden; /* SingleStreamBlock mlp_proj output: int(2/3 * single_expanded) */
+  int prefix_len;      /* RTC trained mode: first prefix_len actions locked to
+                          io.prefix_actions, encoded at t = 1 (graph_safe_action_model.py:196-300;
+                          custom_action_model_chain.py:86-165); 0 = off                       */
 } rldx_msat_config;
 
 typedef struct {
@@ -273,6 +276,7 @@ typedef struct {
   const void* physics_hist;  /* [B, physics_hist, physics_dim] bf16 (NULL: standard)   */
   const void* physics_noise; /* [B, physics_fut, physics_dim] bf16 (NULL: standard)    */
   void* actions;             /* out: [B, horizon, action_dim] bf16                      */
+  const void* prefix_actions; /* [B, prefix_len, action_dim] bf16 (NULL when prefix_len 0) */
 } rldx_msat_io;
 
 /* Copies and re-lays out the weights into a device arena owned by the handle, precomputes the

@@ -657,25 +657,48 @@ def init_weights(module: nn.Module, seed: int, std: float = 0.02) -> nn.Module:
 
 @torch.no_grad()
 def denoise(head: nn.Module, vl_embs, state, embodiment_id, init_noise, physics_hist=None,
-            physics_noise=None, num_steps: int = 4, return_trace: bool = False):
-    """Control step with vanilla_action_head_forward semantics (benchmark_action_model.py:50-123)."""
+            physics_noise=None, num_steps: int = 4, return_trace: bool = False, prefix_actions=None):
+    """Control step with vanilla_action_head_forward semantics (benchmark_action_model.py:50-123).
+
+    prefix_actions (B, d, action_dim): RTC trained-mode inpainting as GraphSafeActionModel.forward
+    (graph_safe_action_model.py:196-300): the first d action tokens are locked to the prefix
+    before every action encoding and after every Euler update, and their encoder time is 1.0
+    while the others use the step's t."""
     msat = head.model
     dt = 1.0 / num_steps
     vl = head.vlln(vl_embs)
     B = vl.shape[0]
     horizon = init_noise.shape[1]
+    d = 0 if prefix_actions is None else prefix_actions.shape[1]
     state_features = head.state_encoder(state, embodiment_id)
     pos_embs = head.position_embedding(torch.arange(horizon)).unsqueeze(0)
     current = init_noise.clone()
+    if d:
+        current[:, :d] = prefix_actions
+
+    def encode(t):
+        timesteps = torch.tensor([t / float(num_steps)], dtype=vl.dtype).expand(B)
+        t_enc = timesteps
+        if d:
+            t_enc = timesteps.unsqueeze(1).expand(-1, horizon).clone()
+            t_enc[:, :d] = 1.0
+            current[:, :d] = prefix_actions
+        af = head.action_encoder(current, t_enc, embodiment_id) + pos_embs
+        return timesteps, torch.cat([state_features, af], dim=1)
+
+    def euler(cur, out):
+        pred = head.action_decoder(out["action"], embodiment_id)[:, -horizon:]
+        cur = cur + dt * pred
+        if d:
+            cur[:, :d] = prefix_actions
+        return cur
+
     if not head.use_physics:
         trace = []
         for t in range(num_steps):
-            timesteps = torch.tensor([t / float(num_steps)], dtype=vl.dtype).expand(B)
-            af = head.action_encoder(current, timesteps, embodiment_id) + pos_embs
-            sa = torch.cat([state_features, af], dim=1)
+            timesteps, sa = encode(t)
             out, hidden = msat(sa, vl, timesteps, return_hidden=True)
-            pred = head.action_decoder(out["action"], embodiment_id)[:, -horizon:]
-            current = current + dt * pred
+            current = euler(current, out)
             if return_trace:
                 trace.append({"hidden": hidden, "out": out, "actions": current})
         return (current, trace) if return_trace else current
@@ -684,13 +707,10 @@ def denoise(head: nn.Module, vl_embs, state, embodiment_id, init_noise, physics_
     physics_fut = physics_noise.clone()
     trace = []
     for t in range(num_steps):
-        timesteps = torch.tensor([t / float(num_steps)], dtype=vl.dtype).expand(B)
-        af = head.action_encoder(current, timesteps, embodiment_id) + pos_embs
-        sa = torch.cat([state_features, af], dim=1)
+        timesteps, sa = encode(t)
         pe = torch.cat([physics_hist_tok, phys.physics_fut_encoder(physics_fut, timesteps)], dim=1)
         out, hidden = msat(sa, vl, timesteps, pe, return_hidden=True)
-        pred = head.action_decoder(out["action"], embodiment_id)[:, -horizon:]
-        current = current + dt * pred
+        current = euler(current, out)
         physics_fut = physics_fut + dt * phys.physics_decoder(out["physics"][:, -phys.physics_fut_len:])
         if return_trace:
             trace.append({"hidden": hidden, "out": out, "actions": current, "physics_fut": physics_fut})

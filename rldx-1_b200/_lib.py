@@ -59,7 +59,7 @@ class MsatConfig(C.Structure):
         ("rope_mode", C.c_int), ("rope_cos_only", C.c_int), ("rope_theta", C.c_float),
         ("rope_max_seq", C.c_int), ("temb_channels", C.c_int), ("use_graph", C.c_int),
         ("standard_path", C.c_int), ("vl_dim", C.c_int), ("depth_single", C.c_int),
-        ("single_expanded", C.c_int), ("single_mlp_hidden", C.c_int),
+        ("single_expanded", C.c_int), ("single_mlp_hidden", C.c_int), ("prefix_len", C.c_int),
     ]
 
 
@@ -111,7 +111,8 @@ class OpProfile(C.Structure):
 
 class MsatIO(C.Structure):
     _fields_ = [("vl", vp), ("state", vp), ("emb_id", vp), ("init_noise", vp),
-                ("physics_hist", vp), ("physics_noise", vp), ("actions", vp)]
+                ("physics_hist", vp), ("physics_noise", vp), ("actions", vp),
+                ("prefix_actions", vp)]
 
 
 # Every exported symbol of include/rldx_b200.h with its ctypes signature.

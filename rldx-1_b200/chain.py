@@ -17,6 +17,10 @@ SingleStreamBlocks over [VL_proj | SA]):
     chain = B200ActionHeadChain(gs_action_model, device, dtype=torch.bfloat16)
     actions = chain(vl_embs, state, embodiment_id, init_noise=None)
 
+Both take `prefix_actions` (B, prefix_len, action_dim) when the model was built for RTC trained
+mode (`gs_action_model.prefix_len > 0`, or the `prefix_len=` argument): those actions stay locked
+and are encoded at t = 1, as in GraphSafeActionModel.forward (graph_safe_action_model.py:196-300).
+
 It reads the weights by the reference's attribute names from a GraphSafeActionModel
 (rldx/inference/action_model/model/graph_safe_action_model.py:27-168) or from an action model
 exposing `.model` (MSAT), `.state_encoder`, `.action_encoder`, `.action_decoder`,
@@ -85,7 +89,8 @@ class _B200HeadChain(nn.Module):
     _physics = True
 
     def __init__(self, gs_action_model: nn.Module, device=None, dtype=torch.bfloat16, *,
-                 num_inference_timesteps: Optional[int] = None, use_graph: bool = True):
+                 num_inference_timesteps: Optional[int] = None, use_graph: bool = True,
+                 prefix_len: Optional[int] = None):
         super().__init__()
         if dtype != torch.bfloat16:
             raise ValueError("the B200 chain computes in bfloat16 only")
@@ -107,9 +112,9 @@ class _B200HeadChain(nn.Module):
             gs_action_model, "num_inference_timesteps", 4))
         self.action_horizon = getattr(gs_action_model, "action_horizon", None)
         self.action_dim = self._act_dec.layer2.W.shape[2]
-        self.prefix_len = getattr(gs_action_model, "prefix_len", 0)
-        if self.prefix_len:
-            raise NotImplementedError("RTC trained-mode prefix inpainting is not bound yet")
+        # RTC trained-mode prefix length, baked into the native plan (the reference bakes it into
+        # its chain: custom_action_model_chain.py:31-35)
+        self.prefix_len = int(prefix_len if prefix_len is not None else getattr(gs_action_model, "prefix_len", 0))
         self.use_graph = use_graph
         self._handle = None
         self._shapes = None
@@ -165,6 +170,7 @@ class _B200HeadChain(nn.Module):
         c.rope_max_seq = int(rope.freqs_cis_0.shape[0])
         c.temb_channels = msat.timestep_encoder.timestep_embedder.linear_1.weight.shape[1]
         c.use_graph = 1 if self.use_graph else 0
+        c.prefix_len = self.prefix_len
         if not isinstance(getattr(msat, "time_token_proj", nn.Identity()), nn.Identity):
             raise NotImplementedError("time_token_proj must be the identity (inner_dim == sa_dim)")
         return c
@@ -240,8 +246,11 @@ class _B200HeadChain(nn.Module):
         return int(_lib.load().rldx_msat_launch_count(self._handle)) if self._handle else 0
 
     # ------------------------------------------------------------------ forward
-    def _step(self, vl_embs, state, embodiment_id, init_noise, physics_hist, physics_init_noise):
+    def _step(self, vl_embs, state, embodiment_id, init_noise, physics_hist, physics_init_noise,
+              prefix_actions):
         B, n_vl, _ = vl_embs.shape
+        if self.prefix_len and prefix_actions is None:
+            raise ValueError(f"this chain was built with prefix_len={self.prefix_len}: prefix_actions is required")
         if state.dim() == 2:
             state = state.unsqueeze(1)
         horizon = self.action_horizon or (init_noise.shape[1] if init_noise is not None else 16)
@@ -272,9 +281,16 @@ class _B200HeadChain(nn.Module):
                 physics_init_noise = torch.randn(B, fut, self._cfg.physics_dim, dtype=bf, device=dev)
             ph, pn = _in(physics_hist), _in(physics_init_noise)
             ph_ptr, pn_ptr = ph.data_ptr(), pn.data_ptr()
+        pre_ptr = None
+        if self.prefix_len:
+            if tuple(prefix_actions.shape) != (B, self.prefix_len, self.action_dim):
+                raise ValueError(f"prefix_actions must be {(B, self.prefix_len, self.action_dim)}, "
+                                 f"got {tuple(prefix_actions.shape)}")
+            pre = _in(prefix_actions)
+            pre_ptr = pre.data_ptr()
         out = torch.empty(B, horizon, self.action_dim, dtype=bf, device=dev)
         io = MsatIO(vl.data_ptr(), st.data_ptr(), ids.data_ptr(), noise.data_ptr(), ph_ptr,
-                    pn_ptr, out.data_ptr())
+                    pn_ptr, out.data_ptr(), pre_ptr)
         stream = torch.cuda.current_stream(dev)
         check(_lib.load().rldx_msat_step(self._handle, C.byref(io), C.c_void_p(stream.cuda_stream)))
         return out
@@ -282,8 +298,9 @@ class _B200HeadChain(nn.Module):
     def _io(self, inp: dict, out: torch.Tensor) -> MsatIO:
         ph = inp["physics_hist"].data_ptr() if self._physics else None
         pn = inp["physics_noise"].data_ptr() if self._physics else None
+        pre = inp["prefix_actions"].data_ptr() if self.prefix_len else None
         return MsatIO(inp["vl"].data_ptr(), inp["state"].data_ptr(), inp["embodiment_id"].data_ptr(),
-                      inp["init_noise"].data_ptr(), ph, pn, out.data_ptr())
+                      inp["init_noise"].data_ptr(), ph, pn, out.data_ptr(), pre)
 
     def forward_host(self, inp: dict, out: torch.Tensor) -> torch.Tensor:
         """One control step from (pinned) host tensors to a host tensor through
@@ -340,11 +357,10 @@ class B200ExpandedActionHeadChain(_B200HeadChain):
 
     def forward(self, vl_embs, state, embodiment_id, init_noise=None, physics_hist=None,
                 physics_init_noise=None, prefix_actions=None):
-        if prefix_actions is not None:
-            raise NotImplementedError("RTC prefix inpainting is not bound yet")
         if physics_hist is None:
             raise ValueError("physics_hist is required by the all-modality chain")
-        return self._step(vl_embs, state, embodiment_id, init_noise, physics_hist, physics_init_noise)
+        return self._step(vl_embs, state, embodiment_id, init_noise, physics_hist, physics_init_noise,
+                          prefix_actions)
 
 
 class B200ActionHeadChain(_B200HeadChain):
@@ -353,6 +369,4 @@ class B200ActionHeadChain(_B200HeadChain):
     _physics = False
 
     def forward(self, vl_embs, state, embodiment_id, init_noise=None, prefix_actions=None, **kwargs):
-        if prefix_actions is not None:
-            raise NotImplementedError("RTC prefix inpainting is not bound yet")
-        return self._step(vl_embs, state, embodiment_id, init_noise, None, None)
+        return self._step(vl_embs, state, embodiment_id, init_noise, None, None, prefix_actions)

@@ -636,7 +636,7 @@ using namespace rldx;
 
 extern "C" {
 
-int rldx_version(void) { return 101; }
+int rldx_version(void) { return 102; }
 
 const char* rldx_last_error(void) { return t_last_error.c_str(); }
 

@@ -454,6 +454,12 @@ struct rldx_msat {
     ck(cudaMemcpyAsync(x, io->init_noise, static_cast<size_t>(B) * c.horizon * c.action_dim * 2,
                        cudaMemcpyDefault, st),
        "noise");
+    if (c.prefix_len > 0) {  // RTC trained mode: the prefix rows of x hold the frozen actions
+      const size_t row = static_cast<size_t>(c.action_dim) * 2;
+      ck(cudaMemcpy2DAsync(x, c.horizon * row, io->prefix_actions, c.prefix_len * row, c.prefix_len * row, B,
+                           cudaMemcpyDefault, st),
+         "prefix_actions");
+    }
     if (standard) return;
     ck(cudaMemcpy2DAsync(phys_hist_in, hc * 2, io->physics_hist, c.physics_dim * 2, c.physics_dim * 2,
                          static_cast<size_t>(B) * c.physics_hist, cudaMemcpyDefault, st),
@@ -492,6 +498,7 @@ void rldx_msat::create(const rldx_msat_config& cfg, const rldx_msat_weights& w) 
   if (!standard && (c.physics_dim <= 0 || c.physics_hist <= 0))
     throw Fail(RLDX_ERR_UNSUPPORTED, "the all-modality path needs the physics stream");
   if (c.depth_single < 0) throw Fail(RLDX_ERR_ARG, "depth_single must be >= 0");
+  if (c.prefix_len < 0 || c.prefix_len >= c.horizon) throw Fail(RLDX_ERR_ARG, "prefix_len must be in [0, horizon)");
   if (c.depth_single > 0) {
     if (!w.single_blocks) throw Fail(RLDX_ERR_ARG, "missing single block weights");
     if (c.single_expanded <= 0 || c.single_expanded % 32 || c.single_mlp_hidden <= 0 ||
@@ -777,11 +784,15 @@ void rldx_msat::precompute(const rldx_msat_weights& w) {
 
   // ---- sinusoids: action encoder / physics future encoder use t, the physics history
   //      encoder uses the token index (embodiment_conditioned_mlp.py:39-59, physics.py:19-25) ----
-  std::vector<uint16_t> row(D);
+  // RTC trained mode: the prefix action tokens are encoded at t = 1 (clean), every step.
+  std::vector<uint16_t> row(D), row_prefix(D);
+  sinusoid_sin_cos(1.0f, D, row_prefix.data());
   for (int s = 0; s < S; ++s) {
     sinusoid_sin_cos(tvals[s], D, row.data());
     for (int r = 0; r < B * c.horizon; ++r)
-      ck(cudaMemcpy(act_cat[s] + static_cast<size_t>(r) * 2 * D + D, row.data(), D * 2, cudaMemcpyHostToDevice), "tau");
+      ck(cudaMemcpy(act_cat[s] + static_cast<size_t>(r) * 2 * D + D,
+                    (r % c.horizon < c.prefix_len ? row_prefix : row).data(), D * 2, cudaMemcpyHostToDevice),
+         "tau");
     for (int r = 0; r < B * c.physics_fut; ++r)
       ck(cudaMemcpy(phf_cat[s] + static_cast<size_t>(r) * 2 * D + D, row.data(), D * 2, cudaMemcpyHostToDevice), "tau");
   }
@@ -1012,12 +1023,17 @@ void rldx_msat::plan() {
       rldx_gemm_desc d1 = catlin(oproj_sa, c.out_dim, dl1_W, dl1_b, B * nsa, c.dec_hidden, c.out_dim, nsa, dec_h, c.dec_hidden);
       d1.act = RLDX_ACT_RELU;
       g2.push_back(d1);
-      rldx_gemm_desc d2 = catlin(dec_h, c.dec_hidden, dl2_W, dl2_b, B * nsa, c.action_dim, c.dec_hidden, nsa, x, adp);
+      // Euler update of action tokens [prefix_len, h) of each observation: rows of the decoder
+      // output before them (time, state, locked prefix) are dropped, so the prefix keeps the
+      // frozen actions (the re-lock of graph_safe_action_model.py:296-300).
+      const int pl = c.prefix_len;
+      rldx_gemm_desc d2 = catlin(dec_h, c.dec_hidden, dl2_W, dl2_b, B * nsa, c.action_dim, c.dec_hidden, nsa,
+                                 x + static_cast<size_t>(pl) * adp, adp);
       d2.epilogue = RLDX_EPI_EULER;
       d2.dt = dt;
       d2.rows_in = nsa;
       d2.rows_out = h;
-      d2.row_skip = nsa - h;
+      d2.row_skip = nsa - h + pl;
       g3.push_back(d2);
       if (!standard) {
         g1.push_back(lin(oln_p, D, pp2_w, pp2_b, B * np, c.out_dim, D, oproj_p, c.out_dim));
@@ -1089,8 +1105,10 @@ int rldx_msat_destroy(rldx_msat* h) {
 static int msat_step_impl(rldx_msat* h, const rldx_msat_io* io, cudaStream_t st) {
   if (!h || !io) return set_error(RLDX_ERR_ARG, "msat_step: null argument");
   if (!io->vl || !io->state || !io->emb_id || !io->init_noise || !io->actions ||
-      (!h->standard && (!io->physics_hist || !io->physics_noise)))
-    return set_error(RLDX_ERR_ARG, "msat_step: every io pointer is required (physics ones on the all-modality path)");
+      (!h->standard && (!io->physics_hist || !io->physics_noise)) || (h->c.prefix_len > 0 && !io->prefix_actions))
+    return set_error(RLDX_ERR_ARG,
+                     "msat_step: every io pointer is required (physics ones on the all-modality path, "
+                     "prefix_actions with prefix_len > 0)");
   return guard([&] {
     h->copy_inputs(io, st);
     if (h->exec)

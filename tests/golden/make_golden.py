@@ -118,23 +118,28 @@ def reference_head(R, cfg: om.MsatHeadConfig):
     return head
 
 
-def run_reference_loop(R, head, cfg, inp):
+def run_reference_loop(R, head, cfg, inp, prefix_actions=None):
+    """The reference's GraphSafeActionModel loop; prefix_actions enables its RTC trained mode
+    (prefix_len = prefix_actions.shape[1])."""
+    d = 0 if prefix_actions is None else prefix_actions.shape[1]
     common = dict(msat=head.model, state_encoder=head.state_encoder, action_encoder=head.action_encoder,
                   action_decoder=head.action_decoder, position_embedding=head.position_embedding,
                   vlln=head.vlln, n_vl=cfg.n_vl, n_sa_pure=cfg.n_state + cfg.horizon,
                   action_horizon=cfg.horizon, action_dim=cfg.action_dim,
-                  num_inference_timesteps=cfg.num_steps, device="cpu", dtype=inp["vl"].dtype)
+                  num_inference_timesteps=cfg.num_steps, device="cpu", dtype=inp["vl"].dtype,
+                  prefix_len=d)
+    extra = {"prefix_actions": prefix_actions} if d else {}
     if not cfg.use_physics:
         gs = R.gs.GraphSafeActionModel(**common)
         with torch.no_grad():
-            return gs(inp["vl"], inp["state"], inp["embodiment_id"], init_noise=inp["init_noise"])
+            return gs(inp["vl"], inp["state"], inp["embodiment_id"], init_noise=inp["init_noise"], **extra)
     gs = R.gs.GraphSafeActionModel(
         **common, physics_cond_encoder=head.physics.physics_cond_encoder,
         physics_fut_encoder=head.physics.physics_fut_encoder, physics_decoder=head.physics.physics_decoder,
         physics_hist_len=cfg.physics_hist, physics_fut_len=cfg.physics_fut, physics_dim=cfg.physics_dim)
     with torch.no_grad():
         return gs(inp["vl"], inp["state"], inp["embodiment_id"], init_noise=inp["init_noise"],
-                  physics_hist=inp["physics_hist"], physics_init_noise=inp["physics_noise"])
+                  physics_hist=inp["physics_hist"], physics_init_noise=inp["physics_noise"], **extra)
 
 
 def run_vanilla_loop(head, cfg, inp):
@@ -208,6 +213,22 @@ def head_fixture(R, dtype, batch: int, cfg: om.MsatHeadConfig = SMALL) -> dict:
             "cos_only_rope": bool(not ref.model.rope_embedder.freqs_cis_0.is_complex())}
 
 
+def rtc_fixture(R, dtype, cfg: om.MsatHeadConfig, prefix_len: int = 3) -> dict:
+    """RTC trained mode: the reference GraphSafeActionModel(prefix_len=3) loop at batch 1 with a
+    seeded frozen prefix (graph_safe_action_model.py:196-300)."""
+    ref = reference_head(R, cfg)
+    om.init_weights(ref, seed=1234)
+    if dtype == torch.bfloat16:
+        ref = ref.to(torch.bfloat16)
+    inp = om.make_inputs(cfg, batch=1, seed=42, dtype=dtype, emb_ids=[1])
+    g = torch.Generator().manual_seed(77)
+    prefix = (0.5 * torch.randn(1, prefix_len, cfg.action_dim, generator=g)).to(dtype)
+    actions = run_reference_loop(R, ref, cfg, inp, prefix_actions=prefix)
+    return {"config": vars(cfg), "seed": 1234, "weight_abs_sum": weight_checksum(ref),
+            "dtype": str(dtype), "batch": 1, "loop": "graph_safe_rtc", "inputs": inp,
+            "prefix_actions": prefix, "actions": actions}
+
+
 def c1_block_fixture(R) -> dict:
     """one ExpandedDoubleStreamBlock, fp32, [cog 256 | act 16 | phys 16]."""
     torch.manual_seed(0)
@@ -233,6 +254,11 @@ def c1_block_fixture(R) -> dict:
 
 def main():
     R = import_reference()
+    for tag, cfg in (("small", SMALL), ("std", STD)):
+        for dtype, dn in ((torch.float32, "fp32"), (torch.bfloat16, "bf16")):
+            torch.save(rtc_fixture(R, dtype, cfg), HERE / f"rtc_{tag}_b1_{dn}.pt")
+    if "--rtc-only" in sys.argv:
+        return
     torch.save(head_fixture(R, torch.float32, 1), HERE / "head_small_b1_fp32.pt")
     torch.save(head_fixture(R, torch.bfloat16, 1), HERE / "head_small_b1_bf16.pt")
     torch.save(head_fixture(R, torch.float32, 2), HERE / "head_small_b2_fp32.pt")

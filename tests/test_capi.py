@@ -26,15 +26,15 @@ def test_every_declared_symbol_is_exported(lib):
 
 
 def test_version_and_error_string(lib):
-    assert lib.rldx_version() == 101
+    assert lib.rldx_version() == 102
     assert isinstance(lib.rldx_last_error(), bytes)
 
 
 def test_struct_layouts_match_header():
     # sizes of the C structs as laid out by the C compiler on this ABI (x86-64 / aarch64 LP64)
     assert C.sizeof(_lib.GemmDesc) == 248
-    assert C.sizeof(_lib.MsatConfig) == 30 * 4
-    assert C.sizeof(_lib.MsatIO) == 7 * 8
+    assert C.sizeof(_lib.MsatConfig) == 31 * 4
+    assert C.sizeof(_lib.MsatIO) == 8 * 8
     assert C.sizeof(_lib.BlockWeights) == 3 * (4 * 16 + 16)
     assert C.sizeof(_lib.SingleBlockWeights) == 2 * (3 * 16 + 16)
 

@@ -21,17 +21,21 @@ def cos_sim(a, b):
     return float((a @ b) / (a.norm() * b.norm() + 1e-30))
 
 
-def run_chain(head_bf16, inp, cuda, use_graph=True):
+def run_chain(head_bf16, inp, cuda, use_graph=True, prefix=None):
     dev = {k: v.to(cuda) for k, v in inp.items()}
+    pre = {}
+    if prefix is not None:
+        pre = {"prefix_actions": prefix.to(cuda, BF)}
+    plen = 0 if prefix is None else prefix.shape[1]
     if head_bf16.use_physics:
-        chain = B200ExpandedActionHeadChain(head_bf16, cuda, use_graph=use_graph)
+        chain = B200ExpandedActionHeadChain(head_bf16, cuda, use_graph=use_graph, prefix_len=plen)
         out = chain(dev["vl"].to(BF), dev["state"].to(BF), dev["embodiment_id"],
                     init_noise=dev["init_noise"].to(BF), physics_hist=dev["physics_hist"].to(BF),
-                    physics_init_noise=dev["physics_noise"].to(BF))
+                    physics_init_noise=dev["physics_noise"].to(BF), **pre)
     else:
-        chain = B200ActionHeadChain(head_bf16, cuda, use_graph=use_graph)
+        chain = B200ActionHeadChain(head_bf16, cuda, use_graph=use_graph, prefix_len=plen)
         out = chain(dev["vl"].to(BF), dev["state"].to(BF), dev["embodiment_id"],
-                    init_noise=dev["init_noise"].to(BF))
+                    init_noise=dev["init_noise"].to(BF), **pre)
     torch.cuda.synchronize()
     return chain, out.cpu()
 
@@ -135,3 +139,34 @@ def test_standard_chain_rejects_physics_head(cuda):
     head = om.init_weights(om.ActionHead(cfg), seed=1).to(BF)
     with pytest.raises(ValueError):
         B200ActionHeadChain(head, cuda)
+
+
+@pytest.mark.parametrize("tag", ["small", "std"])
+def test_rtc_prefix_matches_reference_golden(cuda, tag):
+    """RTC trained mode (3 locked prefix actions) against the reference GraphSafeActionModel with
+    prefix_len=3: the prefix comes back unchanged, the rest within the action tolerance."""
+    fx16 = torch.load(GOLD / f"rtc_{tag}_b1_bf16.pt", weights_only=False)
+    fx32 = torch.load(GOLD / f"rtc_{tag}_b1_fp32.pt", weights_only=False)
+    cfg = om.MsatHeadConfig(**fx16["config"])
+    head = om.init_weights(om.ActionHead(cfg), seed=fx16["seed"]).to(BF)
+    _, out = run_chain(head, fx32["inputs"], cuda, prefix=fx16["prefix_actions"])
+    assert torch.equal(out[:, :3], fx16["prefix_actions"])
+    assert (out.float() - fx16["actions"].float()).abs().max().item() <= 2e-2
+    assert cos_sim(out.float(), fx32["actions"]) >= 0.999
+
+
+def test_rtc_prefix_batch_against_oracle(cuda):
+    """RTC at batch 2 with two embodiments on the all-modality head with single blocks."""
+    cfg = om.MsatHeadConfig(n_vl=64, horizon=16, physics_hist=16, physics_fut=16, dim=256, heads=4,
+                            depth=2, depth_single=1, vl_dim=512, mlp_ratio=3.0, out_dim=128,
+                            action_dim=32, state_dim=64, dec_hidden=128, physics_dim=37,
+                            num_embodiments=4)
+    head = om.init_weights(om.ActionHead(cfg), seed=21).to(BF)
+    inp = om.make_inputs(cfg, batch=2, seed=9, emb_ids=[2, 0])
+    prefix = (0.5 * torch.randn(2, 5, 32, generator=torch.Generator().manual_seed(3))).to(BF)
+    args = [inp[k].to(BF) if inp[k].is_floating_point() else inp[k]
+            for k in ("vl", "state", "embodiment_id", "init_noise", "physics_hist", "physics_noise")]
+    ref16 = om.denoise(head, *args, cfg.num_steps, prefix_actions=prefix)
+    _, out = run_chain(head, inp, cuda, prefix=prefix)
+    assert torch.equal(out[:, :5], prefix)
+    assert_actions_close(out, ref16)

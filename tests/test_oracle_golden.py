@@ -102,3 +102,24 @@ def test_rope_cast_to_bf16_keeps_only_cos():
     assert rope.freqs_cis_1.dtype == torch.bfloat16
     ref = om.precompute_freqs_cis(48, 32, 1e4).real.to(torch.bfloat16)
     assert torch.equal(rope.freqs_cis_1, ref)
+
+
+@pytest.mark.parametrize("name", [f"rtc_{tag}_b1_{dt}.pt" for tag in ("small", "std")
+                                  for dt in ("fp32", "bf16")])
+def test_oracle_rtc_prefix_matches_reference(name):
+    """RTC trained mode (prefix of 3 frozen actions) against the reference GraphSafeActionModel
+    with prefix_len=3, physics and standard topologies."""
+    fx = _load(name)
+    cfg = om.MsatHeadConfig(**fx["config"])
+    head = om.init_weights(om.ActionHead(cfg), seed=fx["seed"])
+    if "bf16" in name:
+        head = head.to(torch.bfloat16)
+    inp = fx["inputs"]
+    phys = (inp["physics_hist"], inp["physics_noise"]) if cfg.use_physics else (None, None)
+    out = om.denoise(head, inp["vl"], inp["state"], inp["embodiment_id"], inp["init_noise"],
+                     *phys, cfg.num_steps, prefix_actions=fx["prefix_actions"])
+    assert torch.equal(out[:, :3], fx["prefix_actions"])
+    if "bf16" in name:
+        assert torch.equal(out, fx["actions"]), (out.float() - fx["actions"].float()).abs().max()
+    else:
+        torch.testing.assert_close(out, fx["actions"], rtol=1e-5, atol=1e-5)
