@@ -122,17 +122,18 @@ int rldx_gemm_ws(const rldx_gemm_desc* problems, int nproblems, void* workspace,
 int rldx_gemm_static_ws(const rldx_gemm_desc* problems, int nproblems, void* stream);
 
 /* ------------------------------------------------------------------------------------------
- * Joint-stream attention (non-causal, head_dim 64, scale 1/8) over [seg0 | seg1 | seg2].
+ * Joint-stream attention (non-causal, scale 1/sqrt(head_dim)) over [seg0 | seg1 | seg2].
  * Replaces the F.scaled_dot_product_attention of ds::fused_attention_3way
  * (rldx/inference/action_model/double_stream/engine/ops/op_fused_attention_3way.py:13-116) and
  * rldx/model/modules/action_model/blocks.py:866-869 (split of the output back into streams).
- *   q, k  [B, H, L, 64] bf16;  vt [B, H, 64, Lp] bf16 (Lp >= L, Lp % 8 == 0)
+ *   head_dim 64 (MSAT) or 128
+ *   q, k  [B, H, L, head_dim] bf16;  vt [B, H, head_dim, Lp] bf16 (Lp >= L, Lp % 8 == 0)
  *   key_mask [B, L] uint8 (1 = attend) or NULL
- *   out[s] [B * seg_len[s], H*64] bf16, nseg in 1..3, sum(seg_len) == L
+ *   out[s] [B * seg_len[s], H*head_dim] bf16, nseg in 1..3, sum(seg_len) == L
  * ------------------------------------------------------------------------------------------ */
 int rldx_joint_attention(const void* q, const void* k, const void* vt, int B, int H, int L, int Lp,
-                         const uint8_t* key_mask, void* const* out, const int* seg_len, int nseg,
-                         void* stream);
+                         int head_dim, const uint8_t* key_mask, void* const* out, const int* seg_len,
+                         int nseg, void* stream);
 
 /* ------------------------------------------------------------------------------------------
  * LayerNorm without affine (eps) over rows of width D (D % 8 == 0, D <= 4096), optionally

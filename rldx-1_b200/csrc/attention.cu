@@ -1,5 +1,6 @@
-// Joint-stream attention for sm_100a: non-causal softmax(Q K^T / sqrt(64)) V over the
-// concatenated [cognition | action | physics] token sequence of one batch element and head.
+// Joint-stream attention for sm_100a: non-causal softmax(Q K^T / sqrt(d)) V over the
+// concatenated [cognition | action | physics] token sequence of one batch element and head,
+// head_dim d = 64 (MSAT) or 128 (the joint-attention sweep shapes).
 //
 // Reference: F.scaled_dot_product_attention over torch.cat([vl, sa, p]) in
 // rldx/model/modules/action_model/blocks.py:826-870 (ExpandedDoubleStreamBlock) and
@@ -7,10 +8,11 @@
 // blocks.py:867-869.  The optional key mask reproduces the -inf masking of masked VL tokens /
 // masked physics samples (blocks.py:843-864).
 //
-// One CTA = one (128-query tile, head, batch element).  Q, K come as [B*H, L, 64] and V as
-// V^T [B*H, 64, Lp] (written by the QKV GEMM epilogue), so every tcgen05 operand is K-major:
-//   S_j  = Q K_j^T          (M=128, N=64 keys, K=64 dims)   -> TMEM, double buffered
-//   O   += P_j V_j          (M=128, N=64 dims, K=64 keys)   -> one TMEM accumulator
+// One CTA = one (128-query tile, head, batch element).  Q, K come as [B*H, L, d] and V as
+// V^T [B*H, d, Lp] (written by the QKV GEMM epilogue), so every tcgen05 operand is K-major:
+//   S_j  = Q K_j^T          (M=128, N=64 keys, K=d dims)    -> TMEM, double buffered
+//   O   += P_j V_j          (M=128, N=d dims, K=64 keys)    -> one TMEM accumulator
+// Q and K tiles are held as d/64 chunks of 64 dims (one 128-byte swizzle atom per row each).
 // The four softmax warps own one query row per thread, so row max / sum need no shuffles.
 // P_j goes to shared memory in the 128-byte-swizzled K-major layout the PV MMA reads.  The
 // running max is rescaled lazily: exponentials use a reference max that only moves when a
@@ -22,20 +24,35 @@ namespace rldx {
 
 constexpr int kAttnThreads = 192;
 constexpr int kKvStages = 3;
-constexpr int kQBytes = 128 * 128;
-constexpr int kKvTileBytes = 64 * 128;
 constexpr int kPBytes = 128 * 128;
 constexpr float kRescaleLog2 = 8.0f;  // lazy-rescale threshold (log2 units)
 constexpr uint32_t kOCol = 128;       // TMEM column of the O accumulator (S buffers at 0, 64)
 
+template <int kHD>
+struct AttnShape {
+  static constexpr int kChunks = kHD / 64;           // 64-dim chunks of a Q / K row
+  static constexpr int kQBytes = 128 * kHD * 2;      // 128 queries
+  static constexpr int kQChunk = 128 * 128;          // one 64-dim chunk of the Q tile
+  static constexpr int kKTileBytes = 64 * kHD * 2;   // 64 keys
+  static constexpr int kKChunk = 64 * 128;           // one 64-dim chunk of a K tile
+  static constexpr int kVTileBytes = kHD * 64 * 2;   // V^T: d rows x 64 keys
+  static constexpr size_t kSmem = 1024 + kQBytes + static_cast<size_t>(kKvStages) * (kKTileBytes + kVTileBytes) +
+                                  2 * kPBytes + 32 * 8;
+};
+
+template <int kHD>
 __global__ void __launch_bounds__(kAttnThreads, 1) joint_attention_kernel(const __grid_constant__ AttnParams P) {
+  using Sh = AttnShape<kHD>;
+  constexpr int kQBytes = Sh::kQBytes;
+  constexpr int kKTileBytes = Sh::kKTileBytes;
+  constexpr int kVTileBytes = Sh::kVTileBytes;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
   uint8_t* sQ = smem;
-  uint8_t* sK = sQ + kQBytes;                       // kKvStages x 8 KB
-  uint8_t* sV = sK + kKvStages * kKvTileBytes;      // kKvStages x 8 KB
-  uint8_t* sP = sV + kKvStages * kKvTileBytes;      // 2 x 16 KB
+  uint8_t* sK = sQ + kQBytes;                       // kKvStages K tiles
+  uint8_t* sV = sK + kKvStages * kKTileBytes;       // kKvStages V^T tiles
+  uint8_t* sP = sV + kKvStages * kVTileBytes;       // 2 x 16 KB
   uint64_t* bars = reinterpret_cast<uint64_t*>(sP + 2 * kPBytes);
   uint64_t* q_full = bars;
   uint64_t* kv_full = bars + 1;
@@ -89,20 +106,24 @@ __global__ void __launch_bounds__(kAttnThreads, 1) joint_attention_kernel(const 
       const uint64_t pol = l2_policy_evict_last();
       griddep_wait();
       mbar_arrive_expect_tx(q_full, kQBytes);
-      tma_load_3d(sQ, &P.tq, q_full, 0, q0, bh, pol);
+#pragma unroll
+      for (int c = 0; c < Sh::kChunks; ++c) tma_load_3d(sQ + c * Sh::kQChunk, &P.tq, q_full, c * 64, q0, bh, pol);
       for (int j = 0; j < nkv; ++j) {
         const int s = j % kKvStages;
         const uint32_t ph = static_cast<uint32_t>(j / kKvStages) & 1u;
         if (!mbar_wait(&kv_empty[s], ph ^ 1u, kErrAttnTimeout + 1)) break;
-        mbar_arrive_expect_tx(&kv_full[s], 2 * kKvTileBytes);
-        tma_load_3d(sK + s * kKvTileBytes, &P.tk, &kv_full[s], 0, j * 64, bh, pol);
-        tma_load_3d(sV + s * kKvTileBytes, &P.tv, &kv_full[s], j * 64, 0, bh, pol);
+        mbar_arrive_expect_tx(&kv_full[s], kKTileBytes + kVTileBytes);
+#pragma unroll
+        for (int c = 0; c < Sh::kChunks; ++c)
+          tma_load_3d(sK + s * kKTileBytes + c * Sh::kKChunk, &P.tk, &kv_full[s], c * 64, j * 64, bh, pol);
+        tma_load_3d(sV + s * kVTileBytes, &P.tv, &kv_full[s], j * 64, 0, bh, pol);
       }
     }
   } else if (warp == 1) {
     // ---------------- MMA issuer ----------------
     if (lane == 0) {
       const uint32_t idesc = umma_idesc_bf16(128, 64);
+      const uint32_t idesc_pv = umma_idesc_bf16(128, kHD);
       const uint32_t q_addr = smem_u32(sQ);
       bool ok = mbar_wait(q_full, 0, kErrAttnTimeout + 2);
       auto issue_s = [&](int j) -> bool {
@@ -113,11 +134,11 @@ __global__ void __launch_bounds__(kAttnThreads, 1) joint_attention_kernel(const 
         if (!mbar_wait(&s_empty[sb], (static_cast<uint32_t>(j >> 1) & 1u) ^ 1u, kErrAttnTimeout + 2))
           return false;
         tc_fence_after();
-        const uint32_t k_addr = smem_u32(sK + s * kKvTileBytes);
+        const uint32_t k_addr = smem_u32(sK + s * kKTileBytes);
 #pragma unroll
-        for (int k = 0; k < 4; ++k)
-          umma_f16(tmem + sb * 64, umma_desc_sw128(q_addr + 32 * k),
-                   umma_desc_sw128(k_addr + 32 * k), idesc, k != 0 ? 1u : 0u);
+        for (int k = 0; k < 4 * Sh::kChunks; ++k)
+          umma_f16(tmem + sb * 64, umma_desc_sw128(q_addr + (k >> 2) * Sh::kQChunk + 32 * (k & 3)),
+                   umma_desc_sw128(k_addr + (k >> 2) * Sh::kKChunk + 32 * (k & 3)), idesc, k != 0 ? 1u : 0u);
         umma_commit(&s_full[sb]);
         return true;
       };
@@ -132,11 +153,11 @@ __global__ void __launch_bounds__(kAttnThreads, 1) joint_attention_kernel(const 
         tc_fence_after();
         const int s = j % kKvStages;
         const uint32_t p_addr = smem_u32(sP + pb * kPBytes);
-        const uint32_t v_addr = smem_u32(sV + s * kKvTileBytes);
+        const uint32_t v_addr = smem_u32(sV + s * kVTileBytes);
 #pragma unroll
         for (int k = 0; k < 4; ++k)
           umma_f16(tmem + kOCol, umma_desc_sw128(p_addr + 32 * k), umma_desc_sw128(v_addr + 32 * k),
-                   idesc, (j | k) != 0 ? 1u : 0u);
+                   idesc_pv, (j | k) != 0 ? 1u : 0u);
         umma_commit(o_done);
         umma_commit(&kv_empty[s]);
         umma_commit(&p_empty[pb]);
@@ -209,7 +230,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1) joint_attention_kernel(const 
         if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
         tc_fence_after();
 #pragma unroll
-        for (int h = 0; h < 2; ++h) {
+        for (int h = 0; h < kHD / 32; ++h) {
           float o[32];
           tmem_ld32(tmem + lane_off + kOCol + 32 * h, o);
           tmem_wait_ld();
@@ -251,29 +272,31 @@ __global__ void __launch_bounds__(kAttnThreads, 1) joint_attention_kernel(const 
     if (ok && nkv > 0) ok = mbar_wait(o_done, static_cast<uint32_t>(nkv - 1) & 1u, kErrAttnTimeout + 3);
     if (__all_sync(0xffffffffu, ok) && nkv > 0) {
       tc_fence_after();
-      float o[64];
-      tmem_ld32(tmem + lane_off + kOCol, *reinterpret_cast<float(*)[32]>(&o[0]));
-      tmem_ld32(tmem + lane_off + kOCol + 32, *reinterpret_cast<float(*)[32]>(&o[32]));
-      tmem_wait_ld();
-      if (qrow < L) {
-        int seg = 0, off = 0;
-        while (seg + 1 < P.nseg && qrow >= off + P.seg_len[seg]) {
-          off += P.seg_len[seg];
-          ++seg;
-        }
-        const float inv_l = 1.0f / l_run;
-        const int ld = P.seg_ld[seg] > 0 ? P.seg_ld[seg] : P.H * 64;
-        __nv_bfloat16* dst = P.seg_out[seg] +
-                             (static_cast<size_t>(b) * P.seg_len[seg] + (qrow - off)) * ld + head * 64;
-        uint4* d4 = reinterpret_cast<uint4*>(dst);
+      int seg = 0, off = 0;
+      while (seg + 1 < P.nseg && qrow >= off + P.seg_len[seg]) {
+        off += P.seg_len[seg];
+        ++seg;
+      }
+      const float inv_l = 1.0f / l_run;
+      const int ld = P.seg_ld[seg] > 0 ? P.seg_ld[seg] : P.H * kHD;
+      uint4* d4 = reinterpret_cast<uint4*>(
+          P.seg_out[seg] + (static_cast<size_t>(b) * P.seg_len[seg] + (qrow - off)) * ld + head * kHD);
 #pragma unroll
-        for (int cc = 0; cc < 8; ++cc) {
-          uint4 u;
-          u.x = pack_bf16x2(o[8 * cc + 0] * inv_l, o[8 * cc + 1] * inv_l);
-          u.y = pack_bf16x2(o[8 * cc + 2] * inv_l, o[8 * cc + 3] * inv_l);
-          u.z = pack_bf16x2(o[8 * cc + 4] * inv_l, o[8 * cc + 5] * inv_l);
-          u.w = pack_bf16x2(o[8 * cc + 6] * inv_l, o[8 * cc + 7] * inv_l);
-          d4[cc] = u;
+      for (int half = 0; half < kHD / 64; ++half) {  // 64 output dims at a time
+        float o[64];
+        tmem_ld32(tmem + lane_off + kOCol + 64 * half, *reinterpret_cast<float(*)[32]>(&o[0]));
+        tmem_ld32(tmem + lane_off + kOCol + 64 * half + 32, *reinterpret_cast<float(*)[32]>(&o[32]));
+        tmem_wait_ld();
+        if (qrow < L) {
+#pragma unroll
+          for (int cc = 0; cc < 8; ++cc) {
+            uint4 u;
+            u.x = pack_bf16x2(o[8 * cc + 0] * inv_l, o[8 * cc + 1] * inv_l);
+            u.y = pack_bf16x2(o[8 * cc + 2] * inv_l, o[8 * cc + 3] * inv_l);
+            u.z = pack_bf16x2(o[8 * cc + 4] * inv_l, o[8 * cc + 5] * inv_l);
+            u.w = pack_bf16x2(o[8 * cc + 6] * inv_l, o[8 * cc + 7] * inv_l);
+            d4[8 * half + cc] = u;
+          }
         }
       }
     }
@@ -286,27 +309,33 @@ __global__ void __launch_bounds__(kAttnThreads, 1) joint_attention_kernel(const 
   }
 }
 
-size_t attention_smem_bytes() {
-  return 1024 + kQBytes + 2 * kKvStages * kKvTileBytes + 2 * kPBytes + 32 * 8;
+size_t attention_smem_bytes(int head_dim) {
+  return head_dim == 128 ? AttnShape<128>::kSmem : AttnShape<64>::kSmem;
 }
 
 cudaError_t attention_prepare_device() {
-  return cudaFuncSetAttribute(joint_attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                              static_cast<int>(attention_smem_bytes()));
+  cudaError_t e = cudaFuncSetAttribute(joint_attention_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       static_cast<int>(AttnShape<64>::kSmem));
+  if (e != cudaSuccess) return e;
+  return cudaFuncSetAttribute(joint_attention_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                              static_cast<int>(AttnShape<128>::kSmem));
 }
 
 cudaError_t launch_attention(const AttnParams& p, cudaStream_t stream, bool pdl) {
+  const int hd = p.head_dim > 0 ? p.head_dim : 64;
+  if (hd != 64 && hd != 128) return cudaErrorInvalidValue;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((p.L + 127) / 128, p.H, p.B);
   cfg.blockDim = dim3(kAttnThreads, 1, 1);
-  cfg.dynamicSmemBytes = attention_smem_bytes();
+  cfg.dynamicSmemBytes = attention_smem_bytes(hd);
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = pdl ? 1 : 0;
-  return cudaLaunchKernelEx(&cfg, joint_attention_kernel, p);
+  return hd == 128 ? cudaLaunchKernelEx(&cfg, joint_attention_kernel<128>, p)
+                   : cudaLaunchKernelEx(&cfg, joint_attention_kernel<64>, p);
 }
 
 }  // namespace rldx

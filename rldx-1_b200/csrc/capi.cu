@@ -636,7 +636,7 @@ using namespace rldx;
 
 extern "C" {
 
-int rldx_version(void) { return 102; }
+int rldx_version(void) { return 103; }
 
 const char* rldx_last_error(void) { return t_last_error.c_str(); }
 
@@ -702,13 +702,14 @@ int rldx_gemm_ws(const rldx_gemm_desc* problems, int nproblems, void* workspace,
 }
 
 int rldx_joint_attention(const void* q, const void* k, const void* vt, int B, int H, int L, int Lp,
-                         const uint8_t* key_mask, void* const* out, const int* seg_len, int nseg,
-                         void* stream) {
+                         int head_dim, const uint8_t* key_mask, void* const* out, const int* seg_len,
+                         int nseg, void* stream) {
   int rc = ensure_device();
   if (rc != RLDX_OK) return rc;
   if (!q || !k || !vt || !out || !seg_len) return set_error(RLDX_ERR_ARG, "attention: null pointer");
   if (B <= 0 || H <= 0 || L <= 0 || Lp < L || Lp % 8 != 0)
     return set_error(RLDX_ERR_ARG, "attention: need B, H, L > 0, Lp >= L, Lp % 8 == 0");
+  if (head_dim != 64 && head_dim != 128) return set_error(RLDX_ERR_UNSUPPORTED, "attention: head_dim must be 64 or 128");
   if (nseg < 1 || nseg > 3) return set_error(RLDX_ERR_ARG, "attention: nseg must be 1..3");
   if (!aligned16(q) || !aligned16(k) || !aligned16(vt))
     return set_error(RLDX_ERR_ARG, "attention: q/k/vt must be 16-byte aligned");
@@ -728,13 +729,16 @@ int rldx_joint_attention(const void* q, const void* k, const void* vt, int B, in
   p.H = H;
   p.B = B;
   p.key_mask = key_mask;
-  p.scale_log2 = 1.4426950408889634f / 8.0f;
+  p.head_dim = head_dim;
+  p.scale_log2 = 1.4426950408889634f / std::sqrt(static_cast<float>(head_dim));
   std::string err;
   const uint64_t bh = static_cast<uint64_t>(B) * H;
-  if (!make_tmap_3d(&p.tq, q, 64, L, bh, 128, static_cast<uint64_t>(L) * 128, 64, 128, 1, &err) ||
-      !make_tmap_3d(&p.tk, k, 64, L, bh, 128, static_cast<uint64_t>(L) * 128, 64, 64, 1, &err) ||
-      !make_tmap_3d(&p.tv, vt, L, 64, bh, static_cast<uint64_t>(Lp) * 2,
-                    static_cast<uint64_t>(Lp) * 128, 64, 64, 1, &err))
+  const uint64_t hd = static_cast<uint64_t>(head_dim);
+  // Q, K: [bh, L, hd] loaded as 64-dim chunks (128-byte rows); V^T: [bh, hd, Lp], 64-key boxes
+  if (!make_tmap_3d(&p.tq, q, hd, L, bh, hd * 2, static_cast<uint64_t>(L) * hd * 2, 64, 128, 1, &err) ||
+      !make_tmap_3d(&p.tk, k, hd, L, bh, hd * 2, static_cast<uint64_t>(L) * hd * 2, 64, 64, 1, &err) ||
+      !make_tmap_3d(&p.tv, vt, L, hd, bh, static_cast<uint64_t>(Lp) * 2, static_cast<uint64_t>(Lp) * hd * 2, 64,
+                    static_cast<uint32_t>(hd), 1, &err))
     return set_error(RLDX_ERR_ARG, err);
   cudaError_t e = launch_attention(p, static_cast<cudaStream_t>(stream), false);
   if (e != cudaSuccess) return cuda_fail(e, "attention launch");

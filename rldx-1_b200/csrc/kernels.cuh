@@ -16,8 +16,9 @@ struct AttnParams {
   int seg_ld[3];                  // row stride of seg_out[s] in elements (0: H*64)
   int nseg;
   float scale_log2;  // log2(e) / sqrt(head_dim)
+  int head_dim;      // 64 or 128 (0: 64)
 };
-size_t attention_smem_bytes();
+size_t attention_smem_bytes(int head_dim);
 cudaError_t attention_prepare_device();
 cudaError_t launch_attention(const AttnParams& p, cudaStream_t stream, bool pdl);
 

@@ -144,21 +144,21 @@ def qkv_desc(x, weight, bias, q_norm, k_norm, rope_cos, rope_sin, q, k, vt, *, t
 
 
 def joint_attention(q, k, vt, seg_lens: Sequence[int], key_mask=None, outs=None):
-    """Non-causal joint attention over concatenated segments; returns one output per segment
-    as [B * seg_len, H * 64]."""
+    """Non-causal joint attention over concatenated segments (q, k [B, H, L, d], vt [B, H, d, Lp],
+    d = 64 or 128); returns one output per segment as [B * seg_len, H * d]."""
     for t, n in ((q, "q"), (k, "k"), (vt, "vt")):
         _need(t, n)
         if not t.is_contiguous():
             raise ValueError(f"{n} must be contiguous")
-    B, H, L, _ = q.shape
+    B, H, L, hd = q.shape
     Lp = vt.shape[-1]
     if outs is None:
-        outs = [torch.empty(B * n, H * 64, dtype=torch.bfloat16, device=q.device) for n in seg_lens]
+        outs = [torch.empty(B * n, H * hd, dtype=torch.bfloat16, device=q.device) for n in seg_lens]
     ptrs = (C.c_void_p * len(outs))(*[o.data_ptr() for o in outs])
     lens = (C.c_int * len(seg_lens))(*seg_lens)
     if key_mask is not None:
         _need(key_mask, "key_mask", torch.uint8)
-    check(load().rldx_joint_attention(_p(q), _p(k), _p(vt), B, H, L, Lp, _p(key_mask), ptrs, lens,
+    check(load().rldx_joint_attention(_p(q), _p(k), _p(vt), B, H, L, Lp, hd, _p(key_mask), ptrs, lens,
                                       len(seg_lens), _stream()))
     return outs
 

@@ -11,14 +11,14 @@ from rldx_b200 import ops  # noqa: E402
 BF = torch.bfloat16
 
 
-def run_case(cuda, B, H, segs, mask=False, seed=0):
+def run_case(cuda, B, H, segs, mask=False, seed=0, hd=64):
     L = sum(segs)
     Lp = (L + 7) // 8 * 8
     g = torch.Generator(device=cuda).manual_seed(seed)
-    q = torch.randn(B, H, L, 64, device=cuda, generator=g).to(BF)
-    k = torch.randn(B, H, L, 64, device=cuda, generator=g).to(BF)
-    v = torch.randn(B, H, L, 64, device=cuda, generator=g).to(BF)
-    vt = torch.zeros(B, H, 64, Lp, dtype=BF, device=cuda)
+    q = torch.randn(B, H, L, hd, device=cuda, generator=g).to(BF)
+    k = torch.randn(B, H, L, hd, device=cuda, generator=g).to(BF)
+    v = torch.randn(B, H, L, hd, device=cuda, generator=g).to(BF)
+    vt = torch.zeros(B, H, hd, Lp, dtype=BF, device=cuda)
     vt[..., :L] = v.transpose(-1, -2)
     key_mask = None
     bias = torch.zeros(B, 1, 1, L, device=cuda)
@@ -28,12 +28,12 @@ def run_case(cuda, B, H, segs, mask=False, seed=0):
         bias = torch.where(key_mask.bool(), 0.0, float("-inf"))[:, None, None, :]
     outs = ops.joint_attention(q, k, vt, segs, key_mask=key_mask)
     torch.cuda.synchronize()
-    s = (q.float() @ k.float().transpose(-1, -2)) / 8.0 + bias
-    ref = torch.softmax(s, dim=-1) @ v.float()  # [B, H, L, 64]
-    ref = ref.permute(0, 2, 1, 3).reshape(B, L, H * 64)
+    s = (q.float() @ k.float().transpose(-1, -2)) / hd ** 0.5 + bias
+    ref = torch.softmax(s, dim=-1) @ v.float()  # [B, H, L, hd]
+    ref = ref.permute(0, 2, 1, 3).reshape(B, L, H * hd)
     off = 0
     for o, n in zip(outs, segs):
-        exp = ref[:, off:off + n].reshape(B * n, H * 64)
+        exp = ref[:, off:off + n].reshape(B * n, H * hd)
         err = (o.float() - exp).abs().max().item()
         assert err < 2e-2, f"segment at {off}: max err {err}"
         off += n
@@ -53,3 +53,13 @@ def test_joint_attention_batched(cuda, B, H):
 
 def test_joint_attention_key_mask(cuda):
     run_case(cuda, 2, 4, [96, 18, 32], mask=True, seed=7)
+
+
+@pytest.mark.parametrize("segs", [[1], [65], [240, 32, 16], [496, 32, 16], [1008, 32, 16]])
+def test_joint_attention_head_dim_128(cuda, segs):
+    """head_dim 128 (the joint-attention sweep's shape: segments (L-48):32:16, 16 heads)."""
+    run_case(cuda, 2, 16, segs, seed=sum(segs), hd=128)
+
+
+def test_joint_attention_head_dim_128_key_mask(cuda):
+    run_case(cuda, 2, 4, [200, 32, 16], mask=True, seed=3, hd=128)
