@@ -1,0 +1,151 @@
+"""Kernel microbenchmarks for BASELINE configs 3 and 4 on one GPU.
+
+    python -m rldx_b200.microbench --suite c3    # memory-bound: Qwen3 QK-RMSNorm+RoPE, SwiGLU
+    python -m rldx_b200.microbench --suite c4    # joint-attention sweep, head_dim 128
+    python -m rldx_b200.microbench --suite all
+
+Each case prints one JSON line: device time per launch group from CUDA events on the launching
+stream (warm-up first, a synchronize on both sides), the algorithmic bytes or FLOPs of the
+case, and the achieved rate as a fraction of the measured peak in MEASURED_PEAKS.json (the
+fallback figures when that file is absent).  Inputs are seeded ~N(0,1) bf16 tensors created on
+the device before timing; every C3 operand is larger than the 126 MB L2, and each C4 iteration
+reads tensors that the previous iteration evicted when they exceed L2 (smaller ones are
+L2-resident, which the line says).
+
+Config 3 (the Qwen3 backbone path: rldx/model/modules/backbone/modeling_qwen3_vl.py:118-122,
+366-371): per-head RMSNorm (cast to bf16, then * weight) + rotate-half RoPE of Q and K
+[65536 tokens, 16 heads, 128], positions 0..4095 repeated, theta 1e6; algorithmic bytes = each
+tensor read once and written once.  SwiGLU silu(gate) * up on [65536, 8960]: gate and up read
+once, the product written once.
+
+Config 4: non-causal joint attention over [cognition | physics | action] segments of lengths
+(L-48):32:16, 16 heads x 128, batch 1-64; FLOPs = 4 * B * H * L^2 * 128.  torch's
+scaled_dot_product_attention on the same q, k, v (the call the reference makes,
+blocks.py:866) is timed beside it for context.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+from pathlib import Path
+
+import torch
+import torch.nn.functional as F
+
+from . import ops
+
+ROOT = Path(__file__).resolve().parent.parent
+BF = torch.bfloat16
+
+
+def peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), float(d["bf16_tflops"]), "measured"
+    return 6650.0, 1590.0, "fallback"
+
+
+def time_ms(fn, iters: int, warmup: int) -> float:
+    """Average device time of fn() over iters calls (CUDA events on the current stream)."""
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    st = torch.cuda.current_stream()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(st)
+    for _ in range(iters):
+        fn()
+    b.record(st)
+    torch.cuda.synchronize()
+    return a.elapsed_time(b) / iters
+
+
+def suite_c3(iters: int, warmup: int):
+    dev = torch.device("cuda", torch.cuda.current_device())
+    hbm, _, src = peaks()
+    g = torch.Generator(device=dev).manual_seed(3)
+    T, H, hd = 65536, 16, 128
+    q = torch.randn(T, H, hd, device=dev, generator=g).to(BF)
+    k = torch.randn(T, H, hd, device=dev, generator=g).to(BF)
+    qw = (1 + 0.1 * torch.randn(hd, device=dev, generator=g)).to(BF)
+    kw = (1 + 0.1 * torch.randn(hd, device=dev, generator=g)).to(BF)
+    pos = (torch.arange(T, device=dev) % 4096).to(torch.int32)
+    inv = 1.0 / (1e6 ** (torch.arange(0, hd, 2, device=dev).float() / hd))
+    emb = torch.outer(torch.arange(4096, device=dev).float(), inv)
+    emb = torch.cat([emb, emb], dim=-1)
+    cos, sin = emb.cos().to(BF), emb.sin().to(BF)
+    qo, ko = torch.empty_like(q), torch.empty_like(k)
+
+    def rope():
+        ops.qk_rmsnorm_rope(q, qw, pos, cos, sin, out=qo)
+        ops.qk_rmsnorm_rope(k, kw, pos, cos, sin, out=ko)
+
+    ms = time_ms(rope, iters, warmup)
+    nbytes = 2 * 2 * q.numel() * 2  # Q and K, each read once and written once
+    yield {"suite": "c3", "kernel": "qk_rmsnorm_rope_kernel", "case": "Q and K [65536, 16, 128], pos % 4096, theta 1e6",
+           "launches": 2, "ms": ms, "bytes": nbytes, "gbs": nbytes / ms / 1e6, "peak_gbs": hbm,
+           "frac": nbytes / ms / 1e6 / hbm, "peak_source": src, "l2": "operands 268 MB each > L2"}
+    del q, k, qo, ko
+
+    rows, N = 65536, 8960
+    x = torch.randn(rows, 2 * N, device=dev, generator=g).to(BF)
+    out = torch.empty(rows, N, dtype=BF, device=dev)
+    gate, up = x[:, :N], x[:, N:]
+    ms = time_ms(lambda: ops.swiglu(gate, up, out=out), iters, warmup)
+    nbytes = 3 * rows * N * 2
+    yield {"suite": "c3", "kernel": "swiglu_kernel", "case": "silu(gate) * up, [65536, 8960]", "launches": 1,
+           "ms": ms, "bytes": nbytes, "gbs": nbytes / ms / 1e6, "peak_gbs": hbm,
+           "frac": nbytes / ms / 1e6 / hbm, "peak_source": src, "l2": "operands 1.17 GB each > L2"}
+
+
+def suite_c4(iters: int, warmup: int, batches=(1, 4, 16, 64), lengths=(288, 544, 1056, 2080, 4128)):
+    dev = torch.device("cuda", torch.cuda.current_device())
+    _, tflops, src = peaks()
+    H, hd = 16, 128
+    for L in lengths:
+        segs = [L - 48, 32, 16]
+        Lp = (L + 7) // 8 * 8
+        for B in batches:
+            g = torch.Generator(device=dev).manual_seed(L * 100 + B)
+            q = torch.randn(B, H, L, hd, device=dev, generator=g).to(BF)
+            k = torch.randn(B, H, L, hd, device=dev, generator=g).to(BF)
+            v = torch.randn(B, H, L, hd, device=dev, generator=g).to(BF)
+            vt = torch.zeros(B, H, hd, Lp, dtype=BF, device=dev)
+            vt[..., :L] = v.transpose(-1, -2)
+            outs = [torch.empty(B * n, H * hd, dtype=BF, device=dev) for n in segs]
+            ms = time_ms(lambda: ops.joint_attention(q, k, vt, segs, outs=outs), iters, warmup)
+            ms_sdpa = time_ms(lambda: F.scaled_dot_product_attention(q, k, v), iters, warmup)
+            flops = 4.0 * B * H * L * L * hd
+            resident = 4 * q.numel() * 2 < 100e6
+            yield {"suite": "c4", "kernel": "joint_attention_kernel<128>", "L": L, "B": B, "H": H, "head_dim": hd,
+                   "segments": segs, "ms": ms, "flops": flops, "tflops": flops / ms / 1e9,
+                   "peak_tflops": tflops, "frac": flops / ms / 1e9 / tflops, "peak_source": src,
+                   "torch_sdpa_ms": ms_sdpa, "l2": "q/k/v/out L2-resident" if resident else "q/k/v/out > L2"}
+            del q, k, v, vt, outs
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--suite", choices=["c3", "c4", "all"], default="all")
+    ap.add_argument("--iters", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--batches", type=str, default="1,4,16,64")
+    ap.add_argument("--lengths", type=str, default="288,544,1056,2080,4128")
+    a = ap.parse_args()
+    if not torch.cuda.is_available():
+        raise SystemExit("microbench needs a CUDA device")
+    if a.suite in ("c3", "all"):
+        for r in suite_c3(a.iters, a.warmup):
+            print(json.dumps(r), flush=True)
+    if a.suite in ("c4", "all"):
+        bs = tuple(int(x) for x in a.batches.split(","))
+        ls = tuple(int(x) for x in a.lengths.split(","))
+        for r in suite_c4(a.iters, a.warmup, bs, ls):
+            print(json.dumps(r), flush=True)
+    assert ops.device_error() == 0, "device error flag set"
+
+
+if __name__ == "__main__":
+    main()
