@@ -162,65 +162,70 @@ cudaError_t launch_copy(const CopyParams& p, int blocks, cudaStream_t stream, bo
 //   n   = bf16(x * rsqrt(mean(x^2) + eps))          (cast to the input dtype first)
 //   y   = bf16(w * n)                                (then the bf16 weight)
 //   out = bf16( bf16(y * cos) + bf16(rotate_half(y) * sin) ),  cos/sin bf16 [P, 128]
-// A half-warp owns one (token, head) row: lane l of the half holds elements 8l..8l+7, the
-// rotate-half partner sits 8 lanes away.
+// A half-warp owns kQkRows consecutive (token, head) rows: lane l of the half holds elements
+// 8l..8l+7 of each, the rotate-half partner sits 8 lanes away.  All x loads of a thread are
+// issued before any arithmetic.  Products and sums of two bf16 values are exact in fp32, so the
+// packed bf16x2 multiply / add (one rounding of the exact result) give the same bits as the
+// fp32-compute-then-round of the reference's bf16 tensor ops, at a quarter of the instructions;
+// the _rn forms keep the compiler from contracting a multiply and an add into one fma.
 // ---------------------------------------------------------------------------------------------
+constexpr int kQkRows = 4;
+
+__device__ __forceinline__ __nv_bfloat162 as_bf2(uint32_t u) { return *reinterpret_cast<__nv_bfloat162*>(&u); }
+__device__ __forceinline__ uint32_t as_u32(__nv_bfloat162 h) { return *reinterpret_cast<uint32_t*>(&h); }
+
 __global__ void __launch_bounds__(256) qk_rmsnorm_rope_kernel(
     const __nv_bfloat16* __restrict__ x, __nv_bfloat16* __restrict__ y,
     const __nv_bfloat16* __restrict__ w, const int* __restrict__ pos,
     const __nv_bfloat16* __restrict__ cos_t, const __nv_bfloat16* __restrict__ sin_t,
-    long long nrows, int heads, float eps) {
-  const long long half_global = (blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x) >> 4;
+    unsigned nrows, unsigned heads, float eps) {
+  const unsigned half_global = (blockIdx.x * blockDim.x + threadIdx.x) >> 4;
   const int hl = threadIdx.x & 15;
-  const bool active = half_global < nrows;
-  const long long row = active ? half_global : 0;
-  const uint4 u = reinterpret_cast<const uint4*>(x + row * 128)[hl];
-  float v[8];
-  unpack_bf16x2(u.x, v[0], v[1]);
-  unpack_bf16x2(u.y, v[2], v[3]);
-  unpack_bf16x2(u.z, v[4], v[5]);
-  unpack_bf16x2(u.w, v[6], v[7]);
-  float ss = 0.0f;
+  const unsigned row0 = half_global * kQkRows;
+  uint4 u[kQkRows];
 #pragma unroll
-  for (int e = 0; e < 8; ++e) ss += v[e] * v[e];
+  for (int k = 0; k < kQkRows; ++k) {
+    const unsigned row = min(row0 + k, nrows - 1);  // clamped: the tail rows are not stored
+    u[k] = __ldcs(reinterpret_cast<const uint4*>(x + static_cast<size_t>(row) * 128) + hl);
+  }
+  uint4 uc[kQkRows], us[kQkRows];
 #pragma unroll
-  for (int o = 8; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-  const float rstd = rsqrtf(ss * (1.0f / 128.0f) + eps);
-  const uint4 uw = reinterpret_cast<const uint4*>(w)[hl];
-  float wv[8];
-  unpack_bf16x2(uw.x, wv[0], wv[1]);
-  unpack_bf16x2(uw.y, wv[2], wv[3]);
-  unpack_bf16x2(uw.z, wv[4], wv[5]);
-  unpack_bf16x2(uw.w, wv[6], wv[7]);
+  for (int k = 0; k < kQkRows; ++k) {
+    const unsigned row = min(row0 + k, nrows - 1);
+    const int p = __ldg(pos + row / heads);
+    uc[k] = __ldg(reinterpret_cast<const uint4*>(cos_t + static_cast<size_t>(p) * 128) + hl);
+    us[k] = __ldg(reinterpret_cast<const uint4*>(sin_t + static_cast<size_t>(p) * 128) + hl);
+  }
+  const uint4 uw = __ldg(reinterpret_cast<const uint4*>(w) + hl);
+  const uint32_t wv[4] = {uw.x, uw.y, uw.z, uw.w};
+  const uint32_t sign = (hl < 8) ? 0x80008000u : 0u;  // rotate_half = cat(-x2, x1)
 #pragma unroll
-  for (int e = 0; e < 8; ++e) v[e] = bf16r(wv[e] * bf16r(v[e] * rstd));
-  float pv[8];
+  for (int k = 0; k < kQkRows; ++k) {
+    const uint32_t xv[4] = {u[k].x, u[k].y, u[k].z, u[k].w};
+    float v[8];
 #pragma unroll
-  for (int e = 0; e < 8; ++e) pv[e] = __shfl_xor_sync(0xffffffffu, v[e], 8);
-  const long long tok = row / heads;
-  const int p = pos[tok];
-  const uint4 uc = reinterpret_cast<const uint4*>(cos_t + static_cast<size_t>(p) * 128)[hl];
-  const uint4 us = reinterpret_cast<const uint4*>(sin_t + static_cast<size_t>(p) * 128)[hl];
-  float c[8], s[8];
-  unpack_bf16x2(uc.x, c[0], c[1]);
-  unpack_bf16x2(uc.y, c[2], c[3]);
-  unpack_bf16x2(uc.z, c[4], c[5]);
-  unpack_bf16x2(uc.w, c[6], c[7]);
-  unpack_bf16x2(us.x, s[0], s[1]);
-  unpack_bf16x2(us.y, s[2], s[3]);
-  unpack_bf16x2(us.z, s[4], s[5]);
-  unpack_bf16x2(us.w, s[6], s[7]);
-  const float sign = (hl < 8) ? -1.0f : 1.0f;  // rotate_half = cat(-x2, x1)
-  float o[8];
+    for (int i = 0; i < 4; ++i) unpack_bf16x2(xv[i], v[2 * i], v[2 * i + 1]);
+    float ss = 0.0f;
 #pragma unroll
-  for (int e = 0; e < 8; ++e) o[e] = bf16r(bf16r(v[e] * c[e]) + bf16r(sign * pv[e] * s[e]));
-  if (active) {
-    uint4 r;
-    r.x = pack_bf16x2(o[0], o[1]);
-    r.y = pack_bf16x2(o[2], o[3]);
-    r.z = pack_bf16x2(o[4], o[5]);
-    r.w = pack_bf16x2(o[6], o[7]);
-    reinterpret_cast<uint4*>(y + row * 128)[hl] = r;
+    for (int e = 0; e < 8; ++e) ss = fmaf(v[e], v[e], ss);
+#pragma unroll
+    for (int o = 8; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    const float rstd = rsqrtf(ss * (1.0f / 128.0f) + eps);
+    uint32_t yv[4], pv[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+      yv[i] = as_u32(__hmul2_rn(as_bf2(wv[i]), __floats2bfloat162_rn(v[2 * i] * rstd, v[2 * i + 1] * rstd)));
+#pragma unroll
+    for (int i = 0; i < 4; ++i) pv[i] = __shfl_xor_sync(0xffffffffu, yv[i], 8) ^ sign;
+    const uint32_t cv[4] = {uc[k].x, uc[k].y, uc[k].z, uc[k].w};
+    const uint32_t sv[4] = {us[k].x, us[k].y, us[k].z, us[k].w};
+    uint32_t ov[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+      ov[i] = as_u32(__hadd2_rn(__hmul2_rn(as_bf2(yv[i]), as_bf2(cv[i])), __hmul2_rn(as_bf2(pv[i]), as_bf2(sv[i]))));
+    if (row0 + k < nrows)
+      __stcs(reinterpret_cast<uint4*>(y + static_cast<size_t>(row0 + k) * 128) + hl,
+             make_uint4(ov[0], ov[1], ov[2], ov[3]));
   }
 }
 
@@ -228,61 +233,80 @@ cudaError_t launch_qk_rmsnorm_rope(const __nv_bfloat16* x, __nv_bfloat16* y, con
                                    const int* pos, const __nv_bfloat16* cos_t,
                                    const __nv_bfloat16* sin_t, long long nrows, int heads,
                                    float eps, cudaStream_t stream) {
-  const long long threads = nrows * 16;
+  if (nrows <= 0 || nrows >= (1ll << 31) || heads <= 0) return cudaErrorInvalidValue;
+  const long long halves = (nrows + kQkRows - 1) / kQkRows;
   const int block = 256;
-  const long long grid = (threads + block - 1) / block;
-  qk_rmsnorm_rope_kernel<<<static_cast<unsigned>(grid), block, 0, stream>>>(x, y, w, pos, cos_t,
-                                                                           sin_t, nrows, heads, eps);
+  const long long grid = (halves * 16 + block - 1) / block;
+  qk_rmsnorm_rope_kernel<<<static_cast<unsigned>(grid), block, 0, stream>>>(
+      x, y, w, pos, cos_t, sin_t, static_cast<unsigned>(nrows), static_cast<unsigned>(heads), eps);
   return cudaGetLastError();
 }
 
 // ---------------------------------------------------------------------------------------------
 // SwiGLU activation: out[t, i] = bf16( bf16(silu(gate[t, i])) * up[t, i] ).
 // gate/up rows are `ld_in` elements apart (the fused [T, 2H] w12 output has gate at column 0
-// and up at column H); 8 elements per thread, grid-stride.
+// and up at column H).  One CTA row-slice: blockIdx.x is the row, blockIdx.y a slice of
+// 256 * kV 16-byte vectors; every load of a thread is issued before the arithmetic.  silu in
+// fp32 with the fast exponential and division intrinsics; the product of two bf16 values is
+// exact, so the packed bf16x2 multiply rounds it exactly like the reference's bf16 tensor op.
 // ---------------------------------------------------------------------------------------------
+template <int kV>
 __global__ void __launch_bounds__(256) swiglu_kernel(const __nv_bfloat16* __restrict__ gate,
                                                      const __nv_bfloat16* __restrict__ up,
-                                                     __nv_bfloat16* __restrict__ out,
-                                                     long long rows, int H, long long ld_in,
-                                                     long long ld_out) {
+                                                     __nv_bfloat16* __restrict__ out, int H,
+                                                     long long ld_in, long long ld_out) {
   const int vpr = H / 8;
-  const long long total = rows * vpr;
-  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
-       i += static_cast<long long>(gridDim.x) * blockDim.x) {
-    const long long r = i / vpr;
-    const int c = static_cast<int>(i - r * vpr);
-    const uint4 ug = reinterpret_cast<const uint4*>(gate + r * ld_in)[c];
-    const uint4 uu = reinterpret_cast<const uint4*>(up + r * ld_in)[c];
-    float g[8], u[8], o[8];
-    unpack_bf16x2(ug.x, g[0], g[1]);
-    unpack_bf16x2(ug.y, g[2], g[3]);
-    unpack_bf16x2(ug.z, g[4], g[5]);
-    unpack_bf16x2(ug.w, g[6], g[7]);
-    unpack_bf16x2(uu.x, u[0], u[1]);
-    unpack_bf16x2(uu.y, u[2], u[3]);
-    unpack_bf16x2(uu.z, u[4], u[5]);
-    unpack_bf16x2(uu.w, u[6], u[7]);
+  const size_t r = blockIdx.x;
+  const int c0 = blockIdx.y * (256 * kV) + threadIdx.x;
+  const uint4* g4 = reinterpret_cast<const uint4*>(gate + r * ld_in);
+  const uint4* u4 = reinterpret_cast<const uint4*>(up + r * ld_in);
+  uint4* o4 = reinterpret_cast<uint4*>(out + r * ld_out);
+  uint4 ug[kV], uu[kV];
 #pragma unroll
-    for (int e = 0; e < 8; ++e) o[e] = bf16r(bf16r(g[e] / (1.0f + expf(-g[e]))) * u[e]);
-    uint4 res;
-    res.x = pack_bf16x2(o[0], o[1]);
-    res.y = pack_bf16x2(o[2], o[3]);
-    res.z = pack_bf16x2(o[4], o[5]);
-    res.w = pack_bf16x2(o[6], o[7]);
-    reinterpret_cast<uint4*>(out + r * ld_out)[c] = res;
+  for (int j = 0; j < kV; ++j) {
+    const int c = c0 + 256 * j;
+    if (c < vpr) {
+      ug[j] = __ldcs(g4 + c);
+      uu[j] = __ldcs(u4 + c);
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < kV; ++j) {
+    const int c = c0 + 256 * j;
+    if (c < vpr) {
+      const uint32_t gv[4] = {ug[j].x, ug[j].y, ug[j].z, ug[j].w};
+      const uint32_t uv[4] = {uu[j].x, uu[j].y, uu[j].z, uu[j].w};
+      uint32_t ov[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        float a, b;
+        unpack_bf16x2(gv[i], a, b);
+        const __nv_bfloat162 s =
+            __floats2bfloat162_rn(__fdividef(a, 1.0f + __expf(-a)), __fdividef(b, 1.0f + __expf(-b)));
+        ov[i] = as_u32(__hmul2_rn(s, as_bf2(uv[i])));
+      }
+      __stcs(o4 + c, make_uint4(ov[0], ov[1], ov[2], ov[3]));
+    }
   }
 }
 
 cudaError_t launch_swiglu(const __nv_bfloat16* gate, const __nv_bfloat16* up, __nv_bfloat16* out,
                           long long rows, int H, long long ld_in, long long ld_out, int sms,
                           cudaStream_t stream) {
-  const long long total = rows * (H / 8);
-  long long grid = (total + 255) / 256;
-  const long long cap = static_cast<long long>(sms) * 8;
-  if (grid > cap) grid = cap;
-  swiglu_kernel<<<static_cast<unsigned>(grid), 256, 0, stream>>>(gate, up, out, rows, H, ld_in,
-                                                                  ld_out);
+  (void)sms;
+  if (rows <= 0 || rows >= (1ll << 31) || H <= 0) return cudaErrorInvalidValue;
+  const int vpr = H / 8;
+  int v = 1;
+  while (v < 8 && 256 * v < vpr) v *= 2;
+  const int slices = (vpr + 256 * v - 1) / (256 * v);
+  if (slices > 65535) return cudaErrorInvalidValue;
+  const dim3 grid(static_cast<unsigned>(rows), static_cast<unsigned>(slices));
+  switch (v) {
+    case 1: swiglu_kernel<1><<<grid, 256, 0, stream>>>(gate, up, out, H, ld_in, ld_out); break;
+    case 2: swiglu_kernel<2><<<grid, 256, 0, stream>>>(gate, up, out, H, ld_in, ld_out); break;
+    case 4: swiglu_kernel<4><<<grid, 256, 0, stream>>>(gate, up, out, H, ld_in, ld_out); break;
+    default: swiglu_kernel<8><<<grid, 256, 0, stream>>>(gate, up, out, H, ld_in, ld_out); break;
+  }
   return cudaGetLastError();
 }
 
