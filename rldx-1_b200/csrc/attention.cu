@@ -192,15 +192,20 @@ __global__ void __launch_bounds__(kAttnThreads, 1) joint_attention_kernel(const 
       __syncwarp();
       if (lane == 0) mbar_arrive(&s_empty[sb]);
 
-      // scale, mask, row max (four independent chains); the key mask, when there is one, is
-      // read as 64 bytes once per tile, so the per-element work stays branch-free
+      // mask, row max of the raw scores (four independent chains; the scale is positive, so it
+      // is applied to the max and folded into the exponent's fma).  Tiles wholly inside the
+      // sequence without a key mask skip the masking; the key mask, when there is one, is read
+      // as 64 bytes once per tile, so the per-element work stays branch-free.
       const int kbase = j * 64;
       const int nvis = L - kbase;  // keys of this tile inside the sequence
       float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
-      if (kmask == nullptr) {
+      if (kmask == nullptr && nvis >= 64) {
+#pragma unroll
+        for (int c = 0; c < 64; ++c) mx4[c & 3] = fmaxf(mx4[c & 3], sv[c]);
+      } else if (kmask == nullptr) {
 #pragma unroll
         for (int c = 0; c < 64; ++c) {
-          sv[c] = (c < nvis) ? sv[c] * scale : -INFINITY;
+          sv[c] = (c < nvis) ? sv[c] : -INFINITY;
           mx4[c & 3] = fmaxf(mx4[c & 3], sv[c]);
         }
       } else {
@@ -210,17 +215,17 @@ __global__ void __launch_bounds__(kAttnThreads, 1) joint_attention_kernel(const 
           if (c < nvis && kmask[kbase + c] != 0) mbits[c >> 5] |= 1u << (c & 31);
 #pragma unroll
         for (int c = 0; c < 64; ++c) {
-          sv[c] = ((mbits[c >> 5] >> (c & 31)) & 1u) ? sv[c] * scale : -INFINITY;
+          sv[c] = ((mbits[c >> 5] >> (c & 31)) & 1u) ? sv[c] : -INFINITY;
           mx4[c & 3] = fmaxf(mx4[c & 3], sv[c]);
         }
       }
-      const float mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3]));
+      const float mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3])) * scale;
 
       // lazy rescale of O and l when this row's max outgrows the reference by 2^8
       const bool grow = mx > m_ref + kRescaleLog2;
       float alpha = 1.0f;
       if (grow) {
-        alpha = (m_ref == -INFINITY) ? 0.0f : exp2f(m_ref - mx);
+        alpha = (m_ref == -INFINITY) ? 0.0f : ex2_approx(m_ref - mx);
         m_ref = mx;
         l_run *= alpha;
       }
@@ -244,7 +249,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1) joint_attention_kernel(const 
       float ps4[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
       for (int c = 0; c < 64; ++c) {
-        sv[c] = exp2f(sv[c] - m_use);
+        sv[c] = ex2_approx(fmaf(sv[c], scale, -m_use));
         ps4[c & 3] += sv[c];
       }
       l_run += (ps4[0] + ps4[1]) + (ps4[2] + ps4[3]);
