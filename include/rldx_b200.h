@@ -130,10 +130,12 @@ int rldx_gemm_static_ws(const rldx_gemm_desc* problems, int nproblems, void* str
  *   q, k  [B, H, L, head_dim] bf16;  vt [B, H, head_dim, Lp] bf16 (Lp >= L, Lp % 8 == 0)
  *   key_mask [B, L] uint8 (1 = attend) or NULL
  *   out[s] [B * seg_len[s], H*head_dim] bf16, nseg in 1..3, sum(seg_len) == L
+ *   tiles_per_cta: 128-query tiles per CTA, 1 or 2 (two softmax warpgroups sharing each K / V
+ *   tile), 0 = chosen from the grid size
  * ------------------------------------------------------------------------------------------ */
 int rldx_joint_attention(const void* q, const void* k, const void* vt, int B, int H, int L, int Lp,
                          int head_dim, const uint8_t* key_mask, void* const* out, const int* seg_len,
-                         int nseg, void* stream);
+                         int nseg, int tiles_per_cta, void* stream);
 
 /* ------------------------------------------------------------------------------------------
  * LayerNorm without affine (eps) over rows of width D (D % 8 == 0, D <= 4096), optionally

@@ -126,7 +126,7 @@ SIGNATURES = {
     "rldx_gemm_ws": (C.c_int, [C.POINTER(GemmDesc), C.c_int, vp, C.c_uint64, vp]),
     "rldx_gemm_static_ws": (C.c_int, [C.POINTER(GemmDesc), C.c_int, vp]),
     "rldx_joint_attention": (C.c_int, [vp, vp, vp, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, vp,
-                                       C.POINTER(vp), C.POINTER(C.c_int), C.c_int, vp]),
+                                       C.POINTER(vp), C.POINTER(C.c_int), C.c_int, C.c_int, vp]),
     "rldx_layernorm": (C.c_int, [vp, i64, vp, i64, C.c_int, C.c_int, C.c_float, vp, vp, vp]),
     "rldx_qk_rmsnorm_rope": (C.c_int, [vp, vp, vp, vp, vp, vp, i64, C.c_int, C.c_int,
                                        C.c_float, vp]),

@@ -636,7 +636,7 @@ using namespace rldx;
 
 extern "C" {
 
-int rldx_version(void) { return 103; }
+int rldx_version(void) { return 104; }
 
 const char* rldx_last_error(void) { return t_last_error.c_str(); }
 
@@ -703,13 +703,14 @@ int rldx_gemm_ws(const rldx_gemm_desc* problems, int nproblems, void* workspace,
 
 int rldx_joint_attention(const void* q, const void* k, const void* vt, int B, int H, int L, int Lp,
                          int head_dim, const uint8_t* key_mask, void* const* out, const int* seg_len,
-                         int nseg, void* stream) {
+                         int nseg, int tiles_per_cta, void* stream) {
   int rc = ensure_device();
   if (rc != RLDX_OK) return rc;
   if (!q || !k || !vt || !out || !seg_len) return set_error(RLDX_ERR_ARG, "attention: null pointer");
   if (B <= 0 || H <= 0 || L <= 0 || Lp < L || Lp % 8 != 0)
     return set_error(RLDX_ERR_ARG, "attention: need B, H, L > 0, Lp >= L, Lp % 8 == 0");
   if (head_dim != 64 && head_dim != 128) return set_error(RLDX_ERR_UNSUPPORTED, "attention: head_dim must be 64 or 128");
+  if (tiles_per_cta < 0 || tiles_per_cta > 2) return set_error(RLDX_ERR_ARG, "attention: tiles_per_cta must be 0, 1 or 2");
   if (nseg < 1 || nseg > 3) return set_error(RLDX_ERR_ARG, "attention: nseg must be 1..3");
   if (!aligned16(q) || !aligned16(k) || !aligned16(vt))
     return set_error(RLDX_ERR_ARG, "attention: q/k/vt must be 16-byte aligned");
@@ -730,6 +731,7 @@ int rldx_joint_attention(const void* q, const void* k, const void* vt, int B, in
   p.B = B;
   p.key_mask = key_mask;
   p.head_dim = head_dim;
+  p.tiles_per_cta = tiles_per_cta;
   p.scale_log2 = 1.4426950408889634f / std::sqrt(static_cast<float>(head_dim));
   std::string err;
   const uint64_t bh = static_cast<uint64_t>(B) * H;

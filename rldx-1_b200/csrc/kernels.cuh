@@ -17,7 +17,9 @@ struct AttnParams {
   int nseg;
   float scale_log2;  // log2(e) / sqrt(head_dim)
   int head_dim;      // 64 or 128 (0: 64)
+  int tiles_per_cta; // 128-query tiles per CTA: 1, 2, or 0 = chosen from the grid size
 };
+int attention_tiles_per_cta(const AttnParams& p, int sms);
 size_t attention_smem_bytes(int head_dim);
 cudaError_t attention_prepare_device();
 cudaError_t launch_attention(const AttnParams& p, cudaStream_t stream, bool pdl);

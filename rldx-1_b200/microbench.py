@@ -100,7 +100,8 @@ def suite_c3(iters: int, warmup: int):
            "frac": nbytes / ms / 1e6 / hbm, "peak_source": src, "l2": "operands 1.17 GB each > L2"}
 
 
-def suite_c4(iters: int, warmup: int, batches=(1, 4, 16, 64), lengths=(288, 544, 1056, 2080, 4128)):
+def suite_c4(iters: int, warmup: int, batches=(1, 4, 16, 64), lengths=(288, 544, 1056, 2080, 4128),
+             tiles: int = 0):
     dev = torch.device("cuda", torch.cuda.current_device())
     _, tflops, src = peaks()
     H, hd = 16, 128
@@ -115,12 +116,12 @@ def suite_c4(iters: int, warmup: int, batches=(1, 4, 16, 64), lengths=(288, 544,
             vt = torch.zeros(B, H, hd, Lp, dtype=BF, device=dev)
             vt[..., :L] = v.transpose(-1, -2)
             outs = [torch.empty(B * n, H * hd, dtype=BF, device=dev) for n in segs]
-            ms = time_ms(lambda: ops.joint_attention(q, k, vt, segs, outs=outs), iters, warmup)
+            ms = time_ms(lambda: ops.joint_attention(q, k, vt, segs, outs=outs, tiles_per_cta=tiles), iters, warmup)
             ms_sdpa = time_ms(lambda: F.scaled_dot_product_attention(q, k, v), iters, warmup)
             flops = 4.0 * B * H * L * L * hd
             resident = 4 * q.numel() * 2 < 100e6
             yield {"suite": "c4", "kernel": "joint_attention_kernel<128>", "L": L, "B": B, "H": H, "head_dim": hd,
-                   "segments": segs, "ms": ms, "flops": flops, "tflops": flops / ms / 1e9,
+                   "segments": segs, "tiles_per_cta": tiles or "auto", "ms": ms, "flops": flops, "tflops": flops / ms / 1e9,
                    "peak_tflops": tflops, "frac": flops / ms / 1e9 / tflops, "peak_source": src,
                    "torch_sdpa_ms": ms_sdpa, "l2": "q/k/v/out L2-resident" if resident else "q/k/v/out > L2"}
             del q, k, v, vt, outs
@@ -133,6 +134,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--batches", type=str, default="1,4,16,64")
     ap.add_argument("--lengths", type=str, default="288,544,1056,2080,4128")
+    ap.add_argument("--tiles", type=int, default=0, help="query tiles per attention CTA (0: automatic)")
     a = ap.parse_args()
     if not torch.cuda.is_available():
         raise SystemExit("microbench needs a CUDA device")
@@ -142,7 +144,7 @@ def main():
     if a.suite in ("c4", "all"):
         bs = tuple(int(x) for x in a.batches.split(","))
         ls = tuple(int(x) for x in a.lengths.split(","))
-        for r in suite_c4(a.iters, a.warmup, bs, ls):
+        for r in suite_c4(a.iters, a.warmup, bs, ls, a.tiles):
             print(json.dumps(r), flush=True)
     assert ops.device_error() == 0, "device error flag set"
 

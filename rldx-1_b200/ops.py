@@ -143,7 +143,7 @@ def qkv_desc(x, weight, bias, q_norm, k_norm, rope_cos, rope_sin, q, k, vt, *, t
     return d
 
 
-def joint_attention(q, k, vt, seg_lens: Sequence[int], key_mask=None, outs=None):
+def joint_attention(q, k, vt, seg_lens: Sequence[int], key_mask=None, outs=None, tiles_per_cta: int = 0):
     """Non-causal joint attention over concatenated segments (q, k [B, H, L, d], vt [B, H, d, Lp],
     d = 64 or 128); returns one output per segment as [B * seg_len, H * d]."""
     for t, n in ((q, "q"), (k, "k"), (vt, "vt")):
@@ -159,7 +159,7 @@ def joint_attention(q, k, vt, seg_lens: Sequence[int], key_mask=None, outs=None)
     if key_mask is not None:
         _need(key_mask, "key_mask", torch.uint8)
     check(load().rldx_joint_attention(_p(q), _p(k), _p(vt), B, H, L, Lp, hd, _p(key_mask), ptrs, lens,
-                                      len(seg_lens), _stream()))
+                                      len(seg_lens), tiles_per_cta, _stream()))
     return outs
 
 

@@ -11,7 +11,7 @@ from rldx_b200 import ops  # noqa: E402
 BF = torch.bfloat16
 
 
-def run_case(cuda, B, H, segs, mask=False, seed=0, hd=64):
+def run_case(cuda, B, H, segs, mask=False, seed=0, hd=64, tiles=0):
     L = sum(segs)
     Lp = (L + 7) // 8 * 8
     g = torch.Generator(device=cuda).manual_seed(seed)
@@ -26,7 +26,7 @@ def run_case(cuda, B, H, segs, mask=False, seed=0, hd=64):
         key_mask = (torch.rand(B, L, device=cuda, generator=g) > 0.3).to(torch.uint8)
         key_mask[:, segs[0]:] = 1  # the action stream is always visible (blocks.py:852)
         bias = torch.where(key_mask.bool(), 0.0, float("-inf"))[:, None, None, :]
-    outs = ops.joint_attention(q, k, vt, segs, key_mask=key_mask)
+    outs = ops.joint_attention(q, k, vt, segs, key_mask=key_mask, tiles_per_cta=tiles)
     torch.cuda.synchronize()
     s = (q.float() @ k.float().transpose(-1, -2)) / hd ** 0.5 + bias
     ref = torch.softmax(s, dim=-1) @ v.float()  # [B, H, L, hd]
@@ -63,3 +63,15 @@ def test_joint_attention_head_dim_128(cuda, segs):
 
 def test_joint_attention_head_dim_128_key_mask(cuda):
     run_case(cuda, 2, 4, [200, 32, 16], mask=True, seed=3, hd=128)
+
+
+@pytest.mark.parametrize("hd", [64, 128])
+@pytest.mark.parametrize("segs", [[1], [100, 28], [129], [200, 18, 32], [256], [300, 30, 20], [512, 18, 32]])
+def test_joint_attention_two_tiles_per_cta(cuda, hd, segs):
+    """Two 128-query tiles per CTA (two softmax warpgroups), including a last CTA whose second
+    tile lies wholly past L."""
+    run_case(cuda, 2, 3, segs, seed=hd + sum(segs), hd=hd, tiles=2)
+
+
+def test_joint_attention_two_tiles_key_mask(cuda):
+    run_case(cuda, 2, 4, [300, 18, 32], mask=True, seed=5, tiles=2)
