@@ -138,6 +138,80 @@ int rldx_joint_attention(const void* q, const void* k, const void* vt, int B, in
                          int nseg, int tiles_per_cta, void* stream);
 
 /* ------------------------------------------------------------------------------------------
+ * QKV preparation of the joint attention from projected [q | k | v] rows: per-head QK RMSNorm
+ * (norms.py:18-22) and interleaved-pair RoPE (ops.py:48-67) into q, k [B, H, L, 64] and
+ * V^T [B, H, 64, Lp].  The RMSNorm + RoPE half of ds::fused_attention_2way / _3way
+ * (rldx/inference/action_model/double_stream/engine/ops/op_fused_attention.py:12-92,
+ * op_fused_attention_3way.py:13-116) and ss::fused_attention_2way / _3way
+ * (single_stream/engine/ops/op_fused_attention.py:12-80, op_fused_attention_3way.py:13-110);
+ * rldx_joint_attention does the SDPA half.
+ *   segments in joint-sequence order (1..3), rows summing to L; qkv rows 3*H*64 wide,
+ *   ld % 8 == 0, 16-byte aligned; rope tables [rows - rope_from, 32] fp32 for the segment's
+ *   rows from rope_from on (rope_cos NULL: no rotation), as the reference ops' per-stream
+ *   tables; batch b of a segment starts batch_stride elements after batch b-1.
+ * ------------------------------------------------------------------------------------------ */
+typedef struct {
+  const void* qkv;
+  int64_t ld;
+  int64_t batch_stride;
+  int rows;
+  int rope_from;
+  const void* q_norm; /* [64] bf16 */
+  const void* k_norm; /* [64] bf16 */
+  const float* rope_cos;
+  const float* rope_sin;
+} rldx_qkv_segment;
+
+int rldx_qkv_prep(const rldx_qkv_segment* segs, int nseg, int B, int H, int L, int Lp, float eps,
+                  void* q, void* k, void* vt, void* stream);
+
+/* ------------------------------------------------------------------------------------------
+ * Residual sums + LayerNorm (no affine) over up to 2 row groups in one launch:
+ *   sum = x (+ y) (+ v1) (+ v2), rows x, y [rows, D] with row stride ld, vectors v1, v2 [D];
+ *   fp32_sum 0: bf16 rounding after each add in the order x, v1, v2, y -- ds::vl_epilogue_ln
+ *     (rldx/inference/action_model/double_stream/engine/ops/op_vl_epilogue_ln.py:13-38,
+ *     new = res + proj_bias + w3_bias + w3_out) and ss::fused_epilogue_ln
+ *     (single_stream/engine/ops/op_fused_epilogue_ln.py:11-30, new = hidden + residual);
+ *   fp32_sum 1: one fp32 sum x + y + v1 + v2 -- ds::grouped_res_ln
+ *     (double_stream/engine/ops/op_grouped_res_ln.py:12-45, LN(res + proj + bias)).
+ *   sum_out (optional) = bf16(sum); ln_out = LN(sum) in fp32, rounded once.  D % 8 == 0,
+ *   D <= 4096, every pointer 16-byte aligned, ld % 8 == 0.
+ * ------------------------------------------------------------------------------------------ */
+typedef struct {
+  const void* x;
+  const void* y;  /* optional */
+  const void* v1; /* optional [D] */
+  const void* v2; /* optional [D] */
+  void* sum_out;  /* optional */
+  void* ln_out;
+  int rows;
+  int D;
+  int64_t ld;
+} rldx_res_ln_segment;
+
+int rldx_res_layernorm(const rldx_res_ln_segment* segs, int nseg, int fp32_sum, float eps, void* stream);
+
+/* ------------------------------------------------------------------------------------------
+ * Bias + SwiGLU over up to 2 row groups, all in fp32 with one rounding:
+ * out = bf16( silu(gate + bias_gate) * (up + bias_up) ) -- ds::grouped_swiglu
+ * (rldx/inference/action_model/double_stream/engine/ops/op_grouped_swiglu.py:12-41 on the
+ * [gate | up] halves of an un-biased w12 output).  H % 8 == 0, 16-byte aligned rows.
+ * ------------------------------------------------------------------------------------------ */
+typedef struct {
+  const void* gate;
+  const void* up;
+  const void* bias_gate; /* [H] */
+  const void* bias_up;   /* [H] */
+  void* out;
+  int64_t ld_in;
+  int64_t ld_out;
+  int rows;
+  int H;
+} rldx_swiglu_bias_segment;
+
+int rldx_swiglu_bias(const rldx_swiglu_bias_segment* segs, int nseg, void* stream);
+
+/* ------------------------------------------------------------------------------------------
  * LayerNorm without affine (eps) over rows of width D (D % 8 == 0, D <= 4096), optionally
  * followed by y * scale1p + shift (AdaLN-zero output projection, both bf16 [D]).
  * Replaces nn.LayerNorm(elementwise_affine=False) (rldx/model/modules/norms.py:35-36), the LN of

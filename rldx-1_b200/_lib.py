@@ -109,6 +109,22 @@ class OpProfile(C.Structure):
                 ("flops", C.c_double)]
 
 
+class QkvSegment(C.Structure):
+    _fields_ = [("qkv", vp), ("ld", i64), ("batch_stride", i64), ("rows", C.c_int),
+                ("rope_from", C.c_int), ("q_norm", vp), ("k_norm", vp), ("rope_cos", vp),
+                ("rope_sin", vp)]
+
+
+class ResLnSegment(C.Structure):
+    _fields_ = [("x", vp), ("y", vp), ("v1", vp), ("v2", vp), ("sum_out", vp), ("ln_out", vp),
+                ("rows", C.c_int), ("D", C.c_int), ("ld", i64)]
+
+
+class SwigluBiasSegment(C.Structure):
+    _fields_ = [("gate", vp), ("up", vp), ("bias_gate", vp), ("bias_up", vp), ("out", vp),
+                ("ld_in", i64), ("ld_out", i64), ("rows", C.c_int), ("H", C.c_int)]
+
+
 class MsatIO(C.Structure):
     _fields_ = [("vl", vp), ("state", vp), ("emb_id", vp), ("init_noise", vp),
                 ("physics_hist", vp), ("physics_noise", vp), ("actions", vp),
@@ -128,6 +144,10 @@ SIGNATURES = {
     "rldx_joint_attention": (C.c_int, [vp, vp, vp, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, vp,
                                        C.POINTER(vp), C.POINTER(C.c_int), C.c_int, C.c_int, vp]),
     "rldx_layernorm": (C.c_int, [vp, i64, vp, i64, C.c_int, C.c_int, C.c_float, vp, vp, vp]),
+    "rldx_qkv_prep": (C.c_int, [C.POINTER(QkvSegment), C.c_int, C.c_int, C.c_int, C.c_int, C.c_int,
+                                C.c_float, vp, vp, vp, vp]),
+    "rldx_res_layernorm": (C.c_int, [C.POINTER(ResLnSegment), C.c_int, C.c_int, C.c_float, vp]),
+    "rldx_swiglu_bias": (C.c_int, [C.POINTER(SwigluBiasSegment), C.c_int, vp]),
     "rldx_qk_rmsnorm_rope": (C.c_int, [vp, vp, vp, vp, vp, vp, i64, C.c_int, C.c_int,
                                        C.c_float, vp]),
     "rldx_swiglu": (C.c_int, [vp, vp, i64, vp, i64, i64, C.c_int, vp]),

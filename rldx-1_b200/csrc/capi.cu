@@ -636,7 +636,7 @@ using namespace rldx;
 
 extern "C" {
 
-int rldx_version(void) { return 104; }
+int rldx_version(void) { return 106; }
 
 const char* rldx_last_error(void) { return t_last_error.c_str(); }
 
@@ -744,6 +744,119 @@ int rldx_joint_attention(const void* q, const void* k, const void* vt, int B, in
     return set_error(RLDX_ERR_ARG, err);
   cudaError_t e = launch_attention(p, static_cast<cudaStream_t>(stream), false);
   if (e != cudaSuccess) return cuda_fail(e, "attention launch");
+  return RLDX_OK;
+}
+
+int rldx_qkv_prep(const rldx_qkv_segment* segs, int nseg, int B, int H, int L, int Lp, float eps,
+                  void* q, void* k, void* vt, void* stream) {
+  int rc = ensure_device();
+  if (rc != RLDX_OK) return rc;
+  if (!segs || !q || !k || !vt) return set_error(RLDX_ERR_ARG, "qkv_prep: null pointer");
+  if (nseg < 1 || nseg > 3 || B <= 0 || H <= 0 || L <= 0 || Lp < L || Lp % 8 != 0)
+    return set_error(RLDX_ERR_ARG, "qkv_prep: need 1..3 segments, B, H, L > 0, Lp >= L, Lp % 8 == 0");
+  if (!aligned16(q) || !aligned16(k) || !aligned16(vt)) return set_error(RLDX_ERR_ARG, "qkv_prep: q/k/vt must be 16-byte aligned");
+  QkvPrepParams p;
+  std::memset(&p, 0, sizeof(p));
+  int sum = 0;
+  for (int i = 0; i < nseg; ++i) {
+    const rldx_qkv_segment& s = segs[i];
+    if (!s.qkv || !s.q_norm || !s.k_norm || s.rows <= 0 || s.ld < 3LL * H * 64 || s.ld % 8 != 0 ||
+        !aligned16(s.qkv) || s.rope_from < 0 || (s.rope_cos != nullptr) != (s.rope_sin != nullptr) ||
+        (B > 1 && s.batch_stride < static_cast<int64_t>(s.rows) * s.ld))
+      return set_error(RLDX_ERR_ARG, "qkv_prep: bad segment");
+    p.seg[i].qkv = static_cast<const __nv_bfloat16*>(s.qkv);
+    p.seg[i].ld = s.ld;
+    p.seg[i].batch_stride = s.batch_stride;
+    p.seg[i].rows = s.rows;
+    p.seg[i].rope_from = s.rope_from;
+    p.seg[i].qn = static_cast<const __nv_bfloat16*>(s.q_norm);
+    p.seg[i].kn = static_cast<const __nv_bfloat16*>(s.k_norm);
+    p.seg[i].cos = s.rope_cos;
+    p.seg[i].sin = s.rope_sin;
+    sum += s.rows;
+  }
+  if (sum != L) return set_error(RLDX_ERR_ARG, "qkv_prep: segment rows must sum to L");
+  p.nseg = nseg;
+  p.B = B;
+  p.H = H;
+  p.L = L;
+  p.Lp = Lp;
+  p.eps = eps;
+  p.q = static_cast<__nv_bfloat16*>(q);
+  p.k = static_cast<__nv_bfloat16*>(k);
+  p.vt = static_cast<__nv_bfloat16*>(vt);
+  cudaError_t e = launch_qkv_prep(p, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "qkv_prep launch");
+  return RLDX_OK;
+}
+
+int rldx_res_layernorm(const rldx_res_ln_segment* segs, int nseg, int fp32_sum, float eps, void* stream) {
+  int rc = ensure_device();
+  if (rc != RLDX_OK) return rc;
+  if (!segs || nseg < 1 || nseg > 2) return set_error(RLDX_ERR_ARG, "res_layernorm: need 1 or 2 segments");
+  ResLnParams p;
+  std::memset(&p, 0, sizeof(p));
+  int row = 0;
+  for (int i = 0; i < nseg; ++i) {
+    const rldx_res_ln_segment& s = segs[i];
+    if (!s.x || !s.ln_out || s.rows <= 0 || s.D <= 0 || s.D % 8 || s.D > 4096 || s.ld < s.D || s.ld % 8 ||
+        !aligned16(s.x) || !aligned16(s.ln_out) || (s.y && !aligned16(s.y)) || (s.v1 && !aligned16(s.v1)) ||
+        (s.v2 && !aligned16(s.v2)) || (s.sum_out && !aligned16(s.sum_out)))
+      return set_error(RLDX_ERR_ARG, "res_layernorm: bad segment (D % 8, D <= 4096, 16-byte aligned rows)");
+    ResLnSeg& d = p.seg[i];
+    d.x = static_cast<const __nv_bfloat16*>(s.x);
+    d.y = static_cast<const __nv_bfloat16*>(s.y);
+    d.v1 = static_cast<const __nv_bfloat16*>(s.v1);
+    d.v2 = static_cast<const __nv_bfloat16*>(s.v2);
+    d.sum_out = static_cast<__nv_bfloat16*>(s.sum_out);
+    d.ln_out = static_cast<__nv_bfloat16*>(s.ln_out);
+    d.rows = s.rows;
+    d.D = s.D;
+    d.ld = static_cast<int>(s.ld);
+    d.row_begin = row;
+    row += s.rows;
+    p.dmax = std::max(p.dmax, s.D);
+  }
+  p.nseg = nseg;
+  p.total_rows = row;
+  p.fp32_sum = fp32_sum ? 1 : 0;
+  p.eps = eps;
+  cudaError_t e = launch_res_ln(p, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "res_layernorm launch");
+  return RLDX_OK;
+}
+
+int rldx_swiglu_bias(const rldx_swiglu_bias_segment* segs, int nseg, void* stream) {
+  int rc = ensure_device();
+  if (rc != RLDX_OK) return rc;
+  if (!segs || nseg < 1 || nseg > 2) return set_error(RLDX_ERR_ARG, "swiglu_bias: need 1 or 2 segments");
+  SwigluBiasParams p;
+  std::memset(&p, 0, sizeof(p));
+  int row = 0;
+  for (int i = 0; i < nseg; ++i) {
+    const rldx_swiglu_bias_segment& s = segs[i];
+    if (!s.gate || !s.up || !s.bias_gate || !s.bias_up || !s.out || s.rows <= 0 || s.H <= 0 || s.H % 8 ||
+        s.ld_in % 8 || s.ld_out % 8 || !aligned16(s.gate) || !aligned16(s.up) || !aligned16(s.bias_gate) ||
+        !aligned16(s.bias_up) || !aligned16(s.out))
+      return set_error(RLDX_ERR_ARG, "swiglu_bias: bad segment (H % 8, 16-byte aligned rows)");
+    SwigluBiasSeg& d = p.seg[i];
+    d.gate = static_cast<const __nv_bfloat16*>(s.gate);
+    d.up = static_cast<const __nv_bfloat16*>(s.up);
+    d.bg = static_cast<const __nv_bfloat16*>(s.bias_gate);
+    d.bu = static_cast<const __nv_bfloat16*>(s.bias_up);
+    d.out = static_cast<__nv_bfloat16*>(s.out);
+    d.ld_in = s.ld_in;
+    d.ld_out = s.ld_out;
+    d.rows = s.rows;
+    d.H = s.H;
+    d.row_begin = row;
+    row += s.rows;
+    p.hmax = std::max(p.hmax, s.H);
+  }
+  p.nseg = nseg;
+  p.total_rows = row;
+  cudaError_t e = launch_swiglu_bias(p, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "swiglu_bias launch");
   return RLDX_OK;
 }
 

@@ -68,6 +68,66 @@ cudaError_t launch_swiglu(const __nv_bfloat16* gate, const __nv_bfloat16* up, __
                           long long rows, int H, long long ld_in, long long ld_out, int sms,
                           cudaStream_t stream);
 
+// ---- residual sums + LayerNorm, bias + SwiGLU (rownorm.cu): the reference's epilogue ops ----
+// sum = x (+ y) (+ v1) (+ v2): rows x, y [rows, D] (row stride ld), vectors v1, v2 [D];
+// fp32_sum = 0: bf16 rounding after each add in the order x, v1, v2, y (eager order of
+// ds::vl_epilogue_ln / ss::fused_epilogue_ln); 1: one fp32 sum in the order x, y, v1, v2 with no
+// rounding (ds::grouped_res_ln).  sum_out (optional) gets bf16(sum); ln_out = LN(sum).
+struct ResLnSeg {
+  const __nv_bfloat16* x;
+  const __nv_bfloat16* y;
+  const __nv_bfloat16* v1;
+  const __nv_bfloat16* v2;
+  __nv_bfloat16* sum_out;
+  __nv_bfloat16* ln_out;
+  int rows, D, ld, row_begin;
+};
+struct ResLnParams {
+  ResLnSeg seg[2];
+  int nseg, total_rows, dmax, fp32_sum;
+  float eps;
+};
+cudaError_t launch_res_ln(const ResLnParams& p, cudaStream_t stream);
+
+// out = bf16( silu(gate + bg) * (up + bu) ) in fp32 (ds::grouped_swiglu), up to 2 segments.
+struct SwigluBiasSeg {
+  const __nv_bfloat16* gate;
+  const __nv_bfloat16* up;
+  const __nv_bfloat16* bg;
+  const __nv_bfloat16* bu;
+  __nv_bfloat16* out;
+  long long ld_in, ld_out;
+  int rows, H, row_begin;
+};
+struct SwigluBiasParams {
+  SwigluBiasSeg seg[2];
+  int nseg, total_rows, hmax;
+};
+cudaError_t launch_swiglu_bias(const SwigluBiasParams& p, cudaStream_t stream);
+
+// ---- QKV preparation of the joint attention (rownorm.cu) ----
+// Segments of the joint sequence, in order: rows of [q | k | v] (3*H*64 wide, row stride ld),
+// per-segment QK RMSNorm weights and RoPE tables ([rows - rope_from, 32] fp32 cos / sin for the
+// segment's rows from rope_from on; null cos: no rotation).
+struct QkvPrepSeg {
+  const __nv_bfloat16* qkv;
+  long long ld, batch_stride;  // elements
+  int rows, rope_from;
+  const __nv_bfloat16* qn;
+  const __nv_bfloat16* kn;
+  const float* cos;
+  const float* sin;
+};
+struct QkvPrepParams {
+  QkvPrepSeg seg[3];
+  int nseg, B, H, L, Lp;
+  float eps;
+  __nv_bfloat16* q;   // [B, H, L, 64]
+  __nv_bfloat16* k;   // [B, H, L, 64]
+  __nv_bfloat16* vt;  // [B, H, 64, Lp]
+};
+cudaError_t launch_qkv_prep(const QkvPrepParams& p, cudaStream_t stream);
+
 // ---- bind-time helpers (relayout.cu) ----
 // dst[i, :] = src[idx[i], :] for rows of `cols` bf16 (row gather).
 cudaError_t launch_gather_rows(const __nv_bfloat16* src, long long ld_src, __nv_bfloat16* dst,

@@ -9,6 +9,8 @@
 //   qk_rmsnorm_rope_kernel  Qwen3-style per-head RMSNorm (cast, then weight) + rotate-half RoPE,
 //                         modeling_qwen3_vl.py:118-122, 357-371, 377-401 (backbone path).
 //   swiglu_kernel         silu(gate) * up, rldx/model/modules/action_model/ops.py:157-161.
+//   res_ln_kernel, swiglu_bias_kernel, qkv_prep_kernel  the op-level epilogue / preparation
+//                         steps of the reference's ds:: and ss:: custom ops (see each kernel).
 #include "kernels.cuh"
 
 namespace rldx {
@@ -307,6 +309,224 @@ cudaError_t launch_swiglu(const __nv_bfloat16* gate, const __nv_bfloat16* up, __
     case 4: swiglu_kernel<4><<<grid, 256, 0, stream>>>(gate, up, out, H, ld_in, ld_out); break;
     default: swiglu_kernel<8><<<grid, 256, 0, stream>>>(gate, up, out, H, ld_in, ld_out); break;
   }
+  return cudaGetLastError();
+}
+
+// ---------------------------------------------------------------------------------------------
+// QKV preparation for the joint attention, from projected [q | k | v] rows (the input of the
+// reference's ds::/ss::fused_attention_{2,3}way ops): per-head RMSNorm of q and k (fp32 rstd,
+// weight then cast, norms.py:18-22), rotation of interleaved pairs with fp32 cos / sin and one
+// rounding (ops.py:48-67), scatter to q, k [B, H, L, 64] and V^T [B, H, 64, Lp].
+// One CTA = 32 consecutive tokens of the joint sequence x one head of one batch element; a warp
+// takes 4 tokens, a lane 2 of the 64 dims.  V goes through shared memory so that V^T is
+// written as 64-byte rows.
+// ---------------------------------------------------------------------------------------------
+__global__ void __launch_bounds__(256) qkv_prep_kernel(const __grid_constant__ QkvPrepParams P) {
+  __shared__ __align__(16) __nv_bfloat16 sv[64][40];  // [dim][token], rows 80 bytes apart
+  const int t0 = blockIdx.x * 32;
+  const int head = blockIdx.y;
+  const int b = blockIdx.z;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int inner = P.H * 64;
+  const size_t bh = static_cast<size_t>(b) * P.H + head;
+#pragma unroll 1
+  for (int i = 0; i < 4; ++i) {
+    const int tl = warp * 4 + i;
+    const int t = t0 + tl;
+    float vx = 0.0f, vy = 0.0f;
+    if (t < P.L) {  // uniform over the warp
+      int s = 0, off = 0;
+      while (s + 1 < P.nseg && t >= off + P.seg[s].rows) {
+        off += P.seg[s].rows;
+        ++s;
+      }
+      const QkvPrepSeg& sg = P.seg[s];
+      const int r = t - off;
+      const __nv_bfloat16* row = sg.qkv + b * sg.batch_stride + static_cast<long long>(r) * sg.ld + head * 64;
+      const bool rot = sg.cos != nullptr && r >= sg.rope_from;
+      float c = 1.0f, sn = 0.0f;
+      if (rot) {
+        c = sg.cos[static_cast<size_t>(r - sg.rope_from) * 32 + lane];
+        sn = sg.sin[static_cast<size_t>(r - sg.rope_from) * 32 + lane];
+      }
+#pragma unroll
+      for (int part = 0; part < 2; ++part) {
+        float x0, x1;
+        unpack_bf16x2(*reinterpret_cast<const uint32_t*>(row + part * inner + 2 * lane), x0, x1);
+        float ss = x0 * x0 + x1 * x1;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+        const float rstd = rsqrtf(ss * (1.0f / 64.0f) + P.eps);
+        const __nv_bfloat16* w = part == 0 ? sg.qn : sg.kn;
+        float w0, w1;
+        unpack_bf16x2(*reinterpret_cast<const uint32_t*>(w + 2 * lane), w0, w1);
+        const float a = bf16r(w0 * (x0 * rstd));
+        const float bb = bf16r(w1 * (x1 * rstd));
+        const uint32_t out = pack_bf16x2(a * c - bb * sn, a * sn + bb * c);
+        __nv_bfloat16* dst = (part == 0 ? P.q : P.k) + (bh * P.L + t) * 64 + 2 * lane;
+        *reinterpret_cast<uint32_t*>(dst) = out;
+      }
+      unpack_bf16x2(*reinterpret_cast<const uint32_t*>(row + 2 * inner + 2 * lane), vx, vy);
+    }
+    sv[2 * lane][tl] = __float2bfloat16_rn(vx);
+    sv[2 * lane + 1][tl] = __float2bfloat16_rn(vy);
+  }
+  __syncthreads();
+  // V^T rows: thread -> (dim d, 8-token group); tokens past L write zeros inside Lp only
+  const int d = threadIdx.x >> 2, grp = threadIdx.x & 3;
+  const int tok = t0 + grp * 8;
+  if (tok < P.Lp) {
+    const uint4 u = *reinterpret_cast<const uint4*>(&sv[d][grp * 8]);
+    *reinterpret_cast<uint4*>(P.vt + (bh * 64 + d) * P.Lp + tok) = u;
+  }
+}
+
+cudaError_t launch_qkv_prep(const QkvPrepParams& p, cudaStream_t stream) {
+  if (p.nseg < 1 || p.nseg > 3 || p.B <= 0 || p.H <= 0 || p.L <= 0 || p.Lp < p.L || p.Lp % 8)
+    return cudaErrorInvalidValue;
+  const dim3 grid(static_cast<unsigned>((p.L + 31) / 32), static_cast<unsigned>(p.H), static_cast<unsigned>(p.B));
+  qkv_prep_kernel<<<grid, 256, 0, stream>>>(p);
+  return cudaGetLastError();
+}
+
+// ---------------------------------------------------------------------------------------------
+// Residual sums + LayerNorm of the reference's epilogue ops (one warp per row):
+//   ds::vl_epilogue_ln  new = bf16 sequence x + v1 + v2 + y, ln = LN(new)
+//     (rldx/inference/action_model/double_stream/engine/kernels/vl_epilogue_ln.py:53-75)
+//   ss::fused_epilogue_ln  new = bf16(x + y), ln = LN(new)
+//     (rldx/inference/action_model/single_stream/engine/kernels/ss_epilogue_ln.py:57-84)
+//   ds::grouped_res_ln  ln = LN(x + y + v1) summed in fp32
+//     (rldx/inference/action_model/double_stream/engine/kernels/grouped_res_ln.py:70-147)
+// ---------------------------------------------------------------------------------------------
+template <int kVec>
+__global__ void __launch_bounds__(128) res_ln_kernel(const __grid_constant__ ResLnParams P) {
+  const int warp_global = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (warp_global >= P.total_rows) return;
+  const ResLnSeg& sg = (P.nseg > 1 && warp_global >= P.seg[1].row_begin) ? P.seg[1] : P.seg[0];
+  const int row = warp_global - sg.row_begin;
+  const int nvec = sg.D / 8;
+  const size_t off = static_cast<size_t>(row) * sg.ld;
+  float x[kVec][8];
+  float sum = 0.0f;
+#pragma unroll
+  for (int i = 0; i < kVec; ++i) {
+    const int v = lane + 32 * i;
+    if (v < nvec) {
+      float a[8], t[8];
+      const uint4 ua = reinterpret_cast<const uint4*>(sg.x + off)[v];
+      unpack_bf16x2(ua.x, a[0], a[1]);
+      unpack_bf16x2(ua.y, a[2], a[3]);
+      unpack_bf16x2(ua.z, a[4], a[5]);
+      unpack_bf16x2(ua.w, a[6], a[7]);
+      auto add = [&](const __nv_bfloat16* p, bool round) {
+        const uint4 u = reinterpret_cast<const uint4*>(p)[v];
+        unpack_bf16x2(u.x, t[0], t[1]);
+        unpack_bf16x2(u.y, t[2], t[3]);
+        unpack_bf16x2(u.z, t[4], t[5]);
+        unpack_bf16x2(u.w, t[6], t[7]);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) a[e] = round ? bf16r(a[e] + t[e]) : a[e] + t[e];
+      };
+      if (P.fp32_sum) {
+        if (sg.y) add(sg.y + off, false);
+        if (sg.v1) add(sg.v1, false);
+        if (sg.v2) add(sg.v2, false);
+      } else {
+        if (sg.v1) add(sg.v1, true);
+        if (sg.v2) add(sg.v2, true);
+        if (sg.y) add(sg.y + off, true);
+      }
+      if (sg.sum_out) {
+        uint4 r;
+        r.x = pack_bf16x2(a[0], a[1]);
+        r.y = pack_bf16x2(a[2], a[3]);
+        r.z = pack_bf16x2(a[4], a[5]);
+        r.w = pack_bf16x2(a[6], a[7]);
+        reinterpret_cast<uint4*>(sg.sum_out + off)[v] = r;
+      }
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        x[i][e] = a[e];
+        sum += a[e];
+      }
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+  const float mean = sum / static_cast<float>(sg.D);
+  float var = 0.0f;
+#pragma unroll
+  for (int i = 0; i < kVec; ++i)
+    if (lane + 32 * i < nvec)
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const float d = x[i][e] - mean;
+        var += d * d;
+      }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) var += __shfl_xor_sync(0xffffffffu, var, o);
+  const float rstd = rsqrtf(var / static_cast<float>(sg.D) + P.eps);
+#pragma unroll
+  for (int i = 0; i < kVec; ++i) {
+    const int v = lane + 32 * i;
+    if (v < nvec) {
+      uint4 r;
+      r.x = pack_bf16x2((x[i][0] - mean) * rstd, (x[i][1] - mean) * rstd);
+      r.y = pack_bf16x2((x[i][2] - mean) * rstd, (x[i][3] - mean) * rstd);
+      r.z = pack_bf16x2((x[i][4] - mean) * rstd, (x[i][5] - mean) * rstd);
+      r.w = pack_bf16x2((x[i][6] - mean) * rstd, (x[i][7] - mean) * rstd);
+      reinterpret_cast<uint4*>(sg.ln_out + off)[v] = r;
+    }
+  }
+}
+
+cudaError_t launch_res_ln(const ResLnParams& p, cudaStream_t stream) {
+  if (p.total_rows <= 0 || p.dmax <= 0 || p.dmax > 4096) return cudaErrorInvalidValue;
+  const unsigned grid = static_cast<unsigned>((p.total_rows + 3) / 4);
+  if (p.dmax <= 32 * 8 * 6) res_ln_kernel<6><<<grid, 128, 0, stream>>>(p);
+  else res_ln_kernel<16><<<grid, 128, 0, stream>>>(p);
+  return cudaGetLastError();
+}
+
+// ---------------------------------------------------------------------------------------------
+// ds::grouped_swiglu: out = bf16( silu(gate + bg) * (up + bu) ), every step in fp32
+// (rldx/inference/action_model/double_stream/engine/kernels/grouped_swiglu.py:150-170).
+// blockIdx.x is the row of the concatenated segments, blockIdx.y a slice of 256 x 8 columns.
+// ---------------------------------------------------------------------------------------------
+__global__ void __launch_bounds__(256) swiglu_bias_kernel(const __grid_constant__ SwigluBiasParams P) {
+  const int grow = blockIdx.x;
+  const SwigluBiasSeg& sg = (P.nseg > 1 && grow >= P.seg[1].row_begin) ? P.seg[1] : P.seg[0];
+  const size_t r = grow - sg.row_begin;
+  const int c = blockIdx.y * 256 + threadIdx.x;
+  if (c >= sg.H / 8) return;
+  const uint4 ug = reinterpret_cast<const uint4*>(sg.gate + r * sg.ld_in)[c];
+  const uint4 uu = reinterpret_cast<const uint4*>(sg.up + r * sg.ld_in)[c];
+  const uint4 bg = reinterpret_cast<const uint4*>(sg.bg)[c];
+  const uint4 bu = reinterpret_cast<const uint4*>(sg.bu)[c];
+  const uint32_t gv[4] = {ug.x, ug.y, ug.z, ug.w}, uv[4] = {uu.x, uu.y, uu.z, uu.w};
+  const uint32_t bgv[4] = {bg.x, bg.y, bg.z, bg.w}, buv[4] = {bu.x, bu.y, bu.z, bu.w};
+  uint32_t ov[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    float g0, g1, u0, u1, a0, a1, b0, b1;
+    unpack_bf16x2(gv[i], g0, g1);
+    unpack_bf16x2(uv[i], u0, u1);
+    unpack_bf16x2(bgv[i], a0, a1);
+    unpack_bf16x2(buv[i], b0, b1);
+    g0 += a0;
+    g1 += a1;
+    u0 += b0;
+    u1 += b1;
+    ov[i] = pack_bf16x2(g0 * __fdividef(1.0f, 1.0f + __expf(-g0)) * u0, g1 * __fdividef(1.0f, 1.0f + __expf(-g1)) * u1);
+  }
+  reinterpret_cast<uint4*>(sg.out + r * sg.ld_out)[c] = make_uint4(ov[0], ov[1], ov[2], ov[3]);
+}
+
+cudaError_t launch_swiglu_bias(const SwigluBiasParams& p, cudaStream_t stream) {
+  if (p.total_rows <= 0 || p.hmax <= 0) return cudaErrorInvalidValue;
+  const dim3 grid(static_cast<unsigned>(p.total_rows), static_cast<unsigned>((p.hmax / 8 + 255) / 256));
+  swiglu_bias_kernel<<<grid, 256, 0, stream>>>(p);
   return cudaGetLastError();
 }
 

@@ -203,6 +203,78 @@ def swiglu(gate, up, out=None):
     return out
 
 
+def qkv_prep(segments, q, k, vt, eps: float = 1e-6) -> None:
+    """Per-head QK RMSNorm + interleaved-pair RoPE of projected [q | k | v] rows into the joint
+    attention layout q, k [B, H, L, 64] and vt [B, H, 64, Lp].  `segments` lists, in joint order,
+    dicts with qkv ([rows, 3*H*64] or [B, rows, 3*H*64]), q_norm, k_norm and optionally
+    rope_cos / rope_sin ([rows - rope_from, 32] fp32) and rope_from."""
+    for t, n in ((q, "q"), (k, "k"), (vt, "vt")):
+        _need(t, n)
+    B, H, L, _ = q.shape
+    Lp = vt.shape[-1]
+    arr = (_lib.QkvSegment * len(segments))()
+    keep = []
+    for i, sg in enumerate(segments):
+        x = sg["qkv"]
+        _need(x, "qkv")
+        if x.stride(-1) != 1:
+            raise ValueError("qkv rows must be row-major")
+        rows = x.shape[-2]
+        arr[i].qkv, arr[i].ld, arr[i].rows = x.data_ptr(), x.stride(-2), rows
+        arr[i].batch_stride = x.stride(0) if x.dim() == 3 else rows * x.stride(-2)
+        qn, kn = sg["q_norm"].contiguous(), sg["k_norm"].contiguous()
+        keep += [qn, kn]
+        arr[i].q_norm, arr[i].k_norm = qn.data_ptr(), kn.data_ptr()
+        if sg.get("rope_cos") is not None:
+            c = sg["rope_cos"].float().contiguous()
+            sn = sg["rope_sin"].float().contiguous()
+            keep += [c, sn]
+            arr[i].rope_cos, arr[i].rope_sin = c.data_ptr(), sn.data_ptr()
+            arr[i].rope_from = int(sg.get("rope_from", 0))
+    check(load().rldx_qkv_prep(arr, len(segments), B, H, L, Lp, eps, _p(q), _p(k), _p(vt), _stream()))
+
+
+def res_layernorm(segments, *, fp32_sum: bool = False, eps: float = 1e-6) -> None:
+    """sum = x (+ y) (+ v1) (+ v2) then LayerNorm, for up to 2 row groups in one launch.
+    `segments`: dicts with x, ln_out and optionally y, v1, v2, sum_out ([rows, D] row-major views,
+    vectors [D]).  fp32_sum False: bf16 rounding after each add in the order x, v1, v2, y;
+    True: one fp32 sum."""
+    arr = (_lib.ResLnSegment * len(segments))()
+    for i, sg in enumerate(segments):
+        x = sg["x"]
+        _need(x, "x")
+        ld = _row_major(x, "x")
+        arr[i].x, arr[i].rows, arr[i].D, arr[i].ld = x.data_ptr(), x.shape[0], x.shape[1], ld
+        for name in ("y", "v1", "v2", "sum_out", "ln_out"):
+            t = sg.get(name)
+            if t is None:
+                continue
+            _need(t, name)
+            if name in ("y", "sum_out", "ln_out") and _row_major(t, name) != ld:
+                raise ValueError(f"{name} must share the row stride of x")
+            setattr(arr[i], name, t.data_ptr())
+    check(load().rldx_res_layernorm(arr, len(segments), 1 if fp32_sum else 0, eps, _stream()))
+
+
+def swiglu_bias(segments) -> None:
+    """out = silu(gate + bias_gate) * (up + bias_up) in fp32, for up to 2 row groups.
+    `segments`: dicts with gate, up ([rows, H] views sharing a row stride), bias_gate, bias_up
+    ([H]) and out ([rows, H])."""
+    arr = (_lib.SwigluBiasSegment * len(segments))()
+    for i, sg in enumerate(segments):
+        g, u, o = sg["gate"], sg["up"], sg["out"]
+        for t, n in ((g, "gate"), (u, "up"), (o, "out"), (sg["bias_gate"], "bias_gate"), (sg["bias_up"], "bias_up")):
+            _need(t, n)
+        ld = _row_major(g, "gate")
+        if _row_major(u, "up") != ld:
+            raise ValueError("gate and up must share a row stride")
+        arr[i].gate, arr[i].up, arr[i].out = g.data_ptr(), u.data_ptr(), o.data_ptr()
+        arr[i].bias_gate, arr[i].bias_up = sg["bias_gate"].data_ptr(), sg["bias_up"].data_ptr()
+        arr[i].ld_in, arr[i].ld_out = ld, _row_major(o, "out")
+        arr[i].rows, arr[i].H = g.shape[0], g.shape[1]
+    check(load().rldx_swiglu_bias(arr, len(segments), _stream()))
+
+
 def device_error() -> int:
     """Reads and clears the device-side error word (synchronizes)."""
     v = C.c_uint(0)

@@ -26,7 +26,7 @@ def test_every_declared_symbol_is_exported(lib):
 
 
 def test_version_and_error_string(lib):
-    assert lib.rldx_version() == 104
+    assert lib.rldx_version() == 106
     assert isinstance(lib.rldx_last_error(), bytes)
 
 
@@ -37,6 +37,9 @@ def test_struct_layouts_match_header():
     assert C.sizeof(_lib.MsatIO) == 8 * 8
     assert C.sizeof(_lib.BlockWeights) == 3 * (4 * 16 + 16)
     assert C.sizeof(_lib.SingleBlockWeights) == 2 * (3 * 16 + 16)
+    assert C.sizeof(_lib.QkvSegment) == 64
+    assert C.sizeof(_lib.ResLnSegment) == 6 * 8 + 2 * 4 + 8
+    assert C.sizeof(_lib.SwigluBiasSegment) == 5 * 8 + 2 * 8 + 2 * 4
 
 
 def test_null_arguments_are_rejected_without_a_device(lib):
