@@ -43,7 +43,7 @@ L2_BYTES = 126 * 1024 * 1024
 def parse_args():
     p = argparse.ArgumentParser()
     p.add_argument("--gpus", type=int, default=1)
-    p.add_argument("--steps", type=int, default=30)
+    p.add_argument("--steps", type=int, default=300)
     p.add_argument("--warmup", type=int, default=5)
     p.add_argument("--batch", type=int, default=1, help="observations per GPU per control step")
     p.add_argument("--impl", choices=["b200", "reference"], default="b200")
@@ -104,7 +104,7 @@ class ClockSampler:
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
-                 "-lms", "200", "-i", str(self.gpu)], stdout=subprocess.PIPE,
+                 "-lms", "100", "-i", str(self.gpu)], stdout=subprocess.PIPE,
                 stderr=subprocess.DEVNULL, text=True)
             self.t = threading.Thread(target=self._read, daemon=True)
             self.t.start()
