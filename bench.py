@@ -1,6 +1,7 @@
 """Benchmark of the MSAT all-modality control step on B200.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--batch B] [--impl b200|reference]
+                    [--workload c2|production|production_addons]
 
 One step = one control step of the action head for B observations per GPU: state encoder,
 physics history encoder and 4 flow-matching Euler steps of [action + physics encoders, 16
@@ -12,6 +13,11 @@ with the config-2 shapes and distributions.
 Multi-GPU (torchrun, one process per GPU): every GPU serves its own observations with a full
 weight copy ("replicas", weak scaling); no collective runs on the step path — torch.distributed
 only supplies the barrier and the max-over-ranks of the timed region.
+
+--workload production / production_addons measures the reference's released head without /
+with add-ons instead (4 double + 8 single blocks, VL width 4096; the shapes of the reference's
+own published action-head benchmark, rldx/inference/action_model/README.md:9-37); the default
+line is config 2.
 
 Printed JSON (rank 0): value = control steps/s of the whole job with inputs resident in HBM;
 e2e = the same through the C ABI with pinned host buffers (host->device inputs and device->host
@@ -47,6 +53,7 @@ def parse_args():
     p.add_argument("--warmup", type=int, default=5)
     p.add_argument("--batch", type=int, default=1, help="observations per GPU per control step")
     p.add_argument("--impl", choices=["b200", "reference"], default="b200")
+    p.add_argument("--workload", choices=["c2", "production", "production_addons"], default="c2")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--cpu-sample-s", type=float, default=20.0, help="CPU baseline time budget")
     p.add_argument("--profile-step", action="store_true",
@@ -165,12 +172,37 @@ def ncu_traffic():
 # ----------------------------------------------------------------------------------------------
 # CPU baseline: the oracle restatement of the reference path (fp32, all host threads)
 # ----------------------------------------------------------------------------------------------
-def cpu_baseline(budget_s: float, steps: int = 8, warmup: int = 1):
+WORKLOADS = {
+    "c2": ("BASELINE config 2: all-modality MSAT control step (4 Euler steps, one CUDA graph)",
+           "MSAT 16 x ExpandedDoubleStreamBlock [VL 512 | SA 18 | P 32], hidden 1536, 24x64"),
+    "production": ("reference's released head, no add-ons (4 Euler steps, one CUDA graph)",
+                   "MSAT 4 x DoubleStreamBlock [VL 64 x 4096 | SA 18 x 1536] + 8 x SingleStreamBlock, "
+                   "24x64, 1244.6M parameters"),
+    "production_addons": ("reference's released head, all add-ons (4 Euler steps, one CUDA graph)",
+                          "MSAT 4 x ExpandedDoubleStreamBlock [VL 80 x 4096 | SA 18 | P 32] + 8 x "
+                          "ExpandedSingleStreamBlock, 24x64, 1842.6M parameters"),
+}
+
+
+def oracle_config(workload: str):
+    """The oracle's MsatHeadConfig of a bench workload."""
+    from oracle import msat_oracle as om
+
+    if workload == "c2":
+        return om.MsatHeadConfig()
+    base = dict(n_vl=64 if workload == "production" else 80, depth=4, depth_single=8, vl_dim=4096,
+                action_dim=64, max_seq_len=512)
+    if workload == "production":
+        base.update(use_physics=False, physics_hist=0, physics_fut=0)
+    return om.MsatHeadConfig(**base)
+
+
+def cpu_baseline(budget_s: float, steps: int = 8, warmup: int = 1, workload: str = "c2"):
     from oracle import msat_oracle as om
 
     threads = os.cpu_count() or 1
     torch.set_num_threads(threads)
-    cfg = om.MsatHeadConfig()  # config 2
+    cfg = oracle_config(workload)
     head = om.init_weights(om.ActionHead(cfg), seed=0)
     inp = om.make_inputs(cfg, batch=1, seed=42)
     msat = head.model
@@ -178,16 +210,20 @@ def cpu_baseline(budget_s: float, steps: int = 8, warmup: int = 1):
         sf = head.state_encoder(inp["state"], inp["embodiment_id"])
         t0 = torch.zeros(1)
         af = head.action_encoder(inp["init_noise"], t0, inp["embodiment_id"])
-        pe = torch.cat([head.physics.physics_cond_encoder(inp["physics_hist"]),
-                        head.physics.physics_fut_encoder(inp["physics_noise"], t0)], dim=1)
         sa = torch.cat([sf, af], 1)
+        if cfg.use_physics:
+            pe = torch.cat([head.physics.physics_cond_encoder(inp["physics_hist"]),
+                            head.physics.physics_fut_encoder(inp["physics_noise"], t0)], dim=1)
+            fwd = lambda: msat(sa, inp["vl"], t0, pe)  # noqa: E731
+        else:
+            fwd = lambda: msat(sa, inp["vl"], t0)  # noqa: E731
         for _ in range(max(1, min(warmup, 2))):
-            msat(sa, inp["vl"], t0, pe)
+            fwd()
         times = []
         start = time.perf_counter()
         while True:
             t = time.perf_counter()
-            msat(sa, inp["vl"], t0, pe)
+            fwd()
             times.append(time.perf_counter() - t)
             if time.perf_counter() - start > budget_s or len(times) >= max(1, steps):
                 break
@@ -195,19 +231,20 @@ def cpu_baseline(budget_s: float, steps: int = 8, warmup: int = 1):
     # one control step = num_steps MSAT forwards (+ encoders/decoders, < 5 % of the work)
     per_step = per_forward * cfg.num_steps
     return {"value": 1.0 / per_step, "unit": "control steps/s", "cores": threads, "kind": "port",
-            "sample": f"{len(times)} MSAT forwards (config 2, fp32, batch 1) timed on the host; "
+            "sample": f"{len(times)} MSAT forwards ({workload}, fp32, batch 1) timed on the host; "
                       f"p50 {per_forward * 1e3:.0f} ms x {cfg.num_steps} Euler steps = one control step"}
 
 
 def run_reference(args):
-    cb = cpu_baseline(args.cpu_sample_s, steps=args.steps, warmup=args.warmup)
+    cb = cpu_baseline(args.cpu_sample_s, steps=args.steps, warmup=args.warmup, workload=args.workload)
+    desc, model = WORKLOADS[args.workload]
     line = {"metric": "control_steps_per_s", "value": cb["value"], "unit": "control steps/s",
             "impl": "reference", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": 1000.0 / cb["value"], "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": {"workload": "BASELINE config 2: all-modality MSAT control step, batch 1",
-                       "model": "MSAT 16 x ExpandedDoubleStreamBlock, hidden 1536, 24x64 heads",
-                       "global_batch": 1, "seq_len": 562, "parallelism": "cpu"},
+            "config": {"workload": desc + ", batch 1", "model": model,
+                       "global_batch": 1, "seq_len": oracle_config(args.workload).n_vl + 18 +
+                       (32 if oracle_config(args.workload).use_physics else 0), "parallelism": "cpu"},
             "cpu_baseline": cb,
             "e2e": {"value": cb["value"], "unit": "control steps/s", "h2d_bytes_per_step": 0,
                     "d2h_bytes_per_step": 0}}
@@ -219,22 +256,24 @@ def run_reference(args):
 # ----------------------------------------------------------------------------------------------
 def run_b200(args, rank, world, local):
     import rldx_b200  # noqa: F401
-    from rldx_b200.chain import B200ExpandedActionHeadChain
-    from rldx_b200.synthetic import HeadDims, random_action_head, random_inputs
+    from rldx_b200.chain import B200ActionHeadChain, B200ExpandedActionHeadChain
+    from rldx_b200.synthetic import PRESETS, random_action_head, random_inputs
 
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
-    dims = HeadDims()
+    dims = PRESETS[args.workload]()
     B = args.batch
     head = random_action_head(dims, seed=0, device=dev)
-    chain = B200ExpandedActionHeadChain(head, dev)
+    chain = (B200ExpandedActionHeadChain if dims.use_physics else B200ActionHeadChain)(head, dev)
     inp = random_inputs(dims, B, seed=42 + rank, device=dev)
     host = random_inputs(dims, B, seed=42 + rank, device="cpu", pin=True)
     out_host = torch.empty(B, dims.horizon, dims.action_dim, dtype=torch.bfloat16).pin_memory()
 
     def step():
-        return chain(inp["vl"], inp["state"], inp["embodiment_id"], inp["init_noise"],
-                     inp["physics_hist"], inp["physics_noise"])
+        if dims.use_physics:
+            return chain(inp["vl"], inp["state"], inp["embodiment_id"], inp["init_noise"],
+                         inp["physics_hist"], inp["physics_noise"])
+        return chain(inp["vl"], inp["state"], inp["embodiment_id"], inp["init_noise"])
 
     step()  # binds: weight arena, tables, graph capture
     torch.cuda.synchronize()
@@ -320,13 +359,12 @@ def run_b200(args, rank, world, local):
         "scaling": "weak",
         "vs_baseline": None,
         "dtype": "bf16",
-        "data": "synthetic (seeded random weights with the reference layout; config-2 shaped inputs)",
-        "config": {"workload": "BASELINE config 2: all-modality MSAT control step (4 Euler steps, one "
-                               "CUDA graph), batch %d per GPU" % B,
-                   "model": "MSAT 16 x ExpandedDoubleStreamBlock [VL 512 | SA 18 | P 32], hidden 1536, 24x64",
+        "data": "synthetic (seeded random weights with the reference layout; shaped inputs)",
+        "config": {"workload": WORKLOADS[args.workload][0] + ", batch %d per GPU" % B,
+                   "model": WORKLOADS[args.workload][1],
                    "global_batch": world * B, "seq_len": dims.tokens,
                    "parallelism": f"replicas x{world} (data parallel, no collective)",
-                   "l2": "flushed between timed steps (256 MB write); weights streamed per step 2.7 GB > L2"},
+                   "l2": "flushed between timed steps (256 MB write); weights streamed per step > L2"},
         "e2e": {"value": n_obs / (e_total * 1e-3), "unit": "control steps/s",
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                 "p50_ms": statistics.median(e_ms)},
@@ -345,7 +383,7 @@ def run_b200(args, rank, world, local):
     }
     line["clocks"] = clocks.summary()
     if world == 1 and not args.no_cpu_baseline:
-        line["cpu_baseline"] = cpu_baseline(args.cpu_sample_s)
+        line["cpu_baseline"] = cpu_baseline(args.cpu_sample_s, workload=args.workload)
     print(json.dumps(line), flush=True)
 
 

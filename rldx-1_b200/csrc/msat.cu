@@ -210,40 +210,49 @@ struct rldx_msat {
     return d;
   }
 
-  // SwiGLUFFN.w12 [2h, dim] (gate rows then up rows) -> [32 gate | 32 up] row groups.
-  void w12_interleave(const rldx_linear& l, int hidden, int dim, bf16** w, bf16** b) {
+  // SwiGLUFFN.w12 [2h, dim] (gate rows then up rows) -> [32 gate | 32 up] row groups over hp =
+  // h rounded up to 32; the padded gate / up rows are zero (silu(0) * 0 = 0, and w3's padded
+  // columns are zero too), so a hidden size like int(2/3 * 16384) = 10922 runs exactly.
+  void w12_interleave(const rldx_linear& l, int hidden, int hp, int dim, bf16** w, bf16** b) {
     if (!l.w || !l.b) throw Fail(RLDX_ERR_ARG, "missing w12");
-    if (hidden % 32) throw Fail(RLDX_ERR_UNSUPPORTED, "SwiGLU hidden must be a multiple of 32");
-    std::vector<int> idx(2 * hidden);
-    for (int g = 0; g < hidden / 32; ++g)
+    if (hp % 32 || hp < hidden) throw Fail(RLDX_ERR_UNSUPPORTED, "padded SwiGLU hidden must be a multiple of 32");
+    const int zero_row = 2 * hidden;  // one zero row after the source rows
+    std::vector<int> idx(2 * hp);
+    for (int g = 0; g < hp / 32; ++g)
       for (int i = 0; i < 32; ++i) {
-        idx[g * 64 + i] = g * 32 + i;
-        idx[g * 64 + 32 + i] = hidden + g * 32 + i;
+        const int r = g * 32 + i;
+        idx[g * 64 + i] = r < hidden ? r : zero_row;
+        idx[g * 64 + 32 + i] = r < hidden ? hidden + r : zero_row;
       }
     int* didx = alloc<int>(idx.size());
     ck(cudaMemcpy(didx, idx.data(), idx.size() * 4, cudaMemcpyHostToDevice), "idx");
-    bf16* src = copy_in(l.w, static_cast<size_t>(2) * hidden * dim, "w12");
-    *w = alloc<bf16>(static_cast<size_t>(2) * hidden * dim);
-    ck(launch_gather_rows(src, dim, *w, dim, didx, 2 * hidden, dim, stream), "gather");
-    bf16* bsrc = copy_in(l.b, static_cast<size_t>(2) * hidden, "w12 bias");
-    *b = alloc<bf16>(static_cast<size_t>(2) * hidden);
-    ck(launch_gather_rows(bsrc, 1, *b, 1, didx, 2 * hidden, 1, stream), "gather bias");
+    bf16* src = alloc<bf16>(static_cast<size_t>(2 * hidden + 1) * dim);  // zero-filled
+    ck(cudaMemcpy(src, l.w, static_cast<size_t>(2) * hidden * dim * 2, cudaMemcpyDefault), "w12");
+    *w = alloc<bf16>(static_cast<size_t>(2) * hp * dim);
+    ck(launch_gather_rows(src, dim, *w, dim, didx, 2 * hp, dim, stream), "gather");
+    bf16* bsrc = alloc<bf16>(static_cast<size_t>(2 * hidden + 1));
+    ck(cudaMemcpy(bsrc, l.b, static_cast<size_t>(2) * hidden * 2, cudaMemcpyDefault), "w12 bias");
+    *b = alloc<bf16>(static_cast<size_t>(2) * hp);
+    ck(launch_gather_rows(bsrc, 1, *b, 1, didx, 2 * hp, 1, stream), "gather bias");
     ck(cudaStreamSynchronize(stream), "gather sync");
     release(src);
     release(bsrc);
     release(didx);
   }
 
+  static int pad32(int v) { return (v + 31) / 32 * 32; }
+
   StreamW bind_stream(const rldx_stream_weights& s, int hidden, int width) {
     StreamW w{};
     const size_t inner = static_cast<size_t>(H) * 64;
-    w.hidden = hidden;
+    const int hp = pad32(hidden);
+    w.hidden = hp;
     w.qkv_w = copy_in(s.qkv.w, 3 * inner * width, "qkv.w");
     w.qkv_b = copy_in(s.qkv.b, 3 * inner, "qkv.b");
     w.proj_w = copy_in(s.proj.w, static_cast<size_t>(width) * inner, "proj.w");
     w.proj_b = copy_in(s.proj.b, width, "proj.b");
-    w12_interleave(s.w12, hidden, width, &w.w12_w, &w.w12_b);
-    w.w3_w = copy_in(s.w3.w, static_cast<size_t>(width) * hidden, "w3.w");
+    w12_interleave(s.w12, hidden, hp, width, &w.w12_w, &w.w12_b);
+    w.w3_w = copy_pad(s.w3.w, width, hidden, hp, "w3.w");  // [width, hidden] -> [width, hp], zero columns
     w.w3_b = copy_in(s.w3.b, width, "w3.b");
     w.qn = copy_in(s.q_norm, 64, "q_norm");
     w.kn = copy_in(s.k_norm, 64, "k_norm");
@@ -263,7 +272,7 @@ struct rldx_msat {
     rldx_linear l12;
     l12.w = static_cast<const uint16_t*>(l1.w) + inner3 * D;
     l12.b = static_cast<const uint16_t*>(l1.b) + inner3;
-    w12_interleave(l12, E, D, &w.w12_w, &w.w12_b);
+    w12_interleave(l12, E, E, D, &w.w12_w, &w.w12_b);
     w.mp_w = copy_in(mp.w, static_cast<size_t>(Mh) * E, "mlp_proj.w");
     w.mp_b = copy_in(mp.b, Mh, "mlp_proj.b");
     w.l2_w = copy_in(l2.w, static_cast<size_t>(D) * (inner + Mh), "linear2.w");
@@ -492,8 +501,8 @@ void rldx_msat::create(const rldx_msat_config& cfg, const rldx_msat_weights& w) 
   if (c.n_state <= 0 || 1 + c.n_state + c.horizon > 128 || c.horizon > 128 ||
       (!standard && c.physics_hist + c.physics_fut > 128))
     throw Fail(RLDX_ERR_UNSUPPORTED, "per-observation action / physics streams must fit 128 rows");
-  if (c.dim % 64 || Dv % 64 || c.mlp_hidden % 32 || c.vl_mlp_hidden % 32 || c.out_dim % 8 || c.dec_hidden % 8)
-    throw Fail(RLDX_ERR_UNSUPPORTED, "dims must be multiples of 64 (dim, vl_dim) / 32 (hidden) / 8");
+  if (c.dim % 64 || Dv % 64 || c.mlp_hidden <= 0 || c.vl_mlp_hidden <= 0 || c.out_dim % 8 || c.dec_hidden % 8)
+    throw Fail(RLDX_ERR_UNSUPPORTED, "dims must be multiples of 64 (dim, vl_dim) / 8 (out_dim, dec_hidden)");
   if (c.dim > 4096 || Dv > 4096) throw Fail(RLDX_ERR_UNSUPPORTED, "dim / vl_dim > 4096");
   if (!standard && (c.physics_dim <= 0 || c.physics_hist <= 0))
     throw Fail(RLDX_ERR_UNSUPPORTED, "the all-modality path needs the physics stream");
@@ -615,9 +624,9 @@ void rldx_msat::create(const rldx_msat_config& cfg, const rldx_msat_weights& w) 
   ovl = alloc<bf16>(static_cast<size_t>(B) * nvl * inner);
   osa = alloc<bf16>(static_cast<size_t>(B) * nsa * inner);
   op = alloc<bf16>(static_cast<size_t>(B) * np * inner);
-  hvl = alloc<bf16>(static_cast<size_t>(B) * nvl * c.vl_mlp_hidden);
-  hsa = alloc<bf16>(static_cast<size_t>(B) * nsa * c.mlp_hidden);
-  hp = alloc<bf16>(static_cast<size_t>(B) * np * c.mlp_hidden);
+  hvl = alloc<bf16>(static_cast<size_t>(B) * nvl * pad32(c.vl_mlp_hidden));
+  hsa = alloc<bf16>(static_cast<size_t>(B) * nsa * pad32(c.mlp_hidden));
+  hp = alloc<bf16>(static_cast<size_t>(B) * np * pad32(c.mlp_hidden));
   state_in = alloc<bf16>(static_cast<size_t>(B) * c.n_state * sdp);
   state_h = alloc<bf16>(static_cast<size_t>(B) * c.n_state * c.dec_hidden);
   state_feat = alloc<bf16>(static_cast<size_t>(B) * c.n_state * D);

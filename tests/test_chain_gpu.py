@@ -170,3 +170,17 @@ def test_rtc_prefix_batch_against_oracle(cuda):
     _, out = run_chain(head, inp, cuda, prefix=prefix)
     assert torch.equal(out[:, :5], prefix)
     assert_actions_close(out, ref16)
+
+
+def test_swiglu_hidden_not_multiple_of_32(cuda):
+    """mlp_ratio 2.5 at width 128: SwiGLU hidden int(2/3 * 320) = 213 (the released head's VL hidden
+    is int(2/3 * 16384) = 10922), padded inside the runtime with zero rows / columns."""
+    cfg = om.MsatHeadConfig(n_vl=40, horizon=16, physics_hist=16, physics_fut=16, dim=128, heads=2,
+                            depth=2, mlp_ratio=2.5, out_dim=64, action_dim=16, state_dim=16,
+                            dec_hidden=64, physics_dim=13, num_embodiments=2)
+    assert cfg.mlp_hidden % 32 != 0
+    head = om.init_weights(om.ActionHead(cfg), seed=9).to(BF)
+    inp = om.make_inputs(cfg, batch=1, seed=2)
+    ref16 = oracle_bf16(head, inp, cfg)
+    _, out = run_chain(head, inp, cuda)
+    assert_actions_close(out, ref16)
