@@ -138,6 +138,31 @@ int rldx_joint_attention(const void* q, const void* k, const void* vt, int B, in
                          int nseg, int tiles_per_cta, void* stream);
 
 /* ------------------------------------------------------------------------------------------
+ * Attention with every option of the kernel, described by a struct:
+ *   q [B, H, L, head_dim]; k [B, kv_heads, L, head_dim]; vt [B, kv_heads, head_dim, Lp];
+ *   kv_heads divides H (grouped-query attention: query head h reads kv head h / (H / kv_heads),
+ *   repeat_kv of rldx/model/modules/backbone/modeling_qwen3_vl.py:139-151), 0 = H;
+ *   causal 1: key j is visible to query i only for j <= i (the decoder prefill's causal mask);
+ *   out[s] with row stride out_ld[s] elements (0: H*head_dim), nseg 1..3, sum(seg_len) == L.
+ * rldx_joint_attention is this with kv_heads = H, causal = 0 and dense outputs.
+ * ------------------------------------------------------------------------------------------ */
+typedef struct {
+  const void* q;
+  const void* k;
+  const void* vt;
+  int B, H, kv_heads, L, Lp, head_dim;
+  int causal;
+  int tiles_per_cta;
+  const uint8_t* key_mask;
+  void* out[3];
+  int seg_len[3];
+  int out_ld[3];
+  int nseg;
+} rldx_attention_desc;
+
+int rldx_attention(const rldx_attention_desc* desc, void* stream);
+
+/* ------------------------------------------------------------------------------------------
  * QKV preparation of the joint attention from projected [q | k | v] rows: per-head QK RMSNorm
  * (norms.py:18-22) and interleaved-pair RoPE (ops.py:48-67) into q, k [B, H, L, 64] and
  * V^T [B, H, 64, Lp].  The RMSNorm + RoPE half of ds::fused_attention_2way / _3way

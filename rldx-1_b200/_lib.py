@@ -109,6 +109,13 @@ class OpProfile(C.Structure):
                 ("flops", C.c_double)]
 
 
+class AttentionDesc(C.Structure):
+    _fields_ = [("q", vp), ("k", vp), ("vt", vp), ("B", C.c_int), ("H", C.c_int),
+                ("kv_heads", C.c_int), ("L", C.c_int), ("Lp", C.c_int), ("head_dim", C.c_int),
+                ("causal", C.c_int), ("tiles_per_cta", C.c_int), ("key_mask", vp),
+                ("out", vp * 3), ("seg_len", C.c_int * 3), ("out_ld", C.c_int * 3), ("nseg", C.c_int)]
+
+
 class QkvSegment(C.Structure):
     _fields_ = [("qkv", vp), ("ld", i64), ("batch_stride", i64), ("rows", C.c_int),
                 ("rope_from", C.c_int), ("q_norm", vp), ("k_norm", vp), ("rope_cos", vp),
@@ -144,6 +151,7 @@ SIGNATURES = {
     "rldx_joint_attention": (C.c_int, [vp, vp, vp, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, vp,
                                        C.POINTER(vp), C.POINTER(C.c_int), C.c_int, C.c_int, vp]),
     "rldx_layernorm": (C.c_int, [vp, i64, vp, i64, C.c_int, C.c_int, C.c_float, vp, vp, vp]),
+    "rldx_attention": (C.c_int, [C.POINTER(AttentionDesc), vp]),
     "rldx_qkv_prep": (C.c_int, [C.POINTER(QkvSegment), C.c_int, C.c_int, C.c_int, C.c_int, C.c_int,
                                 C.c_float, vp, vp, vp, vp]),
     "rldx_res_layernorm": (C.c_int, [C.POINTER(ResLnSegment), C.c_int, C.c_int, C.c_float, vp]),

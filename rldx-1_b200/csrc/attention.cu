@@ -1,6 +1,10 @@
 // Joint-stream attention for sm_100a: non-causal softmax(Q K^T / sqrt(d)) V over the
 // concatenated [cognition | action | physics] token sequence of one batch element and head,
-// head_dim d = 64 (MSAT) or 128 (the joint-attention sweep shapes).
+// head_dim d = 64 (MSAT) or 128 (the joint-attention sweep shapes).  The same kernel serves the
+// decoder prefill of the VLM backbone: causal masking (key j visible to query i iff j <= i; a
+// CTA stops at the key tile of its last query row) and grouped-query heads (query head h reads
+// K / V head h / (H / kv_heads)), as Qwen3's sdpa / eager attention with repeat_kv
+// (rldx/model/modules/backbone/modeling_qwen3_vl.py:139-175, 404-490).
 //
 // Reference: F.scaled_dot_product_attention over torch.cat([vl, sa, p]) in
 // rldx/model/modules/action_model/blocks.py:826-870 (ExpandedDoubleStreamBlock) and
@@ -90,8 +94,11 @@ __global__ void __launch_bounds__(AttnShape<kHD, kG>::kThreads, 1)
   const int head = blockIdx.y;
   const int b = blockIdx.z;
   const int bh = b * P.H + head;
+  const int kvh = P.kv_heads > 0 ? P.kv_heads : P.H;
+  const int bh_kv = b * kvh + head / (P.H / kvh);  // GQA: K / V row of this query head
   const int L = P.L;
-  const int nkv = (L + 63) / 64;
+  // key tiles this CTA needs: all of them, or (causal) those at or before its last query row
+  const int nkv = P.causal ? min((L + 63) / 64, (min(L, q0 + 128 * kG) - 1) / 64 + 1) : (L + 63) / 64;
   const int ng = (kG == 2 && q0 + 128 < L) ? 2 : 1;  // query tiles with rows inside L
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -148,14 +155,14 @@ __global__ void __launch_bounds__(AttnShape<kHD, kG>::kThreads, 1)
           mbar_arrive_expect_tx(&k_full[s], kKTileBytes);
 #pragma unroll
           for (int c = 0; c < Sh::kChunks; ++c)
-            tma_load_3d(sK + s * kKTileBytes + c * Sh::kKChunk, &P.tk, &k_full[s], c * 64, i * 64, bh, pol);
+            tma_load_3d(sK + s * kKTileBytes + c * Sh::kKChunk, &P.tk, &k_full[s], c * 64, i * 64, bh_kv, pol);
         }
         if (i >= 1) {
           const int j = i - 1;
           const int s = j % kVS;
           if (!mbar_wait(&v_empty[s], (static_cast<uint32_t>(j / kVS) & 1u) ^ 1u, kErrAttnTimeout + 1)) break;
           mbar_arrive_expect_tx(&v_full[s], kVTileBytes);
-          tma_load_3d(sV + s * kVTileBytes, &P.tv, &v_full[s], j * 64, 0, bh, pol);
+          tma_load_3d(sV + s * kVTileBytes, &P.tv, &v_full[s], j * 64, 0, bh_kv, pol);
         }
       }
     }
@@ -249,9 +256,12 @@ __global__ void __launch_bounds__(AttnShape<kHD, kG>::kThreads, 1)
       // sequence without a key mask skip the masking; the key mask, when there is one, is read
       // as 64 bytes once per tile, so the per-element work stays branch-free.
       const int kbase = j * 64;
-      const int nvis = L - kbase;  // keys of this tile inside the sequence
+      // keys of this tile visible to this row: inside the sequence and, when causal, <= the row
+      const int nvis = P.causal ? min(L, qrow + 1) - kbase : L - kbase;
       float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
-      if (kmask == nullptr && nvis >= 64) {
+      // a tile below the diagonal for every row of the group needs no mask (warp-uniform test)
+      const bool full_tile = L - kbase >= 64 && (!P.causal || kbase + 63 <= q0 + 128 * g);
+      if (kmask == nullptr && full_tile) {
 #pragma unroll
         for (int c = 0; c < 64; ++c) mx4[c & 3] = fmaxf(mx4[c & 3], sv[c]);
       } else if (kmask == nullptr) {

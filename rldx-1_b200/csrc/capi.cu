@@ -636,7 +636,7 @@ using namespace rldx;
 
 extern "C" {
 
-int rldx_version(void) { return 106; }
+int rldx_version(void) { return 107; }
 
 const char* rldx_last_error(void) { return t_last_error.c_str(); }
 
@@ -698,6 +698,55 @@ int rldx_gemm_ws(const rldx_gemm_desc* problems, int nproblems, void* workspace,
     return set_error(RLDX_ERR_ARG, err);
   cudaError_t e = launch_gemm(params, static_cast<cudaStream_t>(stream), false);
   if (e != cudaSuccess) return cuda_fail(e, "gemm launch");
+  return RLDX_OK;
+}
+
+int rldx_attention(const rldx_attention_desc* d, void* stream) {
+  int rc = ensure_device();
+  if (rc != RLDX_OK) return rc;
+  if (!d || !d->q || !d->k || !d->vt) return set_error(RLDX_ERR_ARG, "attention: null pointer");
+  const int B = d->B, H = d->H, L = d->L, Lp = d->Lp, hd = d->head_dim;
+  const int kvh = d->kv_heads > 0 ? d->kv_heads : H;
+  if (B <= 0 || H <= 0 || L <= 0 || Lp < L || Lp % 8 != 0 || H % kvh != 0)
+    return set_error(RLDX_ERR_ARG, "attention: need B, H, L > 0, Lp >= L, Lp % 8 == 0, kv_heads | H");
+  if (hd != 64 && hd != 128) return set_error(RLDX_ERR_UNSUPPORTED, "attention: head_dim must be 64 or 128");
+  if (d->tiles_per_cta < 0 || d->tiles_per_cta > 2) return set_error(RLDX_ERR_ARG, "attention: tiles_per_cta must be 0, 1 or 2");
+  if (d->nseg < 1 || d->nseg > 3) return set_error(RLDX_ERR_ARG, "attention: nseg must be 1..3");
+  if (!aligned16(d->q) || !aligned16(d->k) || !aligned16(d->vt))
+    return set_error(RLDX_ERR_ARG, "attention: q/k/vt must be 16-byte aligned");
+  AttnParams p;
+  std::memset(&p, 0, sizeof(p));
+  int sum = 0;
+  for (int s = 0; s < d->nseg; ++s) {
+    const int ld = d->out_ld[s] > 0 ? d->out_ld[s] : H * hd;
+    if (d->seg_len[s] <= 0 || !d->out[s] || !aligned16(d->out[s]) || ld % 8 != 0 || ld < H * hd)
+      return set_error(RLDX_ERR_ARG, "attention: bad segment");
+    p.seg_out[s] = static_cast<__nv_bfloat16*>(d->out[s]);
+    p.seg_len[s] = d->seg_len[s];
+    p.seg_ld[s] = ld;
+    sum += d->seg_len[s];
+  }
+  if (sum != L) return set_error(RLDX_ERR_ARG, "attention: segment lengths must sum to L");
+  p.nseg = d->nseg;
+  p.L = L;
+  p.H = H;
+  p.B = B;
+  p.kv_heads = kvh;
+  p.causal = d->causal ? 1 : 0;
+  p.key_mask = d->key_mask;
+  p.head_dim = hd;
+  p.tiles_per_cta = d->tiles_per_cta;
+  p.scale_log2 = 1.4426950408889634f / std::sqrt(static_cast<float>(hd));
+  std::string err;
+  const uint64_t bq = static_cast<uint64_t>(B) * H, bkv = static_cast<uint64_t>(B) * kvh;
+  const uint64_t h64 = static_cast<uint64_t>(hd);
+  if (!make_tmap_3d(&p.tq, d->q, h64, L, bq, h64 * 2, static_cast<uint64_t>(L) * h64 * 2, 64, 128, 1, &err) ||
+      !make_tmap_3d(&p.tk, d->k, h64, L, bkv, h64 * 2, static_cast<uint64_t>(L) * h64 * 2, 64, 64, 1, &err) ||
+      !make_tmap_3d(&p.tv, d->vt, L, h64, bkv, static_cast<uint64_t>(Lp) * 2, static_cast<uint64_t>(Lp) * h64 * 2, 64,
+                    static_cast<uint32_t>(h64), 1, &err))
+    return set_error(RLDX_ERR_ARG, err);
+  cudaError_t e = launch_attention(p, static_cast<cudaStream_t>(stream), false);
+  if (e != cudaSuccess) return cuda_fail(e, "attention launch");
   return RLDX_OK;
 }
 

@@ -18,6 +18,8 @@ struct AttnParams {
   float scale_log2;  // log2(e) / sqrt(head_dim)
   int head_dim;      // 64 or 128 (0: 64)
   int tiles_per_cta; // 128-query tiles per CTA: 1, 2, or 0 = chosen from the grid size
+  int kv_heads;      // K / V heads (GQA: query head h reads kv head h / (H / kv_heads)); 0: H
+  int causal;        // 1: key j visible to query i only for j <= i (decoder prefill)
 };
 int attention_tiles_per_cta(const AttnParams& p, int sms);
 size_t attention_smem_bytes(int head_dim);

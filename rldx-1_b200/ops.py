@@ -163,6 +163,33 @@ def joint_attention(q, k, vt, seg_lens: Sequence[int], key_mask=None, outs=None,
     return outs
 
 
+def attention(q, k, vt, seg_lens: Sequence[int] = None, *, causal: bool = False, key_mask=None,
+              outs=None, tiles_per_cta: int = 0):
+    """Attention through rldx_attention: q [B, H, L, d], k [B, Hkv, L, d], vt [B, Hkv, d, Lp]
+    (Hkv divides H: grouped-query heads), optional causal mask; returns one output per segment
+    as [B * seg_len, H * d] (one segment of L rows by default)."""
+    for t, n in ((q, "q"), (k, "k"), (vt, "vt")):
+        _need(t, n)
+        if not t.is_contiguous():
+            raise ValueError(f"{n} must be contiguous")
+    B, H, L, hd = q.shape
+    seg_lens = list(seg_lens) if seg_lens is not None else [L]
+    if outs is None:
+        outs = [torch.empty(B * n, H * hd, dtype=torch.bfloat16, device=q.device) for n in seg_lens]
+    d = _lib.AttentionDesc()
+    d.q, d.k, d.vt = q.data_ptr(), k.data_ptr(), vt.data_ptr()
+    d.B, d.H, d.kv_heads, d.L, d.Lp, d.head_dim = B, H, k.shape[1], L, vt.shape[-1], hd
+    d.causal, d.tiles_per_cta = 1 if causal else 0, tiles_per_cta
+    if key_mask is not None:
+        _need(key_mask, "key_mask", torch.uint8)
+        d.key_mask = key_mask.data_ptr()
+    for i, (o, n) in enumerate(zip(outs, seg_lens)):
+        d.out[i], d.seg_len[i], d.out_ld[i] = o.data_ptr(), n, _row_major(o, "out")
+    d.nseg = len(seg_lens)
+    check(load().rldx_attention(C.byref(d), _stream()))
+    return outs
+
+
 def layernorm(x, eps: float = 1e-6, scale1p=None, shift=None, out=None):
     """LayerNorm without affine (optionally * scale1p + shift) over the last dim of [rows, D]."""
     _need(x, "x")

@@ -75,3 +75,37 @@ def test_joint_attention_two_tiles_per_cta(cuda, hd, segs):
 
 def test_joint_attention_two_tiles_key_mask(cuda):
     run_case(cuda, 2, 4, [300, 18, 32], mask=True, seed=5, tiles=2)
+
+
+def run_gqa_causal(cuda, B, H, Hkv, L, hd, causal, seed=0, tiles=0):
+    Lp = (L + 7) // 8 * 8
+    g = torch.Generator(device=cuda).manual_seed(seed)
+    q = torch.randn(B, H, L, hd, device=cuda, generator=g).to(BF)
+    k = torch.randn(B, Hkv, L, hd, device=cuda, generator=g).to(BF)
+    v = torch.randn(B, Hkv, L, hd, device=cuda, generator=g).to(BF)
+    vt = torch.zeros(B, Hkv, hd, Lp, dtype=BF, device=cuda)
+    vt[..., :L] = v.transpose(-1, -2)
+    (out,) = ops.attention(q, k, vt, causal=causal, tiles_per_cta=tiles)
+    torch.cuda.synchronize()
+    rep = H // Hkv
+    kf = k.float().repeat_interleave(rep, dim=1)
+    vf = v.float().repeat_interleave(rep, dim=1)
+    s = (q.float() @ kf.transpose(-1, -2)) / hd ** 0.5
+    if causal:
+        s = s.masked_fill(torch.ones(L, L, dtype=torch.bool, device=cuda).triu(1), float("-inf"))
+    ref = (torch.softmax(s, dim=-1) @ vf).permute(0, 2, 1, 3).reshape(B * L, H * hd)
+    err = (out.float() - ref).abs().max().item()
+    assert err < 2e-2, err
+    assert ops.device_error() == 0
+
+
+@pytest.mark.parametrize("L", [1, 63, 64, 65, 128, 129, 300, 848])
+@pytest.mark.parametrize("hd", [64, 128])
+def test_causal_gqa_attention(cuda, L, hd):
+    """Decoder prefill form: causal mask, 16 query heads over 2 kv heads (Qwen3 GQA)."""
+    run_gqa_causal(cuda, 2, 16, 2, L, hd, causal=True, seed=L + hd)
+
+
+def test_gqa_non_causal_and_two_tiles(cuda):
+    run_gqa_causal(cuda, 1, 8, 4, 300, 128, causal=False, seed=1)
+    run_gqa_causal(cuda, 2, 16, 2, 520, 128, causal=True, seed=2, tiles=2)
