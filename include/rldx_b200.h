@@ -212,9 +212,16 @@ typedef struct {
   int rows;
   int D;
   int64_t ld;
+  const void* w;  /* [D] RMSNorm weight (rldx_res_rmsnorm only) */
 } rldx_res_ln_segment;
 
 int rldx_res_layernorm(const rldx_res_ln_segment* segs, int nseg, int fp32_sum, float eps, void* stream);
+
+/* Same sums (bf16 after each add), then Qwen3 RMSNorm with weight instead of LayerNorm:
+ * ln_out = bf16(w * bf16(sum * rsqrt(mean(sum^2) + eps)))  (Qwen3VLTextRMSNorm,
+ * rldx/model/modules/backbone/modeling_qwen3_vl.py:357-374; with y = the residual it is the
+ * reference's fused_epilogue_add2_rmsnorm, rldx/inference/backbone/llm/engine/ops/). */
+int rldx_res_rmsnorm(const rldx_res_ln_segment* segs, int nseg, float eps, void* stream);
 
 /* ------------------------------------------------------------------------------------------
  * Bias + SwiGLU over up to 2 row groups, all in fp32 with one rounding:
@@ -418,6 +425,61 @@ int rldx_msat_profile(rldx_msat* h, const rldx_msat_io* io, rldx_op_profile* ops
  * action state.  With dst == NULL only *rows / *cols are set. */
 int rldx_msat_read_buffer(const rldx_msat* h, int which, void* dst, int64_t dst_bytes,
                           int64_t* rows, int64_t* cols, void* stream);
+
+/* ------------------------------------------------------------------------------------------
+ * VLM backbone prefill: a stack of Qwen3 decoder layers over B sequences of T tokens, captured
+ * as one CUDA graph.  Replaces CustomLLMChain.forward
+ * (rldx/inference/backbone/llm/engine/custom_llm_chain.py:63-170) and the eager
+ * Qwen3VLTextDecoderLayer stack (rldx/model/modules/backbone/modeling_qwen3_vl.py:357-560):
+ * per layer input RMSNorm -> fused q|k|v projection -> per-head q/k RMSNorm + rotate-half RoPE
+ * -> causal grouped-query attention -> o_proj + residual -> post-attention RMSNorm -> SwiGLU MLP
+ * (gate, up, down) + residual; optional final RMSNorm.  No projection has a bias (Qwen3).
+ * RoPE tables are the caller's [T, head_dim] bf16 cos / sin (the rotary embedding's output,
+ * mRoPE included; sin unsigned -- rotate_half supplies the sign).
+ * ------------------------------------------------------------------------------------------ */
+typedef struct rldx_llm rldx_llm;
+
+typedef struct {
+  int batch;      /* sequences per call */
+  int tokens;     /* T, tokens per sequence */
+  int hidden;     /* D */
+  int q_heads;
+  int kv_heads;   /* divides q_heads */
+  int head_dim;   /* 128 */
+  int ffn;        /* MLP intermediate size */
+  int layers;
+  float rms_eps;
+  int final_norm; /* 1: apply the final RMSNorm (CustomLLMChain apply_final_norm) */
+  int use_graph;  /* 1: capture the stack as one CUDA graph */
+} rldx_llm_config;
+
+typedef struct {
+  const void* input_norm; /* [D] */
+  const void* q_proj;     /* [q_heads*head_dim, D] */
+  const void* k_proj;     /* [kv_heads*head_dim, D] */
+  const void* v_proj;     /* [kv_heads*head_dim, D] */
+  const void* q_norm;     /* [head_dim] */
+  const void* k_norm;     /* [head_dim] */
+  const void* o_proj;     /* [D, q_heads*head_dim] */
+  const void* post_norm;  /* [D] */
+  const void* gate_proj;  /* [ffn, D] */
+  const void* up_proj;    /* [ffn, D] */
+  const void* down_proj;  /* [D, ffn] */
+} rldx_llm_layer_weights;
+
+typedef struct {
+  const rldx_llm_layer_weights* layers; /* [layers] (host array of device or host pointers) */
+  const void* final_norm;               /* [D] (final_norm = 1) */
+  const void* rope_cos;                 /* [tokens, head_dim] bf16 */
+  const void* rope_sin;                 /* [tokens, head_dim] bf16 */
+} rldx_llm_weights;
+
+int rldx_llm_create(const rldx_llm_config* cfg, const rldx_llm_weights* w, rldx_llm** out);
+int rldx_llm_destroy(rldx_llm* h);
+/* hidden_in / hidden_out: [batch, tokens, hidden] bf16 device pointers; asynchronous on stream. */
+int rldx_llm_prefill(rldx_llm* h, const void* hidden_in, void* hidden_out, void* stream);
+/* kernel launches of one prefill (graph nodes when captured) */
+int rldx_llm_launch_count(const rldx_llm* h);
 
 #ifdef __cplusplus
 }

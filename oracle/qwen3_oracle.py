@@ -1,0 +1,151 @@
+"""CPU oracle of the VLM backbone prefill: a stack of Qwen3 text decoder layers.
+
+TEST INFRASTRUCTURE ONLY: the checker for rldx_llm_* (rldx-1_b200/csrc/llm.cu).  Only tests/,
+__graft_entry__.smoke() and bench.py's CPU baseline may import it; the product path never does.
+
+Restates rldx/model/modules/backbone/modeling_qwen3_vl.py (the reference's vendored Qwen3-VL
+text model) step for step, with its module tree and parameter names so a reference state_dict
+loads with strict=True:
+  Qwen3VLTextRMSNorm        :357-374  fp32 variance, cast to the input dtype, then * weight
+  rotate_half               :118-122
+  apply_rotary_pos_emb      :377-401  q * cos + rotate_half(q) * sin in the input dtype
+  Qwen3VLTextAttention      :404-490  per-head q/k RMSNorm before RoPE; sdpa with GQA, causal
+  Qwen3VLTextMLP            :493-506  down(silu(gate(x)) * up(x)), no biases
+  Qwen3VLTextDecoderLayer   :509-560  pre-norm residual blocks
+The attention call is transformers' sdpa_attention_forward for a causal prefill without a mask:
+F.scaled_dot_product_attention(q, k, v, scale=head_dim**-0.5, is_causal=True, enable_gqa=True).
+Pinned against golden vectors of the reference's own layers: tests/golden/make_golden_llm.py.
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import torch
+import torch.nn.functional as F
+from torch import nn
+
+
+@dataclass
+class Qwen3Config:
+    """VLM-shaped decoder dims (BASELINE config 5 defaults: hidden 2048, GQA 16 / 2 x 128, FFN 11008)."""
+
+    hidden: int = 2048
+    q_heads: int = 16
+    kv_heads: int = 2
+    head_dim: int = 128
+    ffn: int = 11008
+    layers: int = 12
+    rms_eps: float = 1e-6
+    rope_theta: float = 1e6
+
+
+class RMSNorm(nn.Module):
+    def __init__(self, dim: int, eps: float = 1e-6):
+        super().__init__()
+        self.weight = nn.Parameter(torch.ones(dim))
+        self.variance_epsilon = eps
+
+    def forward(self, x):
+        dt = x.dtype
+        h = x.to(torch.float32)
+        h = h * torch.rsqrt(h.pow(2).mean(-1, keepdim=True) + self.variance_epsilon)
+        return self.weight * h.to(dt)
+
+
+def rotate_half(x):
+    x1, x2 = x[..., : x.shape[-1] // 2], x[..., x.shape[-1] // 2:]
+    return torch.cat((-x2, x1), dim=-1)
+
+
+def apply_rope(q, k, cos, sin):
+    cos, sin = cos.unsqueeze(1), sin.unsqueeze(1)
+    return q * cos + rotate_half(q) * sin, k * cos + rotate_half(k) * sin
+
+
+class Attention(nn.Module):
+    def __init__(self, c: Qwen3Config):
+        super().__init__()
+        self.c = c
+        self.head_dim = c.head_dim
+        self.scaling = c.head_dim ** -0.5
+        self.q_proj = nn.Linear(c.hidden, c.q_heads * c.head_dim, bias=False)
+        self.k_proj = nn.Linear(c.hidden, c.kv_heads * c.head_dim, bias=False)
+        self.v_proj = nn.Linear(c.hidden, c.kv_heads * c.head_dim, bias=False)
+        self.o_proj = nn.Linear(c.q_heads * c.head_dim, c.hidden, bias=False)
+        self.q_norm = RMSNorm(c.head_dim, c.rms_eps)
+        self.k_norm = RMSNorm(c.head_dim, c.rms_eps)
+
+    def forward(self, x, cos, sin):
+        B, T, _ = x.shape
+        shape = (B, T, -1, self.head_dim)
+        q = self.q_norm(self.q_proj(x).view(shape)).transpose(1, 2)
+        k = self.k_norm(self.k_proj(x).view(shape)).transpose(1, 2)
+        v = self.v_proj(x).view(shape).transpose(1, 2)
+        q, k = apply_rope(q, k, cos, sin)
+        o = F.scaled_dot_product_attention(q, k, v, scale=self.scaling, is_causal=T > 1, enable_gqa=True)
+        return self.o_proj(o.transpose(1, 2).reshape(B, T, -1))
+
+
+class MLP(nn.Module):
+    def __init__(self, c: Qwen3Config):
+        super().__init__()
+        self.gate_proj = nn.Linear(c.hidden, c.ffn, bias=False)
+        self.up_proj = nn.Linear(c.hidden, c.ffn, bias=False)
+        self.down_proj = nn.Linear(c.ffn, c.hidden, bias=False)
+
+    def forward(self, x):
+        return self.down_proj(F.silu(self.gate_proj(x)) * self.up_proj(x))
+
+
+class DecoderLayer(nn.Module):
+    def __init__(self, c: Qwen3Config):
+        super().__init__()
+        self.self_attn = Attention(c)
+        self.mlp = MLP(c)
+        self.input_layernorm = RMSNorm(c.hidden, c.rms_eps)
+        self.post_attention_layernorm = RMSNorm(c.hidden, c.rms_eps)
+
+    def forward(self, h, cos, sin):
+        h = h + self.self_attn(self.input_layernorm(h), cos, sin)
+        return h + self.mlp(self.post_attention_layernorm(h))
+
+
+class TextStack(nn.Module):
+    """`layers` decoder layers and the final norm (the text model's `layers` and `norm`)."""
+
+    def __init__(self, c: Qwen3Config):
+        super().__init__()
+        self.c = c
+        self.layers = nn.ModuleList(DecoderLayer(c) for _ in range(c.layers))
+        self.norm = RMSNorm(c.hidden, c.rms_eps)
+
+    @torch.no_grad()
+    def forward(self, h, cos, sin, final_norm: bool = True, return_hidden: bool = False):
+        hidden = []
+        for layer in self.layers:
+            h = layer(h, cos, sin)
+            hidden.append(h)
+        out = self.norm(h) if final_norm else h
+        return (out, hidden) if return_hidden else out
+
+
+def rope_tables(c: Qwen3Config, positions: torch.Tensor, dtype=torch.float32):
+    """1-D text RoPE: cos / sin [T, head_dim] of positions (the default rotary embedding with all
+    three mRoPE sections on the same position, modeling_qwen3_vl.py:293-354)."""
+    inv = 1.0 / (c.rope_theta ** (torch.arange(0, c.head_dim, 2, dtype=torch.int64).float() / c.head_dim))
+    freqs = positions.float()[:, None] * inv[None, :]
+    emb = torch.cat([freqs, freqs], dim=-1)
+    return emb.cos().to(dtype), emb.sin().to(dtype)
+
+
+def init_weights(module: nn.Module, seed: int, std: float = 0.02) -> nn.Module:
+    """Seeded random init: linear weights ~ N(0, std), norm weights ~ 1 + N(0, 0.1)."""
+    g = torch.Generator().manual_seed(seed)
+    with torch.no_grad():
+        for name, p in sorted(module.named_parameters(), key=lambda kv: kv[0]):
+            if name.endswith("norm.weight") or name.endswith("layernorm.weight") or name == "weight":
+                p.copy_((1.0 + 0.1 * torch.randn(p.shape, generator=g)).to(p.dtype))
+            else:
+                p.copy_((torch.randn(p.shape, generator=g) * std).to(p.dtype))
+    return module

@@ -124,12 +124,28 @@ class QkvSegment(C.Structure):
 
 class ResLnSegment(C.Structure):
     _fields_ = [("x", vp), ("y", vp), ("v1", vp), ("v2", vp), ("sum_out", vp), ("ln_out", vp),
-                ("rows", C.c_int), ("D", C.c_int), ("ld", i64)]
+                ("rows", C.c_int), ("D", C.c_int), ("ld", i64), ("w", vp)]
 
 
 class SwigluBiasSegment(C.Structure):
     _fields_ = [("gate", vp), ("up", vp), ("bias_gate", vp), ("bias_up", vp), ("out", vp),
                 ("ld_in", i64), ("ld_out", i64), ("rows", C.c_int), ("H", C.c_int)]
+
+
+class LlmConfig(C.Structure):
+    _fields_ = [("batch", C.c_int), ("tokens", C.c_int), ("hidden", C.c_int), ("q_heads", C.c_int),
+                ("kv_heads", C.c_int), ("head_dim", C.c_int), ("ffn", C.c_int), ("layers", C.c_int),
+                ("rms_eps", C.c_float), ("final_norm", C.c_int), ("use_graph", C.c_int)]
+
+
+class LlmLayerWeights(C.Structure):
+    _fields_ = [(n, vp) for n in ("input_norm", "q_proj", "k_proj", "v_proj", "q_norm", "k_norm", "o_proj",
+                                  "post_norm", "gate_proj", "up_proj", "down_proj")]
+
+
+class LlmWeights(C.Structure):
+    _fields_ = [("layers", C.POINTER(LlmLayerWeights)), ("final_norm", vp), ("rope_cos", vp),
+                ("rope_sin", vp)]
 
 
 class MsatIO(C.Structure):
@@ -152,9 +168,14 @@ SIGNATURES = {
                                        C.POINTER(vp), C.POINTER(C.c_int), C.c_int, C.c_int, vp]),
     "rldx_layernorm": (C.c_int, [vp, i64, vp, i64, C.c_int, C.c_int, C.c_float, vp, vp, vp]),
     "rldx_attention": (C.c_int, [C.POINTER(AttentionDesc), vp]),
+    "rldx_llm_create": (C.c_int, [C.POINTER(LlmConfig), C.POINTER(LlmWeights), C.POINTER(vp)]),
+    "rldx_llm_destroy": (C.c_int, [vp]),
+    "rldx_llm_prefill": (C.c_int, [vp, vp, vp, vp]),
+    "rldx_llm_launch_count": (C.c_int, [vp]),
     "rldx_qkv_prep": (C.c_int, [C.POINTER(QkvSegment), C.c_int, C.c_int, C.c_int, C.c_int, C.c_int,
                                 C.c_float, vp, vp, vp, vp]),
     "rldx_res_layernorm": (C.c_int, [C.POINTER(ResLnSegment), C.c_int, C.c_int, C.c_float, vp]),
+    "rldx_res_rmsnorm": (C.c_int, [C.POINTER(ResLnSegment), C.c_int, C.c_float, vp]),
     "rldx_swiglu_bias": (C.c_int, [C.POINTER(SwigluBiasSegment), C.c_int, vp]),
     "rldx_qk_rmsnorm_rope": (C.c_int, [vp, vp, vp, vp, vp, vp, i64, C.c_int, C.c_int,
                                        C.c_float, vp]),

@@ -636,7 +636,7 @@ using namespace rldx;
 
 extern "C" {
 
-int rldx_version(void) { return 107; }
+int rldx_version(void) { return 108; }
 
 const char* rldx_last_error(void) { return t_last_error.c_str(); }
 
@@ -839,7 +839,17 @@ int rldx_qkv_prep(const rldx_qkv_segment* segs, int nseg, int B, int H, int L, i
   return RLDX_OK;
 }
 
+static int res_norm_impl(const rldx_res_ln_segment* segs, int nseg, int fp32_sum, int rms, float eps, void* stream);
+
 int rldx_res_layernorm(const rldx_res_ln_segment* segs, int nseg, int fp32_sum, float eps, void* stream) {
+  return res_norm_impl(segs, nseg, fp32_sum, 0, eps, stream);
+}
+
+int rldx_res_rmsnorm(const rldx_res_ln_segment* segs, int nseg, float eps, void* stream) {
+  return res_norm_impl(segs, nseg, 0, 1, eps, stream);
+}
+
+static int res_norm_impl(const rldx_res_ln_segment* segs, int nseg, int fp32_sum, int rms, float eps, void* stream) {
   int rc = ensure_device();
   if (rc != RLDX_OK) return rc;
   if (!segs || nseg < 1 || nseg > 2) return set_error(RLDX_ERR_ARG, "res_layernorm: need 1 or 2 segments");
@@ -857,6 +867,8 @@ int rldx_res_layernorm(const rldx_res_ln_segment* segs, int nseg, int fp32_sum, 
     d.y = static_cast<const __nv_bfloat16*>(s.y);
     d.v1 = static_cast<const __nv_bfloat16*>(s.v1);
     d.v2 = static_cast<const __nv_bfloat16*>(s.v2);
+    if (rms && (!s.w || !aligned16(s.w))) return set_error(RLDX_ERR_ARG, "res_rmsnorm: need a 16-byte aligned weight");
+    d.w = static_cast<const __nv_bfloat16*>(s.w);
     d.sum_out = static_cast<__nv_bfloat16*>(s.sum_out);
     d.ln_out = static_cast<__nv_bfloat16*>(s.ln_out);
     d.rows = s.rows;
@@ -869,6 +881,7 @@ int rldx_res_layernorm(const rldx_res_ln_segment* segs, int nseg, int fp32_sum, 
   p.nseg = nseg;
   p.total_rows = row;
   p.fp32_sum = fp32_sum ? 1 : 0;
+  p.rms = rms ? 1 : 0;
   p.eps = eps;
   cudaError_t e = launch_res_ln(p, static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "res_layernorm launch");
@@ -948,11 +961,22 @@ int rldx_qk_rmsnorm_rope(const void* x, void* y, const void* w, const int32_t* p
   if (head_dim != 128) return set_error(RLDX_ERR_UNSUPPORTED, "qk_rmsnorm_rope: head_dim must be 128");
   if (!aligned16(x) || !aligned16(y) || !aligned16(w) || !aligned16(cos_table) || !aligned16(sin_table))
     return set_error(RLDX_ERR_ARG, "qk_rmsnorm_rope: pointers must be 16-byte aligned");
-  cudaError_t e = launch_qk_rmsnorm_rope(
-      static_cast<const __nv_bfloat16*>(x), static_cast<__nv_bfloat16*>(y),
-      static_cast<const __nv_bfloat16*>(w), pos, static_cast<const __nv_bfloat16*>(cos_table),
-      static_cast<const __nv_bfloat16*>(sin_table), tokens * heads, heads, eps,
-      static_cast<cudaStream_t>(stream));
+  if (tokens * heads >= (1LL << 31)) return set_error(RLDX_ERR_UNSUPPORTED, "qk_rmsnorm_rope: too many rows");
+  QkNormRopeParams p;
+  std::memset(&p, 0, sizeof(p));
+  p.x = static_cast<const __nv_bfloat16*>(x);
+  p.x_tok_stride = static_cast<long long>(heads) * 128;
+  p.y = static_cast<__nv_bfloat16*>(y);
+  p.wq = p.wk = static_cast<const __nv_bfloat16*>(w);
+  p.pos = pos;
+  p.cos = static_cast<const __nv_bfloat16*>(cos_table);
+  p.sin = static_cast<const __nv_bfloat16*>(sin_table);
+  p.nrows = static_cast<unsigned>(tokens * heads);
+  p.heads = p.Hq = static_cast<unsigned>(heads);
+  p.T = static_cast<unsigned>(tokens);
+  p.layout = 0;
+  p.eps = eps;
+  cudaError_t e = launch_qk_rmsnorm_rope(p, static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "qk_rmsnorm_rope launch");
   return RLDX_OK;
 }

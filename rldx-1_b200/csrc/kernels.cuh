@@ -62,10 +62,28 @@ struct CopyParams {
 };
 cudaError_t launch_copy(const CopyParams& p, int blocks, cudaStream_t stream, bool pdl);
 
-cudaError_t launch_qk_rmsnorm_rope(const __nv_bfloat16* x, __nv_bfloat16* y, const __nv_bfloat16* w,
-                                   const int* pos, const __nv_bfloat16* cos_t,
-                                   const __nv_bfloat16* sin_t, long long nrows, int heads,
-                                   float eps, cudaStream_t stream);
+// Qwen3 per-head RMSNorm (cast, then weight) + rotate-half RoPE over rows (token, head) of
+// 128 dims.  Token tok's head h is at x + tok * x_tok_stride + h * 128; heads < Hq use wq, the
+// others wk; the RoPE row of a token is pos[tok] (or tok % T without pos).  layout 0 writes
+// y[row * 128]; layout 1 writes the attention layout q [B, Hq, T, 128] / k [B, heads - Hq, T, 128].
+struct QkNormRopeParams {
+  const __nv_bfloat16* x;
+  long long x_tok_stride;
+  __nv_bfloat16* y;
+  __nv_bfloat16* q;
+  __nv_bfloat16* k;
+  const __nv_bfloat16* wq;
+  const __nv_bfloat16* wk;
+  const int* pos;
+  const __nv_bfloat16* cos;
+  const __nv_bfloat16* sin;
+  unsigned nrows, heads, Hq, T;
+  int layout;
+  float eps;
+};
+cudaError_t launch_qk_rmsnorm_rope(const QkNormRopeParams& p, cudaStream_t stream);
+cudaError_t launch_v_transpose(const __nv_bfloat16* v, long long ld, __nv_bfloat16* vt, int B, int T, int Tp,
+                               int Hkv, cudaStream_t stream);
 cudaError_t launch_swiglu(const __nv_bfloat16* gate, const __nv_bfloat16* up, __nv_bfloat16* out,
                           long long rows, int H, long long ld_in, long long ld_out, int sms,
                           cudaStream_t stream);
@@ -75,18 +93,21 @@ cudaError_t launch_swiglu(const __nv_bfloat16* gate, const __nv_bfloat16* up, __
 // fp32_sum = 0: bf16 rounding after each add in the order x, v1, v2, y (eager order of
 // ds::vl_epilogue_ln / ss::fused_epilogue_ln); 1: one fp32 sum in the order x, y, v1, v2 with no
 // rounding (ds::grouped_res_ln).  sum_out (optional) gets bf16(sum); ln_out = LN(sum).
+// rms = 1: Qwen3 RMSNorm instead of LayerNorm: ln_out = bf16(w * bf16(sum * rsqrt(mean(sum^2) + eps)))
+// (rldx/model/modules/backbone/modeling_qwen3_vl.py:357-374), w [D] per segment.
 struct ResLnSeg {
   const __nv_bfloat16* x;
   const __nv_bfloat16* y;
   const __nv_bfloat16* v1;
   const __nv_bfloat16* v2;
+  const __nv_bfloat16* w;
   __nv_bfloat16* sum_out;
   __nv_bfloat16* ln_out;
   int rows, D, ld, row_begin;
 };
 struct ResLnParams {
   ResLnSeg seg[2];
-  int nseg, total_rows, dmax, fp32_sum;
+  int nseg, total_rows, dmax, fp32_sum, rms;
   float eps;
 };
 cudaError_t launch_res_ln(const ResLnParams& p, cudaStream_t stream);

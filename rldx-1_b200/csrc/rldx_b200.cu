@@ -6,3 +6,4 @@
 #include "capi.cu"
 #include "static_ws.cu"
 #include "msat.cu"
+#include "llm.cu"

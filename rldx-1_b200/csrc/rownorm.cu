@@ -176,34 +176,31 @@ constexpr int kQkRows = 4;
 __device__ __forceinline__ __nv_bfloat162 as_bf2(uint32_t u) { return *reinterpret_cast<__nv_bfloat162*>(&u); }
 __device__ __forceinline__ uint32_t as_u32(__nv_bfloat162 h) { return *reinterpret_cast<uint32_t*>(&h); }
 
-__global__ void __launch_bounds__(256) qk_rmsnorm_rope_kernel(
-    const __nv_bfloat16* __restrict__ x, __nv_bfloat16* __restrict__ y,
-    const __nv_bfloat16* __restrict__ w, const int* __restrict__ pos,
-    const __nv_bfloat16* __restrict__ cos_t, const __nv_bfloat16* __restrict__ sin_t,
-    unsigned nrows, unsigned heads, float eps) {
+__global__ void __launch_bounds__(256) qk_rmsnorm_rope_kernel(const __grid_constant__ QkNormRopeParams P) {
   const unsigned half_global = (blockIdx.x * blockDim.x + threadIdx.x) >> 4;
   const int hl = threadIdx.x & 15;
   const unsigned row0 = half_global * kQkRows;
-  uint4 u[kQkRows];
+  uint4 u[kQkRows], uc[kQkRows], us[kQkRows], uw[kQkRows];
 #pragma unroll
   for (int k = 0; k < kQkRows; ++k) {
-    const unsigned row = min(row0 + k, nrows - 1);  // clamped: the tail rows are not stored
-    u[k] = __ldcs(reinterpret_cast<const uint4*>(x + static_cast<size_t>(row) * 128) + hl);
+    const unsigned row = min(row0 + k, P.nrows - 1);  // clamped: the tail rows are not stored
+    const unsigned tok = row / P.heads, head = row - tok * P.heads;
+    u[k] = __ldcs(reinterpret_cast<const uint4*>(P.x + tok * P.x_tok_stride + head * 128) + hl);
   }
-  uint4 uc[kQkRows], us[kQkRows];
 #pragma unroll
   for (int k = 0; k < kQkRows; ++k) {
-    const unsigned row = min(row0 + k, nrows - 1);
-    const int p = __ldg(pos + row / heads);
-    uc[k] = __ldg(reinterpret_cast<const uint4*>(cos_t + static_cast<size_t>(p) * 128) + hl);
-    us[k] = __ldg(reinterpret_cast<const uint4*>(sin_t + static_cast<size_t>(p) * 128) + hl);
+    const unsigned row = min(row0 + k, P.nrows - 1);
+    const unsigned tok = row / P.heads, head = row - tok * P.heads;
+    const int p = P.pos ? __ldg(P.pos + tok) : static_cast<int>(tok % P.T);
+    uc[k] = __ldg(reinterpret_cast<const uint4*>(P.cos + static_cast<size_t>(p) * 128) + hl);
+    us[k] = __ldg(reinterpret_cast<const uint4*>(P.sin + static_cast<size_t>(p) * 128) + hl);
+    uw[k] = __ldg(reinterpret_cast<const uint4*>(head < P.Hq ? P.wq : P.wk) + hl);
   }
-  const uint4 uw = __ldg(reinterpret_cast<const uint4*>(w) + hl);
-  const uint32_t wv[4] = {uw.x, uw.y, uw.z, uw.w};
   const uint32_t sign = (hl < 8) ? 0x80008000u : 0u;  // rotate_half = cat(-x2, x1)
 #pragma unroll
   for (int k = 0; k < kQkRows; ++k) {
     const uint32_t xv[4] = {u[k].x, u[k].y, u[k].z, u[k].w};
+    const uint32_t wv[4] = {uw[k].x, uw[k].y, uw[k].z, uw[k].w};
     float v[8];
 #pragma unroll
     for (int i = 0; i < 4; ++i) unpack_bf16x2(xv[i], v[2 * i], v[2 * i + 1]);
@@ -212,7 +209,7 @@ __global__ void __launch_bounds__(256) qk_rmsnorm_rope_kernel(
     for (int e = 0; e < 8; ++e) ss = fmaf(v[e], v[e], ss);
 #pragma unroll
     for (int o = 8; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-    const float rstd = rsqrtf(ss * (1.0f / 128.0f) + eps);
+    const float rstd = rsqrtf(ss * (1.0f / 128.0f) + P.eps);
     uint32_t yv[4], pv[4];
 #pragma unroll
     for (int i = 0; i < 4; ++i)
@@ -225,22 +222,69 @@ __global__ void __launch_bounds__(256) qk_rmsnorm_rope_kernel(
 #pragma unroll
     for (int i = 0; i < 4; ++i)
       ov[i] = as_u32(__hadd2_rn(__hmul2_rn(as_bf2(yv[i]), as_bf2(cv[i])), __hmul2_rn(as_bf2(pv[i]), as_bf2(sv[i]))));
-    if (row0 + k < nrows)
-      __stcs(reinterpret_cast<uint4*>(y + static_cast<size_t>(row0 + k) * 128) + hl,
-             make_uint4(ov[0], ov[1], ov[2], ov[3]));
+    const unsigned row = row0 + k;
+    if (row < P.nrows) {
+      __nv_bfloat16* dst;
+      if (P.layout == 0) {
+        dst = P.y + static_cast<size_t>(row) * 128;
+      } else {  // attention layout: q [B, Hq, T, 128] or k [B, H - Hq, T, 128]
+        const unsigned tok = row / P.heads, head = row - tok * P.heads;
+        const unsigned b = tok / P.T, t = tok - b * P.T;
+        dst = head < P.Hq ? P.q + ((static_cast<size_t>(b) * P.Hq + head) * P.T + t) * 128
+                          : P.k + ((static_cast<size_t>(b) * (P.heads - P.Hq) + head - P.Hq) * P.T + t) * 128;
+      }
+      __stcs(reinterpret_cast<uint4*>(dst) + hl, make_uint4(ov[0], ov[1], ov[2], ov[3]));
+    }
   }
 }
 
-cudaError_t launch_qk_rmsnorm_rope(const __nv_bfloat16* x, __nv_bfloat16* y, const __nv_bfloat16* w,
-                                   const int* pos, const __nv_bfloat16* cos_t,
-                                   const __nv_bfloat16* sin_t, long long nrows, int heads,
-                                   float eps, cudaStream_t stream) {
-  if (nrows <= 0 || nrows >= (1ll << 31) || heads <= 0) return cudaErrorInvalidValue;
-  const long long halves = (nrows + kQkRows - 1) / kQkRows;
+cudaError_t launch_qk_rmsnorm_rope(const QkNormRopeParams& p, cudaStream_t stream) {
+  if (p.nrows == 0 || p.nrows >= (1u << 31) || p.heads == 0 || p.Hq == 0 || p.Hq > p.heads || p.T == 0)
+    return cudaErrorInvalidValue;
+  const long long halves = (static_cast<long long>(p.nrows) + kQkRows - 1) / kQkRows;
   const int block = 256;
   const long long grid = (halves * 16 + block - 1) / block;
-  qk_rmsnorm_rope_kernel<<<static_cast<unsigned>(grid), block, 0, stream>>>(
-      x, y, w, pos, cos_t, sin_t, static_cast<unsigned>(nrows), static_cast<unsigned>(heads), eps);
+  qk_rmsnorm_rope_kernel<<<static_cast<unsigned>(grid), block, 0, stream>>>(p);
+  return cudaGetLastError();
+}
+
+// ---------------------------------------------------------------------------------------------
+// V^T for the attention kernel from projected rows: v [B*T tokens, row stride ld] with kv head
+// h at columns h*128..h*128+127  ->  vt [B, Hkv, 128, Tp].  One CTA = 32 tokens x one kv head
+// of one batch element, through shared memory so both sides move 16-byte vectors.
+// ---------------------------------------------------------------------------------------------
+__global__ void __launch_bounds__(256) v_transpose_kernel(const __nv_bfloat16* __restrict__ v, long long ld,
+                                                          __nv_bfloat16* __restrict__ vt, int T, int Tp, int Hkv) {
+  __shared__ __align__(16) __nv_bfloat16 tile[128][40];  // [dim][token]
+  const int t0 = blockIdx.x * 32, hv = blockIdx.y, b = blockIdx.z;
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {  // 32 tokens x 16 chunks of 8 dims
+    const int idx = threadIdx.x + 256 * i;
+    const int tl = idx >> 4, ch = idx & 15;
+    const int t = t0 + tl;
+    uint4 u = make_uint4(0u, 0u, 0u, 0u);
+    if (t < T) u = *reinterpret_cast<const uint4*>(v + (static_cast<size_t>(b) * T + t) * ld + hv * 128 + ch * 8);
+    const __nv_bfloat16* e = reinterpret_cast<const __nv_bfloat16*>(&u);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) tile[ch * 8 + j][tl] = e[j];
+  }
+  __syncthreads();
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {  // 128 dims x 4 groups of 8 tokens
+    const int idx = threadIdx.x + 256 * i;
+    const int d = idx >> 2, grp = idx & 3;
+    const int t = t0 + grp * 8;
+    if (t < Tp)
+      *reinterpret_cast<uint4*>(vt + ((static_cast<size_t>(b) * Hkv + hv) * 128 + d) * Tp + t) =
+          *reinterpret_cast<const uint4*>(&tile[d][grp * 8]);
+  }
+}
+
+cudaError_t launch_v_transpose(const __nv_bfloat16* v, long long ld, __nv_bfloat16* vt, int B, int T, int Tp,
+                               int Hkv, cudaStream_t stream) {
+  if (B <= 0 || T <= 0 || Tp < T || Tp % 8 || Hkv <= 0) return cudaErrorInvalidValue;
+  const dim3 grid(static_cast<unsigned>((T + 31) / 32), static_cast<unsigned>(Hkv), static_cast<unsigned>(B));
+  v_transpose_kernel<<<grid, 256, 0, stream>>>(v, ld, vt, T, Tp, Hkv);
   return cudaGetLastError();
 }
 
@@ -454,7 +498,7 @@ __global__ void __launch_bounds__(128) res_ln_kernel(const __grid_constant__ Res
   }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
-  const float mean = sum / static_cast<float>(sg.D);
+  const float mean = P.rms ? 0.0f : sum / static_cast<float>(sg.D);  // RMSNorm: no centring
   float var = 0.0f;
 #pragma unroll
   for (int i = 0; i < kVec; ++i)
@@ -467,6 +511,22 @@ __global__ void __launch_bounds__(128) res_ln_kernel(const __grid_constant__ Res
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) var += __shfl_xor_sync(0xffffffffu, var, o);
   const float rstd = rsqrtf(var / static_cast<float>(sg.D) + P.eps);
+  if (P.rms) {  // cast, then the bf16 weight (packed multiply: exact product, one rounding)
+#pragma unroll
+    for (int i = 0; i < kVec; ++i) {
+      const int v = lane + 32 * i;
+      if (v < nvec) {
+        const uint4 uw = reinterpret_cast<const uint4*>(sg.w)[v];
+        const uint32_t wv[4] = {uw.x, uw.y, uw.z, uw.w};
+        uint32_t ov[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+          ov[k] = as_u32(__hmul2_rn(as_bf2(wv[k]), __floats2bfloat162_rn(x[i][2 * k] * rstd, x[i][2 * k + 1] * rstd)));
+        reinterpret_cast<uint4*>(sg.ln_out + off)[v] = make_uint4(ov[0], ov[1], ov[2], ov[3]);
+      }
+    }
+    return;
+  }
 #pragma unroll
   for (int i = 0; i < kVec; ++i) {
     const int v = lane + 32 * i;
