@@ -2,6 +2,7 @@
 
     python -m rldx_b200.microbench --suite c3    # memory-bound: Qwen3 QK-RMSNorm+RoPE, SwiGLU
     python -m rldx_b200.microbench --suite c4    # joint-attention sweep, head_dim 128
+    python -m rldx_b200.microbench --suite vlm   # config-5 VLM-shaped prefill (12 Qwen3 layers)
     python -m rldx_b200.microbench --suite all
 
 Each case prints one JSON line: device time per launch group from CUDA events on the launching
@@ -17,6 +18,12 @@ Config 3 (the Qwen3 backbone path: rldx/model/modules/backbone/modeling_qwen3_vl
 [65536 tokens, 16 heads, 128], positions 0..4095 repeated, theta 1e6; algorithmic bytes = each
 tensor read once and written once.  SwiGLU silu(gate) * up on [65536, 8960]: gate and up read
 once, the product written once.
+
+VLM prefill (the first part of BASELINE config 5): 12 Qwen3 decoder layers (hidden 2048, GQA
+16 / 2 x 128, SwiGLU 11008) over 848 tokens (4 frames x 196 patches + 64 text) per observation,
+final RMSNorm, seeded random weights and inputs, 1-D RoPE positions 0..847; one call =
+B200LLMChain.forward (the whole stack as one CUDA graph).  FLOPs per call = 2 * tokens *
+(projection weights) + 2 * B * heads * T^2 * 128 (causal attention, half of the square).
 
 Config 4: non-causal joint attention over [cognition | physics | action] segments of lengths
 (L-48):32:16, 16 heads x 128, batch 1-64; FLOPs = 4 * B * H * L^2 * 128.  torch's
@@ -127,9 +134,63 @@ def suite_c4(iters: int, warmup: int, batches=(1, 4, 16, 64), lengths=(288, 544,
             del q, k, v, vt, outs
 
 
+def suite_vlm(iters: int, warmup: int, batches=(1, 8, 32), layers: int = 12, T: int = 848):
+    from types import SimpleNamespace as NS
+
+    from .llm import B200LLMChain
+
+    dev = torch.device("cuda", torch.cuda.current_device())
+    _, tflops, src = peaks()
+    D, Hq, Hkv, hd, Fd = 2048, 16, 2, 128, 11008
+    g = torch.Generator(device=dev).manual_seed(11)
+
+    def w(*shape, mean=0.0, std=0.02):
+        return (torch.randn(*shape, device=dev, generator=g) * std + mean).to(BF)
+
+    def lin(o, i):
+        return NS(weight=w(o, i), bias=None)
+
+    stack = []
+    for _ in range(layers):
+        stack.append(NS(
+            input_layernorm=NS(weight=w(D, mean=1.0, std=0.1), variance_epsilon=1e-6),
+            post_attention_layernorm=NS(weight=w(D, mean=1.0, std=0.1)),
+            self_attn=NS(q_proj=lin(Hq * hd, D), k_proj=lin(Hkv * hd, D), v_proj=lin(Hkv * hd, D),
+                         o_proj=lin(D, Hq * hd), q_norm=NS(weight=w(hd, mean=1.0, std=0.1)),
+                         k_norm=NS(weight=w(hd, mean=1.0, std=0.1))),
+            mlp=NS(gate_proj=lin(Fd, D), up_proj=lin(Fd, D), down_proj=lin(D, Fd))))
+    norm = NS(weight=w(D, mean=1.0, std=0.1))
+    inv = 1.0 / (1e6 ** (torch.arange(0, hd, 2, device=dev).float() / hd))
+    ang = torch.arange(T, device=dev).float()[:, None] * inv[None, :]
+    emb = torch.cat([ang, ang], -1)
+    cos, sin = emb.cos().to(BF), emb.sin().to(BF)
+    ssin = sin.clone()
+    ssin[:, : hd // 2] *= -1
+    per_token = 2 * (D * (Hq + 2 * Hkv) * hd + Hq * hd * D + 3 * D * Fd) * layers
+    for B in batches:
+        chain = B200LLMChain(stack, nn_module(norm), cos, ssin)
+        x = torch.randn(B, T, D, device=dev, generator=g).to(BF)
+        ms = time_ms(lambda: chain(x), iters, warmup)
+        flops = per_token * B * T + 2.0 * B * Hq * T * T * hd * layers
+        yield {"suite": "vlm", "what": "12 x Qwen3 decoder layer prefill + final norm (one CUDA graph)",
+               "B": B, "tokens": T, "layers": layers, "hidden": D, "heads": f"{Hq}/{Hkv}x{hd}", "ffn": Fd,
+               "ms": ms, "ms_per_observation": ms / B, "flops": flops, "tflops": flops / ms / 1e9,
+               "peak_tflops": tflops, "frac": flops / ms / 1e9 / tflops, "peak_source": src,
+               "launches": chain.launches_per_call}
+        del chain, x
+        torch.cuda.empty_cache()
+
+
+def nn_module(ns):
+    """B200LLMChain stores the final norm as a submodule: wrap the weight holder."""
+    m = torch.nn.Module()
+    m.weight = torch.nn.Parameter(ns.weight, requires_grad=False)
+    return m
+
+
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--suite", choices=["c3", "c4", "all"], default="all")
+    ap.add_argument("--suite", choices=["c3", "c4", "vlm", "all"], default="all")
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--batches", type=str, default="1,4,16,64")
@@ -145,6 +206,9 @@ def main():
         bs = tuple(int(x) for x in a.batches.split(","))
         ls = tuple(int(x) for x in a.lengths.split(","))
         for r in suite_c4(a.iters, a.warmup, bs, ls, a.tiles):
+            print(json.dumps(r), flush=True)
+    if a.suite in ("vlm", "all"):
+        for r in suite_vlm(a.iters, a.warmup):
             print(json.dumps(r), flush=True)
     assert ops.device_error() == 0, "device error flag set"
 
