@@ -143,7 +143,10 @@ int rldx_joint_attention(const void* q, const void* k, const void* vt, int B, in
  *   kv_heads divides H (grouped-query attention: query head h reads kv head h / (H / kv_heads),
  *   repeat_kv of rldx/model/modules/backbone/modeling_qwen3_vl.py:139-151), 0 = H;
  *   causal 1: key j is visible to query i only for j <= i (the decoder prefill's causal mask);
- *   out[s] with row stride out_ld[s] elements (0: H*head_dim), nseg 1..3, sum(seg_len) == L.
+ *   out[s] with row stride out_ld[s] elements (0: H*head_dim), nseg 1..3, sum(seg_len) == L;
+ *   causal_block n > 1 makes the mask block-causal (key j visible to query i iff
+ *   j < (i / n + 1) * n); out_dim < head_dim writes only the first out_dim dims of each head
+ *   (a 96-dim head stored zero-padded to 128).
  * rldx_joint_attention is this with kv_heads = H, causal = 0 and dense outputs.
  * ------------------------------------------------------------------------------------------ */
 typedef struct {
@@ -158,6 +161,8 @@ typedef struct {
   int seg_len[3];
   int out_ld[3];
   int nseg;
+  int causal_block;
+  int out_dim;
 } rldx_attention_desc;
 
 int rldx_attention(const rldx_attention_desc* desc, void* stream);
@@ -451,6 +456,12 @@ typedef struct {
   float rms_eps;
   int final_norm; /* 1: apply the final RMSNorm (CustomLLMChain apply_final_norm) */
   int use_graph;  /* 1: capture the stack as one CUDA graph */
+  /* Variants for the memory module's TransformerMemory (rldx/model/modules/memory.py:150-370),
+   * a zero-filled tail gives the Qwen3 decoder: */
+  int no_qk_norm;        /* 1: no per-head q / k RMSNorm (RoPE only) */
+  int norm_weight_first; /* 1: RMSNorm = bf16(w * x * rsqrt(...)) in fp32 (norms.py:18-22);
+                            0: Qwen3's cast, then weight */
+  int causal_block;      /* 0 / 1: token-causal mask; n: block-causal over blocks of n tokens */
 } rldx_llm_config;
 
 typedef struct {

@@ -113,7 +113,8 @@ class AttentionDesc(C.Structure):
     _fields_ = [("q", vp), ("k", vp), ("vt", vp), ("B", C.c_int), ("H", C.c_int),
                 ("kv_heads", C.c_int), ("L", C.c_int), ("Lp", C.c_int), ("head_dim", C.c_int),
                 ("causal", C.c_int), ("tiles_per_cta", C.c_int), ("key_mask", vp),
-                ("out", vp * 3), ("seg_len", C.c_int * 3), ("out_ld", C.c_int * 3), ("nseg", C.c_int)]
+                ("out", vp * 3), ("seg_len", C.c_int * 3), ("out_ld", C.c_int * 3), ("nseg", C.c_int),
+                ("causal_block", C.c_int), ("out_dim", C.c_int)]
 
 
 class QkvSegment(C.Structure):
@@ -135,7 +136,8 @@ class SwigluBiasSegment(C.Structure):
 class LlmConfig(C.Structure):
     _fields_ = [("batch", C.c_int), ("tokens", C.c_int), ("hidden", C.c_int), ("q_heads", C.c_int),
                 ("kv_heads", C.c_int), ("head_dim", C.c_int), ("ffn", C.c_int), ("layers", C.c_int),
-                ("rms_eps", C.c_float), ("final_norm", C.c_int), ("use_graph", C.c_int)]
+                ("rms_eps", C.c_float), ("final_norm", C.c_int), ("use_graph", C.c_int),
+                ("no_qk_norm", C.c_int), ("norm_weight_first", C.c_int), ("causal_block", C.c_int)]
 
 
 class LlmLayerWeights(C.Structure):

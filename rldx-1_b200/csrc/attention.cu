@@ -97,8 +97,11 @@ __global__ void __launch_bounds__(AttnShape<kHD, kG>::kThreads, 1)
   const int kvh = P.kv_heads > 0 ? P.kv_heads : P.H;
   const int bh_kv = b * kvh + head / (P.H / kvh);  // GQA: K / V row of this query head
   const int L = P.L;
-  // key tiles this CTA needs: all of them, or (causal) those at or before its last query row
-  const int nkv = P.causal ? min((L + 63) / 64, (min(L, q0 + 128 * kG) - 1) / 64 + 1) : (L + 63) / 64;
+  // key tiles this CTA needs: all of them, or (causal) those a query row of the CTA can see:
+  // keys j < (i / cb + 1) * cb for row i (cb = 1: j <= i)
+  const int cb = P.causal_block > 1 ? P.causal_block : 1;
+  const int last_row = min(L, q0 + 128 * kG) - 1;
+  const int nkv = P.causal ? min((L + 63) / 64, (min(L, (last_row / cb + 1) * cb) - 1) / 64 + 1) : (L + 63) / 64;
   const int ng = (kG == 2 && q0 + 128 < L) ? 2 : 1;  // query tiles with rows inside L
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -257,10 +260,10 @@ __global__ void __launch_bounds__(AttnShape<kHD, kG>::kThreads, 1)
       // as 64 bytes once per tile, so the per-element work stays branch-free.
       const int kbase = j * 64;
       // keys of this tile visible to this row: inside the sequence and, when causal, <= the row
-      const int nvis = P.causal ? min(L, qrow + 1) - kbase : L - kbase;
+      const int nvis = P.causal ? min(L, (qrow / cb + 1) * cb) - kbase : L - kbase;
       float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
       // a tile below the diagonal for every row of the group needs no mask (warp-uniform test)
-      const bool full_tile = L - kbase >= 64 && (!P.causal || kbase + 63 <= q0 + 128 * g);
+      const bool full_tile = L - kbase >= 64 && (!P.causal || kbase + 63 < ((q0 + 128 * g) / cb + 1) * cb);
       if (kmask == nullptr && full_tile) {
 #pragma unroll
         for (int c = 0; c < 64; ++c) mx4[c & 3] = fmaxf(mx4[c & 3], sv[c]);
@@ -348,9 +351,10 @@ __global__ void __launch_bounds__(AttnShape<kHD, kG>::kThreads, 1)
         ++seg;
       }
       const float inv_l = 1.0f / l_run;
-      const int ld = P.seg_ld[seg] > 0 ? P.seg_ld[seg] : P.H * kHD;
+      const int od = P.out_dim > 0 ? P.out_dim : kHD;  // dims of a head written out
+      const int ld = P.seg_ld[seg] > 0 ? P.seg_ld[seg] : P.H * od;
       uint4* d4 = reinterpret_cast<uint4*>(
-          P.seg_out[seg] + (static_cast<size_t>(b) * P.seg_len[seg] + (qrow - off)) * ld + head * kHD);
+          P.seg_out[seg] + (static_cast<size_t>(b) * P.seg_len[seg] + (qrow - off)) * ld + head * od);
 #pragma unroll
       for (int half = 0; half < kHD / 64; ++half) {  // 64 output dims at a time
         float o[64];
@@ -360,6 +364,7 @@ __global__ void __launch_bounds__(AttnShape<kHD, kG>::kThreads, 1)
         if (qrow < L) {
 #pragma unroll
           for (int cc = 0; cc < 8; ++cc) {
+            if (64 * half + 8 * cc >= od) break;
             uint4 u;
             u.x = pack_bf16x2(o[8 * cc + 0] * inv_l, o[8 * cc + 1] * inv_l);
             u.y = pack_bf16x2(o[8 * cc + 2] * inv_l, o[8 * cc + 3] * inv_l);

@@ -636,7 +636,7 @@ using namespace rldx;
 
 extern "C" {
 
-int rldx_version(void) { return 108; }
+int rldx_version(void) { return 109; }
 
 const char* rldx_last_error(void) { return t_last_error.c_str(); }
 
@@ -733,6 +733,9 @@ int rldx_attention(const rldx_attention_desc* d, void* stream) {
   p.B = B;
   p.kv_heads = kvh;
   p.causal = d->causal ? 1 : 0;
+  p.causal_block = d->causal_block > 1 ? d->causal_block : 1;
+  if (d->out_dim < 0 || d->out_dim > hd || d->out_dim % 8 != 0) return set_error(RLDX_ERR_ARG, "attention: bad out_dim");
+  p.out_dim = d->out_dim;
   p.key_mask = d->key_mask;
   p.head_dim = hd;
   p.tiles_per_cta = d->tiles_per_cta;
@@ -975,6 +978,8 @@ int rldx_qk_rmsnorm_rope(const void* x, void* y, const void* w, const int32_t* p
   p.heads = p.Hq = static_cast<unsigned>(heads);
   p.T = static_cast<unsigned>(tokens);
   p.layout = 0;
+  p.hd = p.out_hd = 128;
+  p.norm = 1;
   p.eps = eps;
   cudaError_t e = launch_qk_rmsnorm_rope(p, static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "qk_rmsnorm_rope launch");

@@ -19,7 +19,10 @@ struct AttnParams {
   int head_dim;      // 64 or 128 (0: 64)
   int tiles_per_cta; // 128-query tiles per CTA: 1, 2, or 0 = chosen from the grid size
   int kv_heads;      // K / V heads (GQA: query head h reads kv head h / (H / kv_heads)); 0: H
-  int causal;        // 1: key j visible to query i only for j <= i (decoder prefill)
+  int causal;        // 1: key j visible to query i only for j < (i / causal_block + 1) * causal_block
+  int causal_block;  // 1 (or 0): token-causal; n: block-causal over blocks of n tokens
+  int out_dim;       // dims per head written to seg_out (<= head_dim, multiple of 8; 0: head_dim);
+                     // a 96-dim head runs zero-padded to 128 and writes its first 96 dims
 };
 int attention_tiles_per_cta(const AttnParams& p, int sms);
 size_t attention_smem_bytes(int head_dim);
@@ -66,9 +69,13 @@ cudaError_t launch_copy(const CopyParams& p, int blocks, cudaStream_t stream, bo
 // 128 dims.  Token tok's head h is at x + tok * x_tok_stride + h * 128; heads < Hq use wq, the
 // others wk; the RoPE row of a token is pos[tok] (or tok % T without pos).  layout 0 writes
 // y[row * 128]; layout 1 writes the attention layout q [B, Hq, T, 128] / k [B, heads - Hq, T, 128].
+// hd: head dims (96 or 128; a row's lanes past hd / 8 idle); out_hd: the head stride of the
+// attention layout (128: 96-dim heads are written into zero-padded 128-dim rows); norm = 0 skips
+// the RMSNorm (RoPE only, the memory module's attention, rldx/model/modules/memory.py:95-112).
 struct QkNormRopeParams {
   const __nv_bfloat16* x;
   long long x_tok_stride;
+  int hd, out_hd, norm;
   __nv_bfloat16* y;
   __nv_bfloat16* q;
   __nv_bfloat16* k;
@@ -83,7 +90,7 @@ struct QkNormRopeParams {
 };
 cudaError_t launch_qk_rmsnorm_rope(const QkNormRopeParams& p, cudaStream_t stream);
 cudaError_t launch_v_transpose(const __nv_bfloat16* v, long long ld, __nv_bfloat16* vt, int B, int T, int Tp,
-                               int Hkv, cudaStream_t stream);
+                               int Hkv, int hd, int out_hd, cudaStream_t stream);
 cudaError_t launch_swiglu(const __nv_bfloat16* gate, const __nv_bfloat16* up, __nv_bfloat16* out,
                           long long rows, int H, long long ld_in, long long ld_out, int sms,
                           cudaStream_t stream);
@@ -108,6 +115,7 @@ struct ResLnSeg {
 struct ResLnParams {
   ResLnSeg seg[2];
   int nseg, total_rows, dmax, fp32_sum, rms;
+  int rms_weight_first;  // 1: bf16(w * (sum * rstd)) in fp32 (rldx/model/modules/norms.py:18-22)
   float eps;
 };
 cudaError_t launch_res_ln(const ResLnParams& p, cudaStream_t stream);

@@ -1,6 +1,9 @@
 // VLM backbone prefill: a stack of Qwen3 decoder layers over B sequences of T tokens, planned
 // once and replayed as one CUDA graph (the counterpart of CustomLLMChain,
-// rldx/inference/backbone/llm/engine/custom_llm_chain.py:63-170).
+// rldx/inference/backbone/llm/engine/custom_llm_chain.py:63-170).  The same runtime runs the
+// memory module's TransformerMemory (rldx/model/modules/memory.py:150-370; CustomMemoryChain,
+// rldx/inference/memory/engine/custom_memory_chain.py:43-174): no q / k norm, weight-then-cast
+// RMSNorm, 96-dim heads (1536 / 16, run zero-padded to 128), block-wise positions.
 //
 // Per layer (Qwen3VLTextDecoderLayer, rldx/model/modules/backbone/modeling_qwen3_vl.py:509-560):
 //   n   = RMSNorm_in(h)                               res_ln_kernel (rms)
@@ -26,6 +29,7 @@ using namespace rldx;
 struct rldx_llm {
   rldx_llm_config c{};
   int B = 0, T = 0, Tp = 0, D = 0, Hq = 0, Hkv = 0, F = 0, Fp = 0, NQKV = 0, M = 0;
+  int hd = 128, phd = 128;  // head dims, and the padded head dims of the attention layout
   std::vector<void*> allocs;
   struct LayerW {
     bf16 *in_norm, *qkv, *qn, *kn, *o, *post_norm, *w12, *down;
@@ -102,6 +106,7 @@ struct rldx_llm {
     p.total_rows = M;
     p.dmax = D;
     p.rms = 1;
+    p.rms_weight_first = c.norm_weight_first ? 1 : 0;
     p.eps = c.rms_eps;
     ops.push_back([p](cudaStream_t st, bool) { return launch_res_ln(p, st); });
   }
@@ -116,7 +121,9 @@ struct rldx_llm {
     F = c.ffn;
     if (B <= 0 || T <= 0 || D <= 0 || Hq <= 0 || Hkv <= 0 || F <= 0 || c.layers <= 0)
       throw Fail(RLDX_ERR_ARG, "llm_create: batch, tokens, hidden, heads, ffn, layers must be positive");
-    if (c.head_dim != 128) throw Fail(RLDX_ERR_UNSUPPORTED, "llm_create: head_dim must be 128");
+    if (c.head_dim != 128 && c.head_dim != 96) throw Fail(RLDX_ERR_UNSUPPORTED, "llm_create: head_dim must be 96 or 128");
+    hd = c.head_dim;  // 96-dim heads run zero-padded to 128 in q, k, V^T
+    if (c.causal_block < 0) throw Fail(RLDX_ERR_ARG, "llm_create: causal_block must be >= 0");
     if (Hq % Hkv) throw Fail(RLDX_ERR_ARG, "llm_create: kv_heads must divide q_heads");
     if (D % 64 || D > 4096) throw Fail(RLDX_ERR_UNSUPPORTED, "llm_create: hidden must be a multiple of 64, <= 4096");
     if (static_cast<long long>(B) * T * (Hq + Hkv) >= (1LL << 31)) throw Fail(RLDX_ERR_UNSUPPORTED, "llm_create: too many rows");
@@ -124,13 +131,13 @@ struct rldx_llm {
     if (c.final_norm && !w.final_norm) throw Fail(RLDX_ERR_ARG, "llm_create: missing final_norm");
     Tp = (T + 7) / 8 * 8;
     Fp = (F + 31) / 32 * 32;
-    NQKV = (Hq + 2 * Hkv) * 128;
+    NQKV = (Hq + 2 * Hkv) * hd;
     M = B * T;
     const char* env = getenv("RLDX_PDL");
     pdl = !(env && env[0] == '0');
     ck(cudaStreamCreateWithFlags(&stream, cudaStreamNonBlocking), "stream");
 
-    const size_t qd = static_cast<size_t>(Hq) * 128, kd = static_cast<size_t>(Hkv) * 128;
+    const size_t qd = static_cast<size_t>(Hq) * hd, kd = static_cast<size_t>(Hkv) * hd;
     for (int i = 0; i < c.layers; ++i) {
       const rldx_llm_layer_weights& s = w.layers[i];
       LayerW l{};
@@ -139,8 +146,10 @@ struct rldx_llm {
       copy_rows(l.qkv, s.q_proj, qd * D, "q_proj");
       copy_rows(l.qkv + qd * D, s.k_proj, kd * D, "k_proj");
       copy_rows(l.qkv + (qd + kd) * D, s.v_proj, kd * D, "v_proj");
-      l.qn = copy_in(s.q_norm, 128, "q_norm");
-      l.kn = copy_in(s.k_norm, 128, "k_norm");
+      if (!c.no_qk_norm) {
+        l.qn = copy_in(s.q_norm, hd, "q_norm");
+        l.kn = copy_in(s.k_norm, hd, "k_norm");
+      }
       l.o = copy_in(s.o_proj, static_cast<size_t>(D) * qd, "o_proj");
       l.post_norm = copy_in(s.post_norm, D, "post_attention_layernorm");
       l.w12 = interleave_w12(s.gate_proj, s.up_proj);
@@ -152,15 +161,15 @@ struct rldx_llm {
       lw.push_back(l);
     }
     if (c.final_norm) final_norm = copy_in(w.final_norm, D, "final norm");
-    cos = copy_in(w.rope_cos, static_cast<size_t>(T) * 128, "rope cos");
-    sin = copy_in(w.rope_sin, static_cast<size_t>(T) * 128, "rope sin");
+    cos = copy_in(w.rope_cos, static_cast<size_t>(T) * hd, "rope cos");
+    sin = copy_in(w.rope_sin, static_cast<size_t>(T) * hd, "rope sin");
 
     h = alloc<bf16>(static_cast<size_t>(M) * D);
     n = alloc<bf16>(static_cast<size_t>(M) * D);
     qkv = alloc<bf16>(static_cast<size_t>(M) * NQKV);
-    q = alloc<bf16>(static_cast<size_t>(B) * Hq * T * 128);
-    k = alloc<bf16>(static_cast<size_t>(B) * Hkv * T * 128);
-    vt = alloc<bf16>(static_cast<size_t>(B) * Hkv * 128 * Tp);
+    q = alloc<bf16>(static_cast<size_t>(B) * Hq * T * phd);  // zero-filled: padded dims stay zero
+    k = alloc<bf16>(static_cast<size_t>(B) * Hkv * T * phd);
+    vt = alloc<bf16>(static_cast<size_t>(B) * Hkv * phd * Tp);
     a = alloc<bf16>(static_cast<size_t>(M) * qd);
     g = alloc<bf16>(static_cast<size_t>(M) * Fp);
 
@@ -198,7 +207,7 @@ struct rldx_llm {
   }
 
   void plan() {
-    const int qd = Hq * 128;
+    const int qd = Hq * hd;
     for (int li = 0; li < c.layers; ++li) {
       const LayerW& l = lw[li];
       push_rmsnorm(h, l.in_norm, n);
@@ -219,12 +228,16 @@ struct rldx_llm {
         p.Hq = static_cast<unsigned>(Hq);
         p.T = static_cast<unsigned>(T);
         p.layout = 1;
+        p.hd = hd;
+        p.out_hd = phd;
+        p.norm = c.no_qk_norm ? 0 : 1;
         p.eps = c.rms_eps;
         ops.push_back([p](cudaStream_t st, bool) { return launch_qk_rmsnorm_rope(p, st); });
-        const bf16* v = qkv + static_cast<size_t>(Hq + Hkv) * 128;
+        const bf16* v = qkv + static_cast<size_t>(Hq + Hkv) * hd;
         bf16* vtp = vt;
-        const int b_ = B, t_ = T, tp_ = Tp, hkv_ = Hkv, ld_ = NQKV;
-        ops.push_back([=](cudaStream_t st, bool) { return launch_v_transpose(v, ld_, vtp, b_, t_, tp_, hkv_, st); });
+        const int b_ = B, t_ = T, tp_ = Tp, hkv_ = Hkv, ld_ = NQKV, hd_ = hd, phd_ = phd;
+        ops.push_back(
+            [=](cudaStream_t st, bool) { return launch_v_transpose(v, ld_, vtp, b_, t_, tp_, hkv_, hd_, phd_, st); });
       }
       {
         AttnParams ap;
@@ -234,12 +247,14 @@ struct rldx_llm {
         ap.B = B;
         ap.kv_heads = Hkv;
         ap.causal = 1;
-        ap.head_dim = 128;
+        ap.causal_block = c.causal_block > 1 ? c.causal_block : 1;
+        ap.head_dim = phd;
+        ap.out_dim = hd;
         ap.seg_out[0] = a;
         ap.seg_len[0] = T;
         ap.seg_ld[0] = qd;
         ap.nseg = 1;
-        ap.scale_log2 = 1.4426950408889634f / std::sqrt(128.0f);
+        ap.scale_log2 = 1.4426950408889634f / std::sqrt(static_cast<float>(hd));
         std::string err;
         const uint64_t bq = static_cast<uint64_t>(B) * Hq, bkv = static_cast<uint64_t>(B) * Hkv;
         if (!make_tmap_3d(&ap.tq, q, 128, T, bq, 256, static_cast<uint64_t>(T) * 256, 64, 128, 1, &err) ||

@@ -179,43 +179,54 @@ __device__ __forceinline__ uint32_t as_u32(__nv_bfloat162 h) { return *reinterpr
 __global__ void __launch_bounds__(256) qk_rmsnorm_rope_kernel(const __grid_constant__ QkNormRopeParams P) {
   const unsigned half_global = (blockIdx.x * blockDim.x + threadIdx.x) >> 4;
   const int hl = threadIdx.x & 15;
+  const int hd = P.hd, nl = hd / 8, hh = nl / 2;  // lanes of a row, lanes of half a row
+  const bool act = hl < nl;                      // lanes past the head's dims idle (96-dim heads)
+  const int hle = act ? hl : 0;
   const unsigned row0 = half_global * kQkRows;
   uint4 u[kQkRows], uc[kQkRows], us[kQkRows], uw[kQkRows];
 #pragma unroll
   for (int k = 0; k < kQkRows; ++k) {
     const unsigned row = min(row0 + k, P.nrows - 1);  // clamped: the tail rows are not stored
     const unsigned tok = row / P.heads, head = row - tok * P.heads;
-    u[k] = __ldcs(reinterpret_cast<const uint4*>(P.x + tok * P.x_tok_stride + head * 128) + hl);
+    u[k] = __ldcs(reinterpret_cast<const uint4*>(P.x + tok * P.x_tok_stride + head * hd) + hle);
   }
 #pragma unroll
   for (int k = 0; k < kQkRows; ++k) {
     const unsigned row = min(row0 + k, P.nrows - 1);
     const unsigned tok = row / P.heads, head = row - tok * P.heads;
     const int p = P.pos ? __ldg(P.pos + tok) : static_cast<int>(tok % P.T);
-    uc[k] = __ldg(reinterpret_cast<const uint4*>(P.cos + static_cast<size_t>(p) * 128) + hl);
-    us[k] = __ldg(reinterpret_cast<const uint4*>(P.sin + static_cast<size_t>(p) * 128) + hl);
-    uw[k] = __ldg(reinterpret_cast<const uint4*>(head < P.Hq ? P.wq : P.wk) + hl);
+    uc[k] = __ldg(reinterpret_cast<const uint4*>(P.cos + static_cast<size_t>(p) * hd) + hle);
+    us[k] = __ldg(reinterpret_cast<const uint4*>(P.sin + static_cast<size_t>(p) * hd) + hle);
+    uw[k] = P.norm ? __ldg(reinterpret_cast<const uint4*>(head < P.Hq ? P.wq : P.wk) + hle) : make_uint4(0, 0, 0, 0);
   }
-  const uint32_t sign = (hl < 8) ? 0x80008000u : 0u;  // rotate_half = cat(-x2, x1)
+  const uint32_t sign = (hl < hh) ? 0x80008000u : 0u;  // rotate_half = cat(-x2, x1)
+  // rotate_half partner: the lane half a row away (within this half-warp)
+  const int src_lane = (threadIdx.x & 16) + (hl < hh ? hl + hh : (act ? hl - hh : hl));
 #pragma unroll
   for (int k = 0; k < kQkRows; ++k) {
     const uint32_t xv[4] = {u[k].x, u[k].y, u[k].z, u[k].w};
     const uint32_t wv[4] = {uw[k].x, uw[k].y, uw[k].z, uw[k].w};
-    float v[8];
-#pragma unroll
-    for (int i = 0; i < 4; ++i) unpack_bf16x2(xv[i], v[2 * i], v[2 * i + 1]);
-    float ss = 0.0f;
-#pragma unroll
-    for (int e = 0; e < 8; ++e) ss = fmaf(v[e], v[e], ss);
-#pragma unroll
-    for (int o = 8; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-    const float rstd = rsqrtf(ss * (1.0f / 128.0f) + P.eps);
     uint32_t yv[4], pv[4];
+    if (P.norm) {
+      float v[8];
 #pragma unroll
-    for (int i = 0; i < 4; ++i)
-      yv[i] = as_u32(__hmul2_rn(as_bf2(wv[i]), __floats2bfloat162_rn(v[2 * i] * rstd, v[2 * i + 1] * rstd)));
+      for (int i = 0; i < 4; ++i) unpack_bf16x2(xv[i], v[2 * i], v[2 * i + 1]);
+      float ss = 0.0f;
+      if (act)
 #pragma unroll
-    for (int i = 0; i < 4; ++i) pv[i] = __shfl_xor_sync(0xffffffffu, yv[i], 8) ^ sign;
+        for (int e = 0; e < 8; ++e) ss = fmaf(v[e], v[e], ss);
+#pragma unroll
+      for (int o = 8; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+      const float rstd = rsqrtf(ss / static_cast<float>(hd) + P.eps);
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+        yv[i] = as_u32(__hmul2_rn(as_bf2(wv[i]), __floats2bfloat162_rn(v[2 * i] * rstd, v[2 * i + 1] * rstd)));
+    } else {
+#pragma unroll
+      for (int i = 0; i < 4; ++i) yv[i] = xv[i];
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) pv[i] = __shfl_sync(0xffffffffu, yv[i], src_lane) ^ sign;
     const uint32_t cv[4] = {uc[k].x, uc[k].y, uc[k].z, uc[k].w};
     const uint32_t sv[4] = {us[k].x, us[k].y, us[k].z, us[k].w};
     uint32_t ov[4];
@@ -223,15 +234,15 @@ __global__ void __launch_bounds__(256) qk_rmsnorm_rope_kernel(const __grid_const
     for (int i = 0; i < 4; ++i)
       ov[i] = as_u32(__hadd2_rn(__hmul2_rn(as_bf2(yv[i]), as_bf2(cv[i])), __hmul2_rn(as_bf2(pv[i]), as_bf2(sv[i]))));
     const unsigned row = row0 + k;
-    if (row < P.nrows) {
+    if (row < P.nrows && act) {
       __nv_bfloat16* dst;
       if (P.layout == 0) {
-        dst = P.y + static_cast<size_t>(row) * 128;
-      } else {  // attention layout: q [B, Hq, T, 128] or k [B, H - Hq, T, 128]
+        dst = P.y + static_cast<size_t>(row) * hd;
+      } else {  // attention layout: q [B, Hq, T, out_hd] or k [B, H - Hq, T, out_hd]
         const unsigned tok = row / P.heads, head = row - tok * P.heads;
         const unsigned b = tok / P.T, t = tok - b * P.T;
-        dst = head < P.Hq ? P.q + ((static_cast<size_t>(b) * P.Hq + head) * P.T + t) * 128
-                          : P.k + ((static_cast<size_t>(b) * (P.heads - P.Hq) + head - P.Hq) * P.T + t) * 128;
+        dst = head < P.Hq ? P.q + ((static_cast<size_t>(b) * P.Hq + head) * P.T + t) * P.out_hd
+                          : P.k + ((static_cast<size_t>(b) * (P.heads - P.Hq) + head - P.Hq) * P.T + t) * P.out_hd;
       }
       __stcs(reinterpret_cast<uint4*>(dst) + hl, make_uint4(ov[0], ov[1], ov[2], ov[3]));
     }
@@ -239,7 +250,8 @@ __global__ void __launch_bounds__(256) qk_rmsnorm_rope_kernel(const __grid_const
 }
 
 cudaError_t launch_qk_rmsnorm_rope(const QkNormRopeParams& p, cudaStream_t stream) {
-  if (p.nrows == 0 || p.nrows >= (1u << 31) || p.heads == 0 || p.Hq == 0 || p.Hq > p.heads || p.T == 0)
+  if (p.nrows == 0 || p.nrows >= (1u << 31) || p.heads == 0 || p.Hq == 0 || p.Hq > p.heads || p.T == 0 ||
+      (p.hd != 96 && p.hd != 128) || (p.layout == 1 && p.out_hd < p.hd))
     return cudaErrorInvalidValue;
   const long long halves = (static_cast<long long>(p.nrows) + kQkRows - 1) / kQkRows;
   const int block = 256;
@@ -254,7 +266,8 @@ cudaError_t launch_qk_rmsnorm_rope(const QkNormRopeParams& p, cudaStream_t strea
 // of one batch element, through shared memory so both sides move 16-byte vectors.
 // ---------------------------------------------------------------------------------------------
 __global__ void __launch_bounds__(256) v_transpose_kernel(const __nv_bfloat16* __restrict__ v, long long ld,
-                                                          __nv_bfloat16* __restrict__ vt, int T, int Tp, int Hkv) {
+                                                          __nv_bfloat16* __restrict__ vt, int T, int Tp, int Hkv,
+                                                          int hd, int out_hd) {
   __shared__ __align__(16) __nv_bfloat16 tile[128][40];  // [dim][token]
   const int t0 = blockIdx.x * 32, hv = blockIdx.y, b = blockIdx.z;
 #pragma unroll
@@ -263,7 +276,8 @@ __global__ void __launch_bounds__(256) v_transpose_kernel(const __nv_bfloat16* _
     const int tl = idx >> 4, ch = idx & 15;
     const int t = t0 + tl;
     uint4 u = make_uint4(0u, 0u, 0u, 0u);
-    if (t < T) u = *reinterpret_cast<const uint4*>(v + (static_cast<size_t>(b) * T + t) * ld + hv * 128 + ch * 8);
+    if (t < T && ch * 8 < hd)
+      u = *reinterpret_cast<const uint4*>(v + (static_cast<size_t>(b) * T + t) * ld + hv * hd + ch * 8);
     const __nv_bfloat16* e = reinterpret_cast<const __nv_bfloat16*>(&u);
 #pragma unroll
     for (int j = 0; j < 8; ++j) tile[ch * 8 + j][tl] = e[j];
@@ -274,17 +288,17 @@ __global__ void __launch_bounds__(256) v_transpose_kernel(const __nv_bfloat16* _
     const int idx = threadIdx.x + 256 * i;
     const int d = idx >> 2, grp = idx & 3;
     const int t = t0 + grp * 8;
-    if (t < Tp)
-      *reinterpret_cast<uint4*>(vt + ((static_cast<size_t>(b) * Hkv + hv) * 128 + d) * Tp + t) =
+    if (t < Tp && d < hd)
+      *reinterpret_cast<uint4*>(vt + ((static_cast<size_t>(b) * Hkv + hv) * out_hd + d) * Tp + t) =
           *reinterpret_cast<const uint4*>(&tile[d][grp * 8]);
   }
 }
 
 cudaError_t launch_v_transpose(const __nv_bfloat16* v, long long ld, __nv_bfloat16* vt, int B, int T, int Tp,
-                               int Hkv, cudaStream_t stream) {
-  if (B <= 0 || T <= 0 || Tp < T || Tp % 8 || Hkv <= 0) return cudaErrorInvalidValue;
+                               int Hkv, int hd, int out_hd, cudaStream_t stream) {
+  if (B <= 0 || T <= 0 || Tp < T || Tp % 8 || Hkv <= 0 || hd % 8 || hd > 128 || out_hd < hd) return cudaErrorInvalidValue;
   const dim3 grid(static_cast<unsigned>((T + 31) / 32), static_cast<unsigned>(Hkv), static_cast<unsigned>(B));
-  v_transpose_kernel<<<grid, 256, 0, stream>>>(v, ld, vt, T, Tp, Hkv);
+  v_transpose_kernel<<<grid, 256, 0, stream>>>(v, ld, vt, T, Tp, Hkv, hd, out_hd);
   return cudaGetLastError();
 }
 
@@ -511,6 +525,27 @@ __global__ void __launch_bounds__(128) res_ln_kernel(const __grid_constant__ Res
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) var += __shfl_xor_sync(0xffffffffu, var, o);
   const float rstd = rsqrtf(var / static_cast<float>(sg.D) + P.eps);
+  if (P.rms && P.rms_weight_first) {  // weight times the fp32 normalised value, one rounding
+#pragma unroll
+    for (int i = 0; i < kVec; ++i) {
+      const int v = lane + 32 * i;
+      if (v < nvec) {
+        const uint4 uw = reinterpret_cast<const uint4*>(sg.w)[v];
+        float wv[8];
+        unpack_bf16x2(uw.x, wv[0], wv[1]);
+        unpack_bf16x2(uw.y, wv[2], wv[3]);
+        unpack_bf16x2(uw.z, wv[4], wv[5]);
+        unpack_bf16x2(uw.w, wv[6], wv[7]);
+        uint4 r;
+        r.x = pack_bf16x2(wv[0] * (x[i][0] * rstd), wv[1] * (x[i][1] * rstd));
+        r.y = pack_bf16x2(wv[2] * (x[i][2] * rstd), wv[3] * (x[i][3] * rstd));
+        r.z = pack_bf16x2(wv[4] * (x[i][4] * rstd), wv[5] * (x[i][5] * rstd));
+        r.w = pack_bf16x2(wv[6] * (x[i][6] * rstd), wv[7] * (x[i][7] * rstd));
+        reinterpret_cast<uint4*>(sg.ln_out + off)[v] = r;
+      }
+    }
+    return;
+  }
   if (P.rms) {  // cast, then the bf16 weight (packed multiply: exact product, one rounding)
 #pragma unroll
     for (int i = 0; i < kVec; ++i) {

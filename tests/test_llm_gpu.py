@@ -88,3 +88,34 @@ def test_llm_ffn_not_multiple_of_32(cuda):
                      use_graph=False)
     x = inp["hidden"].to(cuda)
     assert torch.equal(a(x), b(x))
+
+
+@pytest.mark.parametrize("mask", ["causal", "block"])
+@pytest.mark.parametrize("batch", [1, 2])
+def test_memory_matches_reference_golden(cuda, mask, batch):
+    """The memory module (TransformerMemory: 96-dim heads, RoPE without q/k norm, block-wise
+    positions, weight-then-cast RMSNorm) against the reference's own module's bf16 output."""
+    from oracle import memory_oracle as mo
+    from rldx_b200.llm import B200MemoryChain
+
+    fx = torch.load(GOLD / f"memory_{mask}_b{batch}_bf16.pt", weights_only=False)
+    cfg = mo.MemoryConfig(**fx["config"])
+    mem = mo.init_weights(mo.TransformerMemory(cfg), seed=fx["seed"]).to(BF)
+    chain = B200MemoryChain(mem, cuda)
+    out = chain(fx["inputs"].to(cuda))
+    torch.cuda.synchronize()
+    check_close(out, fx["out"], f"memory {mask}")
+
+
+def test_memory_config5_shapes_against_oracle(cuda):
+    """Config-5 memory: 8 sets x 256 tokens, hidden 1536 (16 heads of 96), SwiGLU 6144, 2 layers."""
+    from oracle import memory_oracle as mo
+    from rldx_b200.llm import B200MemoryChain
+
+    cfg = mo.MemoryConfig()
+    mem = mo.init_weights(mo.TransformerMemory(cfg), seed=4).to(BF)
+    x = torch.randn(1, cfg.tokens, cfg.hidden, generator=torch.Generator().manual_seed(1)).to(BF)
+    ref = mem(x)
+    out = B200MemoryChain(mem, cuda)(x.to(cuda))
+    torch.cuda.synchronize()
+    check_close(out, ref, "config-5 memory")
