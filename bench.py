@@ -1,7 +1,7 @@
 """Benchmark of the MSAT all-modality control step on B200.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--batch B] [--impl b200|reference]
-                    [--workload c2|production|production_addons]
+                    [--workload c2|production|production_addons|c5] [--observations N]
 
 One step = one control step of the action head for B observations per GPU: state encoder,
 physics history encoder and 4 flow-matching Euler steps of [action + physics encoders, 16
@@ -16,8 +16,10 @@ only supplies the barrier and the max-over-ranks of the timed region.
 
 --workload production / production_addons measures the reference's released head without /
 with add-ons instead (4 double + 8 single blocks, VL width 4096; the shapes of the reference's
-own published action-head benchmark, rldx/inference/action_model/README.md:9-37); the default
-line is config 2.
+own published action-head benchmark, rldx/inference/action_model/README.md:9-37); --workload c5
+measures BASELINE config 5, the batched serving step (VLM prefill -> cognition tokens -> memory ->
+MSAT decoder) over --observations observations sharded across the GPUs (strong scaling; see
+run_c5).  The default line is config 2.
 
 Printed JSON (rank 0): value = control steps/s of the whole job with inputs resident in HBM;
 e2e = the same through the C ABI with pinned host buffers (host->device inputs and device->host
@@ -53,7 +55,8 @@ def parse_args():
     p.add_argument("--warmup", type=int, default=5)
     p.add_argument("--batch", type=int, default=1, help="observations per GPU per control step")
     p.add_argument("--impl", choices=["b200", "reference"], default="b200")
-    p.add_argument("--workload", choices=["c2", "production", "production_addons"], default="c2")
+    p.add_argument("--workload", choices=["c2", "production", "production_addons", "c5"], default="c2")
+    p.add_argument("--observations", type=int, default=256, help="config 5: observations per step (whole job)")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--cpu-sample-s", type=float, default=20.0, help="CPU baseline time budget")
     p.add_argument("--profile-step", action="store_true",
@@ -96,7 +99,7 @@ def max_over_ranks(x: float, world: int, device) -> float:
 
 
 class ClockSampler:
-    """nvidia-smi clocks / throttle reasons sampled every 200 ms during the timed region."""
+    """nvidia-smi clocks / throttle reasons sampled every 100 ms during the timed region."""
 
     QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
@@ -236,6 +239,10 @@ def cpu_baseline(budget_s: float, steps: int = 8, warmup: int = 1, workload: str
 
 
 def run_reference(args):
+    if args.workload == "c5":
+        print(json.dumps({"impl": "reference", "unavailable": "the config-5 CPU baseline is not built (its VLM "
+                          "prefill alone is about 1.6 TFLOP per observation on the host cores)"}), flush=True)
+        return
     cb = cpu_baseline(args.cpu_sample_s, steps=args.steps, warmup=args.warmup, workload=args.workload)
     desc, model = WORKLOADS[args.workload]
     line = {"metric": "control_steps_per_s", "value": cb["value"], "unit": "control steps/s",
@@ -387,6 +394,175 @@ def run_b200(args, rank, world, local):
     print(json.dumps(line), flush=True)
 
 
+# ----------------------------------------------------------------------------------------------
+# batched serving step (VLM prefill -> cognition tokens -> memory -> MSAT)
+# ----------------------------------------------------------------------------------------------
+def run_c5(args, rank, world, local):
+    """One step serves `observations` independent observations sharded over the ranks:
+      1. 12 Qwen3 decoder layers (hidden 2048, GQA 16 / 2 x 128, SwiGLU 11008) over 848 tokens
+         (4 frames x 196 patches + 64 text; the 28-layer model truncated at layer 12);
+      2. the last 256 positions are the cognition tokens, projected 2048 -> 1536;
+      3. the memory module (TransformerMemory: 2 layers, 16 heads of 96, SwiGLU 6144) over its ring
+         of 8 cognition sets (7 past + this one, 2048 tokens) -- the ring shifts by one set per step;
+      4. the config-2 MSAT decoder (4 Euler steps) with VL = [cognition | memory output]
+         (concat_memory, 256 + 256 = 512 tokens, rldx/model/core/rldx.py:1207-1250).
+    Seeded random weights, resident inputs (token embeddings, ring, state, physics); every stage
+    is a native handle (B200LLMChain, B200MemoryChain, the GEMM, B200ExpandedActionHeadChain)."""
+    from types import SimpleNamespace as NS
+
+    import rldx_b200  # noqa: F401
+    from rldx_b200 import ops
+    from rldx_b200.chain import B200ExpandedActionHeadChain
+    from rldx_b200.llm import B200LLMChain, B200MemoryChain
+    from rldx_b200.synthetic import HeadDims, random_action_head, random_inputs
+
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    if args.observations % world:
+        raise SystemExit(f"--observations {args.observations} is not divisible by {world} GPUs")
+    B = args.observations // world
+    bf = torch.bfloat16
+    g = torch.Generator(device=dev).manual_seed(100 + rank)
+
+    def w(*shape, mean=0.0, std=0.02):
+        return (torch.randn(*shape, device=dev, generator=g) * std + mean).to(bf)
+
+    def lin(o, i):
+        return NS(weight=w(o, i), bias=None)
+
+    def norm_module(dim):
+        m = torch.nn.Module()
+        m.weight = torch.nn.Parameter(w(dim, mean=1.0, std=0.1), requires_grad=False)
+        return m
+
+    # ---- 1. VLM prefill: 12 Qwen3 layers over 848 tokens ----
+    T, D, Hq, Hkv, hd, Fd, NL = 848, 2048, 16, 2, 128, 11008, 12
+    vlm_layers = [NS(input_layernorm=NS(weight=w(D, mean=1.0, std=0.1), variance_epsilon=1e-6),
+                     post_attention_layernorm=NS(weight=w(D, mean=1.0, std=0.1)),
+                     self_attn=NS(q_proj=lin(Hq * hd, D), k_proj=lin(Hkv * hd, D), v_proj=lin(Hkv * hd, D),
+                                  o_proj=lin(D, Hq * hd), q_norm=NS(weight=w(hd, mean=1.0, std=0.1)),
+                                  k_norm=NS(weight=w(hd, mean=1.0, std=0.1))),
+                     mlp=NS(gate_proj=lin(Fd, D), up_proj=lin(Fd, D), down_proj=lin(D, Fd)))
+                  for _ in range(NL)]
+    inv = 1.0 / (1e6 ** (torch.arange(0, hd, 2, device=dev).float() / hd))
+    ang = torch.arange(T, device=dev).float()[:, None] * inv[None, :]
+    emb = torch.cat([ang, ang], -1)
+    ssin = emb.sin().to(bf)
+    ssin[:, : hd // 2] *= -1
+    vlm = B200LLMChain(vlm_layers, norm_module(D), emb.cos().to(bf), ssin, device=dev)
+    # ---- 2. cognition projection 2048 -> 1536 ----
+    NQ, DM = 256, 1536
+    cog_w, cog_b = w(DM, D), w(DM)
+    # ---- 3. memory: TransformerMemory over 8 sets x 256 tokens ----
+    SETS, HM, FM = 8, 16, 4 * DM
+    hdm = DM // HM
+    mem_layers = [NS(input_layernorm=NS(weight=w(DM, mean=1.0, std=0.1), eps=1e-5),
+                     post_attention_layernorm=NS(weight=w(DM, mean=1.0, std=0.1)),
+                     self_attn=NS(q_proj=lin(DM, DM), k_proj=lin(DM, DM), v_proj=lin(DM, DM), o_proj=lin(DM, DM),
+                                  head_dim=hdm, rotary_emb=NS(inv_freq=1.0 / (10000 ** (torch.arange(0, hdm, 2).float() / hdm)))),
+                     mlp=NS(gate_proj=lin(FM, DM), up_proj=lin(FM, DM), down_proj=lin(DM, FM)))
+                  for _ in range(2)]
+    memory = B200MemoryChain(NS(layers=mem_layers, norm=norm_module(DM), block_attn_size=NQ, use_causal_attn=True,
+                                use_rope=True), dev)
+    # ---- 4. MSAT decoder (config 2) over VL = [cognition | memory output] ----
+    dims = HeadDims()
+    head = random_action_head(dims, seed=0, device=dev)
+    msat = B200ExpandedActionHeadChain(head, dev)
+    a_in = random_inputs(dims, B, seed=42 + rank, device=dev)
+
+    tokens = torch.randn(B, T, D, device=dev, generator=g).to(bf)  # the VLM input embeddings
+    ring = torch.randn(B, SETS * NQ, DM, device=dev, generator=g).to(bf)
+    vl = torch.empty(B, 2 * NQ, DM, dtype=bf, device=dev)
+
+    def step():
+        h = vlm(tokens)                                                   # [B, 848, 2048]
+        cog = h[:, T - NQ:, :].reshape(B * NQ, D)
+        # cognition tokens -> first half of each observation's VL rows (row remap in the epilogue)
+        ops.gemm([ops.gemm_desc(cog, cog_w, vl.view(B * 2 * NQ, DM), cog_b, rows_in=NQ, rows_out=2 * NQ)])
+        ring[:, : (SETS - 1) * NQ].copy_(ring[:, NQ:].clone())               # shift the ring by one set
+        ring[:, (SETS - 1) * NQ:].copy_(vl[:, :NQ])
+        m = memory(ring)                                                  # [B, 2048, 1536]
+        vl[:, NQ:].copy_(m[:, (SETS - 1) * NQ:])                          # concat_memory
+        return msat(vl, a_in["state"], a_in["embodiment_id"], a_in["init_noise"], a_in["physics_hist"],
+                    a_in["physics_noise"])
+
+    step()
+    torch.cuda.synchronize()
+    del head
+    torch.cuda.empty_cache()
+    flush = torch.empty(2 * L2_BYTES // 4, dtype=torch.int32, device=dev)
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    barrier(world)
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clocks:
+        for i in range(args.steps):
+            flush.fill_(i)
+            starts[i].record()
+            step()
+            ends[i].record()
+        torch.cuda.synchronize()
+    barrier(world)
+    ms = [s_.elapsed_time(e_) for s_, e_ in zip(starts, ends)]
+    total_ms = max_over_ranks(sum(ms), world, dev)
+
+    # e2e: the step's VLM input embeddings come from pinned host memory, actions go back
+    host_tokens = tokens.cpu().pin_memory()
+    host_actions = torch.empty(B, dims.horizon, dims.action_dim, dtype=bf).pin_memory()
+    e_ms = []
+    barrier(world)
+    torch.cuda.synchronize()
+    for i in range(args.steps):
+        flush.fill_(i)
+        torch.cuda.synchronize()
+        s_, e_ = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s_.record()
+        tokens.copy_(host_tokens, non_blocking=True)
+        host_actions.copy_(step(), non_blocking=True)
+        e_.record()
+        e_.synchronize()
+        e_ms.append(s_.elapsed_time(e_))
+    barrier(world)
+    e_total = max_over_ranks(sum(e_ms), world, dev)
+
+    vlm_flops = (2 * (D * (Hq + 2 * Hkv) * hd + Hq * hd * D + 3 * D * Fd) * NL * T + 2.0 * Hq * T * T * hd * NL) * B
+    mem_flops = (2 * (4 * DM * DM + 3 * DM * FM) * 2 * SETS * NQ + 2.0 * HM * (SETS * NQ) ** 2 * hdm * 2) * B
+    msat_flops = 4 * (509e9 + 31e9) * B  # per control step (config-2 roofline figures)
+    flops = vlm_flops + mem_flops + 2.0 * NQ * D * DM * B + msat_flops
+    _, tc_peak, peak_kind = measured_peaks()
+    step_s = total_ms / args.steps * 1e-3
+    if rank != 0:
+        return
+    line = {
+        "metric": "observations_per_s", "value": args.observations / step_s, "unit": "observations/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": total_ms / args.steps,
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded random weights and inputs with the config-5 shapes)",
+        "config": {"workload": "BASELINE config 5: batched serving step, %d observations sharded over %d GPU(s)"
+                               % (args.observations, world),
+                   "model": "12 x Qwen3 decoder (2048, GQA 16/2x128, SwiGLU 11008) over 848 tokens -> 256 "
+                            "cognition tokens -> 1536 -> TransformerMemory (2 layers, 8 x 256 tokens) -> "
+                            "config-2 MSAT decoder (VL 256 + 256, 4 Euler steps)",
+                   "global_batch": args.observations, "seq_len": T,
+                   "parallelism": f"data parallel x{world} (observations sharded, no collective)",
+                   "l2": "flushed between timed steps (256 MB write); working set > L2"},
+        "e2e": {"value": args.observations / (e_total / args.steps * 1e-3), "unit": "observations/s",
+                "h2d_bytes_per_step": host_tokens.numel() * 2 * world,
+                "d2h_bytes_per_step": host_actions.numel() * 2 * world},
+        "gpu_launches": (vlm.launches_per_call + memory._chain.launches_per_call + msat.launches_per_step + 1)
+                        * args.steps,
+        "roofline": {"bound": "tensor", "kernel": "whole step (tcgen05 GEMMs dominate)",
+                     "achieved": flops / step_s / 1e12, "peak": tc_peak, "unit": "TFLOP/s",
+                     "frac": flops / step_s / 1e12 / tc_peak, "peak_source": peak_kind, "traffic": None,
+                     "flops_per_step_per_gpu": flops},
+        "clocks": clocks.summary(),
+    }
+    print(json.dumps(line), flush=True)
+
+
 def main():
     args = parse_args()
     if args.impl == "reference":
@@ -396,7 +572,7 @@ def main():
         return
     rank, world, local = dist_setup(args.gpus)
     try:
-        run_b200(args, rank, world, local)
+        (run_c5 if args.workload == "c5" else run_b200)(args, rank, world, local)
     finally:
         if world > 1:
             import torch.distributed as dist
