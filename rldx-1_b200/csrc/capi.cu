@@ -268,7 +268,16 @@ void choose_tiles_uncached(const ProbShape* sh, const int* fixed_bn, int n, int 
         unit_costs(sh[i], bn[i], sp[i], &c);
         units += sh[i].tiles_m * ((sh[i].N + bn[i] - 1) / bn[i]) * sp[i];
       }
-      if (units > kMaxUnits) return 1e299;
+      if (units > kMaxUnits) {
+        // Beyond the explicit schedule's capacity the kernel deals units round-robin; bound
+        // its makespan by the mean load plus the longest unit.
+        double sum = 0.0, mx = 0.0;
+        for (double x : c) {
+          sum += x;
+          mx = std::max(mx, x);
+        }
+        return sum / nsm + mx;
+      }
       return lpt_makespan(c, nsm);
     };
     double mk = eval();
