@@ -102,6 +102,12 @@ int rldx_gemm(const rldx_gemm_desc* problems, int nproblems, void* stream);
  * SMs (0 = the plan would not split).  Same validation as rldx_gemm; launches nothing. */
 int rldx_gemm_workspace_size(const rldx_gemm_desc* problems, int nproblems, uint64_t* bytes);
 
+/* The launch plan that rldx_gemm_ws (given a large enough workspace) uses for these problems;
+ * launches nothing.  plan[0] = 1 when CTA pairs (clusters of two) run cta_group::2 MMAs on
+ * 256-row tiles, plan[1] = CTAs launched, plan[2] = ring stages, plan[3] = tile width (N) of the
+ * first problem (the pair's width in pair mode), plan[4] = its K splits. */
+int rldx_gemm_plan(const rldx_gemm_desc* problems, int nproblems, int* plan);
+
 /* rldx_gemm with a device workspace: problems whose K loop would leave SMs idle are split,
  * each split writes an fp32 partial tile, and the last split of a tile to finish adds the
  * partials in split order (the result does not depend on which finishes last) and runs the

@@ -164,6 +164,7 @@ SIGNATURES = {
     "rldx_device_supported": (C.c_int, []),
     "rldx_gemm": (C.c_int, [C.POINTER(GemmDesc), C.c_int, vp]),
     "rldx_gemm_workspace_size": (C.c_int, [C.POINTER(GemmDesc), C.c_int, C.POINTER(C.c_uint64)]),
+    "rldx_gemm_plan": (C.c_int, [C.POINTER(GemmDesc), C.c_int, C.POINTER(C.c_int)]),
     "rldx_gemm_ws": (C.c_int, [C.POINTER(GemmDesc), C.c_int, vp, C.c_uint64, vp]),
     "rldx_gemm_static_ws": (C.c_int, [C.POINTER(GemmDesc), C.c_int, vp]),
     "rldx_joint_attention": (C.c_int, [vp, vp, vp, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, vp,

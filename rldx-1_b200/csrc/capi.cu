@@ -161,16 +161,19 @@ bool make_tmap_4d(CUtensorMap* m, const void* base, const cuuint64_t (&dims)[4],
 }
 
 // ---- GEMM planning ----------------------------------------------------------------------------
-// Cost model of one work unit on one SM, in nanoseconds, from measurements of this kernel's
-// building blocks on B200: a TMA ring sustains ~114 GB/s of shared-memory fill per SM, the
-// tensor core ~11.3 TFLOP/s per SM (dense bf16, M = 128 whatever the live rows), a unit pays a
-// fixed pipeline fill, an epilogue proportional to its columns, and a K-split unit also writes
-// its fp32 partial tile and (for the last one) reads all partials of the tile back from L2.
+// Cost model of one work unit on one SM, in nanoseconds, from measurements on B200: the SM's
+// copy engine takes one TMA box at a time, at least ~400 cycles per box (up to ~32 KB) and
+// ~92 bytes per cycle beyond, so a ring slot costs the sum of its A and B boxes; the tensor
+// core does ~11.3 TFLOP/s per SM (dense bf16, M = 128 whatever the live rows) on the slots
+// already landed; a unit pays a fixed pipeline fill, an epilogue proportional to its columns,
+// and a K-split unit also writes its fp32 partial tile and (for the last one) reads all
+// partials of the tile back from L2 (~114 bytes per ns).
 constexpr double kFillBytesPerNs = 114.0;
 constexpr double kMmaFlopsPerNs = 11300.0;
 constexpr double kChunkNs = 20.0;
 constexpr double kUnitNs = 1500.0;
-constexpr int kSlotTargetBytes = 48 * 1024;
+constexpr double kTmaOpNs = 210.0;        // one TMA box occupies the SM's copy engine >= ~400 cycles
+constexpr double kTmaBytesPerNs = 175.0;  // ... and streams ~92 bytes per cycle beyond ~36 KB
 constexpr int kMinSplitChunks = 4;
 constexpr int kMaxSplit = 8;
 constexpr size_t kCounterBytes = ((kMaxUnits * 4 + 255) / 256) * 256;
@@ -185,14 +188,29 @@ double epi_ns_per_col(int epi) {
   return (epi == RLDX_EPI_QKV || epi == RLDX_EPI_SWIGLU) ? 26.0 : 15.0;
 }
 
-double chunk_ns(const ProbShape& s, int bn) {
-  const double fill = (s.a_rows + bn) * 128.0 / kFillBytesPerNs;
-  const double mma = 128.0 * bn * 64.0 * 2.0 / kMmaFlopsPerNs;
-  return std::max(fill, mma) + kChunkNs;
+// Ring slots of up to 64 KB: three stages fit beside the barriers, and boxes of 16-64 KB keep
+// the copy engine's per-box cost below the tensor core's time for the slot.
+constexpr int kSlotTargetBytes = 64 * 1024;
+
+// 64-deep K chunks per ring slot (= per TMA box) for a tile of `bn` columns.
+int ksub_for(const ProbShape& s, int bn) {
+  const int per_chunk = (s.a_rows + bn) * 128;
+  return s.kdim3 ? std::max(1, std::min(kSlotTargetBytes / per_chunk, 8)) : 1;
+}
+
+// One ring slot: the A and B boxes go through the SM's copy engine one after the other, the
+// tensor core works on the previous slots meanwhile.
+double slot_ns(const ProbShape& s, int bn, int ksub) {
+  auto op = [](double bytes) { return std::max(kTmaOpNs, bytes / kTmaBytesPerNs); };
+  const double tma = op(s.a_rows * 128.0 * ksub) + op(bn * 128.0 * ksub);
+  const double mma = ksub * 128.0 * bn * 64.0 * 2.0 / kMmaFlopsPerNs;
+  return std::max(tma, mma) + kChunkNs;
 }
 
 double unit_ns(const ProbShape& s, int bn, int chunks, int nsplit) {
-  double t = chunks * chunk_ns(s, bn) + kUnitNs + bn * epi_ns_per_col(s.epi);
+  const int ksub = std::max(1, std::min(ksub_for(s, bn), chunks));
+  double t = ((chunks + ksub - 1) / ksub) * slot_ns(s, bn, ksub);
+  t += kUnitNs + bn * epi_ns_per_col(s.epi);
   if (nsplit > 1) t += s.live_rows * bn * 4.0 * 2.0 / kFillBytesPerNs;
   return t;
 }
@@ -380,6 +398,15 @@ void choose_tiles(const ProbShape* sh, const int* fixed_bn, int n, int nsm, bool
   cache[key] = v;
 }
 
+// RLDX_GEMM_PAIR=0 keeps every launch on single-CTA tiles.
+int pair_mode() {
+  static int v = [] {
+    const char* e = std::getenv("RLDX_GEMM_PAIR");
+    return (e && e[0] == '0') ? 0 : 1;
+  }();
+  return v;
+}
+
 bool split_disabled() {
   static int v = [] {
     const char* e = std::getenv("RLDX_GEMM_SPLIT");
@@ -510,6 +537,21 @@ bool build_gemm_params(const rldx_gemm_desc* d, int n, void* ws, size_t ws_bytes
   for (int i = 0; i < n; ++i) fixed_bn[i] = d[i].tile_n;
   choose_tiles(sh, fixed_bn, n, nsm, can_split, best_bn, best_split);
 
+  // ---- CTA pairs (cta_group::2, 256-row M tiles) for launches with plenty of large tiles ----
+  bool pair = pair_mode() != 0 && nsm >= 2;
+  long long tiles128 = 0;
+  for (int i = 0; i < n && pair; ++i) {
+    pair = !d[i].cat_ids && d[i].M >= 512 && d[i].tile_n == 0;
+    tiles128 += static_cast<long long>((d[i].M + 127) / 128) * ((d[i].N + 127) / 128);
+  }
+  pair = pair && tiles128 >= 4LL * nsm;
+  if (pair) {
+    for (int i = 0; i < n; ++i) {
+      best_bn[i] = d[i].N > 128 ? 256 : 128;
+      best_split[i] = 1;
+    }
+  }
+
   // ---- workspace layout: [tile counters][fp32 partial tiles] ----
   size_t need = 0;
   for (int pass = 0; pass < 2; ++pass) {
@@ -537,6 +579,15 @@ bool build_gemm_params(const rldx_gemm_desc* d, int n, void* ws, size_t ws_bytes
     if (!any || (ws != nullptr && need <= ws_bytes)) break;
     for (int i = 0; i < n; ++i) best_split[i] = 1;  // no (or too small a) workspace
   }
+  params->pair = pair ? 1 : 0;
+  if (pair) {
+    for (int i = 0; i < n; ++i) {
+      GemmProblem& p = params->p[i];
+      p.tiles_m = (p.M + 255) / 256;  // pair tiles; each CTA owns 128 rows (m_step)
+      p.m_step = 128;
+      p.a_rows = 128;
+    }
+  }
   params->ws = reinterpret_cast<float*>(static_cast<uint8_t*>(ws) + kCounterBytes);
   params->counters = static_cast<unsigned int*>(ws);
   if (!ws) {
@@ -548,7 +599,7 @@ bool build_gemm_params(const rldx_gemm_desc* d, int n, void* ws, size_t ws_bytes
   int slot = 0;
   for (int i = 0; i < n; ++i) {
     GemmProblem& p = params->p[i];
-    const int per_chunk = (p.a_rows + p.bn) * 128;
+    const int per_chunk = (p.a_rows + (pair ? p.bn / 2 : p.bn)) * 128;
     p.ksub = p.kdim3 ? std::max(1, std::min({kSlotTargetBytes / per_chunk, 8, p.split_chunks})) : 1;
     slot = std::max(slot, p.ksub * per_chunk);
   }
@@ -573,7 +624,7 @@ bool build_gemm_params(const rldx_gemm_desc* d, int n, void* ws, size_t ws_bytes
         const cuuint32_t box[4] = {64, static_cast<cuuint32_t>(p.bn), static_cast<cuuint32_t>(p.ksub), 1};
         if (!make_tmap_4d(&p.tb, q.b, dims, strides, box, err)) return false;
       } else if (!make_tmap_3d(&p.tb, q.b, 64, p.N, p.nchunks, static_cast<uint64_t>(q.ldb) * 2, 128,
-                               64, p.bn, p.ksub, err)) {
+                               64, pair ? p.bn / 2 : p.bn, p.ksub, err)) {
         return false;
       }
     } else {
@@ -583,7 +634,8 @@ bool build_gemm_params(const rldx_gemm_desc* d, int n, void* ws, size_t ws_bytes
         if (!make_tmap_3d(&p.tb, q.b, q.K, p.N, q.num_cats, static_cast<uint64_t>(q.ldb) * 2,
                           static_cast<uint64_t>(q.b_cat_stride) * 2, 64, p.bn, 1, err))
           return false;
-      } else if (!make_tmap_2d(&p.tb, q.b, q.K, p.N, static_cast<uint64_t>(q.ldb) * 2, 64, p.bn, err)) {
+      } else if (!make_tmap_2d(&p.tb, q.b, q.K, p.N, static_cast<uint64_t>(q.ldb) * 2, 64,
+                               pair ? p.bn / 2 : p.bn, err)) {
         return false;
       }
     }
@@ -598,7 +650,8 @@ bool build_gemm_params(const rldx_gemm_desc* d, int n, void* ws, size_t ws_bytes
   }
   params->nprob = n;
   params->nunits = total;
-  params->ncta = std::min(nsm, total);
+  params->ncta = pair ? 2 * std::min(nsm / 2, total) : std::min(nsm, total);
+  const int nlists = pair ? params->ncta / 2 : params->ncta;  // unit lists: one per CTA or pair
   if (total > kMaxUnits) {
     params->explicit_sched = 0;
     return true;
@@ -621,8 +674,8 @@ bool build_gemm_params(const rldx_gemm_desc* d, int n, void* ws, size_t ws_bytes
   std::stable_sort(us.begin(), us.end(), [](const U& a, const U& b) { return a.cost > b.cost; });
   using Load = std::pair<double, int>;
   std::priority_queue<Load, std::vector<Load>, std::greater<Load>> loads;
-  for (int c = 0; c < params->ncta; ++c) loads.push({0.0, c});
-  std::vector<std::vector<int>> lists(params->ncta);
+  for (int c = 0; c < nlists; ++c) loads.push({0.0, c});
+  std::vector<std::vector<int>> lists(nlists);
   for (const U& u : us) {
     Load l = loads.top();
     loads.pop();
@@ -631,11 +684,11 @@ bool build_gemm_params(const rldx_gemm_desc* d, int n, void* ws, size_t ws_bytes
     loads.push(l);
   }
   int off = 0;
-  for (int c = 0; c < params->ncta; ++c) {
+  for (int c = 0; c < nlists; ++c) {
     params->cta_begin[c] = static_cast<unsigned short>(off);
     for (int id : lists[c]) params->sched[off++] = static_cast<unsigned short>(id);
   }
-  params->cta_begin[params->ncta] = static_cast<unsigned short>(off);
+  params->cta_begin[nlists] = static_cast<unsigned short>(off);
   return true;
 }
 
@@ -645,7 +698,7 @@ using namespace rldx;
 
 extern "C" {
 
-int rldx_version(void) { return 109; }
+int rldx_version(void) { return 110; }
 
 const char* rldx_last_error(void) { return t_last_error.c_str(); }
 
@@ -691,6 +744,24 @@ int rldx_gemm_workspace_size(const rldx_gemm_desc* problems, int nproblems, uint
   if (!build_gemm_params(problems, nproblems, nullptr, 0, &params, &need, &err))
     return set_error(RLDX_ERR_ARG, err);
   *bytes = need;
+  return RLDX_OK;
+}
+
+int rldx_gemm_plan(const rldx_gemm_desc* problems, int nproblems, int* plan) {
+  int rc = ensure_device();
+  if (rc != RLDX_OK) return rc;
+  if (!problems || !plan) return set_error(RLDX_ERR_ARG, "gemm_plan: null argument");
+  static thread_local GemmParams params;
+  std::string err;
+  // planned as if an unbounded workspace were given (the pointer is only recorded, never read)
+  void* any_ws = reinterpret_cast<void*>(static_cast<uintptr_t>(256));
+  if (!build_gemm_params(problems, nproblems, any_ws, SIZE_MAX, &params, nullptr, &err))
+    return set_error(RLDX_ERR_ARG, err);
+  plan[0] = params.pair;
+  plan[1] = params.ncta;
+  plan[2] = params.stages;
+  plan[3] = params.p[0].bn;
+  plan[4] = params.p[0].nsplit;
   return RLDX_OK;
 }
 

@@ -174,6 +174,42 @@ __device__ __forceinline__ void unit_epilogue(const GemmProblem& pr, const RowCt
     };
     uint4 nb, na, nx;
     fetch(set * 8, nb, na, nx);
+    // Plain store (no activation, bias added before the one rounding): two fp32 adds, one paired
+    // round-to-bf16 and, with a residual, one exactly rounded bf16x2 add per two columns -- the
+    // same roundings as the general path below, in a third of the instructions.
+    const bool packed = (kMode == kEpiStore) && (kAct == kActNone) && bias_mode != kBiasPostRound &&
+                        ((ep.ldo | ep.col_off | ep.ld_add) & 7) == 0 && al16(ep.out) &&
+                        (!ep.add || al16(ep.add)) && (!bias_row || al16(bias_row));
+    if (packed) {
+#pragma unroll 1
+      for (int col = set * 8; col < bn; col = next_col(col)) {
+        const int n0 = n_base + col;
+        const int n = pr.N - n0;
+        const uint4 bq = nb, aq = na;
+        fetch(next_col(col), nb, na, nx);
+        float v[8];
+        src.get8(col, rc.live, v);
+        if (!rc.live || n <= 0) continue;
+        if (n < 8) {
+          float y[8];
+#pragma unroll
+          for (int i = 0; i < 8; ++i) y[i] = bf16r(bf16r(v[i] + bf_at(bq, i)) + bf_at(aq, i));
+          store8q(orow + n0, n, y);
+          continue;
+        }
+        const uint32_t bw[4] = {bq.x, bq.y, bq.z, bq.w};
+        const uint32_t aw[4] = {aq.x, aq.y, aq.z, aq.w};
+        uint32_t h[4];
+#pragma unroll
+        for (int p = 0; p < 4; ++p) {
+          __nv_bfloat162 t = __floats2bfloat162_rn(v[2 * p] + bf_lo(bw[p]), v[2 * p + 1] + bf_hi(bw[p]));
+          if (arow) t = __hadd2_rn(t, *reinterpret_cast<const __nv_bfloat162*>(&aw[p]));
+          h[p] = *reinterpret_cast<const uint32_t*>(&t);
+        }
+        *reinterpret_cast<uint4*>(orow + n0) = make_uint4(h[0], h[1], h[2], h[3]);
+      }
+      return;
+    }
 #pragma unroll 1
     for (int col = set * 8; col < bn; col = next_col(col)) {
       const int n0 = n_base + col;
@@ -579,6 +615,199 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_bf16_kernel(const __grid
   }
 }
 
+// ---------------------------------------------------------------------------------------------
+// CTA-pair kernel: clusters of 2 CTAs, cta_group::2 MMAs over 256-row M tiles.
+//
+// Barriers live in both CTAs at the same offsets; which ones are used:
+//   full[s]       rank 0 only: its two producers arrive with the bytes of BOTH CTAs' loads
+//                 (expect_tx of 2x their own), and the TMA loads of both CTAs complete on it;
+//   empty[s]      each CTA's own: the MMA thread commits to both CTAs' barriers after stage s;
+//   acc_full[ab]  each CTA's own: committed to both after the unit's last MMA;
+//   acc_empty[ab] rank 0 only: every epilogue warp of both CTAs arrives (2 x kEpiWarps).
+// ---------------------------------------------------------------------------------------------
+__device__ __forceinline__ int pair_units(const GemmParams& P, int pair, int& first) {
+  const int npairs = P.ncta >> 1;
+  if (P.explicit_sched) {
+    first = P.cta_begin[pair];
+    return P.cta_begin[pair + 1] - first;
+  }
+  first = 0;
+  return (P.nunits - pair + npairs - 1) / npairs;
+}
+
+__device__ __forceinline__ int pair_unit_id(const GemmParams& P, int pair, int first, int i) {
+  return P.explicit_sched ? static_cast<int>(P.sched[first + i]) : pair + i * (P.ncta >> 1);
+}
+
+template <int kMode>
+__global__ void __launch_bounds__(kGemmThreads, 1) gemm_pair_kernel(const __grid_constant__ GemmParams P) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  const int S = P.stages;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + S * P.slot_bytes + kRingSlack);
+  uint64_t* empty = full + kMaxStages;
+  uint64_t* acc_full = empty + kMaxStages;
+  uint64_t* acc_empty = acc_full + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const int pair = static_cast<int>(blockIdx.x >> 1);
+  int first = 0;
+  const int nunits = pair_units(P, pair, first);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&full[s], 2);  // rank 0's A producer + B producer
+      mbar_init(&empty[s], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&acc_full[i], 1);
+      mbar_init(&acc_empty[i], 2 * kEpiWarps);
+    }
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    for (int i = 0; i < P.nprob; ++i) tma_prefetch_desc(&P.p[i].ta);
+  }
+  if (warp == 2 && lane == 0) {
+    for (int i = 0; i < P.nprob; ++i) tma_prefetch_desc(&P.p[i].tb);
+  }
+  if (warp == 1) tmem_alloc_pair(tmem_slot, 2 * kAccCols);
+  tc_fence_before();
+  cluster_sync();  // both CTAs' barriers initialised and TMEM allocated before any pair traffic
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  if (threadIdx.x == 0) griddep_launch();
+
+  if (warp == 0 || warp == 2) {
+    // ---------------- TMA producers: warp 0 = A (this CTA's 128 rows), warp 2 = B (half) -----
+    if (lane == 0) {
+      const bool is_a = (warp == 0);
+      if (is_a) griddep_wait();
+      const uint64_t pol = l2_policy_evict_last();
+      int it = 0;
+      bool ok = true;
+      for (int i = 0; ok && i < nunits; ++i) {
+        const UnitInfo u = decode_unit(P, pair_unit_id(P, pair, first, i));
+        const GemmProblem& pr = P.p[u.pi];
+        const uint32_t a_sub = 128u * 128u;
+        const uint32_t b_sub = static_cast<uint32_t>(pr.bn >> 1) * 128u;
+        const uint32_t bytes = (is_a ? a_sub : b_sub) * static_cast<uint32_t>(pr.ksub);
+        const int a_row0 = u.tm * 256 + static_cast<int>(rank) * 128;
+        const int n0 = u.tn * pr.bn + static_cast<int>(rank) * (pr.bn >> 1);
+        for (int sl = 0; sl < u.nslots; ++sl, ++it) {
+          const int s = it % S;
+          const uint32_t ph = static_cast<uint32_t>(it / S) & 1u;
+          if (!mbar_wait(&empty[s], ph ^ 1u, kErrGemmTimeout + 1)) {
+            ok = false;
+            break;
+          }
+          uint8_t* slot = smem + s * P.slot_bytes;
+          const int chunk = u.c_begin + sl * pr.ksub;
+          if (rank == 0) mbar_arrive_expect_tx(&full[s], 2u * bytes);
+          const uint32_t bar = mapa_shared(smem_u32(&full[s]), 0u);
+          if (is_a) {
+            if (pr.kdim3)
+              tma_load_3d_pair(slot, &pr.ta, bar, 0, a_row0, chunk, pol);
+            else
+              tma_load_2d_pair(slot, &pr.ta, bar, chunk * 64, a_row0, pol);
+          } else {
+            uint8_t* dst = slot + a_sub * pr.ksub;
+            if (pr.kdim3)
+              tma_load_3d_pair(dst, &pr.tb, bar, 0, n0, chunk, pol);
+            else
+              tma_load_2d_pair(dst, &pr.tb, bar, chunk * 64, n0, pol);
+          }
+        }
+      }
+      // The MMA thread's commits arrive on this CTA's empty barriers asynchronously: wait for the
+      // release of every slot still in flight so that none lands after the CTA has exited.
+      for (int t = (it > S ? it - S : 0); ok && t < it; ++t)
+        ok = mbar_wait(&empty[t % S], static_cast<uint32_t>(t / S) & 1u, kErrGemmTimeout + 1);
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer: one thread of rank 0 drives both CTAs' tensor cores ----------
+    if (lane == 0 && rank == 0) {
+      int it = 0;
+      bool ok = true;
+      for (int j = 0; ok && j < nunits; ++j) {
+        const UnitInfo u = decode_unit(P, pair_unit_id(P, pair, first, j));
+        const GemmProblem& pr = P.p[u.pi];
+        const int ab = j & 1;
+        if (!mbar_wait(&acc_empty[ab], (static_cast<uint32_t>(j >> 1) & 1u) ^ 1u, kErrGemmTimeout + 2))
+          break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(ab * kAccCols);
+        const uint32_t idesc = umma_idesc_bf16(256, pr.bn);
+        const uint32_t a_sub = 128u * 128u;
+        const uint32_t b_sub = static_cast<uint32_t>(pr.bn >> 1) * 128u;
+        for (int sl = 0; sl < u.nslots; ++sl, ++it) {
+          const int s = it % S;
+          const uint32_t ph = static_cast<uint32_t>(it / S) & 1u;
+          if (!mbar_wait(&full[s], ph, kErrGemmTimeout + 2)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(smem + s * P.slot_bytes);
+          const uint32_t b_addr = a_addr + a_sub * static_cast<uint32_t>(pr.ksub);
+          const int nsub = min(pr.ksub, u.c_end - (u.c_begin + sl * pr.ksub));
+          for (int sub = 0; sub < nsub; ++sub) {
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+              umma_f16_pair(d_tmem, umma_desc_sw128(a_addr + sub * a_sub + 32 * k),
+                            umma_desc_sw128(b_addr + sub * b_sub + 32 * k), idesc,
+                            (sl | sub | k) != 0 ? 1u : 0u);
+            }
+          }
+          const uint32_t e = smem_u32(&empty[s]);
+          umma_commit_pair(mapa_shared(e, 0u));
+          umma_commit_pair(mapa_shared(e, 1u));
+        }
+        if (!ok) break;
+        const uint32_t f = smem_u32(&acc_full[ab]);
+        umma_commit_pair(mapa_shared(f, 0u));
+        umma_commit_pair(mapa_shared(f, 1u));
+      }
+    }
+  } else {
+    // ---------------- epilogue warps (both CTAs, each over its own 128 rows) ----------------
+    griddep_wait();
+    const int quad = warp & 3;
+    const int set = (warp - kEpiWarp0) >> 2;
+    const int r_local = quad * 32 + lane;
+    const uint32_t lane_off = static_cast<uint32_t>(quad * 32) << 16;
+    const uint32_t rel0 = mapa_shared(smem_u32(&acc_empty[0]), 0u);
+    const uint32_t rel1 = mapa_shared(smem_u32(&acc_empty[1]), 0u);
+    bool ok = true;
+    for (int j = 0; ok && j < nunits; ++j) {
+      const UnitInfo u = decode_unit(P, pair_unit_id(P, pair, first, j));
+      const GemmProblem& pr = P.p[u.pi];
+      const int ab = j & 1;
+      if (!mbar_wait(&acc_full[ab], static_cast<uint32_t>(j >> 1) & 1u, kErrGemmTimeout + 3)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const uint32_t tacc = tmem_base + lane_off + static_cast<uint32_t>(ab * kAccCols);
+      const RowCtx rc = row_ctx(pr, 2 * u.tm + static_cast<int>(rank), r_local);
+      unit_epilogue_act<kMode>(pr, rc, u.tn * pr.bn, set, TmemSrc{tacc});
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(ab ? rel1 : rel0);
+    }
+  }
+  tc_fence_before();
+  cluster_sync();  // no pair traffic (MMA reads, commits, remote arrivals) outlives either CTA
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, 2 * kAccCols);
+  }
+}
+
 // At least 116 KB so that two CTAs never share an SM: a second CTA would only wait in
 // tcgen05.alloc for the first one's 512 TMEM columns.
 size_t gemm_smem_bytes(int stages, int slot_bytes) {
@@ -600,6 +829,10 @@ cudaError_t gemm_prepare_device() {
   set(reinterpret_cast<const void*>(gemm_bf16_kernel<kEpiSwiGLU, true>));
   set(reinterpret_cast<const void*>(gemm_bf16_kernel<kEpiQKV, true>));
   set(reinterpret_cast<const void*>(gemm_bf16_kernel<kEpiEuler, true>));
+  set(reinterpret_cast<const void*>(gemm_pair_kernel<kEpiStore>));
+  set(reinterpret_cast<const void*>(gemm_pair_kernel<kEpiSwiGLU>));
+  set(reinterpret_cast<const void*>(gemm_pair_kernel<kEpiQKV>));
+  set(reinterpret_cast<const void*>(gemm_pair_kernel<kEpiEuler>));
   return e;
 }
 
@@ -609,11 +842,29 @@ cudaError_t launch_gemm(const GemmParams& params, cudaStream_t stream, bool pdl)
   cfg.blockDim = dim3(kGemmThreads, 1, 1);
   cfg.dynamicSmemBytes = gemm_smem_bytes(params.stages, params.slot_bytes);
   cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = pdl ? 1 : 0;
+  if (params.pair) {
+    if (params.ncta % 2 != 0) return cudaErrorInvalidValue;
+    attr[cfg.numAttrs].id = cudaLaunchAttributeClusterDimension;
+    attr[cfg.numAttrs].val.clusterDim.x = 2;
+    attr[cfg.numAttrs].val.clusterDim.y = 1;
+    attr[cfg.numAttrs].val.clusterDim.z = 1;
+    cfg.numAttrs += 1;
+    switch (params.p[0].ep.mode) {
+      case kEpiSwiGLU:
+        return cudaLaunchKernelEx(&cfg, gemm_pair_kernel<kEpiSwiGLU>, params);
+      case kEpiQKV:
+        return cudaLaunchKernelEx(&cfg, gemm_pair_kernel<kEpiQKV>, params);
+      case kEpiEuler:
+        return cudaLaunchKernelEx(&cfg, gemm_pair_kernel<kEpiEuler>, params);
+      default:
+        return cudaLaunchKernelEx(&cfg, gemm_pair_kernel<kEpiStore>, params);
+    }
+  }
   bool split = false;
   for (int i = 0; i < params.nprob; ++i) split = split || params.p[i].nsplit > 1;
   switch (params.p[0].ep.mode) {  // every problem of a launch shares the epilogue mode

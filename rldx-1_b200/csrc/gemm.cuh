@@ -4,6 +4,10 @@
 // Work unit = (problem, 128-row M tile, BN-column N tile, K split).  The host orders the units
 // longest-first and deals them to at most one CTA per SM (LPT schedule, kept in the launch
 // parameters), so the weight-streaming work of all streams is spread evenly over the SMs.
+// Large launches run on CTA pairs instead: the two CTAs of a cluster each load 128 rows of A and
+// half of the B tile, one thread of rank 0 issues cta_group::2 MMAs (M = 256) that read both
+// CTAs' tiles, and each CTA's epilogue finishes its own 128 rows from its own TMEM.  Per SM this
+// halves the B traffic of a 256-wide tile (32 KB instead of 48 KB per 64-deep K chunk).
 // Roles inside a CTA (3 + kEpiWarps warps):
 //
 //   warp 0      TMA producer of A (activations), after griddepcontrol.wait.
@@ -104,6 +108,10 @@ struct GemmParams {
   int nunits;
   int ncta;
   int explicit_sched;       // 1: sched/cta_begin hold the unit list; 0: unit = cta + i * ncta
+  int pair;                 // 1: CTA pairs (clusters of 2) run cta_group::2 MMAs on 256-row M
+                            //    tiles: tiles_m counts 256-row tiles, bn is the pair's N (each
+                            //    CTA loads bn/2 rows of B), a unit's list index is the pair's
+                            //    (cta_begin / striding over ncta / 2 pairs); no K splits
   float* ws;                // K-split partial tiles (fp32)
   unsigned int* counters;   // one arrival counter per split tile; zero between launches
   unsigned short cta_begin[kMaxCtas + 1];

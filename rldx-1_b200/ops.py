@@ -114,6 +114,15 @@ def gemm_workspace_size(descs: Sequence[GemmDesc]) -> int:
     return int(n.value)
 
 
+def gemm_plan(descs: Sequence[GemmDesc]) -> dict:
+    """The launch plan gemm(descs, workspace) uses: CTA pairs or single CTAs, CTAs, ring stages,
+    the first problem's tile width and K splits."""
+    arr = (GemmDesc * len(descs))(*descs)
+    v = (C.c_int * 5)()
+    check(load().rldx_gemm_plan(arr, len(descs), v))
+    return {"pair": bool(v[0]), "ctas": v[1], "stages": v[2], "tile_n": v[3], "splits": v[4]}
+
+
 def linear(x, weight, bias=None, *, act=_lib.ACT_NONE, bias_mode=_lib.BIAS_FUSED, add=None,
            out=None, tile_n=0) -> torch.Tensor:
     """nn.Linear (+activation, +residual) through the tcgen05 GEMM."""

@@ -26,7 +26,7 @@ def test_every_declared_symbol_is_exported(lib):
 
 
 def test_version_and_error_string(lib):
-    assert lib.rldx_version() == 109
+    assert lib.rldx_version() == 110
     assert isinstance(lib.rldx_last_error(), bytes)
 
 

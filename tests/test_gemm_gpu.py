@@ -289,3 +289,126 @@ def test_workspace_too_small_runs_unsplit(cuda):
     ops.gemm(d, workspace=ws)
     torch.cuda.synchronize()
     close(out, r(x.float() @ w.float().t()))
+
+
+# ---- CTA pairs (cta_group::2 MMAs over 256-row tiles): large launches plan onto them ----
+
+def _pair_linear(cuda, M, N, K, seed, act=_lib.ACT_NONE, add=False):
+    g = torch.Generator(device=cuda).manual_seed(seed)
+    x = torch.randn(M, K, device=cuda, generator=g).to(BF)
+    w = (torch.randn(N, K, device=cuda, generator=g) * 0.05).to(BF)
+    b = (torch.randn(N, device=cuda, generator=g) * 0.1).to(BF)
+    res = torch.randn(M, N, device=cuda, generator=g).to(BF) if add else None
+    out = torch.empty(M, N, dtype=BF, device=cuda)
+    d = ops.gemm_desc(x, w, out, b, act=act, add=res)
+    plan = ops.gemm_plan([d])
+    ops.gemm([d])
+    torch.cuda.synchronize()
+    ref = ref_finish(x.float() @ w.float().t(), b, _lib.BIAS_FUSED, act)
+    if add:
+        ref = r(ref + res.float())
+    return plan, out, ref
+
+
+@pytest.mark.parametrize("M,N,K", [(4096, 2560, 1024), (4000, 2500, 1000), (2304, 4352, 1536)])
+def test_pair_tiles_linear(cuda, M, N, K):
+    """Ragged M (not a multiple of 256), N (not a multiple of the pair's half tile) and K (not a
+    multiple of 64: two-dimensional tensor maps) on CTA pairs."""
+    plan, out, ref = _pair_linear(cuda, M, N, K, seed=M + N + K)
+    assert plan["pair"] and plan["ctas"] % 2 == 0, plan
+    close(out, ref)
+    assert ops.device_error() == 0
+
+
+def test_pair_tiles_activation_and_residual(cuda):
+    plan, out, ref = _pair_linear(cuda, 4096, 3072, 512, seed=77, act=_lib.ACT_SILU, add=True)
+    assert plan["pair"], plan
+    close(out, ref)
+
+
+def test_pair_tiles_match_single_cta_tiles(cuda):
+    """The same problem on CTA pairs and on single CTAs (a fixed tile width keeps single CTAs)."""
+    g = torch.Generator(device=cuda).manual_seed(21)
+    M, N, K = 4096, 3072, 768
+    x = torch.randn(M, K, device=cuda, generator=g).to(BF)
+    w = (torch.randn(N, K, device=cuda, generator=g) * 0.05).to(BF)
+    a, b = torch.empty(M, N, dtype=BF, device=cuda), torch.empty(M, N, dtype=BF, device=cuda)
+    da, db = ops.gemm_desc(x, w, a), ops.gemm_desc(x, w, b, tile_n=256)
+    assert ops.gemm_plan([da])["pair"] and not ops.gemm_plan([db])["pair"]
+    ops.gemm([da])
+    ops.gemm([db])
+    torch.cuda.synchronize()
+    close(a, b.float())
+    # both accumulate K in the same chunk order in fp32: the roundings agree almost everywhere
+    assert (a != b).float().mean().item() < 0.02
+
+
+def test_pair_tiles_swiglu_epilogue(cuda):
+    g = torch.Generator(device=cuda).manual_seed(23)
+    M, D, Hd = 2048, 1024, 4096
+    x = torch.randn(M, D, device=cuda, generator=g).to(BF)
+    w12 = (torch.randn(2 * Hd, D, device=cuda, generator=g) * 0.05).to(BF)
+    b12 = (torch.randn(2 * Hd, device=cuda, generator=g) * 0.1).to(BF)
+    idx = torch.cat([torch.cat([torch.arange(gi * 32, gi * 32 + 32), Hd + torch.arange(gi * 32, gi * 32 + 32)])
+                     for gi in range(Hd // 32)]).to(cuda)
+    out = torch.empty(M, Hd, dtype=BF, device=cuda)
+    d = ops.gemm_desc(x, w12[idx].contiguous(), out, b12[idx].contiguous(), epilogue=_lib.EPI_SWIGLU)
+    assert ops.gemm_plan([d])["pair"]
+    ops.gemm([d])
+    torch.cuda.synchronize()
+    y = r(x.float() @ w12.float().t() + b12.float())
+    x1, x2 = y.chunk(2, dim=-1)
+    close(out, r(r(F.silu(x1)) * x2))
+
+
+def test_pair_tiles_grouped_problems(cuda):
+    g = torch.Generator(device=cuda).manual_seed(25)
+    descs, refs, outs, keep = [], [], [], []
+    for M in (4096, 1024, 2000):
+        x = torch.randn(M, 1536, device=cuda, generator=g).to(BF)
+        w = (torch.randn(1536, 1536, device=cuda, generator=g) * 0.03).to(BF)
+        b = (torch.randn(1536, device=cuda, generator=g) * 0.1).to(BF)
+        o = torch.empty(M, 1536, dtype=BF, device=cuda)
+        keep += [x, w, b]
+        descs.append(ops.gemm_desc(x, w, o, b))
+        refs.append(ref_finish(x.float() @ w.float().t(), b, _lib.BIAS_FUSED, 0))
+        outs.append(o)
+    assert ops.gemm_plan(descs)["pair"]
+    ops.gemm(descs)
+    torch.cuda.synchronize()
+    for o, ref in zip(outs, refs):
+        close(o, ref)
+
+
+def test_pair_tiles_qkv_epilogue(cuda):
+    """Per-head RMSNorm + RoPE epilogue on CTA pairs: 256 sequences of 50 tokens, 4 heads."""
+    g = torch.Generator(device=cuda).manual_seed(27)
+    B, H, D, n, L, tok_off = 256, 4, 256, 50, 56, 3
+    Lp = 56
+    x = torch.randn(B * n, D, device=cuda, generator=g).to(BF)
+    w = (torch.randn(3 * H * 64, D, device=cuda, generator=g) * 0.05).to(BF)
+    b = (torch.randn(3 * H * 64, device=cuda, generator=g) * 0.1).to(BF)
+    qn = (1 + 0.1 * torch.randn(64, device=cuda, generator=g)).to(BF)
+    kn = (1 + 0.1 * torch.randn(64, device=cuda, generator=g)).to(BF)
+    ang = torch.rand(L, 32, device=cuda, generator=g) * 6.28
+    cos, sin = torch.cos(ang).contiguous(), torch.sin(ang).contiguous()
+    q = torch.zeros(B, H, L, 64, dtype=BF, device=cuda)
+    k = torch.zeros_like(q)
+    vt = torch.zeros(B, H, 64, Lp, dtype=BF, device=cuda)
+    d = ops.qkv_desc(x, w, b, qn, kn, cos, sin, q, k, vt, tok_off=tok_off, rows_per_batch=n)
+    assert ops.gemm_plan([d])["pair"]
+    ops.gemm([d])
+    torch.cuda.synchronize()
+    y = r(x.float() @ w.float().t() + b.float()).view(B, n, 3, H, 64).permute(2, 0, 3, 1, 4)
+
+    def norm_rope(t, wn):
+        tn = r(wn.float() * (t * torch.rsqrt(t.pow(2).mean(-1, keepdim=True) + 1e-6)))
+        c = cos[tok_off:tok_off + n][None, None]
+        s = sin[tok_off:tok_off + n][None, None]
+        a, bb = tn[..., 0::2], tn[..., 1::2]
+        return r(torch.stack([a * c - bb * s, a * s + bb * c], dim=-1).flatten(-2))
+
+    close(q[:, :, tok_off:tok_off + n], norm_rope(y[0], qn))
+    close(k[:, :, tok_off:tok_off + n], norm_rope(y[1], kn))
+    close(vt[..., tok_off:tok_off + n], y[2].transpose(-1, -2))
+    assert ops.device_error() == 0
