@@ -169,7 +169,7 @@ bool make_tmap_4d(CUtensorMap* m, const void* base, const cuuint64_t (&dims)[4],
 // and a K-split unit also writes its fp32 partial tile and (for the last one) reads all
 // partials of the tile back from L2 (~114 bytes per ns).
 constexpr double kFillBytesPerNs = 114.0;
-constexpr double kMmaFlopsPerNs = 11300.0;
+constexpr double kMmaFlopsPerNs = 15000.0;
 constexpr double kChunkNs = 20.0;
 constexpr double kUnitNs = 1500.0;
 constexpr double kTmaOpNs = 210.0;        // one TMA box occupies the SM's copy engine >= ~400 cycles
@@ -398,6 +398,54 @@ void choose_tiles(const ProbShape* sh, const int* fixed_bn, int n, int nsm, bool
   cache[key] = v;
 }
 
+// Modelled makespan of a single-CTA plan (tile widths and splits given).
+double single_makespan(const ProbShape* sh, int n, int nsm, const int* bn, const int* split) {
+  std::vector<double> c;
+  int units = 0;
+  for (int i = 0; i < n; ++i) {
+    unit_costs(sh[i], bn[i], split[i], &c);
+    units += sh[i].tiles_m * ((sh[i].N + bn[i] - 1) / bn[i]) * split[i];
+  }
+  if (units > kMaxUnits) {
+    double sum = 0.0, mx = 0.0;
+    for (double x : c) {
+      sum += x;
+      mx = std::max(mx, x);
+    }
+    return sum / nsm + mx;
+  }
+  return lpt_makespan(c, nsm);
+}
+
+// One unit of a CTA pair: 256 rows x bn columns, each CTA loading 128 rows of A and bn/2 rows of
+// B per slot and computing 128 x bn on its own tensor core.
+double pair_unit_ns(const ProbShape& s, int bn) {
+  const int bh = bn / 2;
+  const int ksub = s.kdim3 ? std::max(1, std::min(kSlotTargetBytes / ((128 + bh) * 128), 8)) : 1;
+  auto op = [](double bytes) { return std::max(kTmaOpNs, bytes / kTmaBytesPerNs); };
+  const double tma = op(128.0 * 128.0 * ksub) + op(bh * 128.0 * ksub);
+  const double mma = ksub * 128.0 * bn * 64.0 * 2.0 / kMmaFlopsPerNs;
+  const int slots = (s.nchunks + ksub - 1) / ksub;
+  return slots * (std::max(tma, mma) + kChunkNs) + kUnitNs + bn * epi_ns_per_col(s.epi);
+}
+
+double pair_makespan(const ProbShape* sh, int n, int nsm) {
+  std::vector<double> c;
+  for (int i = 0; i < n; ++i) {
+    const int bn = sh[i].N > 128 ? 256 : 128;
+    const int units = ((sh[i].M + 255) / 256) * ((sh[i].N + bn - 1) / bn);
+    const double u = pair_unit_ns(sh[i], bn);
+    for (int k = 0; k < units; ++k) c.push_back(u);
+  }
+  const int npairs = nsm / 2;
+  if (static_cast<int>(c.size()) > kMaxUnits) {
+    double sum = 0.0;
+    for (double x : c) sum += x;
+    return sum / npairs + c[0];
+  }
+  return lpt_makespan(c, npairs);
+}
+
 // RLDX_GEMM_PAIR=0 keeps every launch on single-CTA tiles.
 int pair_mode() {
   static int v = [] {
@@ -537,14 +585,21 @@ bool build_gemm_params(const rldx_gemm_desc* d, int n, void* ws, size_t ws_bytes
   for (int i = 0; i < n; ++i) fixed_bn[i] = d[i].tile_n;
   choose_tiles(sh, fixed_bn, n, nsm, can_split, best_bn, best_split);
 
-  // ---- CTA pairs (cta_group::2, 256-row M tiles) for launches with plenty of large tiles ----
+  // ---- CTA pairs (cta_group::2, 256-row M tiles): launches with plenty of large tiles, and
+  // smaller ones whose modelled makespan on pairs beats the single-CTA plan (a pair halves each
+  // SM's copy-engine boxes per tile: the small-batch projections whose rows fit a few tiles) ----
   bool pair = pair_mode() != 0 && nsm >= 2;
+  bool large = true;
   long long tiles128 = 0;
   for (int i = 0; i < n && pair; ++i) {
-    pair = !d[i].cat_ids && d[i].M >= 512 && d[i].tile_n == 0;
+    pair = !d[i].cat_ids && d[i].tile_n == 0;
+    large = large && d[i].M >= 512;
     tiles128 += static_cast<long long>((d[i].M + 127) / 128) * ((d[i].N + 127) / 128);
   }
-  pair = pair && tiles128 >= 4LL * nsm;
+  if (pair && !(large && tiles128 >= 4LL * nsm)) {
+    const double single_mk = single_makespan(sh, n, nsm, best_bn, best_split);
+    pair = pair_makespan(sh, n, nsm) < 0.9 * single_mk;
+  }
   if (pair) {
     for (int i = 0; i < n; ++i) {
       best_bn[i] = d[i].N > 128 ? 256 : 128;

@@ -83,6 +83,18 @@ struct TmemSrc {
     tmem_ld8(taddr + static_cast<uint32_t>(col), v);
     tmem_wait_ld();
   }
+  // two 8-column groups under one wait
+  __device__ __forceinline__ void get8x2(int c0, int c1, bool /*live*/, float (&v0)[8], float (&v1)[8]) const {
+    __syncwarp();
+    tmem_ld8(taddr + static_cast<uint32_t>(c0), v0);
+    tmem_ld8(taddr + static_cast<uint32_t>(c1), v1);
+    tmem_wait_ld();
+  }
+  __device__ __forceinline__ void get16(int col, bool /*live*/, float (&v)[16]) const {
+    __syncwarp();
+    tmem_ld16(taddr + static_cast<uint32_t>(col), v);
+    tmem_wait_ld();
+  }
 };
 
 // Partial tiles are stored column-major, [split][column][128 rows] per tile, so that the 32
@@ -92,6 +104,20 @@ struct PartSrc {
   size_t split_stride;  // floats between splits (= 128 * BN)
   int nsplit;
   static constexpr int kSplitsInFlight = 4;  // splits whose loads are issued before adding
+  __device__ __forceinline__ void get8x2(int c0, int c1, bool live, float (&v0)[8], float (&v1)[8]) const {
+    get8(c0, live, v0);
+    get8(c1, live, v1);
+  }
+  __device__ __forceinline__ void get16(int col, bool live, float (&v)[16]) const {
+    float a[8], b[8];
+    get8(col, live, a);
+    get8(col + 8, live, b);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      v[i] = a[i];
+      v[8 + i] = b[i];
+    }
+  }
   __device__ __forceinline__ void get8(int col, bool live, float (&v)[8]) const {
 #pragma unroll
     for (int i = 0; i < 8; ++i) v[i] = 0.0f;
@@ -233,28 +259,62 @@ __device__ __forceinline__ void unit_epilogue(const GemmProblem& pr, const RowCt
   } else if constexpr (kMode == kEpiSwiGLU) {
     // every 64 columns: [0,32) gate, [32,64) up of hidden units n0/2 .. n0/2+31 (N % 64 == 0);
     // set s takes the 8-unit groups j = s, s + kEpiSets, ... (j < 4) of each chunk
+    // The bias words of the next group are loaded while the current one is computed; the gate
+    // and up columns come from TMEM under one wait; silu(g) and u are bf16-exact, so their
+    // product rounds once in packed bf16x2 arithmetic exactly as bf16(float(s) * float(u)).
     __nv_bfloat16* orow = ep.out + static_cast<size_t>(rc.out_row) * ep.ldo + ep.col_off;
-#pragma unroll 1
-    for (int c = 0; c < bn; c += 64) {
+    auto bias_of = [&](int c, int j, uint4& bg, uint4& bu) {
       const int n0 = n_base + c;
-      const bool on = rc.live && n0 < pr.N;
+      const bool on = rc.live && c < bn && n0 < pr.N && bias_row;
+      bg = load8q(bias_row + n0 + 8 * j, on, 8);
+      bu = load8q(bias_row + n0 + 32 + 8 * j, on, 8);
+    };
+    int c = 0, j = set;
+    uint4 nbg, nbu;
+    bias_of(c, j, nbg, nbu);
 #pragma unroll 1
-      for (int j = set; j < 4; j += kEpiSets) {
-        const uint4 bg = load8q(bias_row + n0 + 8 * j, on && bias_row, 8);
-        const uint4 bu = load8q(bias_row + n0 + 32 + 8 * j, on && bias_row, 8);
-        float g[8], u[8];
-        src.get8(c + 8 * j, rc.live, g);
-        src.get8(c + 32 + 8 * j, rc.live, u);
-        if (!on) continue;
-        float h[8];
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          const float a = finish_acc(g[i], bf_at(bg, i), bias_mode);
-          const float b = finish_acc(u[i], bf_at(bu, i), bias_mode);
-          h[i] = bf16r(act_fn<kActSilu>(a) * b);
-        }
-        store8q(orow + n0 / 2 + 8 * j, 8, h);
+    while (c < bn) {
+      const uint4 bg = nbg, bu = nbu;
+      int c2 = c, j2 = j + kEpiSets;
+      if (j2 >= 4) {
+        j2 = set;
+        c2 = c + 64;
       }
+      bias_of(c2, j2, nbg, nbu);
+      const int n0 = n_base + c;
+      float g[8], u[8];
+      src.get8x2(c + 8 * j, c + 32 + 8 * j, rc.live, g, u);
+      if (rc.live && n0 < pr.N) {
+        const uint32_t gw[4] = {bg.x, bg.y, bg.z, bg.w};
+        const uint32_t uw[4] = {bu.x, bu.y, bu.z, bu.w};
+        uint32_t hw[4];
+#pragma unroll
+        for (int p = 0; p < 4; ++p) {
+          const float a0 = finish_acc(g[2 * p], bf_lo(gw[p]), bias_mode);
+          const float a1 = finish_acc(g[2 * p + 1], bf_hi(gw[p]), bias_mode);
+          const float b0 = finish_acc(u[2 * p], bf_lo(uw[p]), bias_mode);
+          const float b1 = finish_acc(u[2 * p + 1], bf_hi(uw[p]), bias_mode);
+          const uint32_t sw = pack_exact_bf16x2(act_fn<kActSilu>(a0), act_fn<kActSilu>(a1));
+          const uint32_t bw = pack_exact_bf16x2(b0, b1);
+          const __nv_bfloat162 h = __hmul2_rn(*reinterpret_cast<const __nv_bfloat162*>(&sw),
+                                              *reinterpret_cast<const __nv_bfloat162*>(&bw));
+          hw[p] = *reinterpret_cast<const uint32_t*>(&h);
+        }
+        __nv_bfloat16* dst = orow + n0 / 2 + 8 * j;
+        if (al16(dst)) {
+          *reinterpret_cast<uint4*>(dst) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+        } else {
+          float h[8];
+#pragma unroll
+          for (int p = 0; p < 4; ++p) {
+            h[2 * p] = bf_lo(hw[p]);
+            h[2 * p + 1] = bf_hi(hw[p]);
+          }
+          store8q(dst, 8, h);
+        }
+      }
+      c = c2;
+      j = j2;
     }
   } else {  // kEpiQKV: every 64 columns = one head of q, k or v; set s takes heads s, s+kEpiSets, ...
     const int inner = ep.H * 64;
@@ -277,15 +337,17 @@ __device__ __forceinline__ void unit_epilogue(const GemmProblem& pr, const RowCt
         float4 nc = rc.live ? cp[0] : z4, ns = rc.live ? sp[0] : z4;
         float ss = 0.0f;
         uint4 nb = load8q(hb, rc.live && hb, 8);
+        uint4 nb2 = load8q(hb + 8, rc.live && hb, 8);
 #pragma unroll 1
-        for (int g = 0; g < 64; g += 8) {  // pass 1: sum of squares of the finished head
-          const uint4 bq = nb;
-          nb = load8q(hb + ((g + 8) & 63), rc.live && hb, 8);  // wraps to pass 2's first group
-          float v[8];
-          src.get8(c + g, rc.live, v);
+        for (int g = 0; g < 64; g += 16) {  // pass 1: sum of squares of the finished head
+          const uint4 bq = nb, bq2 = nb2;
+          nb = load8q(hb + ((g + 16) & 63), rc.live && hb, 8);  // wraps to pass 2's first group
+          nb2 = load8q(hb + ((g + 24) & 63), rc.live && hb && g + 16 < 64, 8);
+          float v[16];
+          src.get16(c + g, rc.live, v);
 #pragma unroll
-          for (int i = 0; i < 8; ++i) {
-            const float y = finish_acc(v[i], bf_at(bq, i), kBiasFused);
+          for (int i = 0; i < 16; ++i) {  // columns in order: the same fp32 sum as one at a time
+            const float y = finish_acc(v[i], bf_at(i < 8 ? bq : bq2, i & 7), kBiasFused);
             ss += y * y;
           }
         }
