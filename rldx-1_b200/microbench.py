@@ -1,5 +1,6 @@
-"""Kernel microbenchmarks for BASELINE configs 3 and 4 on one GPU.
+"""Kernel microbenchmarks for BASELINE configs 1, 3 and 4 on one GPU.
 
+    python -m rldx_b200.microbench --suite c1    # one 3-stream MSAT block (config 1 shapes), bf16
     python -m rldx_b200.microbench --suite c3    # memory-bound: Qwen3 QK-RMSNorm+RoPE, SwiGLU
     python -m rldx_b200.microbench --suite c4    # joint-attention sweep, head_dim 128
     python -m rldx_b200.microbench --suite vlm   # config-5 VLM-shaped prefill (12 Qwen3 layers)
@@ -24,6 +25,12 @@ VLM prefill (the first part of BASELINE config 5): 12 Qwen3 decoder layers (hidd
 final RMSNorm, seeded random weights and inputs, 1-D RoPE positions 0..847; one call =
 B200LLMChain.forward (the whole stack as one CUDA graph).  FLOPs per call = 2 * tokens *
 (projection weights) + 2 * B * heads * T^2 * 128 (causal attention, half of the square).
+
+Config 1 on the GPU: one ExpandedDoubleStreamBlock (cognition 256, action 16, physics 16,
+hidden 1024, 16 x 64 heads, SwiGLU 2816, seeded N(0, 0.02) weights, ~N(0,1) streams) through
+B200ExpandedDoubleStreamBlock, replayed as one CUDA graph of 11 launches, batch 1 (the latency
+case) and larger batches (throughput); FLOPs per block = 2 * 288 * 12.58 M (projections) +
+4 * 288^2 * 1024 (attention) = 7.74 GFLOP per batch element.
 
 Config 4: non-causal joint attention over [cognition | physics | action] segments of lengths
 (L-48):32:16, 16 heads x 128, batch 1-64; FLOPs = 4 * B * H * L^2 * 128.  torch's
@@ -181,6 +188,63 @@ def suite_vlm(iters: int, warmup: int, batches=(1, 8, 32), layers: int = 12, T: 
         torch.cuda.empty_cache()
 
 
+def c1_block_module(seed: int = 0):
+    """A module with the reference ExpandedDoubleStreamBlock's attribute names and config-1
+    shapes, seeded N(0, 0.02) weights and biases (RMSNorm scales 1 + N(0, 0.02))."""
+    from torch import nn
+
+    g = torch.Generator().manual_seed(seed)
+    dim, heads, hd, hid = 1024, 16, 64, 2816
+
+    def lin(i, o):
+        m = nn.Linear(i, o)
+        with torch.no_grad():
+            m.weight.copy_(torch.randn(o, i, generator=g) * 0.02)
+            m.bias.copy_(torch.randn(o, generator=g) * 0.02)
+        return m
+
+    blk = nn.Module()
+    blk.num_heads = heads
+    for s in ("sa", "vl", "p"):
+        setattr(blk, f"{s}_qkv", lin(dim, 3 * heads * hd))
+        setattr(blk, f"{s}_proj", lin(heads * hd, dim))
+        mlp = nn.Module()
+        mlp.w12, mlp.w3 = lin(dim, 2 * hid), lin(hid, dim)
+        setattr(blk, f"{s}_mlp", mlp)
+        for qk in ("q", "k"):
+            n = nn.Module()
+            n.weight = nn.Parameter(1 + 0.02 * torch.randn(hd, generator=g), requires_grad=False)
+            setattr(blk, f"{qk}_norm_{s}", n)
+    return blk
+
+
+def suite_c1(iters: int, warmup: int, batches=(1, 8, 64)):
+    from .block import B200ExpandedDoubleStreamBlock
+
+    _, tc_peak, kind = peaks()
+    dev = torch.device("cuda", 0)
+    blk = c1_block_module(0)
+    L, hd = 288, 64
+    inv = 1.0 / (1e4 ** (torch.arange(0, hd, 2).float() / hd))
+    ang = torch.arange(L).float()[:, None] * inv[None, :]
+    pe = torch.polar(torch.ones_like(ang), ang)[None].to(dev)
+    flops = 2 * L * (1024 * 3072 + 1024 * 1024 + 1024 * 5632 + 2816 * 1024) + 4.0 * L * L * 1024
+    for B in batches:
+        g = torch.Generator(device=dev).manual_seed(B)
+        cog = torch.randn(B, 256, 1024, device=dev, generator=g).to(BF)
+        act = torch.randn(B, 16, 1024, device=dev, generator=g).to(BF)
+        phys = torch.randn(B, 16, 1024, device=dev, generator=g).to(BF)
+        gpu = B200ExpandedDoubleStreamBlock(blk, dev, use_graph=True)
+        gpu(act, cog, phys, pe)
+        ms = time_ms(gpu.replay, iters * (10 if B == 1 else 1), warmup)
+        tf = flops * B / (ms * 1e-3) / 1e12
+        yield {"suite": "c1", "what": "one ExpandedDoubleStreamBlock (config-1 shapes), CUDA graph of "
+               f"{gpu.launches} launches", "B": B, "us_per_block": round(ms * 1e3, 2),
+               "gflop_per_block": round(flops * B / 1e9, 2), "tflops": round(tf, 1),
+               "frac_of_peak": round(tf / tc_peak, 3), "peak": f"{tc_peak} TFLOP/s ({kind})",
+               "roofline_us": round(flops * B / (tc_peak * 1e12) * 1e6, 2)}
+
+
 def nn_module(ns):
     """B200LLMChain stores the final norm as a submodule: wrap the weight holder."""
     m = torch.nn.Module()
@@ -190,7 +254,7 @@ def nn_module(ns):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--suite", choices=["c3", "c4", "vlm", "all"], default="all")
+    ap.add_argument("--suite", choices=["c1", "c3", "c4", "vlm", "all"], default="all")
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--batches", type=str, default="1,4,16,64")
@@ -199,6 +263,9 @@ def main():
     a = ap.parse_args()
     if not torch.cuda.is_available():
         raise SystemExit("microbench needs a CUDA device")
+    if a.suite in ("c1", "all"):
+        for r in suite_c1(a.iters, a.warmup):
+            print(json.dumps(r), flush=True)
     if a.suite in ("c3", "all"):
         for r in suite_c3(a.iters, a.warmup):
             print(json.dumps(r), flush=True)
