@@ -248,10 +248,60 @@ def cpu_baseline(budget_s: float, steps: int = 8, warmup: int = 1, workload: str
                       f"p50 {per_forward * 1e3:.0f} ms x {cfg.num_steps} Euler steps = one control step"}
 
 
+def cpu_baseline_c5(budget_s: float):
+    """One observation of the config-5 step on the host cores in fp32, sampled stage by stage: one
+    VLM decoder layer over 848 tokens (x 12 layers), one memory layer over the 2048-token ring
+    (x 2 layers) and one config-2 MSAT forward (x 4 Euler steps); each stage's p50 is multiplied
+    by its repeat count (every repeat has the same shapes)."""
+    from oracle import memory_oracle as mo
+    from oracle import qwen3_oracle as oq
+
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+
+    def p50(fn, n=3):
+        fn()
+        ts = []
+        for _ in range(n):
+            t = time.perf_counter()
+            fn()
+            ts.append(time.perf_counter() - t)
+        return statistics.median(ts)
+
+    g = torch.Generator().manual_seed(1)
+    qc = oq.Qwen3Config(layers=1)
+    stack = oq.init_weights(oq.TextStack(qc), seed=0)
+    T = 848
+    cos, sin = oq.rope_tables(qc, torch.arange(T))
+    h = torch.randn(1, T, qc.hidden, generator=g)
+    with torch.no_grad():
+        vlm = p50(lambda: stack(h, cos[None], sin[None], final_norm=False))
+        mem = mo.init_weights(mo.TransformerMemory(mo.MemoryConfig(layers=1)), seed=0)
+        ring = torch.randn(1, 8 * 256, 1536, generator=g)
+        memory = p50(lambda: mem(ring))
+    del stack, mem
+    msat = 1.0 / cpu_baseline(budget_s, steps=3, workload="c2")["value"]  # 4 MSAT forwards
+    per_obs = 12 * vlm + 2 * memory + msat
+    return {"value": 1.0 / per_obs, "unit": "observations/s", "cores": threads, "kind": "port",
+            "sample": f"one observation in fp32, stage by stage: VLM layer p50 {vlm * 1e3:.0f} ms x 12, memory "
+                      f"layer p50 {memory * 1e3:.0f} ms x 2, MSAT control step {msat * 1e3:.0f} ms"}
+
+
 def run_reference(args):
     if args.workload == "c5":
-        print(json.dumps({"impl": "reference", "unavailable": "the config-5 CPU baseline is not built (its VLM "
-                          "prefill alone is about 1.6 TFLOP per observation on the host cores)"}), flush=True)
+        cb = cpu_baseline_c5(args.cpu_sample_s)
+        line = {"metric": "observations_per_s", "value": cb["value"], "unit": "observations/s",
+                "impl": "reference", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+                "ms_per_step": 1000.0 * args.observations / cb["value"], "higher_is_better": True,
+                "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+                "config": {"workload": "BASELINE config 5: batched serving step (sampled per observation)",
+                           "model": "12 x Qwen3 decoder over 848 tokens -> TransformerMemory (2 layers, 2048 "
+                                    "tokens) -> config-2 MSAT decoder", "global_batch": args.observations,
+                           "seq_len": 848, "parallelism": "cpu"},
+                "cpu_baseline": cb,
+                "e2e": {"value": cb["value"], "unit": "observations/s", "h2d_bytes_per_step": 0,
+                        "d2h_bytes_per_step": 0}}
+        print(json.dumps(line), flush=True)
         return
     cb = cpu_baseline(args.cpu_sample_s, steps=args.steps, warmup=args.warmup, workload=args.workload)
     desc, model = WORKLOADS[args.workload]
@@ -571,6 +621,8 @@ def run_c5(args, rank, world, local):
                      "flops_per_step_per_gpu": flops},
         "clocks": clocks.summary(),
     }
+    if world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline_c5(args.cpu_sample_s)
     print(json.dumps(line), flush=True)
 
 
