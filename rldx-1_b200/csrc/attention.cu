@@ -34,8 +34,12 @@ constexpr float kRescaleLog2 = 8.0f;  // lazy-rescale threshold (log2 units)
 // kG query tiles of 128 rows per CTA share every K / V tile: kG = 1 for latency (more CTAs),
 // kG = 2 for throughput (two softmax warpgroups keep the special-function and ALU pipes busy
 // while the tensor core works on the other tile, and K / V are read once per 256 queries).
+// kW softmax warpgroups per query tile split each 64-key tile's columns (kW = 2: 32 keys per
+// thread); their row maxima meet through shared memory once per tile and their row sums at
+// the end, so the exponentials of one tile take half as long (the short-sequence, batch-1 case
+// is bound by that chain).
 // TMEM columns: S of group g, buffer b at (2g + b) * 64; O of group g at kG * 128 + g * d.
-template <int kHD, int kG>
+template <int kHD, int kG, int kW = 1>
 struct AttnShape {
   static constexpr int kChunks = kHD / 64;           // 64-dim chunks of a Q / K row
   static constexpr int kQBytes = 128 * kHD * 2;      // 128 queries
@@ -47,20 +51,24 @@ struct AttnShape {
   // MMAs are, so the K loads run ahead of the PV work
   static constexpr int kKStages = 3;
   static constexpr int kVStages = (kHD == 128 && kG == 2) ? 2 : 3;
-  static constexpr int kThreads = 64 + 128 * kG;
+  static constexpr int kThreads = 64 + 128 * kG * kW;
+  static constexpr int kCols = 64 / kW;  // keys of a tile per softmax thread
   static constexpr uint32_t kOCol = 128 * kG;
   static constexpr uint32_t kTmemCols = (kG == 1) ? 256 : 512;
-  static constexpr int kBars = 1 + 2 * kKStages + 2 * kVStages + 10 * kG;
+  static constexpr int kBars = 1 + 2 * kKStages + 2 * kVStages + 13 * kG;
+  static constexpr int kXchFloats = kG * (2 + 1) * kW * 128;  // per-tile maxima (2 buffers), sums
   static constexpr size_t kSmem = 1024 + static_cast<size_t>(kG) * kQBytes +
                                   static_cast<size_t>(kKStages) * kKTileBytes +
                                   static_cast<size_t>(kVStages) * kVTileBytes +
-                                  static_cast<size_t>(kG) * 2 * kPBytes + 8 * kBars + 16;
+                                  static_cast<size_t>(kG) * 2 * kPBytes + 8 * kBars + 16 +
+                                  4 * static_cast<size_t>(kXchFloats);
 };
 
-template <int kHD, int kG>
-__global__ void __launch_bounds__(AttnShape<kHD, kG>::kThreads, 1)
+template <int kHD, int kG, int kW>
+__global__ void __launch_bounds__(AttnShape<kHD, kG, kW>::kThreads, 1)
     joint_attention_kernel(const __grid_constant__ AttnParams P) {
-  using Sh = AttnShape<kHD, kG>;
+  using Sh = AttnShape<kHD, kG, kW>;
+  static_assert(kW == 1 || (kW == 2 && kHD == 64 && kG == 1), "column split: head_dim 64, one tile");
   constexpr int kQBytes = Sh::kQBytes;
   constexpr int kKTileBytes = Sh::kKTileBytes;
   constexpr int kVTileBytes = Sh::kVTileBytes;
@@ -80,15 +88,21 @@ __global__ void __launch_bounds__(AttnShape<kHD, kG>::kThreads, 1)
   uint64_t* v_full = k_empty + kKS;
   uint64_t* v_empty = v_full + kVS;
   // per group: s_full[2], s_empty[2], p_full[2], p_empty[2], o_done (one phase per PV MMA),
-  // o_final (one phase: the group's last PV MMA landed)
+  // o_final (one phase: the group's last PV MMA landed), xch[2] (the column warpgroups' row
+  // maxima of a tile are in shared memory), l_xch (their row sums are)
   uint64_t* gbar = v_empty + kVS;
-  auto s_full = [&](int g) { return gbar + 10 * g; };
-  auto s_empty = [&](int g) { return gbar + 10 * g + 2; };
-  auto p_full = [&](int g) { return gbar + 10 * g + 4; };
-  auto p_empty = [&](int g) { return gbar + 10 * g + 6; };
-  auto o_done = [&](int g) { return gbar + 10 * g + 8; };
-  auto o_final = [&](int g) { return gbar + 10 * g + 9; };
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(gbar + 10 * kG);
+  auto s_full = [&](int g) { return gbar + 13 * g; };
+  auto s_empty = [&](int g) { return gbar + 13 * g + 2; };
+  auto p_full = [&](int g) { return gbar + 13 * g + 4; };
+  auto p_empty = [&](int g) { return gbar + 13 * g + 6; };
+  auto o_done = [&](int g) { return gbar + 13 * g + 8; };
+  auto o_final = [&](int g) { return gbar + 13 * g + 9; };
+  auto xch = [&](int g) { return gbar + 13 * g + 10; };
+  auto l_xch = [&](int g) { return gbar + 13 * g + 12; };
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(gbar + 13 * kG);
+  // exchange floats: group g, buffer sb, warpgroup w, row r at xf[((g * 3 + sb) * kW + w) * 128 + r]
+  // (sb = 2: the final row sums)
+  float* xf = reinterpret_cast<float*>(tmem_slot + 4);
 
   const int q0 = blockIdx.x * (128 * kG);
   const int head = blockIdx.y;
@@ -119,12 +133,14 @@ __global__ void __launch_bounds__(AttnShape<kHD, kG>::kThreads, 1)
     for (int g = 0; g < kG; ++g) {
       for (int i = 0; i < 2; ++i) {
         mbar_init(&s_full(g)[i], 1);
-        mbar_init(&s_empty(g)[i], 4);
-        mbar_init(&p_full(g)[i], 4);
+        mbar_init(&s_empty(g)[i], 4 * kW);
+        mbar_init(&p_full(g)[i], 4 * kW);
         mbar_init(&p_empty(g)[i], 1);
+        mbar_init(&xch(g)[i], 4 * kW);
       }
       mbar_init(o_done(g), 1);
       mbar_init(o_final(g), 1);
+      mbar_init(l_xch(g), 4 * kW);
     }
     fence_mbar_init();
   }
@@ -226,7 +242,10 @@ __global__ void __launch_bounds__(AttnShape<kHD, kG>::kThreads, 1)
   } else {
     // ---------------- softmax warpgroups ----------------
     griddep_wait();
-    const int g = (warp - 2) >> 2;
+    const int g = (warp - 2) / (4 * kW);
+    const int wsub = ((warp - 2) >> 2) % kW;  // column share: keys [c0, c0 + kCols) of each tile
+    constexpr int kCols = Sh::kCols;
+    const int c0 = wsub * kCols;
     const int quad = warp & 3;  // TMEM lane quadrant of this warp
     const int r = quad * 32 + lane;
     const int qrow = q0 + 128 * g + r;
@@ -246,9 +265,10 @@ __global__ void __launch_bounds__(AttnShape<kHD, kG>::kThreads, 1)
       ok = mbar_wait(&s_full(g)[sb], ph, kErrAttnTimeout + 3);
       if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
       tc_fence_after();
-      float sv[64];
-      tmem_ld32(tmem + lane_off + (2 * g + sb) * 64, *reinterpret_cast<float(*)[32]>(&sv[0]));
-      tmem_ld32(tmem + lane_off + (2 * g + sb) * 64 + 32, *reinterpret_cast<float(*)[32]>(&sv[32]));
+      float sv[kCols];
+#pragma unroll
+      for (int h = 0; h < kCols / 32; ++h)
+        tmem_ld32(tmem + lane_off + (2 * g + sb) * 64 + c0 + 32 * h, *reinterpret_cast<float(*)[32]>(&sv[32 * h]));
       tmem_wait_ld();
       tc_fence_before();
       __syncwarp();
@@ -259,32 +279,46 @@ __global__ void __launch_bounds__(AttnShape<kHD, kG>::kThreads, 1)
       // sequence without a key mask skip the masking; the key mask, when there is one, is read
       // as 64 bytes once per tile, so the per-element work stays branch-free.
       const int kbase = j * 64;
-      // keys of this tile visible to this row: inside the sequence and, when causal, <= the row
-      const int nvis = P.causal ? min(L, (qrow / cb + 1) * cb) - kbase : L - kbase;
+      // keys of this thread's columns visible to this row: inside the sequence and, when causal,
+      // <= the row
+      const int nvis = (P.causal ? min(L, (qrow / cb + 1) * cb) - kbase : L - kbase) - c0;
       float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
       // a tile below the diagonal for every row of the group needs no mask (warp-uniform test)
       const bool full_tile = L - kbase >= 64 && (!P.causal || kbase + 63 < ((q0 + 128 * g) / cb + 1) * cb);
       if (kmask == nullptr && full_tile) {
 #pragma unroll
-        for (int c = 0; c < 64; ++c) mx4[c & 3] = fmaxf(mx4[c & 3], sv[c]);
+        for (int c = 0; c < kCols; ++c) mx4[c & 3] = fmaxf(mx4[c & 3], sv[c]);
       } else if (kmask == nullptr) {
 #pragma unroll
-        for (int c = 0; c < 64; ++c) {
+        for (int c = 0; c < kCols; ++c) {
           sv[c] = (c < nvis) ? sv[c] : -INFINITY;
           mx4[c & 3] = fmaxf(mx4[c & 3], sv[c]);
         }
       } else {
-        uint32_t mbits[2] = {0u, 0u};  // bit c: key kbase + c visible
+        uint32_t mbits[2] = {0u, 0u};  // bit c: key kbase + c0 + c visible
 #pragma unroll 1
-        for (int c = 0; c < 64; ++c)
-          if (c < nvis && kmask[kbase + c] != 0) mbits[c >> 5] |= 1u << (c & 31);
+        for (int c = 0; c < kCols; ++c)
+          if (c < nvis && kmask[kbase + c0 + c] != 0) mbits[c >> 5] |= 1u << (c & 31);
 #pragma unroll
-        for (int c = 0; c < 64; ++c) {
+        for (int c = 0; c < kCols; ++c) {
           sv[c] = ((mbits[c >> 5] >> (c & 31)) & 1u) ? sv[c] : -INFINITY;
           mx4[c & 3] = fmaxf(mx4[c & 3], sv[c]);
         }
       }
-      const float mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3])) * scale;
+      float mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3]));
+      if constexpr (kW > 1) {
+        // the row's maximum over the whole tile: every column warpgroup publishes its part and
+        // reads the others' (buffer sb is rewritten two tiles later, after every warpgroup has
+        // published tile j + 1, i.e. read tile j)
+        xf[((g * 3 + sb) * kW + wsub) * 128 + r] = mx;
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&xch(g)[sb]);
+        ok = mbar_wait(&xch(g)[sb], ph, kErrAttnTimeout + 3);
+        if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
+#pragma unroll
+        for (int w = 0; w < kW; ++w) mx = fmaxf(mx, xf[((g * 3 + sb) * kW + w) * 128 + r]);
+      }
+      mx *= scale;
 
       // lazy rescale of O and l when this row's max outgrows the reference by 2^8
       const bool grow = mx > m_ref + kRescaleLog2;
@@ -294,7 +328,7 @@ __global__ void __launch_bounds__(AttnShape<kHD, kG>::kThreads, 1)
         m_ref = mx;
         l_run *= alpha;
       }
-      if (j > 0 && __any_sync(0xffffffffu, grow)) {
+      if (wsub == 0 && j > 0 && __any_sync(0xffffffffu, grow)) {
         // O holds PV_0..PV_{j-1}: wait for the last one, scale the rows that moved (S_j was
         // issued after PV_{j-2}, so o_done is at most one phase behind here)
         ok = mbar_wait(o_done(g), static_cast<uint32_t>(j - 1) & 1u, kErrAttnTimeout + 3);
@@ -314,7 +348,7 @@ __global__ void __launch_bounds__(AttnShape<kHD, kG>::kThreads, 1)
       const float m_use = (m_ref == -INFINITY) ? 0.0f : m_ref;
       float ps4[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
-      for (int c = 0; c < 64; ++c) {
+      for (int c = 0; c < kCols; ++c) {
         sv[c] = ex2_approx(fmaf(sv[c], scale, -m_use));
         ps4[c & 3] += sv[c];
       }
@@ -325,13 +359,14 @@ __global__ void __launch_bounds__(AttnShape<kHD, kG>::kThreads, 1)
       if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
       uint8_t* prow = sP + (2 * g + sb) * kPBytes + r * 128;
 #pragma unroll
-      for (int cc = 0; cc < 8; ++cc) {
+      for (int cc = 0; cc < kCols / 8; ++cc) {
         uint4 u;
         u.x = pack_bf16x2(sv[8 * cc + 0], sv[8 * cc + 1]);
         u.y = pack_bf16x2(sv[8 * cc + 2], sv[8 * cc + 3]);
         u.z = pack_bf16x2(sv[8 * cc + 4], sv[8 * cc + 5]);
         u.w = pack_bf16x2(sv[8 * cc + 6], sv[8 * cc + 7]);
-        *reinterpret_cast<uint4*>(prow + ((cc ^ (r & 7)) << 4)) = u;
+        const int chunk = c0 / 8 + cc;
+        *reinterpret_cast<uint4*>(prow + ((chunk ^ (r & 7)) << 4)) = u;
       }
       fence_proxy_async_smem();
       tc_fence_before();
@@ -343,6 +378,20 @@ __global__ void __launch_bounds__(AttnShape<kHD, kG>::kThreads, 1)
     // o_done may be anywhere from two phases behind to complete, which a parity wait on it
     // cannot tell apart.
     if (ok && nkv > 0) ok = mbar_wait(o_final(g), 0u, kErrAttnTimeout + 3);
+    if constexpr (kW > 1) {
+      // the row sum over all keys: each column warpgroup's part, published once at the end
+      if (__all_sync(0xffffffffu, ok) && nkv > 0) {
+        xf[((g * 3 + 2) * kW + wsub) * 128 + r] = l_run;
+        __syncwarp();
+        if (lane == 0) mbar_arrive(l_xch(g));
+        ok = mbar_wait(l_xch(g), 0u, kErrAttnTimeout + 3);
+        if (__all_sync(0xffffffffu, ok)) {
+          l_run = 0.0f;
+#pragma unroll
+          for (int w = 0; w < kW; ++w) l_run += xf[((g * 3 + 2) * kW + w) * 128 + r];
+        }
+      }
+    }
     if (__all_sync(0xffffffffu, ok) && nkv > 0) {
       tc_fence_after();
       int seg = 0, off = 0;
@@ -355,21 +404,26 @@ __global__ void __launch_bounds__(AttnShape<kHD, kG>::kThreads, 1)
       const int ld = P.seg_ld[seg] > 0 ? P.seg_ld[seg] : P.H * od;
       uint4* d4 = reinterpret_cast<uint4*>(
           P.seg_out[seg] + (static_cast<size_t>(b) * P.seg_len[seg] + (qrow - off)) * ld + head * od);
+      // the column warpgroups split the output dims too: warpgroup w writes dims [w * 64 / kW, ...)
+      constexpr int kODims = 64 / kW;
 #pragma unroll
       for (int half = 0; half < kHD / 64; ++half) {  // 64 output dims at a time
-        float o[64];
-        tmem_ld32(tmem + lane_off + o_col + 64 * half, *reinterpret_cast<float(*)[32]>(&o[0]));
-        tmem_ld32(tmem + lane_off + o_col + 64 * half + 32, *reinterpret_cast<float(*)[32]>(&o[32]));
+        float o[kODims];
+        const uint32_t ocol = o_col + 64 * half + wsub * kODims;
+#pragma unroll
+        for (int h = 0; h < kODims / 32; ++h)
+          tmem_ld32(tmem + lane_off + ocol + 32 * h, *reinterpret_cast<float(*)[32]>(&o[32 * h]));
         tmem_wait_ld();
         if (qrow < L) {
 #pragma unroll
-          for (int cc = 0; cc < 8; ++cc) {
+          for (int cc0 = 0; cc0 < kODims / 8; ++cc0) {
+            const int cc = wsub * (kODims / 8) + cc0;  // 8-dim chunk of the 64 of this half
             if (64 * half + 8 * cc >= od) break;
             uint4 u;
-            u.x = pack_bf16x2(o[8 * cc + 0] * inv_l, o[8 * cc + 1] * inv_l);
-            u.y = pack_bf16x2(o[8 * cc + 2] * inv_l, o[8 * cc + 3] * inv_l);
-            u.z = pack_bf16x2(o[8 * cc + 4] * inv_l, o[8 * cc + 5] * inv_l);
-            u.w = pack_bf16x2(o[8 * cc + 6] * inv_l, o[8 * cc + 7] * inv_l);
+            u.x = pack_bf16x2(o[8 * cc0 + 0] * inv_l, o[8 * cc0 + 1] * inv_l);
+            u.y = pack_bf16x2(o[8 * cc0 + 2] * inv_l, o[8 * cc0 + 3] * inv_l);
+            u.z = pack_bf16x2(o[8 * cc0 + 4] * inv_l, o[8 * cc0 + 5] * inv_l);
+            u.w = pack_bf16x2(o[8 * cc0 + 6] * inv_l, o[8 * cc0 + 7] * inv_l);
             d4[8 * half + cc] = u;
           }
         }
@@ -385,15 +439,15 @@ __global__ void __launch_bounds__(AttnShape<kHD, kG>::kThreads, 1)
 }
 
 namespace {
-template <int kHD, int kG>
+template <int kHD, int kG, int kW = 1>
 cudaError_t set_smem() {
-  return cudaFuncSetAttribute(joint_attention_kernel<kHD, kG>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                              static_cast<int>(AttnShape<kHD, kG>::kSmem));
+  return cudaFuncSetAttribute(joint_attention_kernel<kHD, kG, kW>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                              static_cast<int>(AttnShape<kHD, kG, kW>::kSmem));
 }
 
-template <int kHD, int kG>
+template <int kHD, int kG, int kW = 1>
 cudaError_t launch_variant(const AttnParams& p, cudaStream_t stream, bool pdl) {
-  using Sh = AttnShape<kHD, kG>;
+  using Sh = AttnShape<kHD, kG, kW>;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((p.L + 128 * kG - 1) / (128 * kG), p.H, p.B);
   cfg.blockDim = dim3(Sh::kThreads, 1, 1);
@@ -404,16 +458,17 @@ cudaError_t launch_variant(const AttnParams& p, cudaStream_t stream, bool pdl) {
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = pdl ? 1 : 0;
-  return cudaLaunchKernelEx(&cfg, joint_attention_kernel<kHD, kG>, p);
+  return cudaLaunchKernelEx(&cfg, joint_attention_kernel<kHD, kG, kW>, p);
 }
 }  // namespace
 
 size_t attention_smem_bytes(int head_dim) {
-  return head_dim == 128 ? AttnShape<128, 2>::kSmem : AttnShape<64, 2>::kSmem;
+  return head_dim == 128 ? AttnShape<128, 2>::kSmem : std::max(AttnShape<64, 2>::kSmem, AttnShape<64, 1, 2>::kSmem);
 }
 
 cudaError_t attention_prepare_device() {
   cudaError_t e = set_smem<64, 1>();
+  if (e == cudaSuccess) e = set_smem<64, 1, 2>();
   if (e == cudaSuccess) e = set_smem<64, 2>();
   if (e == cudaSuccess) e = set_smem<128, 1>();
   if (e == cudaSuccess) e = set_smem<128, 2>();
@@ -428,12 +483,27 @@ int attention_tiles_per_cta(const AttnParams& p, int sms) {
   return p.tiles_per_cta == 2 ? 2 : 1;
 }
 
+// Two column warpgroups per query tile (head_dim 64) when the launch has no more query tiles
+// than SMs: then every CTA sits alone on its SM and the softmax chain of its tiles is the
+// critical path (the batch-1 control step: 5 tiles x 24 heads).  Larger launches keep one
+// warpgroup per tile, which lets two CTAs share an SM.  RLDX_ATTN_COLS=1 turns the split off.
+bool attention_column_split(const AttnParams& p, int sms) {
+  static int off = [] {
+    const char* e = std::getenv("RLDX_ATTN_COLS");
+    return (e && e[0] == '1') ? 1 : 0;
+  }();
+  const long long tiles = static_cast<long long>((p.L + 127) / 128) * p.H * p.B;
+  return off == 0 && tiles <= sms;
+}
+
 cudaError_t launch_attention(const AttnParams& p, cudaStream_t stream, bool pdl) {
   const int hd = p.head_dim > 0 ? p.head_dim : 64;
   if (hd != 64 && hd != 128) return cudaErrorInvalidValue;
   const int g = attention_tiles_per_cta(p, sm_count());
   if (hd == 128) return g == 2 ? launch_variant<128, 2>(p, stream, pdl) : launch_variant<128, 1>(p, stream, pdl);
-  return g == 2 ? launch_variant<64, 2>(p, stream, pdl) : launch_variant<64, 1>(p, stream, pdl);
+  if (g == 2) return launch_variant<64, 2>(p, stream, pdl);
+  return attention_column_split(p, sm_count()) ? launch_variant<64, 1, 2>(p, stream, pdl)
+                                                : launch_variant<64, 1>(p, stream, pdl);
 }
 
 }  // namespace rldx

@@ -55,6 +55,15 @@ def test_joint_attention_key_mask(cuda):
     run_case(cuda, 2, 4, [96, 18, 32], mask=True, seed=7)
 
 
+# Launches with no more 128-query tiles than SMs split each tile's keys over two softmax
+# warpgroups (head_dim 64); larger ones run one warpgroup per tile.  Both forms, with and
+# without a key mask:
+@pytest.mark.parametrize("B,segs", [(1, [512, 18, 32]), (8, [512, 18, 32]), (2, [1000, 48])])
+@pytest.mark.parametrize("mask", [False, True])
+def test_joint_attention_column_split_and_single_warpgroup(cuda, B, segs, mask):
+    run_case(cuda, B, 24, segs, mask=mask, seed=B * 10 + len(segs) + int(mask))
+
+
 @pytest.mark.parametrize("segs", [[1], [65], [240, 32, 16], [496, 32, 16], [1008, 32, 16]])
 def test_joint_attention_head_dim_128(cuda, segs):
     """head_dim 128 (the joint-attention sweep's shape: segments (L-48):32:16, 16 heads)."""
