@@ -2,6 +2,7 @@
 
     python -m rldx_b200.microbench --suite c1    # one 3-stream MSAT block (config 1 shapes), bf16
     python -m rldx_b200.microbench --suite c3    # memory-bound: Qwen3 QK-RMSNorm+RoPE, SwiGLU
+    python -m rldx_b200.microbench --suite gemm  # tensor-bound GEMMs of the batched (config 5) path
     python -m rldx_b200.microbench --suite c4    # joint-attention sweep, head_dim 128
     python -m rldx_b200.microbench --suite vlm   # config-5 VLM-shaped prefill (12 Qwen3 layers)
     python -m rldx_b200.microbench --suite all
@@ -31,6 +32,12 @@ hidden 1024, 16 x 64 heads, SwiGLU 2816, seeded N(0, 0.02) weights, ~N(0,1) stre
 B200ExpandedDoubleStreamBlock, replayed as one CUDA graph of 11 launches, batch 1 (the latency
 case) and larger batches (throughput); FLOPs per block = 2 * 288 * 12.58 M (projections) +
 4 * 288^2 * 1024 (attention) = 7.74 GFLOP per batch element.
+
+GEMM suite: the large projections of the batched path on their own (plain bf16 store
+epilogue): 8192 x 8192 x 2048, the config-5 VLM w12 at 32 observations (27136 x 22016 x 2048),
+the config-2 QKV at 256 observations (131072 x 4608 x 1536); ten launches replayed as one CUDA
+graph, FLOPs = 2 M N K; the planner's choice (CTA pairs or single CTAs) is in the line, and
+torch.matmul (cuBLAS) on the same operands is timed beside it for context.
 
 Config 4: non-causal joint attention over [cognition | physics | action] segments of lengths
 (L-48):32:16, 16 heads x 128, batch 1-64; FLOPs = 4 * B * H * L^2 * 128.  torch's
@@ -245,6 +252,51 @@ def suite_c1(iters: int, warmup: int, batches=(1, 8, 64)):
                "roofline_us": round(flops * B / (tc_peak * 1e12) * 1e6, 2)}
 
 
+def graph_time_ms(fn, reps: int = 10, iters: int = 10) -> float:
+    """Device time of one fn() call: `reps` calls captured in a CUDA graph, replayed `iters` times."""
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        for _ in range(3):
+            fn()
+    torch.cuda.current_stream().wait_stream(side)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        for _ in range(reps):
+            fn()
+    for _ in range(2):
+        g.replay()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(iters):
+        g.replay()
+    b.record()
+    torch.cuda.synchronize()
+    return a.elapsed_time(b) / (iters * reps)
+
+
+def suite_gemm(shapes=((8192, 8192, 2048), (27136, 22016, 2048), (131072, 4608, 1536))):
+    _, tc_peak, kind = peaks()
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device=dev).manual_seed(0)
+    for M, N, K in shapes:
+        x = torch.randn(M, K, device=dev, generator=g).to(BF)
+        w = (torch.randn(N, K, device=dev, generator=g) * 0.02).to(BF)
+        out = torch.empty(M, N, dtype=BF, device=dev)
+        d = [ops.gemm_desc(x, w, out)]
+        plan = ops.gemm_plan(d)
+        ms = graph_time_ms(lambda: ops.gemm(d))
+        ms_ref = graph_time_ms(lambda: torch.matmul(x, w.t(), out=out))
+        tf = 2.0 * M * N * K / (ms * 1e-3) / 1e12
+        yield {"suite": "gemm", "M": M, "N": N, "K": K, "plan": plan, "us": round(ms * 1e3, 1),
+               "tflops": round(tf, 1), "frac_of_peak": round(tf / tc_peak, 3),
+               "peak": f"{tc_peak} TFLOP/s ({kind}, burst)",
+               "cublas_tflops": round(2.0 * M * N * K / (ms_ref * 1e-3) / 1e12, 1)}
+        del x, w, out
+
+
 def nn_module(ns):
     """B200LLMChain stores the final norm as a submodule: wrap the weight holder."""
     m = torch.nn.Module()
@@ -254,12 +306,14 @@ def nn_module(ns):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--suite", choices=["c1", "c3", "c4", "vlm", "all"], default="all")
+    ap.add_argument("--suite", choices=["c1", "c3", "c4", "vlm", "gemm", "all"], default="all")
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--batches", type=str, default="1,4,16,64")
     ap.add_argument("--lengths", type=str, default="288,544,1056,2080,4128")
     ap.add_argument("--tiles", type=int, default=0, help="query tiles per attention CTA (0: automatic)")
+    ap.add_argument("--gemm-shapes", type=str, default="8192x8192x2048,27136x22016x2048,131072x4608x1536",
+                    help="MxNxK list of the gemm suite")
     a = ap.parse_args()
     if not torch.cuda.is_available():
         raise SystemExit("microbench needs a CUDA device")
@@ -273,6 +327,10 @@ def main():
         bs = tuple(int(x) for x in a.batches.split(","))
         ls = tuple(int(x) for x in a.lengths.split(","))
         for r in suite_c4(a.iters, a.warmup, bs, ls, a.tiles):
+            print(json.dumps(r), flush=True)
+    if a.suite in ("gemm", "all"):
+        shapes = tuple(tuple(int(v) for v in t.split("x")) for t in a.gemm_shapes.split(","))
+        for r in suite_gemm(shapes):
             print(json.dumps(r), flush=True)
     if a.suite in ("vlm", "all"):
         for r in suite_vlm(a.iters, a.warmup):
