@@ -121,10 +121,17 @@ class TextStack(nn.Module):
         self.norm = RMSNorm(c.hidden, c.rms_eps)
 
     @torch.no_grad()
-    def forward(self, h, cos, sin, final_norm: bool = True, return_hidden: bool = False):
+    def forward(self, h, cos, sin, final_norm: bool = True, return_hidden: bool = False,
+                deepstack=None, deepstack_rows=None):
+        """deepstack: per-layer visual features [n, D] added, after layer i < len(deepstack), to
+        the token rows `deepstack_rows` of every sequence (Qwen3VLTextModel._deepstack_process,
+        modeling_qwen3_vl.py:1086-1113: hidden[mask] = hidden[mask] + embeds, one rounding)."""
         hidden = []
-        for layer in self.layers:
+        for i, layer in enumerate(self.layers):
             h = layer(h, cos, sin)
+            if deepstack is not None and i < len(deepstack):
+                h = h.clone()
+                h[:, deepstack_rows] = h[:, deepstack_rows] + deepstack[i].to(h.dtype)
             hidden.append(h)
         out = self.norm(h) if final_norm else h
         return (out, hidden) if return_hidden else out

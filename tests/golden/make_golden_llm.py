@@ -11,7 +11,7 @@ oracle has the same parameter names, so the same seed gives the same weights) an
 per-layer hidden states and the final-norm output.  The RoPE tables come from the reference's
 own rotary embedding with 3-D (mRoPE) position ids of an image grid followed by text.
 
-Usage:  python tests/golden/make_golden_llm.py
+Usage:  python tests/golden/make_golden_llm.py [--deepstack-only]
 """
 
 from __future__ import annotations
@@ -113,11 +113,43 @@ def fixture(mod, dtype, batch):
             "inputs": {"hidden": h0, "cos": cos, "sin": sin}, "hidden": hidden, "out": out}
 
 
+def fixture_deepstack(mod, dtype, batch):
+    """The same stack with deepstack visual features added after layers 0 and 1 to the 64 image
+    tokens of every sequence, through the reference's own Qwen3VLTextModel._deepstack_process
+    (modeling_qwen3_vl.py:1086-1113; it reads nothing from the model instance)."""
+    stack, rotary = reference_stack(mod)
+    oq.init_weights(stack, seed=2024)
+    stack = stack.to(dtype).eval()
+    g = torch.Generator().manual_seed(8)
+    h0 = torch.randn(batch, T, CFG.hidden, generator=g).to(dtype)
+    feats = torch.randn(2, 64, CFG.hidden, generator=g).to(dtype)
+    mask = torch.zeros(batch, T, dtype=torch.bool)
+    mask[:, :64] = True
+    with torch.no_grad():
+        cos, sin = rotary(h0, mrope_positions(batch))
+        hidden = []
+        h = h0
+        for i, layer in enumerate(stack.layers):
+            h = layer(h, position_embeddings=(cos, sin), attention_mask=None)
+            if i < feats.shape[0]:
+                embeds = feats[i].repeat(batch, 1)  # mask order: sequence by sequence
+                h = mod.Qwen3VLTextModel._deepstack_process(None, h, mask, embeds)
+            hidden.append(h.clone())
+        out = stack.norm(h)
+    return {"config": vars(CFG), "seed": 2024, "dtype": str(dtype), "batch": batch,
+            "inputs": {"hidden": h0, "cos": cos, "sin": sin, "deepstack": feats,
+                       "deepstack_rows": torch.arange(64)},
+            "hidden": hidden, "out": out}
+
+
 def main():
     mod = import_reference()
+    only_ds = "--deepstack-only" in sys.argv
     for dtype, dn in ((torch.float32, "fp32"), (torch.bfloat16, "bf16")):
         for batch in (1, 2):
-            torch.save(fixture(mod, dtype, batch), HERE / f"llm_b{batch}_{dn}.pt")
+            if not only_ds:
+                torch.save(fixture(mod, dtype, batch), HERE / f"llm_b{batch}_{dn}.pt")
+            torch.save(fixture_deepstack(mod, dtype, batch), HERE / f"llm_ds_b{batch}_{dn}.pt")
     for f in sorted(HERE.glob("llm_*.pt")):
         print(f.name, f.stat().st_size)
 

@@ -40,3 +40,21 @@ def test_rope_tables_of_text_positions():
     cos, sin = oq.rope_tables(cfg, pos)
     torch.testing.assert_close(cos, fx["inputs"]["cos"][0, 64:], rtol=1e-6, atol=1e-6)
     torch.testing.assert_close(sin, fx["inputs"]["sin"][0, 64:], rtol=1e-6, atol=1e-6)
+
+
+@pytest.mark.parametrize("name", [f"llm_ds_b{b}_{dt}.pt" for b in (1, 2) for dt in ("fp32", "bf16")])
+def test_oracle_deepstack_matches_reference(name):
+    """Deepstack visual features after layers 0 and 1 on the 64 image tokens, against the
+    reference's own _deepstack_process on its decoder layers."""
+    fx = torch.load(GOLD / name, weights_only=False)
+    cfg = oq.Qwen3Config(**fx["config"])
+    dtype = torch.bfloat16 if "bf16" in name else torch.float32
+    stack = oq.init_weights(oq.TextStack(cfg), seed=fx["seed"]).to(dtype)
+    inp = fx["inputs"]
+    out, hidden = stack(inp["hidden"], inp["cos"], inp["sin"], return_hidden=True,
+                        deepstack=inp["deepstack"], deepstack_rows=inp["deepstack_rows"])
+    for got, exp in list(zip(hidden, fx["hidden"])) + [(out, fx["out"])]:
+        if dtype == torch.bfloat16:
+            assert torch.equal(got, exp), (got.float() - exp.float()).abs().max()
+        else:
+            torch.testing.assert_close(got, exp, rtol=1e-5, atol=1e-5)
