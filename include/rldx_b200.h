@@ -468,6 +468,12 @@ typedef struct {
   int norm_weight_first; /* 1: RMSNorm = bf16(w * x * rsqrt(...)) in fp32 (norms.py:18-22);
                             0: Qwen3's cast, then weight */
   int causal_block;      /* 0 / 1: token-causal mask; n: block-causal over blocks of n tokens */
+  /* Deepstack (Qwen3VLTextModel._deepstack_process, modeling_qwen3_vl.py:1086-1113;
+   * CustomLLMChain.forward's deepstack_features, custom_llm_chain.py:137-161): after layer
+   * i < deepstack_layers, hidden[b, row, :] += feature[i, b, j, :] (one bf16 rounding) for the
+   * deepstack_rows token rows listed in rldx_llm_weights.deepstack_row_index.  0: none. */
+  int deepstack_layers;
+  int deepstack_rows;
 } rldx_llm_config;
 
 typedef struct {
@@ -489,6 +495,7 @@ typedef struct {
   const void* final_norm;               /* [D] (final_norm = 1) */
   const void* rope_cos;                 /* [tokens, head_dim] bf16 */
   const void* rope_sin;                 /* [tokens, head_dim] bf16 */
+  const int* deepstack_row_index;       /* [deepstack_rows] host array of token rows (< tokens) */
 } rldx_llm_weights;
 
 int rldx_llm_create(const rldx_llm_config* cfg, const rldx_llm_weights* w, rldx_llm** out);
@@ -497,6 +504,11 @@ int rldx_llm_destroy(rldx_llm* h);
 int rldx_llm_prefill(rldx_llm* h, const void* hidden_in, void* hidden_out, void* stream);
 /* kernel launches of one prefill (graph nodes when captured) */
 int rldx_llm_launch_count(const rldx_llm* h);
+/* Deepstack features of the next prefills: [deepstack_layers, batch, deepstack_rows, hidden]
+ * bf16 (device or host pointer), copied into the handle's buffer asynchronously on stream
+ * (the reference chain copies them into its _deepstack_add buffer per call,
+ * custom_llm_chain.py:138-147).  Requires deepstack_layers > 0 at create. */
+int rldx_llm_set_deepstack(rldx_llm* h, const void* features, void* stream);
 
 #ifdef __cplusplus
 }

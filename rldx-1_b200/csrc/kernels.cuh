@@ -48,6 +48,11 @@ struct LnParams {
 };
 cudaError_t launch_ln(const LnParams& p, cudaStream_t stream, bool pdl);
 
+// x[(b * T + rows[j]) * D + c] = bf16(x + f[(b * nrows + j) * D + c]) for b < B, j < nrows
+// (deepstack feature injection; D % 8 == 0, 16-byte aligned rows)
+cudaError_t launch_rows_add(__nv_bfloat16* x, const int* rows, int nrows, const __nv_bfloat16* f, int B, int T,
+                            int D, cudaStream_t stream);
+
 // Row copy: row i -> group g = i / group_rows, r = i % group_rows (group_rows 0: g = 0, r = i);
 // src + g*src_group_pitch + r*src_pitch -> dst + g*dst_group_pitch + r*dst_pitch.
 struct CopyRegion {

@@ -39,6 +39,9 @@ struct rldx_llm {
   bf16 *h = nullptr, *n = nullptr, *qkv = nullptr, *q = nullptr, *k = nullptr, *vt = nullptr, *a = nullptr,
        *g = nullptr;
   bf16* out = nullptr;  // result of the last op (n after the final norm, else h)
+  int ds_layers = 0, ds_rows = 0;
+  int* ds_index = nullptr;  // [ds_rows] token rows
+  bf16* ds_feat = nullptr;  // [ds_layers][B][ds_rows][D]
   std::vector<std::function<cudaError_t(cudaStream_t, bool)>> ops;
   void* ws = nullptr;
   size_t ws_bytes = 0, ws_need = 0;
@@ -129,6 +132,15 @@ struct rldx_llm {
     if (static_cast<long long>(B) * T * (Hq + Hkv) >= (1LL << 31)) throw Fail(RLDX_ERR_UNSUPPORTED, "llm_create: too many rows");
     if (!w.layers || !w.rope_cos || !w.rope_sin) throw Fail(RLDX_ERR_ARG, "llm_create: missing layers or RoPE tables");
     if (c.final_norm && !w.final_norm) throw Fail(RLDX_ERR_ARG, "llm_create: missing final_norm");
+    if (c.deepstack_layers < 0 || c.deepstack_layers > c.layers || c.deepstack_rows < 0 ||
+        (c.deepstack_layers > 0) != (c.deepstack_rows > 0))
+      throw Fail(RLDX_ERR_ARG, "llm_create: deepstack_layers in [0, layers] and deepstack_rows > 0 together");
+    if (c.deepstack_layers > 0) {
+      if (!w.deepstack_row_index) throw Fail(RLDX_ERR_ARG, "llm_create: missing deepstack_row_index");
+      for (int j = 0; j < c.deepstack_rows; ++j)
+        if (w.deepstack_row_index[j] < 0 || w.deepstack_row_index[j] >= c.tokens)
+          throw Fail(RLDX_ERR_ARG, "llm_create: deepstack row outside the sequence");
+    }
     Tp = (T + 7) / 8 * 8;
     Fp = (F + 31) / 32 * 32;
     NQKV = (Hq + 2 * Hkv) * hd;
@@ -161,6 +173,14 @@ struct rldx_llm {
       lw.push_back(l);
     }
     if (c.final_norm) final_norm = copy_in(w.final_norm, D, "final norm");
+    ds_layers = c.deepstack_layers;
+    ds_rows = c.deepstack_rows;
+    if (ds_layers > 0) {
+      ds_index = alloc<int>(ds_rows);
+      ck(cudaMemcpy(ds_index, w.deepstack_row_index, static_cast<size_t>(ds_rows) * 4, cudaMemcpyHostToDevice),
+         "deepstack rows");
+      ds_feat = alloc<bf16>(static_cast<size_t>(ds_layers) * B * ds_rows * D);  // zero until set
+    }
     cos = copy_in(w.rope_cos, static_cast<size_t>(T) * hd, "rope cos");
     sin = copy_in(w.rope_sin, static_cast<size_t>(T) * hd, "rope sin");
 
@@ -282,6 +302,13 @@ struct rldx_llm {
         d.ld_add = D;
         push_gemm(d);
       }
+      if (li < ds_layers) {  // deepstack: after the layer's output, before the next layer
+        bf16* hp = h;
+        const int* idx = ds_index;
+        const bf16* f = ds_feat + static_cast<size_t>(li) * B * ds_rows * D;
+        const int r_ = ds_rows, b_ = B, t_ = T, d_ = D;
+        ops.push_back([=](cudaStream_t st, bool) { return launch_rows_add(hp, idx, r_, f, b_, t_, d_, st); });
+      }
     }
     out = h;
     if (c.final_norm) {
@@ -346,5 +373,15 @@ int rldx_llm_prefill(rldx_llm* h, const void* hidden_in, void* hidden_out, void*
 }
 
 int rldx_llm_launch_count(const rldx_llm* h) { return h ? static_cast<int>(h->ops.size()) : 0; }
+
+int rldx_llm_set_deepstack(rldx_llm* h, const void* features, void* stream) {
+  if (!h || !features) return set_error(RLDX_ERR_ARG, "llm_set_deepstack: null argument");
+  if (h->ds_layers == 0) return set_error(RLDX_ERR_ARG, "llm_set_deepstack: the handle was created without deepstack");
+  return guard([&] {
+    const size_t bytes = static_cast<size_t>(h->ds_layers) * h->B * h->ds_rows * h->D * 2;
+    ck(cudaMemcpyAsync(h->ds_feat, features, bytes, cudaMemcpyDefault, static_cast<cudaStream_t>(stream)),
+       "deepstack features");
+  });
+}
 
 }  // extern "C"

@@ -59,6 +59,40 @@ __global__ void elementwise_kernel(const __nv_bfloat16* __restrict__ x,
   }
 }
 
+// Deepstack injection (modeling_qwen3_vl.py:1102-1113: hidden[mask] = hidden[mask] + embeds):
+// one thread per 8 columns of a listed row; bf16 + bf16 rounds once (packed, exactly rounded).
+__global__ void rows_add_kernel(__nv_bfloat16* __restrict__ x, const int* __restrict__ rows, int nrows,
+                                const __nv_bfloat16* __restrict__ f, int B, int T, int D) {
+  const int nv = D / 8;
+  const long long total = static_cast<long long>(B) * nrows * nv;
+  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const int v = static_cast<int>(i % nv);
+    const long long bj = i / nv;  // b * nrows + j
+    const int j = static_cast<int>(bj % nrows);
+    const int b = static_cast<int>(bj / nrows);
+    uint4* xp = reinterpret_cast<uint4*>(x + (static_cast<long long>(b) * T + rows[j]) * D) + v;
+    const uint4 fv = reinterpret_cast<const uint4*>(f + bj * D)[v];
+    uint4 xv = *xp;
+    __nv_bfloat162* xh = reinterpret_cast<__nv_bfloat162*>(&xv);
+    const __nv_bfloat162* fh = reinterpret_cast<const __nv_bfloat162*>(&fv);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) xh[k] = __hadd2_rn(xh[k], fh[k]);
+    *xp = xv;
+  }
+}
+
+cudaError_t launch_rows_add(__nv_bfloat16* x, const int* rows, int nrows, const __nv_bfloat16* f, int B, int T,
+                            int D, cudaStream_t stream) {
+  if (nrows <= 0 || B <= 0) return cudaSuccess;
+  if (D % 8) return cudaErrorInvalidValue;
+  const long long total = static_cast<long long>(B) * nrows * (D / 8);
+  long long grid = (total + 255) / 256;
+  if (grid > 4096) grid = 4096;
+  rows_add_kernel<<<static_cast<unsigned>(grid), 256, 0, stream>>>(x, rows, nrows, f, B, T, D);
+  return cudaGetLastError();
+}
+
 cudaError_t launch_elementwise(const __nv_bfloat16* x, __nv_bfloat16* y, long long n, int mode,
                                cudaStream_t stream) {
   if (n <= 0) return cudaSuccess;

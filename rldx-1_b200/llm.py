@@ -13,8 +13,13 @@ reference unwraps it), `norm` the final RMSNorm, `pos_cos` / `signed_sin` the [M
 tables of the reference chain (signed_sin carries rotate_half's sign:
 -sin on the first half, fused_llm_attention.py:787-795).  The weights are copied into the
 native runtime (rldx_llm_create) on the first forward, when the batch size is known; the stack
-then runs as one CUDA graph of hand-written sm_100a kernels.  Deepstack feature injection is
-not bound (the reference adds it for the first layers of its vision-language path).
+then runs as one CUDA graph of hand-written sm_100a kernels.  Deepstack features
+(`deepstack_features[i]` [n, hidden] with `deepstack_flat_indices`, the element indices of the
+n visual token rows in one [tokens, hidden] sequence, as CustomLLMChain takes them,
+custom_llm_chain.py:137-161) are added after layer i to those rows of every sequence, with the
+eager path's single bf16 rounding (Qwen3VLTextModel._deepstack_process,
+modeling_qwen3_vl.py:1102-1113); the rows and the number of deepstack layers are bound on the
+first call.
 """
 
 from __future__ import annotations
@@ -82,19 +87,22 @@ class B200LLMChain(nn.Module):
         self._handle = None
         self._batch = None
         self._keep = []
+        self._ds = None  # (layers, rows) bound at create
 
     def _bf16(self, t: torch.Tensor) -> int:
         t = t.detach().to(device=self.device, dtype=torch.bfloat16).contiguous()
         self._keep.append(t)
         return t.data_ptr()
 
-    def bind(self, batch: int) -> None:
+    def bind(self, batch: int, deepstack_rows: Optional[torch.Tensor] = None, deepstack_layers: int = 0) -> None:
         M = self.cos.shape[0]
+        nrows = 0 if deepstack_rows is None else int(deepstack_rows.numel())
         cfg = LlmConfig(batch=batch, tokens=M, hidden=self.hidden, q_heads=self.q_heads, kv_heads=self.kv_heads,
                         head_dim=self.head_dim, ffn=self.ffn, layers=len(self.layers), rms_eps=self.eps,
                         final_norm=1 if self.apply_final_norm else 0, use_graph=1 if self.use_graph else 0,
                         no_qk_norm=0 if self.qk_norm else 1, norm_weight_first=1 if self.norm_weight_first else 0,
-                        causal_block=self.causal_block)
+                        causal_block=self.causal_block, deepstack_layers=deepstack_layers if nrows else 0,
+                        deepstack_rows=nrows)
         arr = (LlmLayerWeights * len(self.layers))()
         for i, layer in enumerate(self.layers):
             a, m = layer.self_attn, layer.mlp
@@ -105,9 +113,13 @@ class B200LLMChain(nn.Module):
                 self._bf16(a.v_proj.weight), qn, kn,
                 self._bf16(a.o_proj.weight), self._bf16(layer.post_attention_layernorm.weight),
                 self._bf16(m.gate_proj.weight), self._bf16(m.up_proj.weight), self._bf16(m.down_proj.weight))
+        rows_c = None
+        if nrows:
+            rows_c = (C.c_int * nrows)(*[int(r) for r in deepstack_rows.tolist()])
         w = LlmWeights(C.cast(arr, C.POINTER(LlmLayerWeights)),
                        self._bf16(self.norm.weight) if self.apply_final_norm else None,
-                       self.cos.data_ptr(), self.sin.data_ptr())
+                       self.cos.data_ptr(), self.sin.data_ptr(),
+                       C.cast(rows_c, C.POINTER(C.c_int)) if rows_c is not None else None)
         handle = C.c_void_p()
         with torch.cuda.device(self.device):
             rc = _lib.load().rldx_llm_create(C.byref(cfg), C.byref(w), C.byref(handle))
@@ -115,30 +127,56 @@ class B200LLMChain(nn.Module):
         check(rc)
         self._handle = handle
         self._batch = batch
+        self._ds = (deepstack_layers, tuple(deepstack_rows.tolist())) if nrows else None
 
     @property
     def launches_per_call(self) -> int:
         return int(_lib.load().rldx_llm_launch_count(self._handle)) if self._handle else 0
 
+    def _deepstack_rows(self, deepstack_flat_indices: torch.Tensor) -> torch.Tensor:
+        """Token rows of the reference's flat element indices (row * hidden + column, whole rows)."""
+        flat = deepstack_flat_indices.detach().reshape(-1).to("cpu", torch.int64)
+        D = self.hidden
+        if flat.numel() == 0 or flat.numel() % D:
+            raise ValueError("deepstack_flat_indices must cover whole rows of the hidden width")
+        rows = flat.view(-1, D)[:, 0] // D
+        if not torch.equal(flat.view(-1, D), rows[:, None] * D + torch.arange(D)[None, :]):
+            raise NotImplementedError("deepstack_flat_indices must list whole rows, columns in order")
+        return rows
+
     def forward(self, hidden_states: torch.Tensor, deepstack_features=None,
                 deepstack_flat_indices=None) -> torch.Tensor:
-        if deepstack_features is not None:
-            raise NotImplementedError("deepstack feature injection is not bound")
         if hidden_states.dim() == 2:
             hidden_states = hidden_states.unsqueeze(0)
         B, M, D = hidden_states.shape
         if M != self.cos.shape[0] or D != self.hidden:
             raise ValueError(f"hidden_states {tuple(hidden_states.shape)} does not match the chain's "
                              f"[*, {self.cos.shape[0]}, {self.hidden}]")
+        ds = None
+        if deepstack_features is not None and len(deepstack_features) > 0:
+            if deepstack_flat_indices is None:
+                raise ValueError("deepstack_features need deepstack_flat_indices")
+            ds = (min(len(deepstack_features), len(self.layers)), self._deepstack_rows(deepstack_flat_indices))
         if self._handle is None:
-            self.bind(B)
+            self.bind(B, ds[1] if ds else None, ds[0] if ds else 0)
         elif B != self._batch:
             raise ValueError(f"batch {B} differs from the bound batch {self._batch}")
+        if (ds is None) != (self._ds is None) or (ds is not None and (ds[0], tuple(ds[1].tolist())) != self._ds):
+            raise ValueError("deepstack layers / rows differ from the ones bound on the first call")
         x = hidden_states
         if x.device != self.device or x.dtype != torch.bfloat16 or not x.is_contiguous():
             x = x.to(device=self.device, dtype=torch.bfloat16).contiguous()
         out = torch.empty_like(x)
         stream = torch.cuda.current_stream(self.device)
+        if ds is not None:
+            L, rows = ds
+            n = rows.numel()
+            feats = torch.stack([deepstack_features[i].reshape(n, D) for i in range(L)])
+            # every sequence gets the same features (the reference chain's [1, tokens, hidden] buffer)
+            feats = feats.to(device=self.device, dtype=torch.bfloat16)[:, None].expand(L, B, n, D).contiguous()
+            check(_lib.load().rldx_llm_set_deepstack(self._handle, C.c_void_p(feats.data_ptr()),
+                                                     C.c_void_p(stream.cuda_stream)))
+            self._keep_ds = feats  # alive until the copy queued on `stream` has run
         check(_lib.load().rldx_llm_prefill(self._handle, C.c_void_p(x.data_ptr()), C.c_void_p(out.data_ptr()),
                                            C.c_void_p(stream.cuda_stream)))
         return out

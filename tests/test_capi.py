@@ -26,7 +26,7 @@ def test_every_declared_symbol_is_exported(lib):
 
 
 def test_version_and_error_string(lib):
-    assert lib.rldx_version() == 110
+    assert lib.rldx_version() == 111
     assert isinstance(lib.rldx_last_error(), bytes)
 
 
@@ -38,8 +38,8 @@ def test_struct_layouts_match_header():
     assert C.sizeof(_lib.BlockWeights) == 3 * (4 * 16 + 16)
     assert C.sizeof(_lib.SingleBlockWeights) == 2 * (3 * 16 + 16)
     assert C.sizeof(_lib.QkvSegment) == 64
-    assert C.sizeof(_lib.LlmConfig) == 14 * 4 and C.sizeof(_lib.LlmLayerWeights) == 11 * 8
-    assert C.sizeof(_lib.LlmWeights) == 4 * 8
+    assert C.sizeof(_lib.LlmConfig) == 16 * 4 and C.sizeof(_lib.LlmLayerWeights) == 11 * 8
+    assert C.sizeof(_lib.LlmWeights) == 5 * 8
     assert C.sizeof(_lib.AttentionDesc) == 3 * 8 + 8 * 4 + 8 + 3 * 8 + 3 * 4 + 3 * 4 + 3 * 4 + 4
     assert C.sizeof(_lib.ResLnSegment) == 6 * 8 + 2 * 4 + 8 + 8
     assert C.sizeof(_lib.SwigluBiasSegment) == 5 * 8 + 2 * 8 + 2 * 4

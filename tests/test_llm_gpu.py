@@ -56,6 +56,31 @@ def test_llm_matches_reference_golden(cuda, batch):
     check_close(h, fx["hidden"][-1], "last hidden")
 
 
+@pytest.mark.parametrize("batch", [1, 2])
+def test_llm_deepstack_matches_reference_golden(cuda, batch):
+    """Deepstack features after layers 0 and 1 on the 64 image tokens (the reference's
+    _deepstack_process), passed the way CustomLLMChain takes them: per-layer [n, hidden] features
+    and the flat element indices of their rows; repeated calls give the same output."""
+    fx = torch.load(GOLD / f"llm_ds_b{batch}_bf16.pt", weights_only=False)
+    cfg = oq.Qwen3Config(**fx["config"])
+    stack = oq.init_weights(oq.TextStack(cfg), seed=fx["seed"]).to(BF)
+    inp = fx["inputs"]
+    D = cfg.hidden
+    rows = inp["deepstack_rows"]
+    flat = (rows[:, None] * D + torch.arange(D)[None, :]).reshape(-1).to(cuda)
+    feats = [f.to(cuda) for f in inp["deepstack"]]
+    chain = B200LLMChain(stack.layers, stack.norm, inp["cos"][0].to(cuda), signed(inp["sin"][0]).to(cuda))
+    out = chain(inp["hidden"].to(cuda), deepstack_features=feats, deepstack_flat_indices=flat)
+    again = chain(inp["hidden"].to(cuda), deepstack_features=feats, deepstack_flat_indices=flat)
+    torch.cuda.synchronize()
+    check_close(out, fx["out"], "final norm with deepstack")
+    assert torch.equal(out, again)
+    plain = oq.init_weights(oq.TextStack(cfg), seed=fx["seed"]).to(BF)(inp["hidden"], inp["cos"], inp["sin"])
+    assert (out.float().cpu() - plain.float()).abs().max() > 0.1  # the features did change the output
+    with pytest.raises(ValueError):
+        chain(inp["hidden"].to(cuda))  # bound with deepstack: a call without it is shape drift
+
+
 def test_llm_config5_shapes_against_oracle(cuda):
     """One layer at the config-5 decoder dims over 848 tokens (784 image + 64 text), batch 2."""
     cfg = oq.Qwen3Config(hidden=2048, q_heads=16, kv_heads=2, head_dim=128, ffn=11008, layers=1)
