@@ -1,7 +1,7 @@
 """Benchmark of the MSAT all-modality control step on B200.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--batch B] [--impl b200|reference]
-                    [--workload c2|production|production_addons|c5] [--observations N]
+                    [--workload c1|c2|production|production_addons|c5] [--observations N]
 
 One step = one control step of the action head for B observations per GPU: state encoder,
 physics history encoder and 4 flow-matching Euler steps of [action + physics encoders, 16
@@ -19,7 +19,8 @@ with add-ons instead (4 double + 8 single blocks, VL width 4096; the shapes of t
 own published action-head benchmark, rldx/inference/action_model/README.md:9-37); --workload c5
 measures BASELINE config 5, the batched serving step (VLM prefill -> cognition tokens -> memory ->
 MSAT decoder) over --observations observations sharded across the GPUs (strong scaling; see
-run_c5).  The default line is config 2.
+run_c5); --workload c1 measures one config-1 joint block on the GPU (see run_c1) and, with
+--impl reference, the config-1 fp32 CPU block.  The default line is config 2.
 
 Printed JSON (rank 0): value = control steps/s of the whole job with inputs resident in HBM;
 e2e = the same through the C ABI with pinned host buffers (host->device inputs and device->host
@@ -55,7 +56,7 @@ def parse_args():
     p.add_argument("--warmup", type=int, default=5)
     p.add_argument("--batch", type=int, default=1, help="observations per GPU per control step")
     p.add_argument("--impl", choices=["b200", "reference"], default="b200")
-    p.add_argument("--workload", choices=["c2", "production", "production_addons", "c5"], default="c2")
+    p.add_argument("--workload", choices=["c1", "c2", "production", "production_addons", "c5"], default="c2")
     p.add_argument("--observations", type=int, default=256, help="config 5: observations per step (whole job)")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--cpu-sample-s", type=float, default=20.0, help="CPU baseline time budget")
@@ -287,7 +288,135 @@ def cpu_baseline_c5(budget_s: float):
                       f"layer p50 {memory * 1e3:.0f} ms x 2, MSAT control step {msat * 1e3:.0f} ms"}
 
 
+def c1_inputs(batch: int, seed: int = 11):
+    """Config-1 streams: cognition 256, action 16, physics 16 tokens of width 1024, ~N(0,1); RoPE
+    (theta 1e4) over the joint positions 0..287 as a complex [1, 288, 32] table."""
+    g = torch.Generator().manual_seed(seed)
+    cog = torch.randn(batch, 256, 1024, generator=g)
+    act = torch.randn(batch, 16, 1024, generator=g)
+    phys = torch.randn(batch, 16, 1024, generator=g)
+    inv = 1.0 / (1e4 ** (torch.arange(0, 64, 2).float() / 64))
+    ang = torch.arange(288).float()[:, None] * inv[None, :]
+    return act, cog, phys, torch.polar(torch.ones_like(ang), ang)[None]
+
+
+def cpu_baseline_c1(budget_s: float, steps: int = 20):
+    """BASELINE config 1 as specified: the reference block (oracle restatement, same module tree)
+    in fp32 eager on the host cores, batch 1, p50 over up to `steps` runs."""
+    from oracle import msat_oracle as om
+
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    blk = om.init_weights(om.ExpandedDoubleStreamBlock(1024, 16, 64, 2816, 2816), seed=7)
+    act, cog, phys, pe = c1_inputs(1)
+    times = []
+    with torch.no_grad():
+        for _ in range(3):
+            blk(act, cog, phys, pe)
+        start = time.perf_counter()
+        while len(times) < steps and time.perf_counter() - start < budget_s:
+            t = time.perf_counter()
+            blk(act, cog, phys, pe)
+            times.append(time.perf_counter() - t)
+    p50 = statistics.median(times)
+    return {"value": 1.0 / p50, "unit": "blocks/s", "cores": threads, "kind": "port",
+            "sample": f"{len(times)} fp32 block forwards (batch 1) on the host, p50 {p50 * 1e3:.1f} ms"}
+
+
+def run_c1(args, rank, world, local):
+    """BASELINE config 1 on the GPU: one ExpandedDoubleStreamBlock (cognition 256, action 16,
+    physics 16, hidden 1024, 16 x 64 heads, SwiGLU 2816) in bf16 through
+    B200ExpandedDoubleStreamBlock (11 launches replayed as one CUDA graph), `--batch`
+    independent sequences per GPU; seeded N(0, 0.02) weights."""
+    import rldx_b200  # noqa: F401
+    from rldx_b200.block import B200ExpandedDoubleStreamBlock
+    from rldx_b200.microbench import c1_block_module
+
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    B = args.batch
+    gpu = B200ExpandedDoubleStreamBlock(c1_block_module(0), dev, use_graph=True)
+    act, cog, phys, pe = c1_inputs(B, seed=11 + rank)
+    d_in = [t.to(dev, torch.bfloat16) for t in (act, cog, phys)]
+    gpu(*d_in, pe.to(dev))
+    flush = torch.empty(2 * L2_BYTES // 4, dtype=torch.int32, device=dev)
+    for _ in range(args.warmup):
+        gpu.replay()
+    torch.cuda.synchronize()
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    barrier(world)
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clocks:
+        for i in range(args.steps):
+            flush.fill_(i)  # the block's 75 MB of weights would otherwise stay in L2
+            starts[i].record()
+            gpu.replay()
+            ends[i].record()
+        torch.cuda.synchronize()
+    barrier(world)
+    total_ms = max_over_ranks(sum(s_.elapsed_time(e_) for s_, e_ in zip(starts, ends)), world, dev)
+    # e2e: the streams from pinned host memory through the public forward, outputs back to the host
+    h_in = [t.to(torch.bfloat16).pin_memory() for t in (act, cog, phys)]
+    h_out = [torch.empty(B, n, 1024, dtype=torch.bfloat16).pin_memory() for n in (16, 256, 16)]
+    pe_d = pe.to(dev)
+    e_ms = []
+    barrier(world)
+    for i in range(args.steps):
+        flush.fill_(i)
+        torch.cuda.synchronize()
+        s_, e_ = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s_.record()
+        outs = gpu(*h_in, pe_d)
+        for o, h in zip(outs, h_out):
+            h.copy_(o, non_blocking=True)
+        e_.record()
+        e_.synchronize()
+        e_ms.append(s_.elapsed_time(e_))
+    barrier(world)
+    e_total = max_over_ranks(sum(e_ms), world, dev)
+    flops = (2 * 288 * (1024 * 3072 + 1024 * 1024 + 1024 * 5632 + 2816 * 1024) + 4.0 * 288 * 288 * 1024) * B
+    _, tc_peak, peak_kind = measured_peaks()
+    step_s = total_ms / args.steps * 1e-3
+    if rank != 0:
+        return
+    line = {
+        "metric": "blocks_per_s", "value": world / step_s, "unit": "blocks/s (batch of %d sequences each)" % B,
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": total_ms / args.steps,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded N(0, 0.02) weights, N(0, 1) streams with the config-1 shapes)",
+        "config": {"workload": "BASELINE config 1 on the GPU: one 3-stream ExpandedDoubleStreamBlock",
+                   "model": "cognition 256 / action 16 / physics 16 tokens, hidden 1024, 16x64 heads, SwiGLU 2816",
+                   "global_batch": B * world, "seq_len": 288, "parallelism": f"replicas x{world}",
+                   "l2": "flushed between timed steps (256 MB write)"},
+        "e2e": {"value": world / (e_total / args.steps * 1e-3), "unit": "blocks/s",
+                "h2d_bytes_per_step": sum(t.numel() * 2 for t in h_in) * world,
+                "d2h_bytes_per_step": sum(t.numel() * 2 for t in h_out) * world},
+        "gpu_launches": gpu.launches * args.steps,
+        "roofline": {"bound": "tensor", "kernel": "whole block (batch 1 is launch-bound: 11 dependent launches)",
+                     "achieved": flops / step_s / 1e12, "peak": tc_peak, "unit": "TFLOP/s",
+                     "frac": flops / step_s / 1e12 / tc_peak, "peak_source": peak_kind, "traffic": None},
+        "clocks": clocks.summary(),
+    }
+    if world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline_c1(args.cpu_sample_s)
+    print(json.dumps(line), flush=True)
+
+
 def run_reference(args):
+    if args.workload == "c1":
+        cb = cpu_baseline_c1(args.cpu_sample_s, steps=max(args.steps, 3))
+        line = {"metric": "blocks_per_s", "value": cb["value"], "unit": "blocks/s (batch of 1 sequence each)",
+                "impl": "reference", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+                "ms_per_step": 1000.0 / cb["value"], "higher_is_better": True, "scaling": "weak",
+                "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+                "config": {"workload": "BASELINE config 1: one 3-stream joint block, fp32, CPU eager",
+                           "model": "cognition 256 / action 16 / physics 16 tokens, hidden 1024, 16x64 heads, "
+                                    "SwiGLU 2816", "global_batch": 1, "seq_len": 288, "parallelism": "cpu"},
+                "cpu_baseline": cb,
+                "e2e": {"value": cb["value"], "unit": "blocks/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+        print(json.dumps(line), flush=True)
+        return
     if args.workload == "c5":
         cb = cpu_baseline_c5(args.cpu_sample_s)
         line = {"metric": "observations_per_s", "value": cb["value"], "unit": "observations/s",
@@ -635,7 +764,7 @@ def main():
         return
     rank, world, local = dist_setup(args.gpus)
     try:
-        (run_c5 if args.workload == "c5" else run_b200)(args, rank, world, local)
+        {"c5": run_c5, "c1": run_c1}.get(args.workload, run_b200)(args, rank, world, local)
     finally:
         if world > 1:
             import torch.distributed as dist
