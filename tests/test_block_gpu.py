@@ -74,3 +74,29 @@ def test_c1_block_near_fp32_reference_and_graph_replay(cuda):
         # bf16 against the fp32 reference block: signatures agree to bf16 precision
         assert cos_sim(o[0].float().cpu() @ proj, fx["signature"][name]) >= 0.999, name
         assert cos_sim(o[0, 0].float().cpu(), fx["first_rows"][name]) >= 0.999, name
+
+
+def test_config2_blocks_per_layer_cosine_against_fp32(cuda):
+    """The north-star tolerance per layer: four ExpandedDoubleStreamBlocks at config-2 widths
+    ([VL 512 | SA 18 | P 32], 1536 wide, 24 x 64 heads, SwiGLU 4096); each layer's bf16 output,
+    from the bf16-rounded fp32 input of that layer, has cosine >= 0.9999 against the fp32
+    reference block, stream by stream."""
+    cfg = om.MsatHeadConfig()
+    g = torch.Generator().manual_seed(21)
+    sa = torch.randn(1, 18, cfg.dim, generator=g)
+    vl = torch.randn(1, 512, cfg.dim, generator=g)
+    p = torch.randn(1, 32, cfg.dim, generator=g)
+    pe = om.RoPEEmbedder1D(64, [64], 1e4, 1024)(torch.arange(562).view(1, 562, 1))
+    for layer in range(4):
+        blk = om.init_weights(om.ExpandedDoubleStreamBlock(cfg.dim, cfg.heads, 64, cfg.mlp_hidden,
+                                                           cfg.vl_mlp_hidden), seed=100 + layer)
+        with torch.no_grad():
+            ref = blk(sa, vl, p, pe)
+        out = B200ExpandedDoubleStreamBlock(blk, cuda)(sa.to(cuda, BF), vl.to(cuda, BF), p.to(cuda, BF),
+                                                        pe.to(cuda))
+        torch.cuda.synchronize()
+        for name, o, r in zip(("sa", "vl", "p"), out, ref):
+            c = cos_sim(o.float().cpu(), r)
+            assert c >= 0.9999, (layer, name, c)
+        sa, vl, p = ref
+    assert ops.device_error() == 0
