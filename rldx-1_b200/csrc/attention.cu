@@ -346,13 +346,22 @@ __global__ void __launch_bounds__(AttnShape<kHD, kG, kW>::kThreads, 1)
         tmem_wait_st();
       }
       const float m_use = (m_ref == -INFINITY) ? 0.0f : m_ref;
-      float ps4[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+      // exponent arguments two at a time (packed fma), the row sum in four chains (column c adds
+      // to chain c & 3, in column order) two chains per packed add
+      const float2 sc2 = make_float2(scale, scale), nm2 = make_float2(-m_use, -m_use);
 #pragma unroll
-      for (int c = 0; c < kCols; ++c) {
-        sv[c] = ex2_approx(fmaf(sv[c], scale, -m_use));
-        ps4[c & 3] += sv[c];
+      for (int c = 0; c < kCols; c += 2) {
+        const float2 t = fma_f32x2(make_float2(sv[c], sv[c + 1]), sc2, nm2);
+        sv[c] = ex2_approx(t.x);
+        sv[c + 1] = ex2_approx(t.y);
       }
-      l_run += (ps4[0] + ps4[1]) + (ps4[2] + ps4[3]);
+      float2 ps01 = make_float2(0.0f, 0.0f), ps23 = make_float2(0.0f, 0.0f);
+#pragma unroll
+      for (int c = 0; c < kCols; c += 4) {
+        ps01 = add_f32x2(ps01, make_float2(sv[c], sv[c + 1]));
+        ps23 = add_f32x2(ps23, make_float2(sv[c + 2], sv[c + 3]));
+      }
+      l_run += (ps01.x + ps01.y) + (ps23.x + ps23.y);
 
       // P_j -> shared memory (K-major, 128-byte swizzle: chunk c of row r at (c ^ (r & 7)) * 16)
       ok = mbar_wait(&p_empty(g)[sb], ph ^ 1u, kErrAttnTimeout + 3);
