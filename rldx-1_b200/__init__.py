@@ -6,6 +6,7 @@ VLM-backbone prefill and memory module that feed them in batched serving.
   rldx_b200.block.B200ExpandedDoubleStreamBlock one joint block (ExpandedDoubleStreamBlock)
   rldx_b200.llm.B200LLMChain                    drop-in for CustomLLMChain (Qwen3 decoder prefill)
   rldx_b200.llm.B200MemoryChain                 drop-in for CustomMemoryChain (TransformerMemory)
+  rldx_b200.llm.B200MemoryCache                 GraphSafeVLA's memory window + _process_memory
   rldx_b200.serve.apply_optimization            installs the native head behind model.get_action
   rldx_b200.torch_ops                           torch.ops.b200msat.* (the reference's ds::/ss:: ops)
   rldx_b200.ops                                 per-kernel wrappers (tests, op-level use)

@@ -244,3 +244,55 @@ class B200MemoryChain(nn.Module):
         elif M != self._tokens:
             raise ValueError(f"{M} tokens differ from the bound {self._tokens}")
         return self._chain(inputs_embeds)
+
+
+class B200MemoryCache(nn.Module):
+    """The recurrent memory of the VLA on the native memory chain: the counterpart of
+    GraphSafeVLA's memory state and _process_memory (rldx/inference/model/graph_safe_vla.py:38-68,
+    106-140):
+
+        mem = B200MemoryCache(gs_memory, memory_config, batch=B, device="cuda:0")
+        vl = mem(vl_embs)          # [B, n_q, d] backbone cognition tokens -> decoder VL tokens
+        mem.reset_memory()         # new episode: the cached sets go back to zeros
+
+    Each call shifts the cache of the last `memory_length` sets of `memory_n_cog_tokens` tokens
+    by one set, appends the current set (the last memory_n_cog_tokens of the n_cog_tokens
+    cognition tokens), runs TransformerMemory over the cache (B200MemoryChain) and returns the
+    cognition tokens followed by the memory output of the newest set (concat_memory), or the
+    passed-through tokens followed by it.  One cache per sequence of the batch (the reference
+    keeps one, batch 1); the cache lives on the device and is updated in place."""
+
+    def __init__(self, gs_memory, memory_config: dict, batch: int = 1, device=None, *, use_graph: bool = True):
+        super().__init__()
+        self.n_q = int(memory_config["n_cog_tokens"])
+        self.n_cog_mem = int(memory_config["memory_n_cog_tokens"])
+        self.n_cog_pass = self.n_q - self.n_cog_mem
+        self.memory_length = int(memory_config["memory_length"])
+        self.concat_memory = bool(memory_config["concat_memory"])
+        d = int(memory_config["hidden_size"])
+        self.chain = B200MemoryChain(gs_memory, device, use_graph=use_graph)
+        self.device = self.chain.device
+        K, n = self.memory_length, self.n_cog_mem
+        self._cached_cog = torch.zeros(batch, K * n, d, dtype=torch.bfloat16, device=self.device)
+        self._cache_tmp = torch.zeros_like(self._cached_cog)
+
+    def reset_memory(self) -> None:
+        self._cached_cog.zero_()
+
+    def forward(self, vl_embs: torch.Tensor) -> torch.Tensor:
+        if vl_embs.shape[0] != self._cached_cog.shape[0] or vl_embs.shape[-1] != self._cached_cog.shape[-1]:
+            raise ValueError(f"vl_embs {tuple(vl_embs.shape)} does not match the cache "
+                             f"[{self._cached_cog.shape[0]}, *, {self._cached_cog.shape[-1]}]")
+        cog_all = vl_embs[:, -self.n_q:, :]
+        cog_current = cog_all[:, self.n_cog_pass:, :]
+        n = self.n_cog_mem
+        self._cache_tmp[:, :-n, :].copy_(self._cached_cog[:, n:, :])
+        self._cache_tmp[:, -n:, :].copy_(cog_current)
+        self._cached_cog.copy_(self._cache_tmp)
+        memory_out = self.chain(self._cached_cog)
+        cog_augmented = memory_out[:, -n:, :]
+        if self.concat_memory:
+            return torch.cat([cog_all.to(cog_augmented.dtype), cog_augmented], dim=1)
+        if self.n_cog_pass > 0:
+            return torch.cat([cog_all[:, : self.n_cog_pass, :].to(cog_augmented.dtype), cog_augmented], dim=1)
+        return cog_augmented

@@ -12,6 +12,7 @@ pytestmark = pytest.mark.gpu
 
 import rldx_b200  # noqa: E402,F401
 from rldx_b200.llm import B200LLMChain  # noqa: E402
+from oracle import memory_oracle as om_  # noqa: E402
 from oracle import qwen3_oracle as oq  # noqa: E402
 
 GOLD = Path(__file__).resolve().parent / "golden"
@@ -144,3 +145,31 @@ def test_memory_config5_shapes_against_oracle(cuda):
     out = B200MemoryChain(mem, cuda)(x.to(cuda))
     torch.cuda.synchronize()
     check_close(out, ref, "config-5 memory")
+
+
+@pytest.mark.parametrize("concat", [True, False])
+def test_memory_cache_over_consecutive_calls(cuda, concat):
+    """B200MemoryCache against GraphSafeVLA's sliding-window memory (graph_safe_vla.py:106-140)
+    restated on the pinned oracle: three calls in a row (the cache fills set by set), two
+    sequences, 40 cognition tokens of which the last 32 enter a 3-set memory."""
+    from rldx_b200.llm import B200MemoryCache
+
+    cfg = om_.MemoryConfig(hidden=192, ffn=768, layers=2, heads=2, kv_heads=2, rms_eps=1e-5, block=32, sets=3)
+    mem = om_.init_weights(om_.TransformerMemory(cfg), seed=4).to(BF)
+    mcfg = {"n_cog_tokens": 40, "memory_n_cog_tokens": 32, "memory_length": 3, "concat_memory": concat,
+            "hidden_size": 192}
+    dev_cache = B200MemoryCache(mem, mcfg, batch=2, device=cuda)
+    cached = torch.zeros(2, 96, 192, dtype=BF)
+    g = torch.Generator().manual_seed(12)
+    for step in range(3):
+        vl = torch.randn(2, 50, 192, generator=g).to(BF)
+        cog_all = vl[:, -40:]
+        cached = torch.cat([cached[:, 32:], cog_all[:, 8:]], dim=1)
+        aug = mem(cached)[:, -32:]
+        ref = torch.cat([cog_all, aug], 1) if concat else torch.cat([cog_all[:, :8], aug], 1)
+        out = dev_cache(vl.to(cuda))
+        torch.cuda.synchronize()
+        assert out.shape == ref.shape
+        check_close(out, ref, f"step {step}")
+    dev_cache.reset_memory()
+    assert int(dev_cache._cached_cog.abs().sum().item()) == 0
