@@ -1,7 +1,7 @@
 """Generates the golden fixtures in this directory from the REFERENCE implementation.
 
-Runs only where the reference checkout is available (default /root/reference, or
-$RLDX_REFERENCE).  It imports the reference's own modules — MSAT / ExpandedDoubleStreamBlock
+Runs only where the reference checkout is available ($RLDX_REFERENCE, by default a
+`reference` directory beside this repository).  It imports the reference's own modules — MSAT / ExpandedDoubleStreamBlock
 (rldx/model/modules/action_model/{msat,blocks,ops}.py), the embodiment MLPs, the physics
 encoders and rldx/inference/action_model/model/graph_safe_action_model.py:GraphSafeActionModel
 (the reference's graph-safe denoise loop) — with three stand-ins that touch no arithmetic of
@@ -34,7 +34,7 @@ from torch import nn
 
 HERE = Path(__file__).resolve().parent
 REPO = HERE.parents[1]
-REF = Path(os.environ.get("RLDX_REFERENCE", "/root/reference"))
+REF = Path(os.environ.get("RLDX_REFERENCE", REPO.parent / "reference"))
 sys.path.insert(0, str(REPO))
 
 from oracle import msat_oracle as om  # noqa: E402

@@ -1,7 +1,7 @@
 """Generates the VLM-prefill golden fixtures (llm_*.pt) from the REFERENCE implementation.
 
-Runs only where the reference checkout is available (default /root/reference, or
-$RLDX_REFERENCE).  It imports the reference's vendored Qwen3-VL text model
+Runs only where the reference checkout is available ($RLDX_REFERENCE, by default a
+`reference` directory beside this repository).  It imports the reference's vendored Qwen3-VL text model
 (rldx/model/modules/backbone/modeling_qwen3_vl.py: Qwen3VLTextDecoderLayer, Qwen3VLTextRMSNorm,
 Qwen3VLTextRotaryEmbedding) under stub parent packages (so rldx/__init__.py's HF processor
 imports are skipped; transformers 5 lacks the "default" RoPE init the module looks up, so the
@@ -27,7 +27,7 @@ from torch import nn
 
 HERE = Path(__file__).resolve().parent
 REPO = HERE.parents[1]
-REF = Path(os.environ.get("RLDX_REFERENCE", "/root/reference"))
+REF = Path(os.environ.get("RLDX_REFERENCE", REPO.parent / "reference"))
 sys.path.insert(0, str(REPO))
 
 from oracle import qwen3_oracle as oq  # noqa: E402

@@ -1,7 +1,7 @@
 """Generates the memory-module golden fixtures (memory_*.pt) from the REFERENCE implementation.
 
-Runs only where the reference checkout is available (default /root/reference, or
-$RLDX_REFERENCE).  It imports the reference's own TransformerMemory
+Runs only where the reference checkout is available ($RLDX_REFERENCE, by default a
+`reference` directory beside this repository).  It imports the reference's own TransformerMemory
 (rldx/model/modules/memory.py) under stub parent packages, with a `diffusers` stand-in that
 only supplies the SinusoidalPositionalEmbedding name the module imports (unused with RoPE) and
 a stand-in for rldx.utils.dist.rank_zero_print (a print), initialises it with
@@ -25,7 +25,7 @@ from torch import nn
 
 HERE = Path(__file__).resolve().parent
 REPO = HERE.parents[1]
-REF = Path(os.environ.get("RLDX_REFERENCE", "/root/reference"))
+REF = Path(os.environ.get("RLDX_REFERENCE", REPO.parent / "reference"))
 sys.path.insert(0, str(REPO))
 
 from oracle import memory_oracle as mo  # noqa: E402
