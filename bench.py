@@ -11,8 +11,10 @@ init with the reference module layout (no checkpoint ships); inputs are seeded s
 with the config-2 shapes and distributions.
 
 Multi-GPU (torchrun, one process per GPU): every GPU serves its own observations with a full
-weight copy ("replicas", weak scaling); no collective runs on the step path — torch.distributed
-only supplies the barrier and the max-over-ranks of the timed region.
+weight copy ("replicas", weak scaling); no collective runs on the step path — a gloo process
+group (host-side, no NCCL communicator) only supplies the barrier and the max-over-ranks of the
+timed region.  Every config-2 line also carries `batched`: BASELINE config 5 (256 observations
+per step, strong-scaled over the N GPUs), the batched half of the headline metric.
 
 --workload production / production_addons measures the reference's released head without /
 with add-ons instead (4 double + 8 single blocks, VL width 4096; the shapes of the reference's
@@ -25,8 +27,10 @@ run_c5); --workload c1 measures one config-1 joint block on the GPU (see run_c1)
 Printed JSON (rank 0): value = control steps/s of the whole job with inputs resident in HBM;
 e2e = the same through the C ABI with pinned host buffers (host->device inputs and device->host
 actions inside the timed region); roofline of the dominant kernel (the grouped tcgen05 GEMM)
-from a per-launch event-timed pass; cpu_baseline = the CPU restatement of the reference path
-(oracle/, fp32, all host threads) on a bounded sample.
+and `rooflines` of every kernel kind (GEMM, attention, LayerNorm): each kind's share of an
+event-timed eager pass over the same launch list, scaled onto the graph-replayed ms_per_step,
+so the kinds add up to the timed step; cpu_baseline = the CPU restatement of the reference
+path (oracle/, fp32, all host threads) on a bounded sample.
 """
 
 from __future__ import annotations
@@ -62,6 +66,9 @@ def parse_args():
     p.add_argument("--cpu-sample-s", type=float, default=20.0, help="CPU baseline time budget")
     p.add_argument("--profile-step", action="store_true",
                    help="bracket one extra step with cudaProfilerStart/Stop (ncu --profile-from-start off)")
+    p.add_argument("--no-batched", action="store_true",
+                   help="config-2 line without the `batched` (config 5) object")
+    p.add_argument("--batched-steps", type=int, default=5, help="timed steps of the `batched` object")
     return p.parse_args()
 
 
@@ -75,8 +82,9 @@ def dist_setup(n):
         import torch.distributed as dist
 
         torch.cuda.set_device(local)
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
-                                device_id=torch.device("cuda", local))
+        # host-side group: the barrier and the max over ranks only (no NCCL communicator exists,
+        # the step path has no collective)
+        dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=300))
     if n != world and world > 1:
         raise SystemExit(f"--gpus {n} but WORLD_SIZE {world}")
     return rank, world, local
@@ -94,7 +102,7 @@ def max_over_ranks(x: float, world: int, device) -> float:
         return x
     import torch.distributed as dist
 
-    t = torch.tensor([x], dtype=torch.float64, device=device)
+    t = torch.tensor([x], dtype=torch.float64)
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
     return float(t.item())
 
@@ -473,6 +481,7 @@ def run_b200(args, rank, world, local):
 
     step()  # binds: weight arena, tables, graph capture
     torch.cuda.synchronize()
+    launches = chain.launches_per_step  # kernel nodes of the captured control step
     del head  # the runtime holds its own copy of every weight
     torch.cuda.empty_cache()
     flush = torch.empty(2 * L2_BYTES // 4, dtype=torch.int32, device=dev)
@@ -523,21 +532,46 @@ def run_b200(args, rank, world, local):
         torch.cuda.synchronize()
         torch.cuda.profiler.stop()
 
-    # ---- per-launch pass for the roofline of the dominant kernel ----
+    status = chain.device_status(wait=True)
+    if status:
+        raise RuntimeError(f"control step recorded device error 0x{status:x}")
+
+    # ---- per-kind rooflines: the kinds' shares of an event-timed eager pass over the same
+    #      launch list, scaled onto the graph-replayed step (so they add up to ms_per_step) ----
     prof = chain.profile(inp)
-    gem = [p for p in prof if p[0] == "gemm"]
-    g_ms = sum(p[2] for p in gem)
-    g_bytes = sum(p[3] for p in gem)
-    g_flops = sum(p[4] for p in gem)
     hbm_peak, tc_peak, peak_kind = measured_peaks()
-    achieved = (g_bytes / len(gem)) / (g_ms / len(gem) * 1e-3) / 1e9
-    tflops = g_flops / (g_ms * 1e-3) / 1e12
-    by_kind = {}
+    ms_step = total_ms / args.steps
+    eager_total = sum(p[2] for p in prof)
+    kinds = {}
     for p in prof:
-        d = by_kind.setdefault(p[0], [0, 0.0])
-        d[0] += 1
-        d[1] += p[2]
+        d = kinds.setdefault(p[0], {"launches": 0, "eager_ms": 0.0, "bytes": 0.0, "flops": 0.0})
+        d["launches"] += 1
+        d["eager_ms"] += p[2]
+        d["bytes"] += p[3]
+        d["flops"] += p[4]
+    rooflines = {}
+    for k, d in kinds.items():
+        share = d["eager_ms"] / eager_total
+        k_ms = share * ms_step  # this kind's time inside one graph-replayed step
+        r = {"launches": d["launches"], "share": share, "ms_in_step": k_ms,
+             "avg_launch_us": k_ms / d["launches"] * 1e3, "eager_ms": d["eager_ms"]}
+        if k in ("gemm", "layernorm", "copy"):
+            gbs = d["bytes"] / (k_ms * 1e-3) / 1e9
+            r.update({"bound": "hbm", "achieved": gbs, "peak": hbm_peak, "unit": "GB/s", "frac": gbs / hbm_peak,
+                      "bytes_per_step": d["bytes"]})
+        if k in ("gemm", "attention"):
+            tf = d["flops"] / (k_ms * 1e-3) / 1e12
+            key = "tensor_" if k == "gemm" else ""
+            r.update({key + "bound": "tensor", key + "achieved": tf, key + "peak": tc_peak,
+                      key + "unit": "TFLOP/s", key + "frac": tf / tc_peak, "flops_per_step": d["flops"]})
+        rooflines[k] = r
+    g = rooflines["gemm"]
     traffic = ncu_traffic()
+    batched = None
+    if not args.no_batched and args.workload == "c2":
+        del chain
+        torch.cuda.empty_cache()
+        batched = c5_measure(rank, world, local, args.observations, args.batched_steps, max(3, min(args.warmup, 3)))
 
     if rank != 0:
         return
@@ -549,7 +583,7 @@ def run_b200(args, rank, world, local):
         "n_gpus": world,
         "steps": args.steps,
         "warmup": args.warmup,
-        "ms_per_step": total_ms / args.steps,
+        "ms_per_step": ms_step,
         "p50_ms_per_control_step": p50,
         "higher_is_better": True,
         "scaling": "weak",
@@ -564,20 +598,24 @@ def run_b200(args, rank, world, local):
         "e2e": {"value": n_obs / (e_total * 1e-3), "unit": "control steps/s",
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                 "p50_ms": statistics.median(e_ms)},
-        "gpu_launches": chain.launches_per_step * args.steps,
+        "gpu_launches": launches * args.steps,
         "roofline": {"bound": "hbm", "kernel": "gemm_bf16_kernel (grouped tcgen05 GEMM, all launches of a step)",
-                     "achieved": achieved, "peak": hbm_peak, "unit": "GB/s", "frac": achieved / hbm_peak,
+                     "achieved": g["achieved"], "peak": hbm_peak, "unit": "GB/s", "frac": g["frac"],
                      "peak_source": peak_kind,
+                     "time_source": "share of an event-timed eager pass x graph-replayed ms_per_step",
                      # ncu DRAM bytes of a captured launch, scaled by its ratio to the algorithmic
                      # bytes onto the average launch of the step (one capture, not every launch)
-                     "traffic": (traffic["dram_bytes"] / traffic["algorithmic_bytes"] * g_bytes / len(gem))
-                                if traffic else None,
+                     "traffic": (traffic["dram_bytes"] / traffic["algorithmic_bytes"] * g["bytes_per_step"]
+                                 / g["launches"]) if traffic else None,
                      "traffic_source": traffic.get("capture") if traffic else None,
-                     "bytes_per_launch": g_bytes / len(gem), "avg_launch_us": g_ms / len(gem) * 1e3,
-                     "tensor_tflops": tflops, "tensor_frac": tflops / tc_peak},
-        "breakdown_ms": {k: {"launches": v[0], "ms": round(v[1], 4)} for k, v in by_kind.items()},
+                     "bytes_per_launch": g["bytes_per_step"] / g["launches"],
+                     "avg_launch_us": g["avg_launch_us"],
+                     "tensor_tflops": g["tensor_achieved"], "tensor_frac": g["tensor_frac"]},
+        "rooflines": rooflines,
     }
     line["clocks"] = clocks.summary()
+    if batched is not None:
+        line["batched"] = batched
     if world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(args.cpu_sample_s, workload=args.workload)
     print(json.dumps(line), flush=True)
@@ -586,8 +624,9 @@ def run_b200(args, rank, world, local):
 # ----------------------------------------------------------------------------------------------
 # batched serving step (VLM prefill -> cognition tokens -> memory -> MSAT)
 # ----------------------------------------------------------------------------------------------
-def run_c5(args, rank, world, local):
-    """One step serves `observations` independent observations sharded over the ranks:
+def c5_measure(rank, world, local, observations: int, steps: int, warmup: int) -> dict:
+    """BASELINE config 5 on this rank's GPU: one step serves `observations` independent
+    observations sharded over the ranks (observations / world here):
       1. 12 Qwen3 decoder layers (hidden 2048, GQA 16 / 2 x 128, SwiGLU 11008) over 848 tokens
          (4 frames x 196 patches + 64 text; the 28-layer model truncated at layer 12);
       2. the last 256 positions are the cognition tokens, projected 2048 -> 1536;
@@ -596,7 +635,8 @@ def run_c5(args, rank, world, local):
       4. the config-2 MSAT decoder (4 Euler steps) with VL = [cognition | memory output]
          (concat_memory, 256 + 256 = 512 tokens, rldx/model/core/rldx.py:1207-1250).
     Seeded random weights, resident inputs (token embeddings, ring, state, physics); every stage
-    is a native handle (B200LLMChain, B200MemoryChain, the GEMM, B200ExpandedActionHeadChain)."""
+    is a native handle (B200LLMChain, B200MemoryChain, the GEMM, B200ExpandedActionHeadChain).
+    Returns the whole-job figures (max over ranks) on every rank."""
     from types import SimpleNamespace as NS
 
     import rldx_b200  # noqa: F401
@@ -607,9 +647,9 @@ def run_c5(args, rank, world, local):
 
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
-    if args.observations % world:
-        raise SystemExit(f"--observations {args.observations} is not divisible by {world} GPUs")
-    B = args.observations // world
+    if observations % world:
+        raise SystemExit(f"--observations {observations} is not divisible by {world} GPUs")
+    B = observations // world
     bf = torch.bfloat16
     g = torch.Generator(device=dev).manual_seed(100 + rank)
 
@@ -680,15 +720,15 @@ def run_c5(args, rank, world, local):
     del head
     torch.cuda.empty_cache()
     flush = torch.empty(2 * L2_BYTES // 4, dtype=torch.int32, device=dev)
-    for _ in range(args.warmup):
+    for _ in range(warmup):
         step()
     torch.cuda.synchronize()
-    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
     barrier(world)
     torch.cuda.synchronize()
     with ClockSampler(local) as clocks:
-        for i in range(args.steps):
+        for i in range(steps):
             flush.fill_(i)
             starts[i].record()
             step()
@@ -704,7 +744,7 @@ def run_c5(args, rank, world, local):
     e_ms = []
     barrier(world)
     torch.cuda.synchronize()
-    for i in range(args.steps):
+    for i in range(steps):
         flush.fill_(i)
         torch.cuda.synchronize()
         s_, e_ = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -716,6 +756,9 @@ def run_c5(args, rank, world, local):
         e_ms.append(s_.elapsed_time(e_))
     barrier(world)
     e_total = max_over_ranks(sum(e_ms), world, dev)
+    status = max(vlm.device_status(), memory._chain.device_status(), msat.device_status())
+    if status:
+        raise RuntimeError(f"config-5 step recorded device error 0x{status:x}")
 
     vlm_flops = (2 * (D * (Hq + 2 * Hkv) * hd + Hq * hd * D + 3 * D * Fd) * NL * T + 2.0 * Hq * T * T * hd * NL) * B
     mem_flops = (2 * (4 * DM * DM + 3 * DM * FM) * 2 * SETS * NQ + 2.0 * HM * (SETS * NQ) ** 2 * hdm * 2) * B
@@ -723,33 +766,40 @@ def run_c5(args, rank, world, local):
     flops = vlm_flops + mem_flops + 2.0 * NQ * D * DM * B + msat_flops
     # a step of a second or more runs under the 1 kW power cap: the sustained GEMM peak applies
     tc_peak, peak_kind = sustained_tensor_peak()
-    step_s = total_ms / args.steps * 1e-3
-    if rank != 0:
-        return
-    line = {
-        "metric": "observations_per_s", "value": args.observations / step_s, "unit": "observations/s",
-        "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": total_ms / args.steps,
-        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
-        "data": "synthetic (seeded random weights and inputs with the config-5 shapes)",
+    step_s = total_ms / steps * 1e-3
+    launches = vlm.launches_per_call + memory._chain.launches_per_call + msat.launches_per_step + 1
+    return {
+        "metric": "observations_per_s", "value": observations / step_s, "unit": "observations/s",
+        "n_gpus": world, "steps": steps, "warmup": warmup, "ms_per_step": total_ms / steps,
+        "higher_is_better": True, "scaling": "strong",
         "config": {"workload": "BASELINE config 5: batched serving step, %d observations sharded over %d GPU(s)"
-                               % (args.observations, world),
+                               % (observations, world),
                    "model": "12 x Qwen3 decoder (2048, GQA 16/2x128, SwiGLU 11008) over 848 tokens -> 256 "
                             "cognition tokens -> 1536 -> TransformerMemory (2 layers, 8 x 256 tokens) -> "
                             "config-2 MSAT decoder (VL 256 + 256, 4 Euler steps)",
-                   "global_batch": args.observations, "seq_len": T,
+                   "global_batch": observations, "seq_len": T,
                    "parallelism": f"data parallel x{world} (observations sharded, no collective)",
                    "l2": "flushed between timed steps (256 MB write); working set > L2"},
-        "e2e": {"value": args.observations / (e_total / args.steps * 1e-3), "unit": "observations/s",
+        "e2e": {"value": observations / (e_total / steps * 1e-3), "unit": "observations/s",
                 "h2d_bytes_per_step": host_tokens.numel() * 2 * world,
                 "d2h_bytes_per_step": host_actions.numel() * 2 * world},
-        "gpu_launches": (vlm.launches_per_call + memory._chain.launches_per_call + msat.launches_per_step + 1)
-                        * args.steps,
+        "gpu_launches": launches * steps,
         "roofline": {"bound": "tensor", "kernel": "whole step (tcgen05 GEMMs dominate)",
                      "achieved": flops / step_s / 1e12, "peak": tc_peak, "unit": "TFLOP/s",
                      "frac": flops / step_s / 1e12 / tc_peak, "peak_source": peak_kind, "traffic": None,
                      "flops_per_step_per_gpu": flops},
         "clocks": clocks.summary(),
     }
+
+
+def run_c5(args, rank, world, local):
+    """BASELINE config 5 as the line's own workload (see c5_measure)."""
+    m = c5_measure(rank, world, local, args.observations, args.steps, args.warmup)
+    if rank != 0:
+        return
+    line = dict(m)
+    line.update({"vs_baseline": None, "dtype": "bf16",
+                 "data": "synthetic (seeded random weights and inputs with the config-5 shapes)"})
     if world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline_c5(args.cpu_sample_s)
     print(json.dumps(line), flush=True)

@@ -35,6 +35,18 @@ const char* rldx_last_error(void);
 /* Reads and clears the device-side error word (0 = none).  Synchronizes the device. */
 int rldx_get_device_error(unsigned int* code);
 
+/* Bound of every wait inside the kernels, in SM clock cycles (default 4e9, about 2 s at full
+ * clock), for the current device; [1e3, 1e11].  A wait that runs out records a device error
+ * and its kernel returns.  Set it between steps, not while kernels of the library run.
+ * No counterpart in the reference (its Triton kernels have no waits). */
+int rldx_set_wait_limit(int64_t cycles);
+int rldx_get_wait_limit(int64_t* cycles);
+
+/* Self-test of the bounded wait: one warp waits on a barrier that nothing arrives on, gives up
+ * after limit_cycles ([1e3, 4e9]) and records device error 0x400; the kernel then returns.
+ * Asynchronous on `stream`.  No counterpart in the reference. */
+int rldx_wait_selftest(int64_t limit_cycles, void* stream);
+
 /* 1 if the current device is an sm_100 part the kernels were built for, else 0. */
 int rldx_device_supported(void);
 
@@ -122,9 +134,12 @@ int rldx_gemm_ws(const rldx_gemm_desc* problems, int nproblems, void* workspace,
  * an 8 MiB static device array of the library.  For callers that cannot allocate device
  * memory when they run a GEMM (allocator-free serving paths, C-ABI hosts without a CUDA
  * allocator).  No counterpart in the reference.  Allocates nothing.  The first call on a
- * device sets the scratch up (address lookup and a synchronous zero-fill): make it before any
- * stream capture.  Plans needing more than 8 MiB of workspace fail with RLDX_ERR_UNSUPPORTED.
- * One scratch per device: calls that overlap on the GPU race, so order them on one stream. */
+ * device looks the scratch's device address up (cudaGetSymbolAddress, kept for the process;
+ * not valid across a cudaDeviceReset): make it before any stream capture.  Every call clears
+ * the arrival counters first (a cudaMemsetAsync of a few KB on `stream`).  Plans needing more
+ * than 8 MiB of workspace fail with RLDX_ERR_UNSUPPORTED (rldx_gemm_ws with too small a
+ * workspace runs them unsplit instead).  One scratch per device: calls that overlap on the
+ * GPU race, so order them on one stream. */
 int rldx_gemm_static_ws(const rldx_gemm_desc* problems, int nproblems, void* stream);
 
 /* ------------------------------------------------------------------------------------------
@@ -410,14 +425,34 @@ int rldx_msat_destroy(rldx_msat* h);
 int rldx_msat_step(rldx_msat* h, const rldx_msat_io* io, void* stream);
 
 /* One control step with io in host memory (pinned for full speed): host->device copies, the
- * step, device->host copy of the actions, stream synchronize. */
+ * step, device->host copy of the actions, stream synchronize.  Returns RLDX_ERR_DEVICE when a
+ * device error code was recorded: raised by a kernel of this step, or left by earlier work
+ * (the step's first launch takes and clears such a code, so the step itself runs clean; the
+ * message says which).  Replaces the reference's fall-back-on-failure
+ * (rldx/inference/serve_optimization.py:432-516) with an error on the step that failed. */
 int rldx_msat_step_host(rldx_msat* h, const rldx_msat_io* io, void* stream);
+
+/* Device status of the handle's last step (rldx_msat_step is asynchronous): *code = 0 when no
+ * device error was recorded, else the code (see rldx_msat_step_host).  wait = 1 waits for the
+ * step to finish; wait = 0 reports 0 while it is still running.  Reading clears the status. */
+int rldx_msat_status(rldx_msat* h, int wait, unsigned int* code);
+
+/* Launches from the start of a control step up to and including the last one of block `block`
+ * (double blocks first, then single blocks; -1: the launches before the first block, i.e. the
+ * encoders) of Euler step `step`: with rldx_msat_run_partial
+ * and rldx_msat_read_buffer this exposes the residual streams after every block (per-layer
+ * parity against the reference's blocks).  No counterpart in the reference. */
+int rldx_msat_block_end(const rldx_msat* h, int step, int block, int* n_ops);
+
+/* Runs the first n_ops launches of a control step eagerly (no graph) on `stream` after the
+ * input copies; io holds device pointers.  Asynchronous.  No counterpart in the reference. */
+int rldx_msat_run_partial(rldx_msat* h, const rldx_msat_io* io, int n_ops, void* stream);
 
 /* Number of kernel launches one control step performs (graph nodes when captured). */
 int rldx_msat_launch_count(const rldx_msat* h);
 
 typedef struct {
-  int kind;     /* 0 GEMM, 1 joint attention, 2 layernorm, 3 row copy                       */
+  int kind;     /* 0 GEMM, 1 joint attention, 2 layernorm, 3 row copy, 4 status word         */
   int grid;     /* CTAs launched                                                            */
   float ms;     /* device time between CUDA events recorded around the launch               */
   double bytes; /* algorithmic HBM bytes: every operand read once, every result written once */
@@ -504,6 +539,9 @@ int rldx_llm_destroy(rldx_llm* h);
 int rldx_llm_prefill(rldx_llm* h, const void* hidden_in, void* hidden_out, void* stream);
 /* kernel launches of one prefill (graph nodes when captured) */
 int rldx_llm_launch_count(const rldx_llm* h);
+
+/* Device status of the handle's last rldx_llm_prefill, as rldx_msat_status. */
+int rldx_llm_status(rldx_llm* h, int wait, unsigned int* code);
 /* Deepstack features of the next prefills: [deepstack_layers, batch, deepstack_rows, hidden]
  * bf16 (device or host pointer), copied into the handle's buffer asynchronously on stream
  * (the reference chain copies them into its _deepstack_add buffer per call,

@@ -194,6 +194,13 @@ SIGNATURES = {
                                     C.POINTER(C.c_int), vp]),
     "rldx_msat_read_buffer": (C.c_int, [vp, C.c_int, vp, i64, C.POINTER(i64), C.POINTER(i64),
                                         vp]),
+    "rldx_msat_status": (C.c_int, [vp, C.c_int, C.POINTER(C.c_uint)]),
+    "rldx_msat_block_end": (C.c_int, [vp, C.c_int, C.c_int, C.POINTER(C.c_int)]),
+    "rldx_msat_run_partial": (C.c_int, [vp, C.POINTER(MsatIO), C.c_int, vp]),
+    "rldx_llm_status": (C.c_int, [vp, C.c_int, C.POINTER(C.c_uint)]),
+    "rldx_set_wait_limit": (C.c_int, [i64]),
+    "rldx_get_wait_limit": (C.c_int, [C.POINTER(i64)]),
+    "rldx_wait_selftest": (C.c_int, [i64, vp]),
 }
 
 _LIB = None

@@ -292,8 +292,41 @@ class _B200HeadChain(nn.Module):
         io = MsatIO(vl.data_ptr(), st.data_ptr(), ids.data_ptr(), noise.data_ptr(), ph_ptr,
                     pn_ptr, out.data_ptr(), pre_ptr)
         stream = torch.cuda.current_stream(dev)
+        # a device error recorded by an earlier (asynchronous) step surfaces here, before more
+        # work is queued behind it
+        self._raise_on_device_error(wait=False)
         check(_lib.load().rldx_msat_step(self._handle, C.byref(io), C.c_void_p(stream.cuda_stream)))
         return out
+
+    def _raise_on_device_error(self, wait: bool) -> None:
+        code = self.device_status(wait)
+        if code:
+            raise _lib.RldxError(_lib.RLDX_ERR_DEVICE, f"device error 0x{code:x} recorded by a control step")
+
+    def device_status(self, wait: bool = True) -> int:
+        """Device error code of the last control step (0: none; with wait=False, 0 while it is
+        still running).  Reading clears it."""
+        if self._handle is None:
+            return 0
+        code = C.c_uint(0)
+        check(_lib.load().rldx_msat_status(self._handle, 1 if wait else 0, C.byref(code)))
+        return int(code.value)
+
+    def block_end(self, step: int, block: int) -> int:
+        """Launches from the start of a control step through the last one of `block` (double
+        blocks, then single blocks) of Euler step `step`."""
+        n = C.c_int(0)
+        check(_lib.load().rldx_msat_block_end(self._handle, step, block, C.byref(n)))
+        return int(n.value)
+
+    def run_partial(self, inp: dict, n_ops: int) -> None:
+        """Runs the first n_ops launches of a control step on device inputs (read_buffer then
+        shows the residual streams at that point)."""
+        out = torch.empty(inp["init_noise"].shape, dtype=torch.bfloat16, device=self.device)
+        io = self._io(inp, out)
+        stream = torch.cuda.current_stream(self.device)
+        check(_lib.load().rldx_msat_run_partial(self._handle, C.byref(io), n_ops,
+                                                C.c_void_p(stream.cuda_stream)))
 
     def _io(self, inp: dict, out: torch.Tensor) -> MsatIO:
         ph = inp["physics_hist"].data_ptr() if self._physics else None
@@ -324,7 +357,7 @@ class _B200HeadChain(nn.Module):
         stream = torch.cuda.current_stream(self.device)
         check(lib.rldx_msat_profile(self._handle, C.byref(io), arr, n, C.byref(got),
                                     C.c_void_p(stream.cuda_stream)))
-        kinds = ("gemm", "attention", "layernorm", "copy")
+        kinds = ("gemm", "attention", "layernorm", "copy", "status")
         return [(kinds[a.kind], a.grid, a.ms, a.bytes, a.flops) for a in arr[:got.value]]
 
     def read_buffer(self, which: int) -> torch.Tensor:

@@ -55,7 +55,7 @@ struct AttnShape {
   static constexpr int kCols = 64 / kW;  // keys of a tile per softmax thread
   static constexpr uint32_t kOCol = 128 * kG;
   static constexpr uint32_t kTmemCols = (kG == 1) ? 256 : 512;
-  static constexpr int kBars = 1 + 2 * kKStages + 2 * kVStages + 13 * kG;
+  static constexpr int kBars = 1 + 2 * kKStages + 2 * kVStages + 13 * kG + 1;  // + drain
   static constexpr int kXchFloats = kG * (2 + 1) * kW * 128;  // per-tile maxima (2 buffers), sums
   static constexpr size_t kSmem = 1024 + static_cast<size_t>(kG) * kQBytes +
                                   static_cast<size_t>(kKStages) * kKTileBytes +
@@ -99,7 +99,8 @@ __global__ void __launch_bounds__(AttnShape<kHD, kG, kW>::kThreads, 1)
   auto o_final = [&](int g) { return gbar + 13 * g + 9; };
   auto xch = [&](int g) { return gbar + 13 * g + 10; };
   auto l_xch = [&](int g) { return gbar + 13 * g + 12; };
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(gbar + 13 * kG);
+  uint64_t* drain = gbar + 13 * kG;  // failure path: the issued MMAs have landed
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   // exchange floats: group g, buffer sb, warpgroup w, row r at xf[((g * 3 + sb) * kW + w) * 128 + r]
   // (sb = 2: the final row sums)
   float* xf = reinterpret_cast<float*>(tmem_slot + 4);
@@ -142,6 +143,7 @@ __global__ void __launch_bounds__(AttnShape<kHD, kG, kW>::kThreads, 1)
       mbar_init(o_final(g), 1);
       mbar_init(l_xch(g), 4 * kW);
     }
+    mbar_init(drain, 1);
     fence_mbar_init();
   }
   if (warp == 0 && lane == 0) {
@@ -167,10 +169,14 @@ __global__ void __launch_bounds__(AttnShape<kHD, kG, kW>::kThreads, 1)
         for (int c = 0; c < Sh::kChunks; ++c)
           tma_load_3d(sQ + g * kQBytes + c * Sh::kQChunk, &P.tq, q_full, c * 64, q0 + 128 * g, bh, pol);
       // K(i) and V(i - 1) per step: K leads by one tile (S_{j+1} is issued before PV_j)
-      for (int i = 0; i <= nkv; ++i) {
+      bool ok = true;
+      for (int i = 0; ok && i <= nkv; ++i) {
         if (i < nkv) {
           const int s = i % kKS;
-          if (!mbar_wait(&k_empty[s], (static_cast<uint32_t>(i / kKS) & 1u) ^ 1u, kErrAttnTimeout + 1)) break;
+          if (!mbar_wait(&k_empty[s], (static_cast<uint32_t>(i / kKS) & 1u) ^ 1u, kErrAttnTimeout + 1)) {
+            ok = false;
+            break;
+          }
           mbar_arrive_expect_tx(&k_full[s], kKTileBytes);
 #pragma unroll
           for (int c = 0; c < Sh::kChunks; ++c)
@@ -179,11 +185,15 @@ __global__ void __launch_bounds__(AttnShape<kHD, kG, kW>::kThreads, 1)
         if (i >= 1) {
           const int j = i - 1;
           const int s = j % kVS;
-          if (!mbar_wait(&v_empty[s], (static_cast<uint32_t>(j / kVS) & 1u) ^ 1u, kErrAttnTimeout + 1)) break;
+          if (!mbar_wait(&v_empty[s], (static_cast<uint32_t>(j / kVS) & 1u) ^ 1u, kErrAttnTimeout + 1)) {
+            ok = false;
+            break;
+          }
           mbar_arrive_expect_tx(&v_full[s], kVTileBytes);
           tma_load_3d(sV + s * kVTileBytes, &P.tv, &v_full[s], j * 64, 0, bh_kv, pol);
         }
       }
+      if (!ok) settle_issued_copies();  // loads already issued land before the CTA exits
     }
   } else if (warp == 1) {
     // ---------------- MMA issuer ----------------
@@ -219,7 +229,10 @@ __global__ void __launch_bounds__(AttnShape<kHD, kG, kW>::kThreads, 1)
         }
         const int pb = j & 1;
         const int s = j % kVS;
-        if (!mbar_wait(&v_full[s], static_cast<uint32_t>(j / kVS) & 1u, kErrAttnTimeout + 2)) break;
+        if (!mbar_wait(&v_full[s], static_cast<uint32_t>(j / kVS) & 1u, kErrAttnTimeout + 2)) {
+          ok = false;
+          break;
+        }
         const uint32_t v_addr = smem_u32(sV + s * kVTileBytes);
         for (int g = 0; ok && g < ng; ++g) {
           if (!mbar_wait(&p_full(g)[pb], static_cast<uint32_t>(j >> 1) & 1u, kErrAttnTimeout + 2)) {
@@ -237,6 +250,10 @@ __global__ void __launch_bounds__(AttnShape<kHD, kG, kW>::kThreads, 1)
           if (j == nkv - 1) umma_commit(o_final(g));
         }
         if (ok) umma_commit(&v_empty[s]);
+      }
+      if (!ok) {  // the MMAs already issued finish before TMEM is released
+        umma_commit(drain);
+        mbar_wait_teardown(drain, 0u);
       }
     }
   } else {

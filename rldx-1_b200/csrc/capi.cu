@@ -629,9 +629,11 @@ bool build_gemm_params(const rldx_gemm_desc* d, int n, void* ws, size_t ws_bytes
         cnt += p.tiles_m * p.tiles_n;
       }
     }
-    need = any ? kCounterBytes + off_f * 4 : 0;
+    // the arrival counters of every split tile must fit the counter block ahead of the partials
+    const bool counters_fit = static_cast<size_t>(cnt) * sizeof(unsigned int) <= kCounterBytes;
+    need = (any && counters_fit) ? kCounterBytes + off_f * 4 : 0;
     if (ws_needed) *ws_needed = std::max(*ws_needed, need);
-    if (!any || (ws != nullptr && need <= ws_bytes)) break;
+    if (!any || (counters_fit && ws != nullptr && need <= ws_bytes)) break;
     for (int i = 0; i < n; ++i) best_split[i] = 1;  // no (or too small a) workspace
   }
   params->pair = pair ? 1 : 0;

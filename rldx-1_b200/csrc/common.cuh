@@ -3,8 +3,9 @@
 //
 // Every wait on an mbarrier is bounded by a limit on the SM cycle counter.  A wait
 // that runs out records an error code in `g_rldx_err` (first error wins) and returns false;
-// callers then skip the rest of their work, release TMEM and return, so a lost arrival never
-// hangs the GPU.  The host reads and clears the code through rldx_get_device_error().
+// callers then skip the rest of their work, let the copies and tensor-core work they issued
+// land (bounded too), release TMEM and return, so a lost arrival never hangs the GPU.  The
+// host reads and clears the code through rldx_get_device_error() or a runtime's step status.
 #pragma once
 #include <cuda.h>
 #include <cuda_bf16.h>
@@ -22,11 +23,14 @@ enum DeviceError : unsigned int {
   kErrGemmTimeout = 0x100,   // + role (1 producer, 2 mma, 3 epilogue)
   kErrAttnTimeout = 0x200,   // + role
   kErrTeardownTimeout = 0x300,
+  kErrSelftestTimeout = 0x400,  // rldx_wait_selftest: a wait on a barrier nothing arrives on
 };
 
-// Bound of one mbarrier wait in SM clock cycles (about 2 s at the B200's 1.9 GHz, 4 s at a
-// throttled 1 GHz).  Healthy waits last microseconds.
+// Default bound of one mbarrier wait in SM clock cycles (about 2 s at the B200's 1.9 GHz, 4 s
+// at a throttled 1 GHz).  Healthy waits last microseconds.  The bound in force is the device
+// variable below, which rldx_set_wait_limit() changes at run time.
 constexpr long long kWaitLimitCycles = 4000000000ll;
+__device__ long long g_rldx_wait_limit = kWaitLimitCycles;
 
 __device__ __forceinline__ void record_error(unsigned int code) {
   atomicCAS(&g_rldx_err, 0u, code);
@@ -74,25 +78,60 @@ __device__ __forceinline__ bool error_raised() {
   return *reinterpret_cast<volatile unsigned int*>(&g_rldx_err) != 0u;
 }
 
+__device__ __forceinline__ long long wait_limit_cycles() {
+  return *reinterpret_cast<volatile long long*>(&g_rldx_wait_limit);
+}
+
 // Bounded wait for the phase of `bar` with the given parity to complete.  The hot loop only
 // polls the barrier: reading %globaltimer or global memory on every poll delays the wake-up
 // after the phase completes by up to a microsecond, which serialises every producer/consumer
 // hand-off.  Every 256 polls it reads the SM cycle counter (the bound) and the shared error
-// word, so that sibling roles give up quickly once one of them has.
+// word, so that sibling roles give up quickly once one of them has.  limit_cycles <= 0 takes
+// the library's bound (g_rldx_wait_limit), read once when the first poll fails.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, unsigned int err_code,
-                                          long long limit_cycles = kWaitLimitCycles) {
+                                          long long limit_cycles = 0) {
   if (mbar_try_wait(bar, parity)) return true;
+  const long long limit = limit_cycles > 0 ? limit_cycles : wait_limit_cycles();
   const long long t0 = clock64();
   for (uint32_t n = 1;; ++n) {
     if (mbar_try_wait(bar, parity)) return true;
     if ((n & 255u) == 0u) {
       if (error_raised()) return false;  // a sibling role already gave up: do not wait it out
-      if (clock64() - t0 > limit_cycles) {
+      if (clock64() - t0 > limit) {
         record_error(err_code);
         return false;
       }
     }
   }
+}
+
+// Teardown wait after a failure: like mbar_wait but it does not give up because an error is
+// already recorded (that is why it runs), only when the bound runs out.
+__device__ __forceinline__ bool mbar_wait_teardown(uint64_t* bar, uint32_t parity) {
+  const long long limit = wait_limit_cycles();
+  const long long t0 = clock64();
+  for (uint32_t n = 1;; ++n) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((n & 255u) == 0u && clock64() - t0 > limit) {
+      record_error(kErrTeardownTimeout);
+      return false;
+    }
+  }
+}
+
+__device__ __forceinline__ unsigned long long globaltimer_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+// After a producer gave up, the TMA loads it already issued still land in this CTA's shared
+// memory (their completions are counted on ring barriers that nobody will wait for).  Before
+// the CTA may exit they must be done: a fixed grace period, far above the microseconds a load
+// takes even from a busy HBM, bounds that without another barrier per load.
+__device__ __forceinline__ void settle_issued_copies() {
+  const unsigned long long t0 = globaltimer_ns();
+  while (globaltimer_ns() - t0 < 200000ull) __nanosleep(1000);
 }
 
 // ---------------------------------------------------------------------------------------------

@@ -474,7 +474,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_bf16_kernel(const __grid
   uint64_t* empty = full + kMaxStages;
   uint64_t* acc_full = empty + kMaxStages;
   uint64_t* acc_empty = acc_full + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
+  uint64_t* drain = acc_empty + 2;  // failure path: the issued MMAs have landed
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   uint32_t* bcast = tmem_slot + 1;
 
   const int warp = threadIdx.x >> 5;
@@ -491,6 +492,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_bf16_kernel(const __grid
       mbar_init(&acc_full[i], 1);
       mbar_init(&acc_empty[i], kEpiWarps);  // one arrival per epilogue warp
     }
+    mbar_init(drain, 1);
     fence_mbar_init();
   }
   if (warp == 0 && lane == 0) {
@@ -557,6 +559,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_bf16_kernel(const __grid
           }
         }
       }
+      if (!ok) settle_issued_copies();  // loads already issued land before the CTA exits
     }
   } else if (warp == 1) {
     // ---------------- MMA issuer ----------------
@@ -567,8 +570,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_bf16_kernel(const __grid
         const UnitInfo u = decode_unit(P, unit_id(P, first, j));
         const GemmProblem& pr = P.p[u.pi];
         const int ab = j & 1;
-        if (!mbar_wait(&acc_empty[ab], (static_cast<uint32_t>(j >> 1) & 1u) ^ 1u, kErrGemmTimeout + 2))
+        if (!mbar_wait(&acc_empty[ab], (static_cast<uint32_t>(j >> 1) & 1u) ^ 1u, kErrGemmTimeout + 2)) {
+          ok = false;
           break;
+        }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(ab * kAccCols);
         const uint32_t idesc = umma_idesc_bf16(128, pr.bn);
@@ -597,6 +602,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_bf16_kernel(const __grid
         }
         if (!ok) break;
         umma_commit(&acc_full[ab]);
+      }
+      if (!ok) {  // the MMAs already issued finish before TMEM is released
+        umma_commit(drain);
+        mbar_wait_teardown(drain, 0u);
       }
     }
   } else {
@@ -711,7 +720,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_pair_kernel(const __grid
   uint64_t* empty = full + kMaxStages;
   uint64_t* acc_full = empty + kMaxStages;
   uint64_t* acc_empty = acc_full + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
+  uint64_t* drain = acc_empty + 2;  // failure path (rank 0): the issued pair MMAs have landed
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -729,6 +739,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_pair_kernel(const __grid
       mbar_init(&acc_full[i], 1);
       mbar_init(&acc_empty[i], 2 * kEpiWarps);
     }
+    mbar_init(drain, 1);
     fence_mbar_init();
   }
   if (warp == 0 && lane == 0) {
@@ -789,6 +800,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_pair_kernel(const __grid
       // release of every slot still in flight so that none lands after the CTA has exited.
       for (int t = (it > S ? it - S : 0); ok && t < it; ++t)
         ok = mbar_wait(&empty[t % S], static_cast<uint32_t>(t / S) & 1u, kErrGemmTimeout + 1);
+      if (!ok) settle_issued_copies();  // loads already issued land before the CTA exits
     }
   } else if (warp == 1) {
     // ---------------- MMA issuer: one thread of rank 0 drives both CTAs' tensor cores ----------
@@ -799,8 +811,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_pair_kernel(const __grid
         const UnitInfo u = decode_unit(P, pair_unit_id(P, pair, first, j));
         const GemmProblem& pr = P.p[u.pi];
         const int ab = j & 1;
-        if (!mbar_wait(&acc_empty[ab], (static_cast<uint32_t>(j >> 1) & 1u) ^ 1u, kErrGemmTimeout + 2))
+        if (!mbar_wait(&acc_empty[ab], (static_cast<uint32_t>(j >> 1) & 1u) ^ 1u, kErrGemmTimeout + 2)) {
+          ok = false;
           break;
+        }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(ab * kAccCols);
         const uint32_t idesc = umma_idesc_bf16(256, pr.bn);
@@ -833,6 +847,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_pair_kernel(const __grid
         const uint32_t f = smem_u32(&acc_full[ab]);
         umma_commit_pair(mapa_shared(f, 0u));
         umma_commit_pair(mapa_shared(f, 1u));
+      }
+      if (!ok) {  // the pair MMAs already issued finish before either CTA releases TMEM
+        umma_commit_pair(mapa_shared(smem_u32(drain), 0u));
+        mbar_wait_teardown(drain, 0u);
       }
     }
   } else {

@@ -34,4 +34,21 @@ bool build_gemm_params(const rldx_gemm_desc* d, int n, void* ws, size_t ws_bytes
 
 int sm_count();
 
+// Device status of one runtime handle (status.cu): two mapped pinned host words written by
+// the one-thread kernels that open and close its launch list (slot 0: an error code left by
+// earlier work, slot 1: a code raised during the step) and the completion event of its last
+// step.
+struct StepStatus {
+  unsigned int* host = nullptr;
+  unsigned int* dev = nullptr;
+  cudaEvent_t done = nullptr;
+  bool init();
+  void release();
+  // *code = the recorded code (0: none; nothing is known yet when !wait and the last step is
+  // still running), *which = 1 when it was raised during the step.  Clears both slots.
+  int read(bool wait, unsigned int* code, unsigned int* which);
+};
+// *slot = g_rldx_err, g_rldx_err = 0 (one thread)
+cudaError_t launch_status_take(unsigned int* slot_dev, cudaStream_t stream);
+
 }  // namespace rldx

@@ -43,6 +43,7 @@ struct rldx_llm {
   int* ds_index = nullptr;  // [ds_rows] token rows
   bf16* ds_feat = nullptr;  // [ds_layers][B][ds_rows][D]
   std::vector<std::function<cudaError_t(cudaStream_t, bool)>> ops;
+  StepStatus status;  // device error codes of the last call (status.cu)
   void* ws = nullptr;
   size_t ws_bytes = 0, ws_need = 0;
   bool sizing = false;
@@ -193,6 +194,7 @@ struct rldx_llm {
     a = alloc<bf16>(static_cast<size_t>(M) * qd);
     g = alloc<bf16>(static_cast<size_t>(M) * Fp);
 
+    if (!status.init()) throw Fail(RLDX_ERR_CUDA, "step status: mapped host memory");
     if (split_k_enabled()) {  // first pass: the workspace the K-split plans want
       sizing = true;
       plan();
@@ -205,10 +207,11 @@ struct rldx_llm {
     }
     plan();
     run_ops(stream);  // warm-up (loads every kernel)
+    ck(cudaEventRecord(status.done, stream), "status event");
     ck(cudaStreamSynchronize(stream), "warm-up");
-    unsigned int derr = 0;
-    ck(cudaMemcpyFromSymbol(&derr, g_rldx_err, 4), "device error");
-    if (derr) throw Fail(RLDX_ERR_DEVICE, "device error during warm-up: " + std::to_string(derr));
+    unsigned int derr = 0, during = 0;
+    if (status.read(true, &derr, &during) != RLDX_OK) throw Fail(RLDX_ERR_CUDA, "warm-up status");
+    if (derr && during) throw Fail(RLDX_ERR_DEVICE, "device error during warm-up: " + std::to_string(derr));
     if (c.use_graph) {
       ck(cudaStreamBeginCapture(stream, cudaStreamCaptureModeThreadLocal), "begin capture");
       try {
@@ -226,8 +229,14 @@ struct rldx_llm {
     }
   }
 
+  void push_status(int which) {
+    unsigned int* slot = status.dev + which;
+    ops.push_back([slot](cudaStream_t st, bool) { return launch_status_take(slot, st); });
+  }
+
   void plan() {
     const int qd = Hq * hd;
+    push_status(0);  // a code left by earlier work -> slot 0; the call starts from a clean word
     for (int li = 0; li < c.layers; ++li) {
       const LayerW& l = lw[li];
       push_rmsnorm(h, l.in_norm, n);
@@ -315,6 +324,7 @@ struct rldx_llm {
       push_rmsnorm(h, final_norm, n);
       out = n;
     }
+    push_status(1);  // a code raised during the call -> slot 1
   }
 
   void run_ops(cudaStream_t st) {
@@ -328,6 +338,7 @@ void free_llm(rldx_llm* h) {
   if (h->graph) cudaGraphDestroy(h->graph);
   for (void* p : h->allocs) cudaFree(p);
   if (h->stream) cudaStreamDestroy(h->stream);
+  h->status.release();
   h->allocs.clear();
 }
 }  // namespace
@@ -369,7 +380,14 @@ int rldx_llm_prefill(rldx_llm* h, const void* hidden_in, void* hidden_out, void*
     else
       h->run_ops(st);
     ck(cudaMemcpyAsync(hidden_out, h->out, bytes, cudaMemcpyDefault, st), "hidden out");
+    ck(cudaEventRecord(h->status.done, st), "status event");
   });
+}
+
+int rldx_llm_status(rldx_llm* h, int wait, unsigned int* code) {
+  if (!h || !code) return set_error(RLDX_ERR_ARG, "llm_status: null argument");
+  unsigned int during = 0;
+  return h->status.read(wait != 0, code, &during);
 }
 
 int rldx_llm_launch_count(const rldx_llm* h) { return h ? static_cast<int>(h->ops.size()) : 0; }

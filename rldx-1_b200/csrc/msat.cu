@@ -36,13 +36,14 @@ namespace {
 using bf16 = __nv_bfloat16;
 
 struct Op {
-  enum Kind { kGemm, kAttn, kLn, kCopy } kind;
+  enum Kind { kGemm, kAttn, kLn, kCopy, kStatus } kind;
   int grid;
   double bytes, flops;  // algorithmic traffic / work of the launch
   GemmParams g;
   AttnParams a;
   LnParams l;
   CopyParams c;
+  unsigned int* slot;  // kStatus: device address of the status word this launch fills
 };
 
 uint16_t f2bf_bits(float f) {
@@ -155,6 +156,11 @@ struct rldx_msat {
   std::vector<bf16*> act_cat, phf_cat;
 
   std::vector<Op> ops;
+  // block_marks[step * nblocks + i]: launches from the start of the list up to and including
+  // the last one of block i (double blocks, then single blocks) of Euler step `step`
+  std::vector<int> block_marks;
+  std::vector<int> step_marks;  // launches before the first block of each Euler step
+  StepStatus status;
   // K-split workspace shared by every GEMM launch of the step (launches are stream-ordered):
   // tile arrival counters (zero between launches) followed by fp32 partial tiles.
   void* gemm_ws = nullptr;
@@ -429,11 +435,22 @@ struct rldx_msat {
     ops.push_back(o);
   }
 
-  void run_ops(cudaStream_t st, cudaEvent_t* ev = nullptr) {
+  void push_status(int which) {
+    Op o;
+    std::memset(&o, 0, sizeof(o));
+    o.kind = Op::kStatus;
+    o.grid = 1;
+    o.slot = status.dev + which;
+    ops.push_back(o);
+  }
+
+  // Launches ops [0, n) (all of them when n < 0).
+  void run_ops(cudaStream_t st, cudaEvent_t* ev = nullptr, int n = -1) {
     if (ev) ck(cudaEventRecord(ev[0], st), "event");
-    for (size_t i = 0; i < ops.size(); ++i) {
+    const size_t end = n < 0 ? ops.size() : std::min(ops.size(), static_cast<size_t>(n));
+    for (size_t i = 0; i < end; ++i) {
       const Op& o = ops[i];
-      const bool p = pdl && i > 0 && !ev;
+      const bool p = pdl && i > 0 && !ev && ops[i - 1].kind != Op::kStatus;
       cudaError_t e = cudaSuccess;
       switch (o.kind) {
         case Op::kGemm:
@@ -447,6 +464,9 @@ struct rldx_msat {
           break;
         case Op::kCopy:
           e = launch_copy(o.c, o.grid, st, p);
+          break;
+        case Op::kStatus:
+          e = launch_status_take(o.slot, st);
           break;
       }
       ck(e, "launch");
@@ -651,11 +671,14 @@ void rldx_msat::create(const rldx_msat_config& cfg, const rldx_msat_weights& w) 
   pdec_h = alloc<bf16>(static_cast<size_t>(B) * np * D);
 
   precompute(w);
+  if (!status.init()) throw Fail(RLDX_ERR_CUDA, "step status: mapped host memory");
   if (split_k_enabled()) {
     sizing = true;  // first pass: workspace the K-split plans want
     plan();
     sizing = false;
     ops.clear();
+    block_marks.clear();
+    step_marks.clear();
     if (ws_need > 0) {
       gemm_ws = alloc<uint8_t>(ws_need);  // zero-filled: the tile counters start at zero
       gemm_ws_bytes = ws_need;
@@ -665,10 +688,11 @@ void rldx_msat::create(const rldx_msat_config& cfg, const rldx_msat_weights& w) 
 
   // Warm-up run (loads every kernel), then capture.
   run_ops(stream);
+  ck(cudaEventRecord(status.done, stream), "status event");
   ck(cudaStreamSynchronize(stream), "warm-up");
-  unsigned int derr = 0;
-  ck(cudaMemcpyFromSymbol(&derr, g_rldx_err, 4), "device error");
-  if (derr) throw Fail(RLDX_ERR_DEVICE, "device error during warm-up: " + std::to_string(derr));
+  unsigned int derr = 0, during = 0;
+  if (status.read(true, &derr, &during) != RLDX_OK) throw Fail(RLDX_ERR_CUDA, "warm-up status");
+  if (derr && during) throw Fail(RLDX_ERR_DEVICE, "device error during warm-up: " + std::to_string(derr));
   if (c.use_graph) {
     ck(cudaStreamBeginCapture(stream, cudaStreamCaptureModeThreadLocal), "begin capture");
     try {
@@ -821,6 +845,7 @@ void rldx_msat::plan() {
   const int hist = c.physics_hist, fut = c.physics_fut;
   const float dt = 1.0f / static_cast<float>(S);
   const int ns = standard ? 2 : 3;  // streams / row groups: VL, SA (, P)
+  push_status(0);  // a code left by earlier work -> slot 0; the step starts from a clean word
 
   // ---- once per control step: state encoder, physics history encoder ----
   {
@@ -921,6 +946,7 @@ void rldx_msat::plan() {
     const int rows[3] = {nvl, nsa, np};
     const int wd[3] = {Dv, D, D};
     const int toff[3] = {0, nvl, nvl + nsa};
+    step_marks.push_back(static_cast<int>(ops.size()));
     for (int blk = 0; blk < c.depth; ++blk) {
       const StreamW* sw[3] = {&wvl[blk], &wsa[blk], standard ? nullptr : &wp[blk]};
       auto ln_all = [&]() {
@@ -967,6 +993,7 @@ void rldx_msat::plan() {
         }
         push_gemm(d);
       }
+      block_marks.push_back(static_cast<int>(ops.size()));
     }
     // ---- (Expanded)SingleStreamBlocks over [VL_proj | time, S/A (| P)] ----
     if (c.depth_single > 0) {
@@ -1014,6 +1041,7 @@ void rldx_msat::plan() {
           }
           push_gemm(d);
         }
+        block_marks.push_back(static_cast<int>(ops.size()));
       }
     }
     // ---- output projections, decoders, Euler updates ----
@@ -1062,6 +1090,7 @@ void rldx_msat::plan() {
       push_gemm(g3);
     }
   }
+  push_status(1);  // a code raised during the step -> slot 1
 }
 
 namespace {
@@ -1081,7 +1110,16 @@ void free_all(rldx_msat* h) {
   if (h->graph) cudaGraphDestroy(h->graph);
   for (void* p : h->allocs) cudaFree(p);
   if (h->stream) cudaStreamDestroy(h->stream);
+  h->status.release();
   h->allocs.clear();
+}
+
+int device_status_error(unsigned int code, unsigned int during, const char* what) {
+  return set_error(RLDX_ERR_DEVICE, std::string(what) + ": device error 0x" + [&] {
+    char b[16];
+    std::snprintf(b, sizeof(b), "%x", code);
+    return std::string(b);
+  }() + (during ? " raised during the step" : " left by earlier work (the step itself ran clean)"));
 }
 }  // namespace
 
@@ -1125,6 +1163,7 @@ static int msat_step_impl(rldx_msat* h, const rldx_msat_io* io, cudaStream_t st)
     else
       h->run_ops(st);
     h->copy_outputs(io, st);
+    ck(cudaEventRecord(h->status.done, st), "status event");
   });
 }
 
@@ -1137,7 +1176,38 @@ int rldx_msat_step_host(rldx_msat* h, const rldx_msat_io* io, void* stream) {
   if (rc != RLDX_OK) return rc;
   cudaError_t e = cudaStreamSynchronize(static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "msat_step_host sync");
+  unsigned int code = 0, during = 0;
+  rc = h->status.read(true, &code, &during);
+  if (rc != RLDX_OK) return rc;
+  if (code) return device_status_error(code, during, "msat_step_host");
   return RLDX_OK;
+}
+
+int rldx_msat_status(rldx_msat* h, int wait, unsigned int* code) {
+  if (!h || !code) return set_error(RLDX_ERR_ARG, "msat_status: null argument");
+  unsigned int during = 0;
+  return h->status.read(wait != 0, code, &during);
+}
+
+int rldx_msat_block_end(const rldx_msat* h, int step, int block, int* n_ops) {
+  if (!h || !n_ops) return set_error(RLDX_ERR_ARG, "msat_block_end: null argument");
+  const int nblocks = h->c.depth + h->c.depth_single;
+  if (step < 0 || step >= h->S || block < -1 || block >= nblocks)
+    return set_error(RLDX_ERR_ARG, "msat_block_end: step / block out of range");
+  *n_ops = block < 0 ? h->step_marks[step] : h->block_marks[static_cast<size_t>(step) * nblocks + block];
+  return RLDX_OK;
+}
+
+int rldx_msat_run_partial(rldx_msat* h, const rldx_msat_io* io, int n_ops, void* stream) {
+  if (!h || !io) return set_error(RLDX_ERR_ARG, "msat_run_partial: null argument");
+  if (n_ops < 0 || n_ops > static_cast<int>(h->ops.size()))
+    return set_error(RLDX_ERR_ARG, "msat_run_partial: n_ops outside [0, launch count]");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  return guard([&] {
+    h->copy_inputs(io, st);
+    h->run_ops(st, nullptr, n_ops);
+    ck(cudaEventRecord(h->status.done, st), "status event");
+  });
 }
 
 int rldx_msat_profile(rldx_msat* h, const rldx_msat_io* io, rldx_op_profile* out, int max_ops,

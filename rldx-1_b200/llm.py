@@ -177,9 +177,21 @@ class B200LLMChain(nn.Module):
             check(_lib.load().rldx_llm_set_deepstack(self._handle, C.c_void_p(feats.data_ptr()),
                                                      C.c_void_p(stream.cuda_stream)))
             self._keep_ds = feats  # alive until the copy queued on `stream` has run
+        code = self.device_status(wait=False)  # an error recorded by an earlier asynchronous call
+        if code:
+            raise _lib.RldxError(_lib.RLDX_ERR_DEVICE, f"device error 0x{code:x} recorded by a prefill")
         check(_lib.load().rldx_llm_prefill(self._handle, C.c_void_p(x.data_ptr()), C.c_void_p(out.data_ptr()),
                                            C.c_void_p(stream.cuda_stream)))
         return out
+
+    def device_status(self, wait: bool = True) -> int:
+        """Device error code of the last prefill (0: none; with wait=False, 0 while it is still
+        running).  Reading clears it."""
+        if self._handle is None:
+            return 0
+        code = C.c_uint(0)
+        check(_lib.load().rldx_llm_status(self._handle, 1 if wait else 0, C.byref(code)))
+        return int(code.value)
 
     def __del__(self):
         h = self.__dict__.pop("_handle", None)

@@ -316,3 +316,20 @@ def device_error() -> int:
     v = C.c_uint(0)
     check(load().rldx_get_device_error(C.byref(v)))
     return int(v.value)
+
+
+def set_wait_limit(cycles: int) -> None:
+    """Bound of every in-kernel wait in SM cycles (current device)."""
+    check(load().rldx_set_wait_limit(int(cycles)))
+
+
+def get_wait_limit() -> int:
+    v = C.c_int64(0)
+    check(load().rldx_get_wait_limit(C.byref(v)))
+    return int(v.value)
+
+
+def wait_selftest(limit_cycles: int) -> None:
+    """Launches the bounded-wait self-test on the current stream: a wait on a barrier nothing
+    arrives on runs out after `limit_cycles` and records device error 0x400."""
+    check(load().rldx_wait_selftest(int(limit_cycles), _stream()))

@@ -70,6 +70,13 @@ def test_joint_attention_head_dim_128(cuda, segs):
     run_case(cuda, 2, 16, segs, seed=sum(segs), hd=128)
 
 
+@pytest.mark.parametrize("segs", [[2032, 32, 16], [4080, 32, 16]])
+def test_joint_attention_head_dim_128_long(cuda, segs):
+    """The two longest lengths of the joint-attention sweep (L 2080 and 4128, segments
+    (L-48):32:16, 16 heads of 128)."""
+    run_case(cuda, 1, 16, segs, seed=sum(segs), hd=128)
+
+
 def test_joint_attention_head_dim_128_key_mask(cuda):
     run_case(cuda, 2, 4, [200, 32, 16], mask=True, seed=3, hd=128)
 

@@ -1,0 +1,143 @@
+"""Parity of the exact control step bench.py times: BASELINE config 2 (16 ExpandedDoubleStream
+blocks over [VL 512 | SA 18 | P 32], width 1536, 24 x 64 heads, 4 Euler steps, 36 embodiments)
+through B200ExpandedActionHeadChain with its default launch plan (K splits on, column-split
+attention), against the oracle (the reference's eager path restated on the CPU):
+
+  * bf16 actions against the oracle's bf16 eager control step: max-abs <= 2e-2 (two bf16 ulps
+    of the reference value where that is larger, on at most 1 % of the elements), cosine
+    >= 0.9999;
+  * per layer: the residual streams after every block of Euler steps 0 and 3, read from the
+    runtime, against the fp32 block of the same (bf16-valued) weights run on the runtime's own
+    bf16 input of that block: cosine >= 0.9999 for every stream.
+
+Reference comparator: rldx/inference/action_model/benchmark_action_model.py:50-123 (eager
+action-head forward), tolerance from the north-star (max-abs 2e-2 on bf16 actions, per-layer
+cosine 0.9999 against fp32).  A module that kept its complex RoPE tables (full rotation,
+rldx/inference/action_model/engine/custom_msat_chain.py:50-54) is bound too.
+"""
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+import rldx_b200  # noqa: E402,F401
+from oracle import msat_oracle as om  # noqa: E402
+from rldx_b200.chain import B200ExpandedActionHeadChain  # noqa: E402
+
+BF = torch.bfloat16
+
+
+def cos_sim(a, b):
+    a, b = a.double().flatten(), b.double().flatten()
+    return float((a @ b) / (a.norm() * b.norm() + 1e-30))
+
+
+def fast_init(module: torch.nn.Module, seed: int, cuda, std: float = 0.02) -> torch.nn.Module:
+    """Seeded init like om.init_weights (N(0, std), RMSNorm scales 1 + N(0, std)) with the random
+    numbers drawn on the GPU: the config-2 head has 1.4 G parameters, which the CPU generator
+    takes a minute to fill."""
+    g = torch.Generator(device=cuda).manual_seed(seed)
+    with torch.no_grad():
+        for name, p in sorted(module.named_parameters(), key=lambda kv: kv[0]):
+            noise = torch.randn(p.shape, generator=g, device=cuda, dtype=torch.float32) * std
+            if name.endswith(("norm_sa.weight", "norm_vl.weight", "norm_p.weight", "q_norm.weight",
+                              "k_norm.weight")):
+                noise = noise + 1.0
+            p.copy_(noise.cpu().to(p.dtype))
+    return module
+
+
+def assert_actions_close(out, ref16):
+    ref = ref16.float()
+    d = (out.float() - ref).abs()
+    ulp = torch.exp2(torch.floor(torch.log2(ref.abs().clamp_min(1e-30))) - 7)
+    bound = torch.maximum(torch.full_like(ref, 2e-2), 2 * ulp)
+    assert float((d - bound).max()) <= 0, (float(d.max()), float(ref.abs().max()))
+    assert int((d > 2e-2).sum()) <= max(1, d.numel() // 100), int((d > 2e-2).sum())
+    assert cos_sim(out.float(), ref) >= 0.9999
+
+
+def full_rotation(head: torch.nn.Module, cfg) -> None:
+    """Gives a bf16-cast head back its complex RoPE tables (a module that kept them)."""
+    rope = head.model.rope_embedder
+    for i, d in enumerate(rope.axes_dim):
+        setattr(rope, f"freqs_cis_{i}", om.precompute_freqs_cis(d, cfg.max_seq_len, cfg.rope_theta))
+
+
+@pytest.fixture(scope="module")
+def c2(cuda):
+    cfg = om.MsatHeadConfig()  # BASELINE config 2 (= synthetic.HeadDims(), the bench workload)
+    head = fast_init(om.ActionHead(cfg), seed=0, cuda=cuda).to(BF)  # cos-only RoPE (bf16 module)
+    inp = om.make_inputs(cfg, batch=1, seed=42)
+    chain = B200ExpandedActionHeadChain(head, cuda)
+    dev = {k: v.to(cuda) for k, v in inp.items()}
+    dev = {k: (v.to(BF) if v.is_floating_point() else v) for k, v in dev.items()}
+    out = chain(dev["vl"], dev["state"], dev["embodiment_id"], dev["init_noise"], dev["physics_hist"],
+                dev["physics_noise"])
+    torch.cuda.synchronize()
+    assert chain.device_status() == 0
+    return cfg, head, inp, dev, chain, out.cpu()
+
+
+def test_config2_actions_match_oracle_bf16(c2):
+    cfg, head, inp, _, chain, out = c2
+    # the plan bench.py times: K splits and the column-split attention are part of it
+    assert chain.launches_per_step > 400
+    args = [inp[k].to(BF) if inp[k].is_floating_point() else inp[k]
+            for k in ("vl", "state", "embodiment_id", "init_noise", "physics_hist", "physics_noise")]
+    ref16 = om.denoise(head, *args, cfg.num_steps)
+    assert_actions_close(out, ref16)
+
+
+@pytest.mark.parametrize("step", [0, 3])
+def test_config2_per_layer_cosine_against_fp32(c2, cuda, step):
+    cfg, head, _, dev, chain, _ = c2
+    msat = head.model
+    n_vl, n_sa, n_p = cfg.n_vl, 1 + cfg.n_state + cfg.horizon, cfg.physics_hist + cfg.physics_fut
+    pe = msat.rope_embedder(msat.position_ids(1, n_vl, n_sa, n_p))  # the bf16 module's table
+
+    def streams():
+        torch.cuda.synchronize()
+        vl, sa, p = (chain.read_buffer(i) for i in (0, 1, 2))
+        torch.cuda.synchronize()
+        return (sa.cpu().float().view(1, n_sa, -1), vl.cpu().float().view(1, n_vl, -1),
+                p.cpu().float().view(1, n_p, -1))
+
+    chain.run_partial(dev, chain.block_end(step, -1))
+    x = streams()
+    for i in range(cfg.depth):
+        blk32 = msat.double_blocks[i].float()  # fp32 arithmetic on the bf16-valued weights
+        with torch.no_grad():
+            ref = blk32(*x, pe)
+        msat.double_blocks[i].to(BF)
+        chain.run_partial(dev, chain.block_end(step, i))
+        out = streams()
+        for name, o, r in zip(("sa", "vl", "p"), out, ref):
+            c = cos_sim(o, r)
+            assert c >= 0.9999, (step, i, name, c)
+        x = out
+    assert chain.device_status() == 0
+
+
+def test_full_rotation_rope_through_the_chain(cuda):
+    """A head whose RoPE tables stayed complex (full rotation) at config-2 widths with fewer
+    blocks and cognition tokens, both RoPE layouts of the all-modality path."""
+    for mode in ("rope_sa_only", "rope_vl_sa"):
+        cfg = om.MsatHeadConfig(n_vl=128, depth=2, positional_embeddings=mode)
+        head = fast_init(om.ActionHead(cfg), seed=3, cuda=cuda).to(BF)
+        full_rotation(head, cfg)
+        assert head.model.rope_embedder.freqs_cis_0.is_complex()
+        inp = om.make_inputs(cfg, batch=2, seed=5, emb_ids=[4, 0])
+        args = [inp[k].to(BF) if inp[k].is_floating_point() else inp[k]
+                for k in ("vl", "state", "embodiment_id", "init_noise", "physics_hist", "physics_noise")]
+        ref16 = om.denoise(head, *args, cfg.num_steps)
+        chain = B200ExpandedActionHeadChain(head, cuda)
+        d = [a.to(cuda) for a in args]
+        out = chain(*d).cpu()
+        assert chain._cfg.rope_cos_only == 0
+        assert_actions_close(out, ref16)
+        # the cos-only form of the same weights gives other actions: the rotation really ran
+        head_c = fast_init(om.ActionHead(cfg), seed=3, cuda=cuda).to(BF)
+        out_c = B200ExpandedActionHeadChain(head_c, cuda)(*d).cpu()
+        assert not torch.equal(out_c, out)

@@ -51,3 +51,10 @@ def test_null_arguments_are_rejected_without_a_device(lib):
     assert lib.rldx_msat_step(None, None, None) == _lib.RLDX_ERR_ARG
     assert lib.rldx_msat_create(None, None, None) == _lib.RLDX_ERR_ARG
     assert lib.rldx_msat_destroy(None) == _lib.RLDX_OK
+    code = C.c_uint(7)
+    assert lib.rldx_msat_status(None, 1, C.byref(code)) == _lib.RLDX_ERR_ARG
+    assert lib.rldx_llm_status(None, 1, C.byref(code)) == _lib.RLDX_ERR_ARG
+    n = C.c_int(0)
+    assert lib.rldx_msat_block_end(None, 0, 0, C.byref(n)) == _lib.RLDX_ERR_ARG
+    assert lib.rldx_msat_run_partial(None, None, 0, None) == _lib.RLDX_ERR_ARG
+    assert lib.rldx_get_wait_limit(None) == _lib.RLDX_ERR_ARG

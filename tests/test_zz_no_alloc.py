@@ -61,6 +61,21 @@ def test_static_scratch_matches_caller_workspace(cuda):
     assert ops.device_error() == 0
 
 
+def test_static_scratch_call_allocates_no_device_memory(cuda):
+    """A warm call leaves the device's free memory where it was: the K-split partials and
+    counters live in the library's static array, and nothing else is allocated."""
+    keep, descs, outs = _problems(cuda, 78)
+    _static(descs)  # first call on this device: looks the scratch address up
+    torch.cuda.synchronize()
+    free0, _ = torch.cuda.mem_get_info()
+    for _ in range(3):
+        _static(descs)
+    torch.cuda.synchronize()
+    free1, _ = torch.cuda.mem_get_info()
+    assert free1 == free0, (free0, free1)
+    assert ops.device_error() == 0
+
+
 def test_static_scratch_rejects_plans_that_do_not_fit(cuda):
     g = torch.Generator(device=cuda).manual_seed(5)
     x = torch.randn(512, 8192, device=cuda, generator=g).to(BF)
