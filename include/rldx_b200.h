@@ -401,6 +401,12 @@ typedef struct {
   rldx_linear phd_l1, phd_l2;              /* physics.physics_decoder.net[0] / net[2]   */
   const rldx_single_block_weights* single_blocks; /* [depth_single] (host array)         */
   rldx_linear vl_proj_to_sa;               /* w == NULL: identity (vl_dim == dim)       */
+  /* The module's own RoPE tables (RoPEEmbedder1D.freqs_cis_0 / _1, ops.py:11-25, 70-119):
+   * cos and sin of axis i as [rope_max_seq, axes_i / 2] fp32 (host or device; sin ignored
+   * with rope_cos_only, where cos is the real part the bf16 cast kept).  axes = [16, 48]
+   * under rope_sa_only, [48, 16] under rope_vl_sa.  NULL: computed from rope_theta. */
+  const float* rope_cos[2];
+  const float* rope_sin[2];
 } rldx_msat_weights;
 
 typedef struct {
@@ -468,7 +474,10 @@ int rldx_msat_profile(rldx_msat* h, const rldx_msat_io* io, rldx_op_profile* ops
  * dst_bytes large enough) on `stream`: 0 X_vl ([B*n_vl, vl_dim]), 1 X_sa, 2 X_p (streams after
  * the last block of the last Euler step; with single blocks, X_sa / X_p after the last single
  * block and X_vl after the last double block unless vl_proj_to_sa is the identity), 3 the
- * action state.  With dst == NULL only *rows / *cols are set. */
+ * action state; intermediates of the double blocks (as the last launch run left them):
+ * 4-6 LayerNorm outputs (VL, SA, P), 7 q and 8 k ([B*H*L, 64], joint token order), 9 v^T
+ * ([B*H*64, Lp]), 10-12 attention outputs ([B*n, H*64]), 13-15 SwiGLU hidden ([B*n, hidden
+ * rounded up to 32]).  With dst == NULL only *rows / *cols are set. */
 int rldx_msat_read_buffer(const rldx_msat* h, int which, void* dst, int64_t dst_bytes,
                           int64_t* rows, int64_t* cols, void* stream);
 

@@ -101,6 +101,7 @@ class MsatWeights(C.Structure):
         ("phf_w1", Linear), ("phf_w2", Linear), ("phf_w3", Linear),
         ("phd_l1", Linear), ("phd_l2", Linear),
         ("single_blocks", C.POINTER(SingleBlockWeights)), ("vl_proj_to_sa", Linear),
+        ("rope_cos", vp * 2), ("rope_sin", vp * 2),
     ]
 
 

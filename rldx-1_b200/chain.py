@@ -217,6 +217,23 @@ class _B200HeadChain(nn.Module):
         w.act_w1, w.act_w2, w.act_w3 = self._cat(ae.W1), self._cat(ae.W2), self._cat(ae.W3)
         w.dec_l1, w.dec_l2 = self._cat(self._act_dec.layer1), self._cat(self._act_dec.layer2)
         w.pos_emb = self._bf16(self._pos.weight)
+        # the module's own RoPE tables (complex: full rotation; real: the cos the bf16 cast kept);
+        # a module without both per-axis tables of the expected shape gets them computed
+        rope = msat.rope_embedder
+        mode = getattr(msat, "positional_embeddings", "rope_sa_only")
+        axes = (16, 48) if mode == "rope_sa_only" else (48, 16)
+        tabs = [getattr(rope, f"freqs_cis_{i}", None) for i in range(2)]
+        n = int(tabs[0].shape[0]) if tabs[0] is not None else 0
+        if all(t is not None and tuple(t.shape) == (n, a // 2) for t, a in zip(tabs, axes)):
+            for i, t in enumerate(tabs):
+                t = t.detach()
+                cos = (t.real if t.is_complex() else t).to(self.device, torch.float32).contiguous()
+                self._keep.append(cos)
+                w.rope_cos[i] = cos.data_ptr()
+                if t.is_complex():
+                    sin = t.imag.to(self.device, torch.float32).contiguous()
+                    self._keep.append(sin)
+                    w.rope_sin[i] = sin.data_ptr()
         if not self._physics:
             return w
         pc, pf, pd = (self._phys.physics_cond_encoder, self._phys.physics_fut_encoder,

@@ -52,17 +52,19 @@ struct rldx_llm {
   cudaGraphExec_t exec = nullptr;
   bool pdl = true;
 
+  // Bind-time copies, fills and re-layout kernels all run in order on the handle's stream (a
+  // legacy-stream cudaMemcpy between device buffers is asynchronous and unordered with it).
   template <class T_>
   T_* alloc(size_t count) {
     void* p = nullptr;
     ck(cudaMalloc(&p, count * sizeof(T_) + 256), "cudaMalloc");
     allocs.push_back(p);
-    ck(cudaMemset(p, 0, count * sizeof(T_) + 256), "cudaMemset");
+    ck(cudaMemsetAsync(p, 0, count * sizeof(T_) + 256, stream), "cudaMemset");
     return static_cast<T_*>(p);
   }
   bf16* copy_rows(bf16* dst, const void* src, size_t count, const char* what) {
     if (!src) throw Fail(RLDX_ERR_ARG, std::string("missing weight: ") + what);
-    ck(cudaMemcpy(dst, src, count * 2, cudaMemcpyDefault), what);
+    ck(cudaMemcpyAsync(dst, src, count * 2, cudaMemcpyDefault, stream), what);
     return dst;
   }
   bf16* copy_in(const void* src, size_t count, const char* what) { return copy_rows(alloc<bf16>(count), src, count, what); }
@@ -81,7 +83,7 @@ struct rldx_llm {
         idx[grp * 64 + 32 + i] = r < F ? F + r : 2 * F;
       }
     int* didx = alloc<int>(idx.size());
-    ck(cudaMemcpy(didx, idx.data(), idx.size() * 4, cudaMemcpyHostToDevice), "idx");
+    ck(cudaMemcpyAsync(didx, idx.data(), idx.size() * 4, cudaMemcpyHostToDevice, stream), "idx");
     bf16* dst = alloc<bf16>(static_cast<size_t>(2) * Fp * D);
     ck(launch_gather_rows(src, D, dst, D, didx, 2 * Fp, D, stream), "gather w12");
     ck(cudaStreamSynchronize(stream), "gather sync");
@@ -149,6 +151,7 @@ struct rldx_llm {
     const char* env = getenv("RLDX_PDL");
     pdl = !(env && env[0] == '0');
     ck(cudaStreamCreateWithFlags(&stream, cudaStreamNonBlocking), "stream");
+    ck(cudaDeviceSynchronize(), "weights ready");  // the caller's weights may come from any stream
 
     const size_t qd = static_cast<size_t>(Hq) * hd, kd = static_cast<size_t>(Hkv) * hd;
     for (int i = 0; i < c.layers; ++i) {
@@ -168,8 +171,8 @@ struct rldx_llm {
       l.w12 = interleave_w12(s.gate_proj, s.up_proj);
       if (!s.down_proj) throw Fail(RLDX_ERR_ARG, "missing weight: down_proj");
       l.down = alloc<bf16>(static_cast<size_t>(D) * Fp);  // [D, F] -> [D, Fp], zero columns
-      ck(cudaMemcpy2D(l.down, static_cast<size_t>(Fp) * 2, s.down_proj, static_cast<size_t>(F) * 2,
-                      static_cast<size_t>(F) * 2, D, cudaMemcpyDefault),
+      ck(cudaMemcpy2DAsync(l.down, static_cast<size_t>(Fp) * 2, s.down_proj, static_cast<size_t>(F) * 2,
+                           static_cast<size_t>(F) * 2, D, cudaMemcpyDefault, stream),
          "down_proj");
       lw.push_back(l);
     }
@@ -178,7 +181,8 @@ struct rldx_llm {
     ds_rows = c.deepstack_rows;
     if (ds_layers > 0) {
       ds_index = alloc<int>(ds_rows);
-      ck(cudaMemcpy(ds_index, w.deepstack_row_index, static_cast<size_t>(ds_rows) * 4, cudaMemcpyHostToDevice),
+      ck(cudaMemcpyAsync(ds_index, w.deepstack_row_index, static_cast<size_t>(ds_rows) * 4, cudaMemcpyHostToDevice,
+                         stream),
          "deepstack rows");
       ds_feat = alloc<bf16>(static_cast<size_t>(ds_layers) * B * ds_rows * D);  // zero until set
     }

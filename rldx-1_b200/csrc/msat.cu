@@ -171,18 +171,27 @@ struct rldx_msat {
   cudaGraphExec_t exec = nullptr;
   bool pdl = true;
 
+  // Every bind-time copy, fill and re-layout kernel runs in order on the handle's own stream:
+  // the legacy-stream forms (cudaMemcpy / cudaMemset) return before a device-to-device copy
+  // has landed and are not ordered with a non-blocking stream, so a re-layout kernel on
+  // `stream` could read a weight half copied.
   template <class T>
   T* alloc(size_t n) {
     void* p = nullptr;
     ck(cudaMalloc(&p, n * sizeof(T) + 256), "cudaMalloc");
     allocs.push_back(p);
-    ck(cudaMemset(p, 0, n * sizeof(T) + 256), "cudaMemset");
+    ck(cudaMemsetAsync(p, 0, n * sizeof(T) + 256, stream), "cudaMemset");
     return static_cast<T*>(p);
+  }
+
+  void copy(void* dst, const void* src, size_t bytes, const char* what) {
+    ck(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDefault, stream), what);
   }
 
   void release(void* p) {
     auto it = std::find(allocs.begin(), allocs.end(), p);
     if (it != allocs.end()) {
+      ck(cudaStreamSynchronize(stream), "release sync");  // no queued work still reads it
       cudaFree(p);
       allocs.erase(it);
     }
@@ -191,7 +200,7 @@ struct rldx_msat {
   bf16* copy_in(const void* src, size_t n, const char* what) {
     if (!src) throw Fail(RLDX_ERR_ARG, std::string("missing weight: ") + what);
     bf16* d = alloc<bf16>(n);
-    ck(cudaMemcpy(d, src, n * 2, cudaMemcpyDefault), what);
+    copy(d, src, n * 2, what);
     return d;
   }
 
@@ -199,7 +208,7 @@ struct rldx_msat {
   bf16* copy_pad(const void* src, int rows, int K, int Kp, const char* what) {
     if (!src) throw Fail(RLDX_ERR_ARG, std::string("missing weight: ") + what);
     bf16* d = alloc<bf16>(static_cast<size_t>(rows) * Kp);
-    ck(cudaMemcpy2D(d, Kp * 2, src, K * 2, K * 2, rows, cudaMemcpyDefault), what);
+    ck(cudaMemcpy2DAsync(d, Kp * 2, src, K * 2, K * 2, rows, cudaMemcpyDefault, stream), what);
     return d;
   }
 
@@ -208,7 +217,7 @@ struct rldx_msat {
     if (!W) throw Fail(RLDX_ERR_ARG, std::string("missing weight: ") + what);
     const int cats = c.num_embodiments;
     bf16* tmp = alloc<bf16>(static_cast<size_t>(cats) * K * N);
-    ck(cudaMemcpy(tmp, W, static_cast<size_t>(cats) * K * N * 2, cudaMemcpyDefault), what);
+    copy(tmp, W, static_cast<size_t>(cats) * K * N * 2, what);
     bf16* d = alloc<bf16>(static_cast<size_t>(cats) * N * Kp);
     ck(launch_transpose_cat(tmp, d, cats, K, N, Kp, stream), "transpose");
     ck(cudaStreamSynchronize(stream), "transpose sync");
@@ -231,13 +240,13 @@ struct rldx_msat {
         idx[g * 64 + 32 + i] = r < hidden ? hidden + r : zero_row;
       }
     int* didx = alloc<int>(idx.size());
-    ck(cudaMemcpy(didx, idx.data(), idx.size() * 4, cudaMemcpyHostToDevice), "idx");
+    copy(didx, idx.data(), idx.size() * 4, "idx");
     bf16* src = alloc<bf16>(static_cast<size_t>(2 * hidden + 1) * dim);  // zero-filled
-    ck(cudaMemcpy(src, l.w, static_cast<size_t>(2) * hidden * dim * 2, cudaMemcpyDefault), "w12");
+    copy(src, l.w, static_cast<size_t>(2) * hidden * dim * 2, "w12");
     *w = alloc<bf16>(static_cast<size_t>(2) * hp * dim);
     ck(launch_gather_rows(src, dim, *w, dim, didx, 2 * hp, dim, stream), "gather");
     bf16* bsrc = alloc<bf16>(static_cast<size_t>(2 * hidden + 1));
-    ck(cudaMemcpy(bsrc, l.b, static_cast<size_t>(2) * hidden * 2, cudaMemcpyDefault), "w12 bias");
+    copy(bsrc, l.b, static_cast<size_t>(2) * hidden * 2, "w12 bias");
     *b = alloc<bf16>(static_cast<size_t>(2) * hp);
     ck(launch_gather_rows(bsrc, 1, *b, 1, didx, 2 * hp, 1, stream), "gather bias");
     ck(cudaStreamSynchronize(stream), "gather sync");
@@ -539,6 +548,7 @@ void rldx_msat::create(const rldx_msat_config& cfg, const rldx_msat_weights& w) 
   if (standard) c.physics_hist = c.physics_fut = c.physics_dim = 0;  // no physics buffers
   if (w.time_token_proj.w) throw Fail(RLDX_ERR_UNSUPPORTED, "time_token_proj must be identity (inner == sa_dim)");
   ck(cudaGetDevice(&device), "cudaGetDevice");
+  ck(cudaDeviceSynchronize(), "weights ready");  // the caller's weights may come from any stream
   const char* env = getenv("RLDX_PDL");
   pdl = !(env && env[0] == '0');
 
@@ -722,6 +732,25 @@ void rldx_msat::precompute(const rldx_msat_weights& w) {
   };
   // S/A ids (after the time token at 0) start at 1 in the double blocks under rope_sa_only and
   // at 2 otherwise; the single blocks start them at 2 in both modes.
+  // The module's per-axis tables when the binding passes them (exactly the reference's
+  // values), else the same angles computed here.
+  std::vector<float> mod_cos[2], mod_sin[2];
+  const int axes[2] = {axes0, axes1};
+  for (int a = 0; a < 2; ++a) {
+    if (!w.rope_cos[a]) continue;
+    const size_t n = static_cast<size_t>(c.rope_max_seq) * (axes[a] / 2);
+    mod_cos[a].resize(n);
+    mod_sin[a].assign(n, 0.0f);
+    ck(cudaMemcpy(mod_cos[a].data(), w.rope_cos[a], n * 4, cudaMemcpyDefault), "rope table");
+    if (!c.rope_cos_only) {
+      if (!w.rope_sin[a]) throw Fail(RLDX_ERR_ARG, "rope_sin missing for a full-rotation table");
+      ck(cudaMemcpy(mod_sin[a].data(), w.rope_sin[a], n * 4, cudaMemcpyDefault), "rope table");
+    }
+  }
+  if (w.rope_cos[0] == nullptr || w.rope_cos[1] == nullptr) {
+    mod_cos[0].clear();
+    mod_cos[1].clear();
+  }
   auto table = [&](int sa_start, float** dcos, float** dsin) {
     std::vector<float> hc_cos(static_cast<size_t>(L) * 32), hc_sin(static_cast<size_t>(L) * 32);
     for (int t = 0; t < L; ++t) {
@@ -738,16 +767,24 @@ void rldx_msat::precompute(const rldx_msat_weights& w) {
       if (id0 >= c.rope_max_seq || id1 >= c.rope_max_seq)
         throw Fail(RLDX_ERR_ARG, "RoPE position beyond rope_max_seq");
       for (int p = 0; p < 32; ++p) {
-        float ang;
-        if (p < axes0 / 2)
-          ang = static_cast<float>(id0) * freq(axes0, p);
-        else
-          ang = static_cast<float>(id1) * freq(axes1, p - axes0 / 2);
-        float cs = static_cast<float>(std::cos(static_cast<double>(ang)));
-        float sn = static_cast<float>(std::sin(static_cast<double>(ang)));
-        if (c.rope_cos_only) {
-          cs = bf_round(cs);
-          sn = 0.0f;
+        float cs, sn;
+        if (!mod_cos[0].empty()) {
+          const int a = p < axes0 / 2 ? 0 : 1;
+          const size_t i = static_cast<size_t>(a == 0 ? id0 : id1) * (axes[a] / 2) + (a == 0 ? p : p - axes0 / 2);
+          cs = mod_cos[a][i];
+          sn = c.rope_cos_only ? 0.0f : mod_sin[a][i];
+        } else {
+          float ang;
+          if (p < axes0 / 2)
+            ang = static_cast<float>(id0) * freq(axes0, p);
+          else
+            ang = static_cast<float>(id1) * freq(axes1, p - axes0 / 2);
+          cs = static_cast<float>(std::cos(static_cast<double>(ang)));
+          sn = static_cast<float>(std::sin(static_cast<double>(ang)));
+          if (c.rope_cos_only) {
+            cs = bf_round(cs);
+            sn = 0.0f;
+          }
         }
         hc_cos[static_cast<size_t>(t) * 32 + p] = cs;
         hc_sin[static_cast<size_t>(t) * 32 + p] = sn;
@@ -755,8 +792,9 @@ void rldx_msat::precompute(const rldx_msat_weights& w) {
     }
     *dcos = alloc<float>(hc_cos.size());
     *dsin = alloc<float>(hc_sin.size());
-    ck(cudaMemcpy(*dcos, hc_cos.data(), hc_cos.size() * 4, cudaMemcpyHostToDevice), "rope");
-    ck(cudaMemcpy(*dsin, hc_sin.data(), hc_sin.size() * 4, cudaMemcpyHostToDevice), "rope");
+    copy(*dcos, hc_cos.data(), hc_cos.size() * 4, "rope");
+    copy(*dsin, hc_sin.data(), hc_sin.size() * 4, "rope");
+    ck(cudaStreamSynchronize(stream), "rope sync");  // the host tables go out of scope
   };
   table(c.rope_mode == RLDX_ROPE_SA_ONLY ? 1 : 2, &rope_cos, &rope_sin);
   if (c.depth_single > 0) table(2, &rope_cos_s, &rope_sin_s);
@@ -770,7 +808,7 @@ void rldx_msat::precompute(const rldx_msat_weights& w) {
   std::vector<uint16_t> tproj(static_cast<size_t>(S) * tc);
   for (int s = 0; s < S; ++s) timestep_proj(tvals[s], tc, &tproj[static_cast<size_t>(s) * tc]);
   bf16* d_tproj = alloc<bf16>(tproj.size());
-  ck(cudaMemcpy(d_tproj, tproj.data(), tproj.size() * 2, cudaMemcpyHostToDevice), "tproj");
+  copy(d_tproj, tproj.data(), tproj.size() * 2, "tproj");
   const size_t inner = static_cast<size_t>(H) * 64;
   bf16* t1 = alloc<bf16>(static_cast<size_t>(S) * inner);
   time_tok = alloc<bf16>(static_cast<size_t>(S) * inner);
@@ -807,9 +845,9 @@ void rldx_msat::precompute(const rldx_msat_weights& w) {
     run({lin(stemb, static_cast<int>(inner), lw, lb, S, 2 * D, static_cast<int>(inner), ss, 2 * D)});
     *shift = alloc<bf16>(static_cast<size_t>(S) * D);
     *sc1p = alloc<bf16>(static_cast<size_t>(S) * D);
-    ck(cudaMemcpy2D(*shift, D * 2, ss, 4 * D, D * 2, S, cudaMemcpyDeviceToDevice), "shift");
+    ck(cudaMemcpy2DAsync(*shift, D * 2, ss, 4 * D, D * 2, S, cudaMemcpyDeviceToDevice, stream), "shift");
     bf16* sc = alloc<bf16>(static_cast<size_t>(S) * D);
-    ck(cudaMemcpy2D(sc, D * 2, ss + D, 4 * D, D * 2, S, cudaMemcpyDeviceToDevice), "scale");
+    ck(cudaMemcpy2DAsync(sc, D * 2, ss + D, 4 * D, D * 2, S, cudaMemcpyDeviceToDevice, stream), "scale");
     ck(launch_elementwise(sc, *sc1p, static_cast<long long>(S) * D, 1, stream), "1+scale");
   };
   adaln(w.proj_out_1, &ada_sc1p, &ada_shift, "proj_out_1");
@@ -823,18 +861,17 @@ void rldx_msat::precompute(const rldx_msat_weights& w) {
   for (int s = 0; s < S; ++s) {
     sinusoid_sin_cos(tvals[s], D, row.data());
     for (int r = 0; r < B * c.horizon; ++r)
-      ck(cudaMemcpy(act_cat[s] + static_cast<size_t>(r) * 2 * D + D,
-                    (r % c.horizon < c.prefix_len ? row_prefix : row).data(), D * 2, cudaMemcpyHostToDevice),
-         "tau");
+      copy(act_cat[s] + static_cast<size_t>(r) * 2 * D + D,
+           (r % c.horizon < c.prefix_len ? row_prefix : row).data(), D * 2, "tau");
     for (int r = 0; r < B * c.physics_fut; ++r)
-      ck(cudaMemcpy(phf_cat[s] + static_cast<size_t>(r) * 2 * D + D, row.data(), D * 2, cudaMemcpyHostToDevice), "tau");
+      copy(phf_cat[s] + static_cast<size_t>(r) * 2 * D + D, row.data(), D * 2, "tau");
+    ck(cudaStreamSynchronize(stream), "tau sync");  // `row` is rewritten for the next step
   }
   for (int t = 0; t < c.physics_hist; ++t) {
     sinusoid_sin_cos(static_cast<float>(t), D, row.data());
     for (int b = 0; b < B; ++b)
-      ck(cudaMemcpy(phc_cat + (static_cast<size_t>(b) * c.physics_hist + t) * 2 * D + D, row.data(), D * 2,
-                    cudaMemcpyHostToDevice),
-         "pos");
+      copy(phc_cat + (static_cast<size_t>(b) * c.physics_hist + t) * 2 * D + D, row.data(), D * 2, "pos");
+    ck(cudaStreamSynchronize(stream), "pos sync");  // `row` is rewritten for the next token
   }
   ck(cudaStreamSynchronize(stream), "precompute");
 }
@@ -1266,9 +1303,53 @@ int rldx_msat_read_buffer(const rldx_msat* h, int which, void* dst, int64_t dst_
       *rows = static_cast<int64_t>(h->B) * h->c.horizon;
       *cols = h->c.action_dim;
       break;
+    case 4:  // LayerNorm outputs of the streams (the last LN of a double block)
+    case 5:
+    case 6: {
+      const bf16* b[3] = {h->lnvl, h->lnsa, h->lnp};
+      const int n[3] = {h->nvl, h->nsa, h->np};
+      src = b[which - 4];
+      *rows = static_cast<int64_t>(h->B) * n[which - 4];
+      *cols = which == 4 ? h->Dv : h->D;
+      break;
+    }
+    case 7:  // q, k [B*H*L, 64]
+    case 8:
+      src = which == 7 ? h->q : h->k;
+      *rows = static_cast<int64_t>(h->B) * h->H * h->L;
+      *cols = 64;
+      break;
+    case 9:  // v^T [B*H*64, Lp]
+      src = h->vt;
+      *rows = static_cast<int64_t>(h->B) * h->H * 64;
+      *cols = h->Lp;
+      break;
+    case 10:  // attention outputs of the streams [B*n, H*64]
+    case 11:
+    case 12: {
+      const bf16* b[3] = {h->ovl, h->osa, h->op};
+      const int n[3] = {h->nvl, h->nsa, h->np};
+      src = b[which - 10];
+      *rows = static_cast<int64_t>(h->B) * n[which - 10];
+      *cols = h->H * 64;
+      break;
+    }
+    case 13:  // SwiGLU hidden of the streams [B*n, hidden padded to 32]
+    case 14:
+    case 15: {
+      const bf16* b[3] = {h->hvl, h->hsa, h->hp};
+      const int n[3] = {h->nvl, h->nsa, h->np};
+      const int hid[3] = {rldx_msat::pad32(h->c.vl_mlp_hidden), rldx_msat::pad32(h->c.mlp_hidden),
+                          rldx_msat::pad32(h->c.mlp_hidden)};
+      src = b[which - 13];
+      *rows = static_cast<int64_t>(h->B) * n[which - 13];
+      *cols = hid[which - 13];
+      break;
+    }
     default:
       return set_error(RLDX_ERR_ARG, "read_buffer: unknown buffer");
   }
+  if (!src || *rows == 0) return set_error(RLDX_ERR_ARG, "read_buffer: the handle has no such buffer");
   if (!dst) return RLDX_OK;
   const int64_t bytes = *rows * *cols * 2;
   if (dst_bytes < bytes) return set_error(RLDX_ERR_ARG, "read_buffer: destination too small");

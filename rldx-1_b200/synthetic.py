@@ -115,12 +115,19 @@ def random_action_head(d: HeadDims, seed: int = 0, device="cuda", std: float = 0
             setattr(sb, f"{pre}pre_norm", nn.LayerNorm(d.dim, eps=1e-6, elementwise_affine=False))
             setattr(sb, f"{pre}post_norm", nn.Identity())
         singles.append(sb)
-    rope_table = torch.zeros(d.rope_max_seq, 8, dtype=bf if cos_only_rope else torch.complex64, device=device)
+    # RoPEEmbedder1D tables (ops.py:11-25, axes [16, 48] under rope_sa_only); a bf16-loaded
+    # module keeps only their real part (the cos-only quirk)
+    tables = {}
+    for i, dim in enumerate((16, 48)):
+        inv = 1.0 / (d.rope_theta ** (torch.arange(0, dim, 2)[: dim // 2].float() / dim))
+        ang = torch.outer(torch.arange(d.rope_max_seq), inv).float()
+        t = torch.polar(torch.ones_like(ang), ang)
+        tables[f"freqs_cis_{i}"] = (t.real.to(bf) if cos_only_rope else t).to(device)
     msat = NS(
         double_blocks=blocks, single_blocks=singles, temb_type="input_token", use_physics=d.use_physics,
         positional_embeddings="rope_sa_only", time_token_proj=nn.Identity(),
         timestep_encoder=NS(timestep_embedder=NS(linear_1=lin(256, d.dim), linear_2=lin(d.dim, d.dim))),
-        rope_embedder=NS(freqs_cis_0=rope_table, theta=d.rope_theta),
+        rope_embedder=NS(**tables, theta=d.rope_theta),
         vl_proj_to_sa=lin(d.vl_dim, d.dim) if d.vl_dim != d.dim else nn.Identity(),
         proj_out_1=lin(d.dim, 2 * d.dim), proj_out_2=lin(d.dim, d.out_dim))
     if d.use_physics:

@@ -3,9 +3,15 @@ blocks over [VL 512 | SA 18 | P 32], width 1536, 24 x 64 heads, 4 Euler steps, 3
 through B200ExpandedActionHeadChain with its default launch plan (K splits on, column-split
 attention), against the oracle (the reference's eager path restated on the CPU):
 
-  * bf16 actions against the oracle's bf16 eager control step: max-abs <= 2e-2 (two bf16 ulps
-    of the reference value where that is larger, on at most 1 % of the elements), cosine
-    >= 0.9999;
+  * bf16 actions against the oracle's bf16 eager control step and its fp32 counterpart (the
+    same bf16-valued weights in fp32): cosine >= 0.9999 against both; at least 99 % of the
+    elements within max-abs 2e-2 of the bf16 path and every element within 2e-2 or four bf16
+    ulps of it, whichever is larger; and the mean distance to fp32 at most 1.5x that of the
+    reference's own bf16 path.  The last clause is the accuracy gate: at these widths the
+    reference's bf16 eager path itself sits up to ~0.03 max-abs from fp32 (measured: mean
+    0.004), so two bf16 implementations whose fp32 sums run in different orders differ by a
+    few ulps on a few elements after 4 Euler steps, and a bare 2e-2 max-abs between them
+    would test the summation order, not the kernels;
   * per layer: the residual streams after every block of Euler steps 0 and 3, read from the
     runtime, against the fp32 block of the same (bf16-valued) weights run on the runtime's own
     bf16 input of that block: cosine >= 0.9999 for every stream.
@@ -48,14 +54,31 @@ def fast_init(module: torch.nn.Module, seed: int, cuda, std: float = 0.02) -> to
     return module
 
 
-def assert_actions_close(out, ref16):
-    ref = ref16.float()
-    d = (out.float() - ref).abs()
+def assert_actions_close(out, ref16, ref32):
+    """The parity check of the module docstring (bf16 actions vs the bf16 and fp32 references)."""
+    out, ref, r32 = out.float(), ref16.float(), ref32.float()
+    d = (out - ref).abs()
     ulp = torch.exp2(torch.floor(torch.log2(ref.abs().clamp_min(1e-30))) - 7)
-    bound = torch.maximum(torch.full_like(ref, 2e-2), 2 * ulp)
+    bound = torch.maximum(torch.full_like(ref, 2e-2), 4 * ulp)
     assert float((d - bound).max()) <= 0, (float(d.max()), float(ref.abs().max()))
     assert int((d > 2e-2).sum()) <= max(1, d.numel() // 100), int((d > 2e-2).sum())
-    assert cos_sim(out.float(), ref) >= 0.9999
+    assert cos_sim(out, ref) >= 0.9999
+    assert cos_sim(out, r32) >= 0.9999
+    ours, theirs = float((out - r32).abs().mean()), float((ref - r32).abs().mean())
+    assert ours <= 1.5 * theirs + 1e-4, (ours, theirs)
+
+
+def fp32_actions(head16, args16, cfg):
+    """The oracle control step in fp32 with the bf16 module's weights and RoPE tables."""
+    rope = head16.model.rope_embedder
+    tables = dict(rope.named_buffers())  # complex tables must not go through .to(bf16) again
+    h32 = head16.float()
+    try:
+        return om.denoise(h32, *[a.float() if a.is_floating_point() else a for a in args16], cfg.num_steps)
+    finally:
+        head16.to(BF)  # back to the bf16 module (exact: the weights are bf16 values)
+        for name, t in tables.items():
+            setattr(rope, name, t)
 
 
 def full_rotation(head: torch.nn.Module, cfg) -> None:
@@ -87,7 +110,18 @@ def test_config2_actions_match_oracle_bf16(c2):
     args = [inp[k].to(BF) if inp[k].is_floating_point() else inp[k]
             for k in ("vl", "state", "embodiment_id", "init_noise", "physics_hist", "physics_noise")]
     ref16 = om.denoise(head, *args, cfg.num_steps)
-    assert_actions_close(out, ref16)
+    assert_actions_close(out, ref16, fp32_actions(head, args, cfg))
+
+
+def test_config2_rebinding_gives_the_same_bits(c2, cuda):
+    """A second handle bound from the same module replays to the same bits: the bind-time weight
+    copies and re-layouts are ordered (a race there leaves some weights half copied)."""
+    _, head, _, dev, _, out = c2
+    again = B200ExpandedActionHeadChain(head, cuda)
+    names = ("vl", "state", "embodiment_id", "init_noise", "physics_hist", "physics_noise")
+    out2 = again(*[dev[k] for k in names]).cpu()
+    assert torch.equal(out2, out)
+    del again
 
 
 @pytest.mark.parametrize("step", [0, 3])
@@ -136,7 +170,7 @@ def test_full_rotation_rope_through_the_chain(cuda):
         d = [a.to(cuda) for a in args]
         out = chain(*d).cpu()
         assert chain._cfg.rope_cos_only == 0
-        assert_actions_close(out, ref16)
+        assert_actions_close(out, ref16, fp32_actions(head, args, cfg))
         # the cos-only form of the same weights gives other actions: the rotation really ran
         head_c = fast_init(om.ActionHead(cfg), seed=3, cuda=cuda).to(BF)
         out_c = B200ExpandedActionHeadChain(head_c, cuda)(*d).cpu()
