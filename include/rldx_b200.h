@@ -105,6 +105,10 @@ typedef struct {
   int L, Lp, H, tok_off;
   float eps;
   int tile_n; /* 0 = choose automatically, else 64/128/192/256 */
+  /* RLDX_EPI_QKV: 1 promises that the RoPE of every row of this problem is the identity (cos 1,
+   * sin 0 in its table rows, e.g. position 0 on every axis): the epilogue then skips the tables.
+   * 0 (the safe default) reads them. */
+  int rope_identity;
 } rldx_gemm_desc;
 
 /* Runs up to 4 independent problems in one persistent launch (no K split). */

@@ -44,7 +44,7 @@ class GemmDesc(C.Structure):
         ("q", vp), ("k", vp), ("vt", vp),
         ("L", C.c_int), ("Lp", C.c_int), ("H", C.c_int), ("tok_off", C.c_int),
         ("eps", C.c_float),
-        ("tile_n", C.c_int),
+        ("tile_n", C.c_int), ("rope_identity", C.c_int),
     ]
 
 

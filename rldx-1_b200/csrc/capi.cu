@@ -446,11 +446,12 @@ double pair_makespan(const ProbShape* sh, int n, int nsm) {
   return lpt_makespan(c, npairs);
 }
 
-// RLDX_GEMM_PAIR=0 keeps every launch on single-CTA tiles.
+// RLDX_GEMM_PAIR=0 keeps every launch on single-CTA tiles; =2 runs every launch that can on
+// CTA pairs (A/B measurement).
 int pair_mode() {
   static int v = [] {
     const char* e = std::getenv("RLDX_GEMM_PAIR");
-    return (e && e[0] == '0') ? 0 : 1;
+    return (e && e[0] == '0') ? 0 : (e && e[0] == '2') ? 2 : 1;
   }();
   return v;
 }
@@ -550,6 +551,7 @@ bool validate_gemm_problem(const rldx_gemm_desc& d, GemmProblem* p, std::string*
   e.H = d.H;
   e.tok_off = d.tok_off;
   e.eps = d.eps > 0.0f ? d.eps : 1e-6f;
+  e.rope_identity = d.rope_identity ? 1 : 0;
   return true;
 }
 
@@ -596,7 +598,7 @@ bool build_gemm_params(const rldx_gemm_desc* d, int n, void* ws, size_t ws_bytes
     large = large && d[i].M >= 512;
     tiles128 += static_cast<long long>((d[i].M + 127) / 128) * ((d[i].N + 127) / 128);
   }
-  if (pair && !(large && tiles128 >= 4LL * nsm)) {
+  if (pair && pair_mode() != 2 && !(large && tiles128 >= 4LL * nsm)) {
     const double single_mk = single_makespan(sh, n, nsm, best_bn, best_split);
     pair = pair_makespan(sh, n, nsm) < 0.9 * single_mk;
   }

@@ -10,6 +10,8 @@
 //   QK RMSNorm (weight then cast)     rldx/model/modules/norms.py:18-22
 //   RoPE on interleaved pairs         rldx/model/modules/action_model/ops.py:48-67
 //   Euler update                      rldx/model/core/rldx.py:716-723
+#include <type_traits>
+
 #include "gemm.cuh"
 
 namespace rldx {
@@ -104,9 +106,34 @@ struct PartSrc {
   size_t split_stride;  // floats between splits (= 128 * BN)
   int nsplit;
   static constexpr int kSplitsInFlight = 4;  // splits whose loads are issued before adding
+  // two groups: the loads of both (two splits at a time) are issued before their sums are formed,
+  // so one L2 round trip serves 16 columns
   __device__ __forceinline__ void get8x2(int c0, int c1, bool live, float (&v0)[8], float (&v1)[8]) const {
-    get8(c0, live, v0);
-    get8(c1, live, v1);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) v0[i] = v1[i] = 0.0f;
+    if (!live) return;
+    const float* b0 = col0 + static_cast<size_t>(c0) * 128;
+    const float* b1 = col0 + static_cast<size_t>(c1) * 128;
+#pragma unroll 1
+    for (int s0 = 0; s0 < nsplit; s0 += 2) {
+      float a0[2][8], a1[2][8];
+#pragma unroll
+      for (int t = 0; t < 2; ++t)
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const bool on = s0 + t < nsplit;
+          a0[t][i] = on ? __ldcg(b0 + (s0 + t) * split_stride + i * 128) : 0.0f;
+          a1[t][i] = on ? __ldcg(b1 + (s0 + t) * split_stride + i * 128) : 0.0f;
+        }
+#pragma unroll
+      for (int t = 0; t < 2; ++t)  // added in split order
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+          if (s0 + t < nsplit) {
+            v0[i] += a0[t][i];
+            v1[i] += a1[t][i];
+          }
+    }
   }
   __device__ __forceinline__ void get16(int col, bool live, float (&v)[16]) const {
     float a[8], b[8];
@@ -206,6 +233,39 @@ __device__ __forceinline__ void unit_epilogue(const GemmProblem& pr, const RowCt
     const bool packed = (kMode == kEpiStore) && (kAct == kActNone) && bias_mode != kBiasPostRound &&
                         ((ep.ldo | ep.col_off | ep.ld_add) & 7) == 0 && al16(ep.out) &&
                         (!ep.add || al16(ep.add)) && (!bias_row || al16(bias_row));
+    if constexpr (std::is_same<Src, PartSrc>::value) {
+      // the last unit of a K-split tile: two column groups per L2 round trip for the partials,
+      // their bias / residual loads issued in the same round
+#pragma unroll 1
+      for (int col = set * 8; col < bn; col += 16 * kEpiSets) {
+        const int colb = min(col + 8 * kEpiSets, bn - 8);
+        const bool second = col + 8 * kEpiSets < bn;
+        uint4 b0, a0, x0, b1, a1, x1;
+        fetch(col, b0, a0, x0);
+        fetch(second ? col + 8 * kEpiSets : bn, b1, a1, x1);
+        float v[2][8];
+        src.get8x2(col, colb, rc.live, v[0], v[1]);
+        if (!rc.live) continue;
+        const uint4 bb[2] = {b0, b1}, aa[2] = {a0, a1}, xx[2] = {x0, x1};
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const int c = col + h * 8 * kEpiSets;
+          const int n0 = n_base + c;
+          const int n = pr.N - n0;
+          if ((h == 1 && !second) || n <= 0) continue;
+          float y[8];
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            float t = act_fn<kAct>(finish_acc(v[h][i], bf_at(bb[h], i), bias_mode));
+            t = bf16r(t + bf_at(aa[h], i));
+            if constexpr (kMode == kEpiEuler) t = bf16r(bf_at(xx[h], i) + bf16r(dt * t));
+            y[i] = t;
+          }
+          store8q(orow + n0, n, y);
+        }
+      }
+      return;
+    }
     if (packed) {
 #pragma unroll 1
       for (int col = set * 8; col < bn; col = next_col(col)) {
@@ -319,6 +379,9 @@ __device__ __forceinline__ void unit_epilogue(const GemmProblem& pr, const RowCt
   } else {  // kEpiQKV: every 64 columns = one head of q, k or v; set s takes heads s, s+kEpiSets, ...
     const int inner = ep.H * 64;
     const int tok = ep.tok_off + rc.t;
+    // rows whose RoPE is the identity (cos 1, sin 0) read no tables: their per-row table loads
+    // are the epilogue's L1 misses (bias and norm weights are shared by every row)
+    const bool rope = !ep.rope_identity;
 #pragma unroll 1
     for (int c = 64 * set; c < bn; c += 64 * kEpiSets) {
       const int n0 = n_base + c;
@@ -334,7 +397,8 @@ __device__ __forceinline__ void unit_epilogue(const GemmProblem& pr, const RowCt
         const float4 z4 = make_float4(0.f, 0.f, 0.f, 0.f);
         // operands of pass 2's first group: in flight during pass 1
         uint4 nw = load8q(w, rc.live, 8);
-        float4 nc = rc.live ? cp[0] : z4, ns = rc.live ? sp[0] : z4;
+        const float4 one4 = make_float4(1.f, 1.f, 1.f, 1.f);
+        float4 nc = (rc.live && rope) ? cp[0] : one4, ns = (rc.live && rope) ? sp[0] : z4;
         float ss = 0.0f;
         uint4 nb = load8q(hb, rc.live && hb, 8);
         uint4 nb2 = load8q(hb + 8, rc.live && hb, 8);
@@ -360,8 +424,8 @@ __device__ __forceinline__ void unit_epilogue(const GemmProblem& pr, const RowCt
           const bool more = rc.live && g + 8 < 64;
           nb = load8q(hb + g + 8, more && hb, 8);
           nw = load8q(w + g + 8, more, 8);
-          nc = more ? cp[g / 8 + 1] : z4;
-          ns = more ? sp[g / 8 + 1] : z4;
+          nc = (more && rope) ? cp[g / 8 + 1] : one4;
+          ns = (more && rope) ? sp[g / 8 + 1] : z4;
           float v[8];
           src.get8(c + g, rc.live, v);
           if (!rc.live) continue;
@@ -374,8 +438,13 @@ __device__ __forceinline__ void unit_epilogue(const GemmProblem& pr, const RowCt
             const float x1 = finish_acc(v[2 * p + 1], bf_at(bq, 2 * p + 1), kBiasFused);
             const float a = bf16r(bf_at(wq, 2 * p) * (x0 * rstd));
             const float b = bf16r(bf_at(wq, 2 * p + 1) * (x1 * rstd));
-            y[2 * p] = bf16r(a * cc[p] - b * sv[p]);
-            y[2 * p + 1] = bf16r(a * sv[p] + b * cc[p]);
+            if (rope) {
+              y[2 * p] = bf16r(a * cc[p] - b * sv[p]);
+              y[2 * p + 1] = bf16r(a * sv[p] + b * cc[p]);
+            } else {  // cos 1, sin 0: the rotation returns a and b (bf16 already)
+              y[2 * p] = a;
+              y[2 * p + 1] = b;
+            }
           }
           store8q(dst + g, 8, y);
         }

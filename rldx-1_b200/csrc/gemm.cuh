@@ -18,9 +18,11 @@
 //               into one of two TMEM accumulators (2 x 256 columns), so the epilogue of one
 //               unit overlaps the main loop of the next.
 //   warps 3..    epilogue: kEpiSets warps per TMEM lane quadrant (thread = output row) split
-//               the unit's columns; tcgen05.ld of 8 fp32 columns at a time and the fused row
-//               epilogue (bias / activation / residual / SwiGLU / QK-RMSNorm+RoPE / Euler
-//               update), written straight to global memory.  K-split units write fp32
+//               the unit's columns.  A unit's operands (bias, residual, norm weights, RoPE
+//               rows) are fetched before its accumulator is ready, then tcgen05.ld brings up to
+//               32 fp32 columns per wait into the fused row epilogue (bias / activation /
+//               residual / SwiGLU / QK-RMSNorm+RoPE / Euler update), written straight to
+//               global memory.  K-split units write fp32
 //               partial tiles to a workspace; the last of a tile's units to finish (arrival
 //               counter) adds the partials in split order and runs the epilogue, so results do
 //               not depend on which CTA finishes last.
@@ -78,6 +80,7 @@ struct GemmEpilogue {
   __nv_bfloat16* vt;      // [B, H, 64, Lp]
   int L, Lp, H, tok_off;
   float eps;
+  int rope_identity;  // every row's RoPE is the identity (cos 1, sin 0): the tables are not read
 };
 
 struct __align__(64) GemmProblem {

@@ -146,6 +146,8 @@ struct rldx_msat {
   int sdp = 0, adp = 0;  // padded state / action dims (multiples of 8)
 
   float *rope_cos = nullptr, *rope_sin = nullptr;
+  // host copies of the two [L, 32] tables (double blocks, single blocks): which rows rotate
+  std::vector<float> host_cos[2], host_sin[2];
   bf16 *time_tok = nullptr, *ada_sc1p = nullptr, *ada_shift = nullptr, *pada_sc1p = nullptr,
        *pada_shift = nullptr;
 
@@ -399,6 +401,16 @@ struct rldx_msat {
     d.tok_off = tok_off;
     d.rows_in = rows;
     d.rows_out = rows;
+    // rows whose table entries are all cos 1 / sin 0 (position 0 on both axes: the VL tokens
+    // under rope_sa_only) need no rotation: the epilogue then reads no tables
+    const int which = (rc == rope_cos) ? 0 : 1;
+    bool identity = !host_cos[which].empty();
+    for (int t = tok_off; identity && t < tok_off + rows; ++t)
+      for (int p = 0; p < 32 && identity; ++p)
+        identity = host_cos[which][static_cast<size_t>(t) * 32 + p] == 1.0f &&
+                   host_sin[which][static_cast<size_t>(t) * 32 + p] == 0.0f;
+    d.rope_identity = identity ? 1 : 0;
+    (void)rs;
     return d;
   }
 
@@ -751,7 +763,7 @@ void rldx_msat::precompute(const rldx_msat_weights& w) {
     mod_cos[0].clear();
     mod_cos[1].clear();
   }
-  auto table = [&](int sa_start, float** dcos, float** dsin) {
+  auto table = [&](int sa_start, float** dcos, float** dsin, int which) {
     std::vector<float> hc_cos(static_cast<size_t>(L) * 32), hc_sin(static_cast<size_t>(L) * 32);
     for (int t = 0; t < L; ++t) {
       int id0 = 0, id1 = 0;
@@ -794,10 +806,12 @@ void rldx_msat::precompute(const rldx_msat_weights& w) {
     *dsin = alloc<float>(hc_sin.size());
     copy(*dcos, hc_cos.data(), hc_cos.size() * 4, "rope");
     copy(*dsin, hc_sin.data(), hc_sin.size() * 4, "rope");
-    ck(cudaStreamSynchronize(stream), "rope sync");  // the host tables go out of scope
+    ck(cudaStreamSynchronize(stream), "rope sync");
+    host_cos[which] = std::move(hc_cos);
+    host_sin[which] = std::move(hc_sin);
   };
-  table(c.rope_mode == RLDX_ROPE_SA_ONLY ? 1 : 2, &rope_cos, &rope_sin);
-  if (c.depth_single > 0) table(2, &rope_cos_s, &rope_sin_s);
+  table(c.rope_mode == RLDX_ROPE_SA_ONLY ? 1 : 2, &rope_cos, &rope_sin, 0);
+  if (c.depth_single > 0) table(2, &rope_cos_s, &rope_sin_s, 1);
 
   // ---- timestep embedding per Euler step (ops.py:123-133), baked like
   //      custom_expanded_action_model_chain.py:57-66 ----

@@ -133,7 +133,7 @@ def linear(x, weight, bias=None, *, act=_lib.ACT_NONE, bias_mode=_lib.BIAS_FUSED
 
 
 def qkv_desc(x, weight, bias, q_norm, k_norm, rope_cos, rope_sin, q, k, vt, *, tok_off: int,
-             rows_per_batch: int, tile_n: int = 0) -> GemmDesc:
+             rows_per_batch: int, tile_n: int = 0, rope_identity: bool = False) -> GemmDesc:
     """QKV projection of one stream with fused per-head RMSNorm + RoPE, scattered into the joint
     attention layout q, k [B, H, L, 64] and vt [B, H, 64, Lp]."""
     B, H, L, hd = q.shape
@@ -149,6 +149,7 @@ def qkv_desc(x, weight, bias, q_norm, k_norm, rope_cos, rope_sin, q, k, vt, *, t
     d.rope_cos, d.rope_sin = rope_cos.data_ptr(), rope_sin.data_ptr()
     d.q, d.k, d.vt = q.data_ptr(), k.data_ptr(), vt.data_ptr()
     d.L, d.Lp, d.H, d.tok_off = L, vt.shape[-1], H, tok_off
+    d.rope_identity = 1 if rope_identity else 0
     return d
 
 
