@@ -355,6 +355,10 @@ typedef struct {
   int prefix_len;      /* RTC trained mode: first prefix_len actions locked to
                           io.prefix_actions, encoded at t = 1 (graph_safe_action_model.py:196-300;
                           custom_action_model_chain.py:86-165); 0 = off                       */
+  int key_mask;        /* 1: steps may pass key masks (io.vl_mask / io.physics_mask): a second
+                          graph whose attention masks those keys is captured beside the
+                          unmasked one (rldx/model/modules/action_model/blocks.py:557-576,
+                          843-864; msat.py:517-531, 716-745)                                  */
 } rldx_msat_config;
 
 typedef struct {
@@ -422,6 +426,14 @@ typedef struct {
   const void* physics_noise; /* [B, physics_fut, physics_dim] bf16 (NULL: standard)    */
   void* actions;             /* out: [B, horizon, action_dim] bf16                      */
   const void* prefix_actions; /* [B, prefix_len, action_dim] bf16 (NULL when prefix_len 0) */
+  /* Key masks (handles created with key_mask = 1; NULL = every key visible): uint8, nonzero =
+   * visible.  vl_mask [B, n_vl] masks backbone tokens as keys of every block (the reference's
+   * backbone_attention_mask, rldx/model/core/rldx.py:619-621); physics_mask [B] masks all physics
+   * tokens of an observation (PhysicsInferenceState.attn_mask, physics_head.py:232-244; the
+   * all-modality path only).  Action / state / time keys are always visible.  An all-ones mask
+   * gives the unmasked result. */
+  const uint8_t* vl_mask;
+  const uint8_t* physics_mask;
 } rldx_msat_io;
 
 /* Copies and re-lays out the weights into a device arena owned by the handle, precomputes the

@@ -207,6 +207,12 @@ class SwiGLUFFN(nn.Module):
         return self.w3(F.silu(x1) * x2)
 
 
+def _key_mask(parts, dtype):
+    """Additive SDPA mask over the concatenated key segments: -inf where a key is masked (0)."""
+    kv = torch.cat(parts, dim=1)[:, None, None, :]
+    return torch.where(kv == 0, torch.tensor(float("-inf"), dtype=dtype), torch.tensor(0.0, dtype=dtype))
+
+
 def _split_heads(x, h):
     B, N, D = x.shape
     return x.view(B, N, h, D // h).permute(0, 2, 1, 3).contiguous()
@@ -452,25 +458,35 @@ class MSAT(nn.Module):
             ids[:, n_x:, 1] = torch.arange(n_p)
         return ids
 
-    def forward_standard(self, hidden_states, encoder_hidden_states, timestep, return_hidden=False):
-        """Standard path without physics (msat.py:363-556)."""
+    def forward_standard(self, hidden_states, encoder_hidden_states, timestep, return_hidden=False,
+                         encoder_attention_mask=None):
+        """Standard path without physics (msat.py:363-556); a VL key mask as blocks.py:557-576 and
+        msat.py:517-531 (VL keys masked, time / S / A keys always visible)."""
         temb = self.timestep_encoder(timestep)
         time_token = self.time_token_proj(temb).unsqueeze(1)
         sa = torch.cat([time_token, hidden_states], dim=1)
         vl = encoder_hidden_states
         B = sa.shape[0]
         pe = self.rope_embedder(self.position_ids_standard(B, vl.shape[1], sa.shape[1]))
+        mask = None
+        if encoder_attention_mask is not None:
+            vm = encoder_attention_mask
+            mask = _key_mask([vm, torch.ones(B, sa.shape[1], dtype=vm.dtype)], sa.dtype)
         hidden = []
         for blk in self.double_blocks:
-            sa, vl = blk(sa, vl, pe)
+            sa, vl = blk(sa, vl, pe, mask)
             if return_hidden:
                 hidden.append((sa, vl))
         time_token, sa = sa[:, :self.num_temb_tokens], sa[:, self.num_temb_tokens:]
         if len(self.single_blocks):
             x = torch.cat([self.vl_proj_to_sa(vl), time_token, sa], dim=1)
             pe_s = self.rope_embedder(self.position_ids_single(B, vl.shape[1], sa.shape[1]))
+            mask_s = None
+            if encoder_attention_mask is not None:
+                vm = encoder_attention_mask
+                mask_s = _key_mask([vm, torch.ones(B, x.shape[1] - vl.shape[1], dtype=vm.dtype)], x.dtype)
             for blk in self.single_blocks:
-                x = blk(x, pe_s)
+                x = blk(x, pe_s, mask_s)
                 if return_hidden:
                     hidden.append((x,))
             sa = x[:, -sa.shape[1]:]
@@ -482,7 +498,8 @@ class MSAT(nn.Module):
     def forward(self, hidden_states, encoder_hidden_states, timestep, physics_embs=None,
                 encoder_attention_mask=None, physics_attention_mask=None, return_hidden=False):
         if not self.use_physics:
-            return self.forward_standard(hidden_states, encoder_hidden_states, timestep, return_hidden)
+            return self.forward_standard(hidden_states, encoder_hidden_states, timestep, return_hidden,
+                                         encoder_attention_mask)
         temb = self.timestep_encoder(timestep)
         time_token = self.time_token_proj(temb).unsqueeze(1)
         sa = torch.cat([time_token, hidden_states], dim=1)
@@ -508,8 +525,18 @@ class MSAT(nn.Module):
         if len(self.single_blocks):
             x = torch.cat([self.vl_proj_to_sa(vl), time_token, sa], dim=1)
             pe_s = self.rope_embedder(self.position_ids_single(B, vl.shape[1], sa.shape[1], p.shape[1]))
+            mask_s = None  # [VL_proj + time + S/A | P] (msat.py:716-745)
+            if encoder_attention_mask is not None or physics_attention_mask is not None:
+                if encoder_attention_mask is not None:
+                    vm = encoder_attention_mask
+                    xm = torch.cat([vm, torch.ones(B, x.shape[1] - vl.shape[1], dtype=vm.dtype)], dim=1)
+                else:
+                    xm = torch.ones(B, x.shape[1], dtype=x.dtype)
+                pm = (physics_attention_mask[:, None].expand(-1, p.shape[1]).to(xm.dtype)
+                      if physics_attention_mask is not None else torch.ones(B, p.shape[1], dtype=xm.dtype))
+                mask_s = _key_mask([xm, pm], x.dtype)
             for blk in self.single_blocks:
-                x, p = blk(x, pe_s, None, p)
+                x, p = blk(x, pe_s, mask_s, p)
                 if return_hidden:
                     hidden.append((x, p))
             sa = x[:, -sa.shape[1]:]
@@ -657,13 +684,21 @@ def init_weights(module: nn.Module, seed: int, std: float = 0.02) -> nn.Module:
 
 @torch.no_grad()
 def denoise(head: nn.Module, vl_embs, state, embodiment_id, init_noise, physics_hist=None,
-            physics_noise=None, num_steps: int = 4, return_trace: bool = False, prefix_actions=None):
+            physics_noise=None, num_steps: int = 4, return_trace: bool = False, prefix_actions=None,
+            vl_mask=None, physics_mask=None):
     """Control step with vanilla_action_head_forward semantics (benchmark_action_model.py:50-123).
 
     prefix_actions (B, d, action_dim): RTC trained-mode inpainting as GraphSafeActionModel.forward
     (graph_safe_action_model.py:196-300): the first d action tokens are locked to the prefix
     before every action encoding and after every Euler update, and their encoder time is 1.0
-    while the others use the step's t."""
+    while the others use the step's t.
+
+    vl_mask (B, n_vl) / physics_mask (B,): key masks (1 = visible) of the backbone tokens and of
+    each observation's physics tokens, as get_action_with_features passes them to MSAT
+    (rldx/model/core/rldx.py:619-621, 660-666; physics_head.py:232-244); an all-ones VL mask is
+    dropped like the reference does."""
+    if vl_mask is not None and bool(vl_mask.all()):
+        vl_mask = None
     msat = head.model
     dt = 1.0 / num_steps
     vl = head.vlln(vl_embs)
@@ -697,7 +732,7 @@ def denoise(head: nn.Module, vl_embs, state, embodiment_id, init_noise, physics_
         trace = []
         for t in range(num_steps):
             timesteps, sa = encode(t)
-            out, hidden = msat(sa, vl, timesteps, return_hidden=True)
+            out, hidden = msat(sa, vl, timesteps, encoder_attention_mask=vl_mask, return_hidden=True)
             current = euler(current, out)
             if return_trace:
                 trace.append({"hidden": hidden, "out": out, "actions": current})
@@ -709,7 +744,8 @@ def denoise(head: nn.Module, vl_embs, state, embodiment_id, init_noise, physics_
     for t in range(num_steps):
         timesteps, sa = encode(t)
         pe = torch.cat([physics_hist_tok, phys.physics_fut_encoder(physics_fut, timesteps)], dim=1)
-        out, hidden = msat(sa, vl, timesteps, pe, return_hidden=True)
+        out, hidden = msat(sa, vl, timesteps, pe, encoder_attention_mask=vl_mask,
+                           physics_attention_mask=physics_mask, return_hidden=True)
         current = euler(current, out)
         physics_fut = physics_fut + dt * phys.physics_decoder(out["physics"][:, -phys.physics_fut_len:])
         if return_trace:

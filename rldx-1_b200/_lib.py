@@ -60,6 +60,7 @@ class MsatConfig(C.Structure):
         ("rope_max_seq", C.c_int), ("temb_channels", C.c_int), ("use_graph", C.c_int),
         ("standard_path", C.c_int), ("vl_dim", C.c_int), ("depth_single", C.c_int),
         ("single_expanded", C.c_int), ("single_mlp_hidden", C.c_int), ("prefix_len", C.c_int),
+        ("key_mask", C.c_int),
     ]
 
 
@@ -155,7 +156,7 @@ class LlmWeights(C.Structure):
 class MsatIO(C.Structure):
     _fields_ = [("vl", vp), ("state", vp), ("emb_id", vp), ("init_noise", vp),
                 ("physics_hist", vp), ("physics_noise", vp), ("actions", vp),
-                ("prefix_actions", vp)]
+                ("prefix_actions", vp), ("vl_mask", vp), ("physics_mask", vp)]
 
 
 # Every exported symbol of include/rldx_b200.h with its ctypes signature.

@@ -171,6 +171,7 @@ class _B200HeadChain(nn.Module):
         c.temb_channels = msat.timestep_encoder.timestep_embedder.linear_1.weight.shape[1]
         c.use_graph = 1 if self.use_graph else 0
         c.prefix_len = self.prefix_len
+        c.key_mask = 1  # masked steps replay a second graph; unmasked ones pay nothing for it
         if not isinstance(getattr(msat, "time_token_proj", nn.Identity()), nn.Identity):
             raise NotImplementedError("time_token_proj must be the identity (inner_dim == sa_dim)")
         return c
@@ -264,7 +265,7 @@ class _B200HeadChain(nn.Module):
 
     # ------------------------------------------------------------------ forward
     def _step(self, vl_embs, state, embodiment_id, init_noise, physics_hist, physics_init_noise,
-              prefix_actions):
+              prefix_actions, vl_attention_mask=None, physics_attention_mask=None):
         B, n_vl, _ = vl_embs.shape
         if self.prefix_len and prefix_actions is None:
             raise ValueError(f"this chain was built with prefix_len={self.prefix_len}: prefix_actions is required")
@@ -305,9 +306,18 @@ class _B200HeadChain(nn.Module):
                                  f"got {tuple(prefix_actions.shape)}")
             pre = _in(prefix_actions)
             pre_ptr = pre.data_ptr()
+        vm_ptr = pm_ptr = None
+        if vl_attention_mask is not None:
+            vm = _in((vl_attention_mask != 0).reshape(B, n_vl), torch.uint8)
+            vm_ptr = vm.data_ptr()
+        if physics_attention_mask is not None:
+            if not self._physics:
+                raise ValueError("physics_attention_mask needs the physics stream")
+            pm = _in((physics_attention_mask != 0).reshape(B), torch.uint8)
+            pm_ptr = pm.data_ptr()
         out = torch.empty(B, horizon, self.action_dim, dtype=bf, device=dev)
         io = MsatIO(vl.data_ptr(), st.data_ptr(), ids.data_ptr(), noise.data_ptr(), ph_ptr,
-                    pn_ptr, out.data_ptr(), pre_ptr)
+                    pn_ptr, out.data_ptr(), pre_ptr, vm_ptr, pm_ptr)
         stream = torch.cuda.current_stream(dev)
         # a device error recorded by an earlier (asynchronous) step surfaces here, before more
         # work is queued behind it
@@ -349,8 +359,10 @@ class _B200HeadChain(nn.Module):
         ph = inp["physics_hist"].data_ptr() if self._physics else None
         pn = inp["physics_noise"].data_ptr() if self._physics else None
         pre = inp["prefix_actions"].data_ptr() if self.prefix_len else None
+        vm = inp["vl_mask"].data_ptr() if inp.get("vl_mask") is not None else None  # uint8 [B, n_vl]
+        pm = inp["physics_mask"].data_ptr() if inp.get("physics_mask") is not None else None  # uint8 [B]
         return MsatIO(inp["vl"].data_ptr(), inp["state"].data_ptr(), inp["embodiment_id"].data_ptr(),
-                      inp["init_noise"].data_ptr(), ph, pn, out.data_ptr(), pre)
+                      inp["init_noise"].data_ptr(), ph, pn, out.data_ptr(), pre, vm, pm)
 
     def forward_host(self, inp: dict, out: torch.Tensor) -> torch.Tensor:
         """One control step from (pinned) host tensors to a host tensor through
@@ -406,11 +418,16 @@ class B200ExpandedActionHeadChain(_B200HeadChain):
     _physics = True
 
     def forward(self, vl_embs, state, embodiment_id, init_noise=None, physics_hist=None,
-                physics_init_noise=None, prefix_actions=None):
+                physics_init_noise=None, prefix_actions=None, vl_attention_mask=None,
+                physics_attention_mask=None):
+        """vl_attention_mask [B, n_vl] (1 = visible) / physics_attention_mask [B]: key masks of the
+        backbone tokens and of each observation's physics tokens, as the reference passes
+        backbone_attention_mask and physics_mask to MSAT (rldx/model/core/rldx.py:619-621, 660-666);
+        the reference's graph-safe chains take no masks."""
         if physics_hist is None:
             raise ValueError("physics_hist is required by the all-modality chain")
         return self._step(vl_embs, state, embodiment_id, init_noise, physics_hist, physics_init_noise,
-                          prefix_actions)
+                          prefix_actions, vl_attention_mask, physics_attention_mask)
 
 
 class B200ActionHeadChain(_B200HeadChain):
@@ -418,5 +435,9 @@ class B200ActionHeadChain(_B200HeadChain):
 
     _physics = False
 
-    def forward(self, vl_embs, state, embodiment_id, init_noise=None, prefix_actions=None, **kwargs):
-        return self._step(vl_embs, state, embodiment_id, init_noise, None, None, prefix_actions)
+    def forward(self, vl_embs, state, embodiment_id, init_noise=None, prefix_actions=None,
+                vl_attention_mask=None, **kwargs):
+        """vl_attention_mask [B, n_vl] (1 = visible): key mask of the backbone tokens
+        (rldx/model/core/rldx.py:619-621)."""
+        return self._step(vl_embs, state, embodiment_id, init_noise, None, None, prefix_actions,
+                          vl_attention_mask)

@@ -176,6 +176,11 @@ cudaError_t launch_transpose_cat(const __nv_bfloat16* src, __nv_bfloat16* dst, i
 cudaError_t launch_elementwise(const __nv_bfloat16* x, __nv_bfloat16* y, long long n, int mode,
                                cudaStream_t stream);
 
+// kmask [B, L]: VL keys (t < nvl) from vl [B, nvl], then nsa visible keys, then the physics
+// keys from p [B] (nonzero = visible)
+cudaError_t launch_key_mask(uint8_t* kmask, const uint8_t* vl, const uint8_t* p, int B, int L, int nvl,
+                            int nsa, cudaStream_t stream);
+
 cudaError_t gemm_prepare_device();
 
 }  // namespace rldx

@@ -36,7 +36,7 @@ namespace {
 using bf16 = __nv_bfloat16;
 
 struct Op {
-  enum Kind { kGemm, kAttn, kLn, kCopy, kStatus } kind;
+  enum Kind { kGemm, kAttn, kLn, kCopy, kStatus, kMask } kind;
   int grid;
   double bytes, flops;  // algorithmic traffic / work of the launch
   GemmParams g;
@@ -158,6 +158,12 @@ struct rldx_msat {
   std::vector<bf16*> act_cat, phf_cat;
 
   std::vector<Op> ops;
+  // Masked form of the step (cfg.key_mask): the same launches, the attention ones reading the key
+  // mask kmask [B, L], built in the graph from the per-step inputs vlmask_in / pmask_in
+  std::vector<Op> ops_m;
+  uint8_t *kmask = nullptr, *vlmask_in = nullptr, *pmask_in = nullptr;
+  cudaGraph_t graph_m = nullptr;
+  cudaGraphExec_t exec_m = nullptr;
   // block_marks[step * nblocks + i]: launches from the start of the list up to and including
   // the last one of block i (double blocks, then single blocks) of Euler step `step`
   std::vector<int> block_marks;
@@ -465,13 +471,14 @@ struct rldx_msat {
     ops.push_back(o);
   }
 
-  // Launches ops [0, n) (all of them when n < 0).
-  void run_ops(cudaStream_t st, cudaEvent_t* ev = nullptr, int n = -1) {
+  // Launches ops [0, n) of `list` (all of them when n < 0; `list` null: the unmasked step).
+  void run_ops(cudaStream_t st, cudaEvent_t* ev = nullptr, int n = -1, const std::vector<Op>* list = nullptr) {
+    const std::vector<Op>& L_ = list ? *list : ops;
     if (ev) ck(cudaEventRecord(ev[0], st), "event");
-    const size_t end = n < 0 ? ops.size() : std::min(ops.size(), static_cast<size_t>(n));
+    const size_t end = n < 0 ? L_.size() : std::min(L_.size(), static_cast<size_t>(n));
     for (size_t i = 0; i < end; ++i) {
-      const Op& o = ops[i];
-      const bool p = pdl && i > 0 && !ev && ops[i - 1].kind != Op::kStatus;
+      const Op& o = L_[i];
+      const bool p = pdl && i > 0 && !ev && L_[i - 1].kind != Op::kStatus && L_[i - 1].kind != Op::kMask;
       cudaError_t e = cudaSuccess;
       switch (o.kind) {
         case Op::kGemm:
@@ -489,10 +496,25 @@ struct rldx_msat {
         case Op::kStatus:
           e = launch_status_take(o.slot, st);
           break;
+        case Op::kMask:
+          e = launch_key_mask(kmask, vlmask_in, pmask_in, B, L, nvl, nsa, st);
+          break;
       }
       ck(e, "launch");
       if (ev) ck(cudaEventRecord(ev[i + 1], st), "event");
     }
+  }
+
+  // Per-step key masks into the static mask inputs (an absent mask: every key visible).
+  void copy_masks(const rldx_msat_io* io, cudaStream_t st) {
+    if (io->vl_mask)
+      ck(cudaMemcpyAsync(vlmask_in, io->vl_mask, static_cast<size_t>(B) * nvl, cudaMemcpyDefault, st), "vl_mask");
+    else
+      ck(cudaMemsetAsync(vlmask_in, 1, static_cast<size_t>(B) * nvl, st), "vl_mask");
+    if (io->physics_mask)
+      ck(cudaMemcpyAsync(pmask_in, io->physics_mask, static_cast<size_t>(B), cudaMemcpyDefault, st), "physics_mask");
+    else
+      ck(cudaMemsetAsync(pmask_in, 1, static_cast<size_t>(B), st), "physics_mask");
   }
 
   void copy_inputs(const rldx_msat_io* io, cudaStream_t st) {
@@ -707,9 +729,25 @@ void rldx_msat::create(const rldx_msat_config& cfg, const rldx_msat_weights& w) 
     }
   }
   plan();
+  if (c.key_mask) {
+    kmask = alloc<uint8_t>(static_cast<size_t>(B) * L);
+    vlmask_in = alloc<uint8_t>(static_cast<size_t>(B) * nvl);
+    pmask_in = alloc<uint8_t>(B);
+    ck(cudaMemsetAsync(vlmask_in, 1, static_cast<size_t>(B) * nvl, stream), "mask fill");
+    ck(cudaMemsetAsync(pmask_in, 1, B, stream), "mask fill");
+    ops_m = ops;
+    for (Op& o : ops_m)
+      if (o.kind == Op::kAttn) o.a.key_mask = kmask;
+    Op m;
+    std::memset(&m, 0, sizeof(m));
+    m.kind = Op::kMask;
+    m.grid = 1;
+    ops_m.insert(ops_m.begin() + 1, m);  // after the opening status launch
+  }
 
   // Warm-up run (loads every kernel), then capture.
   run_ops(stream);
+  if (c.key_mask) run_ops(stream, nullptr, -1, &ops_m);
   ck(cudaEventRecord(status.done, stream), "status event");
   ck(cudaStreamSynchronize(stream), "warm-up");
   unsigned int derr = 0, during = 0;
@@ -728,6 +766,20 @@ void rldx_msat::create(const rldx_msat_config& cfg, const rldx_msat_weights& w) 
     ck(cudaStreamEndCapture(stream, &graph), "end capture");
     ck(cudaGraphInstantiate(&exec, graph, 0), "instantiate");
     ck(cudaGraphUpload(exec, stream), "upload");
+    if (c.key_mask) {
+      ck(cudaStreamBeginCapture(stream, cudaStreamCaptureModeThreadLocal), "begin capture");
+      try {
+        run_ops(stream, nullptr, -1, &ops_m);
+      } catch (...) {
+        cudaGraph_t g = nullptr;
+        cudaStreamEndCapture(stream, &g);
+        if (g) cudaGraphDestroy(g);
+        throw;
+      }
+      ck(cudaStreamEndCapture(stream, &graph_m), "end capture");
+      ck(cudaGraphInstantiate(&exec_m, graph_m, 0), "instantiate");
+      ck(cudaGraphUpload(exec_m, stream), "upload");
+    }
     ck(cudaStreamSynchronize(stream), "upload sync");
   }
 }
@@ -1159,6 +1211,8 @@ int guard(const std::function<void()>& f) {
 void free_all(rldx_msat* h) {
   if (h->exec) cudaGraphExecDestroy(h->exec);
   if (h->graph) cudaGraphDestroy(h->graph);
+  if (h->exec_m) cudaGraphExecDestroy(h->exec_m);
+  if (h->graph_m) cudaGraphDestroy(h->graph_m);
   for (void* p : h->allocs) cudaFree(p);
   if (h->stream) cudaStreamDestroy(h->stream);
   h->status.release();
@@ -1207,12 +1261,24 @@ static int msat_step_impl(rldx_msat* h, const rldx_msat_io* io, cudaStream_t st)
     return set_error(RLDX_ERR_ARG,
                      "msat_step: every io pointer is required (physics ones on the all-modality path, "
                      "prefix_actions with prefix_len > 0)");
+  const bool masked = io->vl_mask != nullptr || io->physics_mask != nullptr;
+  if (masked && !h->c.key_mask)
+    return set_error(RLDX_ERR_STATE, "msat_step: key masks need a handle created with key_mask = 1");
+  if (io->physics_mask && h->standard)
+    return set_error(RLDX_ERR_ARG, "msat_step: physics_mask on a head without the physics stream");
   return guard([&] {
     h->copy_inputs(io, st);
-    if (h->exec)
+    if (masked) {
+      h->copy_masks(io, st);
+      if (h->exec_m)
+        ck(cudaGraphLaunch(h->exec_m, st), "graph launch");
+      else
+        h->run_ops(st, nullptr, -1, &h->ops_m);
+    } else if (h->exec) {
       ck(cudaGraphLaunch(h->exec, st), "graph launch");
-    else
+    } else {
       h->run_ops(st);
+    }
     h->copy_outputs(io, st);
     ck(cudaEventRecord(h->status.done, st), "status event");
   });

@@ -93,6 +93,24 @@ cudaError_t launch_rows_add(__nv_bfloat16* x, const int* rows, int nrows, const 
   return cudaGetLastError();
 }
 
+// Key mask of the joint sequence [VL | SA | P] of every observation: VL keys from the backbone
+// mask, action / state / time keys visible, physics keys from the observation's physics mask.
+__global__ void key_mask_kernel(uint8_t* __restrict__ kmask, const uint8_t* __restrict__ vl,
+                                const uint8_t* __restrict__ p, int B, int L, int nvl, int nsa) {
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < B * L; i += gridDim.x * blockDim.x) {
+    const int b = i / L, t = i - b * L;
+    const uint8_t m = t < nvl ? vl[b * nvl + t] : (t < nvl + nsa ? 1 : p[b]);
+    kmask[i] = m != 0 ? 1 : 0;
+  }
+}
+
+cudaError_t launch_key_mask(uint8_t* kmask, const uint8_t* vl, const uint8_t* p, int B, int L, int nvl,
+                            int nsa, cudaStream_t stream) {
+  const int n = B * L;
+  key_mask_kernel<<<(n + 255) / 256 < 148 ? (n + 255) / 256 : 148, 256, 0, stream>>>(kmask, vl, p, B, L, nvl, nsa);
+  return cudaGetLastError();
+}
+
 cudaError_t launch_elementwise(const __nv_bfloat16* x, __nv_bfloat16* y, long long n, int mode,
                                cudaStream_t stream) {
   if (n <= 0) return cudaSuccess;

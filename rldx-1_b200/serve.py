@@ -107,9 +107,11 @@ class B200Dispatcher:
             if use_memory:
                 backbone_outputs = fm._apply_memory_inference(backbone_outputs, reset_memory)
         vl = _get(backbone_outputs, "backbone_features")
+        # masked backbone tokens: the VL key mask of every block; an all-ones mask is dropped, as
+        # get_action_with_features does (rldx/model/core/rldx.py:619-621)
         mask = _get(backbone_outputs, "backbone_attention_mask")
-        if mask is not None and not bool(torch.as_tensor(mask).all()):
-            return self._drift(merged, "masked backbone tokens (backbone_attention_mask) are not bound")
+        if mask is not None and bool(torch.as_tensor(mask).all()):
+            mask = None
         state = _get(action_inputs, "state")
         emb = _get(action_inputs, "embodiment_id")
         device, dtype = vl.device, torch.bfloat16
@@ -118,13 +120,14 @@ class B200Dispatcher:
         horizon = int(getattr(am, "action_horizon", None) or am.config.action_horizon)
         action_dim = am.action_decoder.layer2.W.shape[2]
 
-        physics_hist = physics_noise = None
+        physics_hist = physics_noise = physics_mask = None
         if self._has_physics:
             ph = _get(action_inputs, "physics")
             if ph is None:
                 return self._drift(merged, "the physics head needs action_input.physics")
             hist_len, fut_len = am.physics.physics_hist_len, am.physics.physics_fut_len
             physics_hist = ph[:, :hist_len].to(device=device, dtype=dtype)
+            physics_mask = _get(action_inputs, "physics_mask")  # PhysicsHead.prepare_inference's attn_mask
             # drawn first, as PhysicsHead.prepare_inference does (physics_head.py:232-268)
             physics_noise = torch.randn(B, fut_len, am.physics.physics_dim, dtype=dtype, device=device)
         init_noise = torch.randn(B, horizon, action_dim, dtype=dtype, device=device)
@@ -146,9 +149,11 @@ class B200Dispatcher:
         try:
             if self._has_physics:
                 actions = self._chain(vl, state, emb, init_noise, physics_hist=physics_hist,
-                                      physics_init_noise=physics_noise, prefix_actions=prefix)
+                                      physics_init_noise=physics_noise, prefix_actions=prefix,
+                                      vl_attention_mask=mask,
+                                      physics_attention_mask=None if physics_mask is None else physics_mask.view(-1))
             else:
-                actions = self._chain(vl, state, emb, init_noise, prefix_actions=prefix)
+                actions = self._chain(vl, state, emb, init_noise, prefix_actions=prefix, vl_attention_mask=mask)
         except ValueError as e:
             if "differ from the bound shapes" in str(e):
                 return self._drift(merged, str(e))

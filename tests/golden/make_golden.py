@@ -142,10 +142,15 @@ def run_reference_loop(R, head, cfg, inp, prefix_actions=None):
                   physics_hist=inp["physics_hist"], physics_init_noise=inp["physics_noise"], **extra)
 
 
-def run_vanilla_loop(head, cfg, inp):
+def run_vanilla_loop(head, cfg, inp, vl_mask=None, physics_mask=None):
     """vanilla_action_head_forward (benchmark_action_model.py:50-123) around the reference
     modules; unlike GraphSafeActionModel (whose static RoPE table is built for batch 1) it
-    accepts any batch."""
+    accepts any batch.  vl_mask / physics_mask go to MSAT as encoder_attention_mask /
+    physics_attention_mask, as get_action_with_features passes them
+    (rldx/model/core/rldx.py:619-621, 660-666)."""
+    masks = {}
+    if vl_mask is not None:
+        masks["encoder_attention_mask"] = vl_mask
     with torch.no_grad():
         dt = 1.0 / cfg.num_steps
         vl, B = inp["vl"], inp["vl"].shape[0]
@@ -156,7 +161,8 @@ def run_vanilla_loop(head, cfg, inp):
             for t in range(cfg.num_steps):
                 ts = torch.tensor([t / float(cfg.num_steps)], dtype=vl.dtype).expand(B)
                 af = head.action_encoder(cur, ts, inp["embodiment_id"]) + pos
-                mo = head.model(hidden_states=torch.cat([sf, af], 1), encoder_hidden_states=vl, timestep=ts)
+                mo = head.model(hidden_states=torch.cat([sf, af], 1), encoder_hidden_states=vl, timestep=ts,
+                                **masks)
                 cur = cur + dt * head.action_decoder(mo, inp["embodiment_id"])[:, -cfg.horizon:]
             return cur
         phys = head.physics
@@ -166,8 +172,10 @@ def run_vanilla_loop(head, cfg, inp):
             ts = torch.tensor([t / float(cfg.num_steps)], dtype=vl.dtype).expand(B)
             af = head.action_encoder(cur, ts, inp["embodiment_id"]) + pos
             pe = torch.cat([hist, phys.physics_fut_encoder(fut, ts)], dim=1)
+            if physics_mask is not None:
+                masks["physics_attention_mask"] = physics_mask
             mo = head.model(hidden_states=torch.cat([sf, af], 1), encoder_hidden_states=vl,
-                            timestep=ts, physics_embs=pe)
+                            timestep=ts, physics_embs=pe, **masks)
             cur = cur + dt * head.action_decoder(mo["action"], inp["embodiment_id"])[:, -cfg.horizon:]
             fut = fut + dt * phys.physics_decoder(mo["physics"][:, -phys.physics_fut_len:])
         return cur
@@ -213,6 +221,25 @@ def head_fixture(R, dtype, batch: int, cfg: om.MsatHeadConfig = SMALL) -> dict:
             "cos_only_rope": bool(not ref.model.rope_embedder.freqs_cis_0.is_complex())}
 
 
+def masked_fixture(R, dtype, cfg: om.MsatHeadConfig) -> dict:
+    """Masked backbone tokens (and, on the physics topologies, a masked physics stream) at batch
+    2 through the vanilla loop: observation 0 hides VL tokens 3, 7 and 10..13, observation 1 its
+    last 6; physics mask [1, 0]."""
+    ref = reference_head(R, cfg)
+    om.init_weights(ref, seed=1234)
+    if dtype == torch.bfloat16:
+        ref = ref.to(torch.bfloat16)
+    inp = om.make_inputs(cfg, batch=2, seed=42, dtype=dtype, emb_ids=[1, 2])
+    vl_mask = torch.ones(2, cfg.n_vl, dtype=torch.long)
+    vl_mask[0, [3, 7, 10, 11, 12, 13]] = 0
+    vl_mask[1, -6:] = 0
+    physics_mask = torch.tensor([1, 0], dtype=torch.long) if cfg.use_physics else None
+    actions = run_vanilla_loop(ref, cfg, inp, vl_mask=vl_mask, physics_mask=physics_mask)
+    return {"config": vars(cfg), "seed": 1234, "weight_abs_sum": weight_checksum(ref),
+            "dtype": str(dtype), "batch": 2, "loop": "vanilla_masked", "inputs": inp,
+            "vl_mask": vl_mask, "physics_mask": physics_mask, "actions": actions}
+
+
 def rtc_fixture(R, dtype, cfg: om.MsatHeadConfig, prefix_len: int = 3) -> dict:
     """RTC trained mode: the reference GraphSafeActionModel(prefix_len=3) loop at batch 1 with a
     seeded frozen prefix (graph_safe_action_model.py:196-300)."""
@@ -254,6 +281,11 @@ def c1_block_fixture(R) -> dict:
 
 def main():
     R = import_reference()
+    for tag, cfg in (("small", SMALL), ("std", STD), ("physss", PHYS_SS)):
+        for dtype, dn in ((torch.float32, "fp32"), (torch.bfloat16, "bf16")):
+            torch.save(masked_fixture(R, dtype, cfg), HERE / f"masked_{tag}_b2_{dn}.pt")
+    if "--masked-only" in sys.argv:
+        return
     for tag, cfg in (("small", SMALL), ("std", STD)):
         for dtype, dn in ((torch.float32, "fp32"), (torch.bfloat16, "bf16")):
             torch.save(rtc_fixture(R, dtype, cfg), HERE / f"rtc_{tag}_b1_{dn}.pt")

@@ -33,8 +33,8 @@ def test_version_and_error_string(lib):
 def test_struct_layouts_match_header():
     # sizes of the C structs as laid out by the C compiler on this ABI (x86-64 / aarch64 LP64)
     assert C.sizeof(_lib.GemmDesc) == 256
-    assert C.sizeof(_lib.MsatConfig) == 31 * 4
-    assert C.sizeof(_lib.MsatIO) == 8 * 8
+    assert C.sizeof(_lib.MsatConfig) == 32 * 4
+    assert C.sizeof(_lib.MsatIO) == 10 * 8
     assert C.sizeof(_lib.BlockWeights) == 3 * (4 * 16 + 16)
     assert C.sizeof(_lib.SingleBlockWeights) == 2 * (3 * 16 + 16)
     assert C.sizeof(_lib.QkvSegment) == 64

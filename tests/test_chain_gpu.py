@@ -184,3 +184,34 @@ def test_swiglu_hidden_not_multiple_of_32(cuda):
     ref16 = oracle_bf16(head, inp, cfg)
     _, out = run_chain(head, inp, cuda)
     assert_actions_close(out, ref16)
+
+
+@pytest.mark.parametrize("tag", ["small", "std", "physss"])
+def test_masked_keys_match_reference_golden(cuda, tag):
+    """Masked backbone tokens (and, with physics, a masked physics stream) through the chain's
+    masked graph, against the reference modules run with encoder_attention_mask /
+    physics_attention_mask (tests/golden/masked_*); the same handle serves an unmasked step
+    right after with the unmasked graph's bits."""
+    fx16 = torch.load(GOLD / f"masked_{tag}_b2_bf16.pt", weights_only=False)
+    fx32 = torch.load(GOLD / f"masked_{tag}_b2_fp32.pt", weights_only=False)
+    cfg = om.MsatHeadConfig(**fx16["config"])
+    head = om.init_weights(om.ActionHead(cfg), seed=fx16["seed"]).to(BF)
+    inp = {k: v.to(cuda) for k, v in fx32["inputs"].items()}
+    args = [inp["vl"].to(BF), inp["state"].to(BF), inp["embodiment_id"], inp["init_noise"].to(BF)]
+    if cfg.use_physics:
+        chain = B200ExpandedActionHeadChain(head, cuda)
+        phys = dict(physics_hist=inp["physics_hist"].to(BF), physics_init_noise=inp["physics_noise"].to(BF))
+        out = chain(*args, **phys, vl_attention_mask=fx16["vl_mask"].to(cuda),
+                    physics_attention_mask=fx16["physics_mask"].to(cuda)).cpu()
+    else:
+        chain = B200ActionHeadChain(head, cuda)
+        phys = {}
+        out = chain(*args, vl_attention_mask=fx16["vl_mask"].to(cuda)).cpu()
+    err16 = (out.float() - fx16["actions"].float()).abs().max().item()
+    assert err16 <= 2e-2, err16
+    assert cos_sim(out.float(), fx32["actions"]) >= 0.999
+    assert chain.device_status() == 0
+    unmasked = chain(*args, **phys).cpu()
+    _, fresh = run_chain(head, fx32["inputs"], cuda)
+    assert torch.equal(unmasked, fresh)
+    assert not torch.equal(unmasked, out)

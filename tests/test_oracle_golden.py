@@ -123,3 +123,30 @@ def test_oracle_rtc_prefix_matches_reference(name):
         assert torch.equal(out, fx["actions"]), (out.float() - fx["actions"].float()).abs().max()
     else:
         torch.testing.assert_close(out, fx["actions"], rtol=1e-5, atol=1e-5)
+
+
+@pytest.mark.parametrize("name", [f"masked_{tag}_b2_{dt}.pt" for tag in ("small", "std", "physss")
+                                  for dt in ("fp32", "bf16")])
+def test_oracle_masked_keys_match_reference(name):
+    """Masked backbone tokens (and a masked physics stream on the physics topologies): the key
+    masks of every block kind (double, expanded double, single, expanded single) against the
+    reference modules run with encoder_attention_mask / physics_attention_mask."""
+    fx = _load(name)
+    cfg = om.MsatHeadConfig(**fx["config"])
+    head = om.init_weights(om.ActionHead(cfg), seed=fx["seed"])
+    dtype = torch.bfloat16 if "bf16" in name else torch.float32
+    if dtype == torch.bfloat16:
+        head = head.to(torch.bfloat16)
+    inp = fx["inputs"]
+    phys = (inp["physics_hist"], inp["physics_noise"]) if cfg.use_physics else (None, None)
+    out = om.denoise(head, inp["vl"], inp["state"], inp["embodiment_id"], inp["init_noise"],
+                     *phys, cfg.num_steps, vl_mask=fx["vl_mask"], physics_mask=fx["physics_mask"])
+    ref = fx["actions"]
+    if dtype == torch.float32:
+        torch.testing.assert_close(out, ref, rtol=1e-5, atol=1e-5)
+    else:
+        assert torch.equal(out, ref), (out.float() - ref.float()).abs().max()
+    # the masks matter: the unmasked control step gives other actions
+    free = om.denoise(head, inp["vl"], inp["state"], inp["embodiment_id"], inp["init_noise"],
+                      *phys, cfg.num_steps)
+    assert not torch.equal(free, out)

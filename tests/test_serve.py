@@ -53,8 +53,10 @@ class FakeRLDX(nn.Module):
             fut = torch.randn(B, p.physics_fut_len, p.physics_dim, dtype=BF, device=dev)
             phys = (inputs["physics"][:, :p.physics_hist_len].cpu(), fut.cpu())
         noise = torch.randn(B, head.action_horizon, head.action_dim, dtype=BF, device=dev)
+        mask = inputs.get("mask")
         out = om.denoise(head.cpu(), vl.cpu(), inputs["state"].cpu(), inputs["embodiment_id"].cpu(),
-                         noise.cpu(), *phys, head.num_inference_timesteps)
+                         noise.cpu(), *phys, head.num_inference_timesteps,
+                         vl_mask=None if mask is None else mask.cpu())
         return BatchFeature({"action_pred": out.to(dev)})
 
 
@@ -133,3 +135,56 @@ def test_dispatcher_shape_drift(cuda):
     model2.get_action(inputs=_request(cfg, cuda, B=1))
     with pytest.raises(serve.ShapeDrift):
         model2.get_action(inputs=_request(cfg, cuda, B=2))
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("physics", [True, False])
+def test_dispatcher_serves_masked_backbone_tokens(cuda, physics):
+    """A request whose backbone_attention_mask hides some tokens is served natively (the VL key
+    mask of every block), matching the model's own masked get_action; an all-ones mask is
+    dropped like the reference does."""
+    cfg = _cfg(physics)
+    head = om.init_weights(om.ActionHead(cfg), seed=7).to(BF)
+    model = FakeRLDX(head)
+    req = _request(cfg, cuda)
+    mask = torch.ones(req["vl"].shape[0], cfg.n_vl, dtype=torch.long, device=cuda)
+    mask[:, 5:9] = 0
+    req["mask"] = mask
+    torch.manual_seed(11)
+    ref = model.get_action(inputs=dict(req))["action_pred"]
+    head.to(cuda)
+    serve.apply_optimization(model, "B200")
+    n0 = model.vanilla_calls
+    torch.manual_seed(11)
+    out = model.get_action(inputs=dict(req))["action_pred"]
+    torch.cuda.synchronize()
+    assert model.get_action.calls == 1 and model.vanilla_calls == n0  # served natively
+    assert (out.float().cpu() - ref.float().cpu()).abs().max().item() <= 2e-2
+
+
+def test_compile_levels_map_to_paths():
+    """The reference server's --compile levels (run_rldx_server.py:117) plus `b200`."""
+    from rldx_b200 import server
+
+    assert server.parse_compile_level(None) is None
+    assert server.parse_compile_level("none") is None
+    assert server.parse_compile_level("submodule") == "B"
+    assert server.parse_compile_level("fullgraph") == "D"
+    assert server.parse_compile_level("b200") == "B200"
+    with pytest.raises(ValueError):
+        server.parse_compile_level("max")
+    with pytest.raises(ValueError, match="guided"):
+        server.validate_compile_level("b200", "guided")
+    assert server.validate_compile_level("b200", "trained") == "B200"
+    assert server.validate_compile_level("submodule", "guided") == "B"
+
+
+def test_compile_level_b200_installs_the_dispatcher():
+    from rldx_b200 import server
+
+    cfg = _cfg(True)
+    model = FakeRLDX(om.init_weights(om.ActionHead(cfg), seed=1))
+    policy = SimpleNamespace(model=model)
+    info = server.apply_compile_level(policy, "b200")
+    assert info["path"] == "B200" and isinstance(model.get_action, serve.B200Dispatcher)
+    assert server.apply_compile_level(policy, "none") is None
