@@ -257,11 +257,25 @@ def cpu_baseline(budget_s: float, steps: int = 8, warmup: int = 1, workload: str
                       f"p50 {per_forward * 1e3:.0f} ms x {cfg.num_steps} Euler steps = one control step"}
 
 
+def c5_prompt_ids() -> torch.Tensor:
+    """The config-5 prompt: 8 text ids, 4 frames of (image-start marker, 196 patch ids, image-end
+    marker), 48 text ids -- 848 ids, 784 of them patches.  Video-token compression takes the rows
+    from the first to the last image-start marker (the three old frames, 594 rows)."""
+    frame = [151652] + [151655] * 196 + [151653]
+    return torch.tensor(list(range(8)) + frame * 4 + list(range(48)))
+
+
+C5_COG = 256        # cognition tokens appended after the prompt (the backbone's cog-token append)
+C5_LAYERS = 12      # the 28-layer VLM truncated at layer 12
+C5_COMPRESS_AT = 4  # LayerWrapper internal_projection (rldx/model/modules/backbone/modeling_vtc.py:158-164)
+
+
 def cpu_baseline_c5(budget_s: float):
     """One observation of the config-5 step on the host cores in fp32, sampled stage by stage: one
-    VLM decoder layer over 848 tokens (x 12 layers), one memory layer over the 2048-token ring
-    (x 2 layers) and one config-2 MSAT forward (x 4 Euler steps); each stage's p50 is multiplied
-    by its repeat count (every repeat has the same shapes)."""
+    VLM decoder layer over the 1104 prompt + cognition tokens (x 4 layers before the compression),
+    one over the 511 tokens after it (x 8), one memory layer over the 2048-token ring (x 2 layers)
+    and one config-2 MSAT forward (x 4 Euler steps); each stage's p50 is multiplied by its repeat
+    count (every repeat has the same shapes)."""
     from oracle import memory_oracle as mo
     from oracle import qwen3_oracle as oq
 
@@ -280,20 +294,25 @@ def cpu_baseline_c5(budget_s: float):
     g = torch.Generator().manual_seed(1)
     qc = oq.Qwen3Config(layers=1)
     stack = oq.init_weights(oq.TextStack(qc), seed=0)
-    T = 848
+    T = c5_prompt_ids().numel() + C5_COG
+    begin, end = oq.find_compress_rows(c5_prompt_ids()[None])
+    T2 = T - (end[0] - begin[0]) + 1
     cos, sin = oq.rope_tables(qc, torch.arange(T))
     h = torch.randn(1, T, qc.hidden, generator=g)
     with torch.no_grad():
         vlm = p50(lambda: stack(h, cos[None], sin[None], final_norm=False))
+        vlm2 = p50(lambda: stack(h[:, :T2], cos[None, :T2], sin[None, :T2], final_norm=False))
         mem = mo.init_weights(mo.TransformerMemory(mo.MemoryConfig(layers=1)), seed=0)
         ring = torch.randn(1, 8 * 256, 1536, generator=g)
         memory = p50(lambda: mem(ring))
     del stack, mem
     msat = 1.0 / cpu_baseline(budget_s, steps=3, workload="c2")["value"]  # 4 MSAT forwards
-    per_obs = 12 * vlm + 2 * memory + msat
+    per_obs = C5_COMPRESS_AT * vlm + (C5_LAYERS - C5_COMPRESS_AT) * vlm2 + 2 * memory + msat
     return {"value": 1.0 / per_obs, "unit": "observations/s", "cores": threads, "kind": "port",
-            "sample": f"one observation in fp32, stage by stage: VLM layer p50 {vlm * 1e3:.0f} ms x 12, memory "
-                      f"layer p50 {memory * 1e3:.0f} ms x 2, MSAT control step {msat * 1e3:.0f} ms"}
+            "sample": f"one observation in fp32, stage by stage: VLM layer p50 {vlm * 1e3:.0f} ms x "
+                      f"{C5_COMPRESS_AT} ({T} tokens) + {vlm2 * 1e3:.0f} ms x {C5_LAYERS - C5_COMPRESS_AT} "
+                      f"({T2} tokens after compression), memory layer p50 {memory * 1e3:.0f} ms x 2, MSAT "
+                      f"control step {msat * 1e3:.0f} ms"}
 
 
 def c1_inputs(batch: int, seed: int = 11):
@@ -432,9 +451,11 @@ def run_reference(args):
                 "ms_per_step": 1000.0 * args.observations / cb["value"], "higher_is_better": True,
                 "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
                 "config": {"workload": "BASELINE config 5: batched serving step (sampled per observation)",
-                           "model": "12 x Qwen3 decoder over 848 tokens -> TransformerMemory (2 layers, 2048 "
-                                    "tokens) -> config-2 MSAT decoder", "global_batch": args.observations,
-                           "seq_len": 848, "parallelism": "cpu"},
+                           "model": "12 x Qwen3 decoder over 848 prompt + 256 cognition tokens, video-token "
+                                    "compression before layer 4 (1104 -> 511 tokens) -> TransformerMemory "
+                                    "(2 layers, 2048 tokens) -> config-2 MSAT decoder",
+                           "global_batch": args.observations, "seq_len": c5_prompt_ids().numel() + C5_COG,
+                           "parallelism": "cpu"},
                 "cpu_baseline": cb,
                 "e2e": {"value": cb["value"], "unit": "observations/s", "h2d_bytes_per_step": 0,
                         "d2h_bytes_per_step": 0}}
@@ -627,8 +648,11 @@ def run_b200(args, rank, world, local):
 def c5_measure(rank, world, local, observations: int, steps: int, warmup: int) -> dict:
     """BASELINE config 5 on this rank's GPU: one step serves `observations` independent
     observations sharded over the ranks (observations / world here):
-      1. 12 Qwen3 decoder layers (hidden 2048, GQA 16 / 2 x 128, SwiGLU 11008) over 848 tokens
-         (4 frames x 196 patches + 64 text; the 28-layer model truncated at layer 12);
+      1. 12 Qwen3 decoder layers (hidden 2048, GQA 16 / 2 x 128, SwiGLU 11008) over the 848-id
+         prompt (4 frames x 196 patches + 64 text ids, c5_prompt_ids) followed by 256 cognition
+         tokens (1104 tokens; the 28-layer model truncated at layer 12), with video-token
+         compression before layer 4: the three old frames' 594 rows become one mean token, so
+         layers 4..11 run on 511 tokens;
       2. the last 256 positions are the cognition tokens, projected 2048 -> 1536;
       3. the memory module (TransformerMemory: 2 layers, 16 heads of 96, SwiGLU 6144) over its ring
          of 8 cognition sets (7 past + this one, 2048 tokens) -- the ring shifts by one set per step;
@@ -642,7 +666,7 @@ def c5_measure(rank, world, local, observations: int, steps: int, warmup: int) -
     import rldx_b200  # noqa: F401
     from rldx_b200 import ops
     from rldx_b200.chain import B200ExpandedActionHeadChain
-    from rldx_b200.llm import B200LLMChain, B200MemoryChain
+    from rldx_b200.llm import B200LLMChain, B200MemoryChain, find_compress_info
     from rldx_b200.synthetic import HeadDims, random_action_head, random_inputs
 
     dev = torch.device("cuda", local)
@@ -664,8 +688,9 @@ def c5_measure(rank, world, local, observations: int, steps: int, warmup: int) -
         m.weight = torch.nn.Parameter(w(dim, mean=1.0, std=0.1), requires_grad=False)
         return m
 
-    # ---- 1. VLM prefill: 12 Qwen3 layers over 848 tokens ----
-    T, D, Hq, Hkv, hd, Fd, NL = 848, 2048, 16, 2, 128, 11008, 12
+    # ---- 1. VLM prefill: 12 Qwen3 layers over 848 prompt + 256 cognition tokens, compressed ----
+    ids = c5_prompt_ids()
+    T, D, Hq, Hkv, hd, Fd, NL = ids.numel() + C5_COG, 2048, 16, 2, 128, 11008, C5_LAYERS
     vlm_layers = [NS(input_layernorm=NS(weight=w(D, mean=1.0, std=0.1), variance_epsilon=1e-6),
                      post_attention_layernorm=NS(weight=w(D, mean=1.0, std=0.1)),
                      self_attn=NS(q_proj=lin(Hq * hd, D), k_proj=lin(Hkv * hd, D), v_proj=lin(Hkv * hd, D),
@@ -678,7 +703,11 @@ def c5_measure(rank, world, local, observations: int, steps: int, warmup: int) -
     emb = torch.cat([ang, ang], -1)
     ssin = emb.sin().to(bf)
     ssin[:, : hd // 2] *= -1
-    vlm = B200LLMChain(vlm_layers, norm_module(D), emb.cos().to(bf), ssin, device=dev)
+    wrapped = [NS(layer=layer, layer_idx=i, internal_projection=C5_COMPRESS_AT, img_pattern=[151652])
+               for i, layer in enumerate(vlm_layers)]
+    ci = find_compress_info(wrapped, ids[None].expand(B, -1), n_cog_tokens=C5_COG)
+    vlm = B200LLMChain(wrapped, norm_module(D), emb.cos().to(bf), ssin, device=dev, compress_info=ci)
+    T2 = ci["static_out_len"]
     # ---- 2. cognition projection 2048 -> 1536 ----
     NQ, DM = 256, 1536
     cog_w, cog_b = w(DM, D), w(DM)
@@ -704,8 +733,8 @@ def c5_measure(rank, world, local, observations: int, steps: int, warmup: int) -
     vl = torch.empty(B, 2 * NQ, DM, dtype=bf, device=dev)
 
     def step():
-        h = vlm(tokens)                                                   # [B, 848, 2048]
-        cog = h[:, T - NQ:, :].reshape(B * NQ, D)
+        h = vlm(tokens)                                                   # [B, 511, 2048]
+        cog = h[:, T2 - NQ:, :].reshape(B * NQ, D)
         # cognition tokens -> first half of each observation's VL rows (row remap in the epilogue)
         ops.gemm([ops.gemm_desc(cog, cog_w, vl.view(B * 2 * NQ, DM), cog_b, rows_in=NQ, rows_out=2 * NQ)])
         ring[:, : (SETS - 1) * NQ].copy_(ring[:, NQ:].clone())               # shift the ring by one set
@@ -760,7 +789,10 @@ def c5_measure(rank, world, local, observations: int, steps: int, warmup: int) -
     if status:
         raise RuntimeError(f"config-5 step recorded device error 0x{status:x}")
 
-    vlm_flops = (2 * (D * (Hq + 2 * Hkv) * hd + Hq * hd * D + 3 * D * Fd) * NL * T + 2.0 * Hq * T * T * hd * NL) * B
+    per_token = 2 * (D * (Hq + 2 * Hkv) * hd + Hq * hd * D + 3 * D * Fd)
+    na = C5_COMPRESS_AT
+    vlm_flops = (per_token * (na * T + (NL - na) * T2)
+                 + 2.0 * Hq * hd * (na * T * T + (NL - na) * T2 * T2)) * B  # causal: half of QK^T + PV
     mem_flops = (2 * (4 * DM * DM + 3 * DM * FM) * 2 * SETS * NQ + 2.0 * HM * (SETS * NQ) ** 2 * hdm * 2) * B
     msat_flops = 4 * (509e9 + 31e9) * B  # per control step (config-2 roofline figures)
     flops = vlm_flops + mem_flops + 2.0 * NQ * D * DM * B + msat_flops
@@ -774,8 +806,9 @@ def c5_measure(rank, world, local, observations: int, steps: int, warmup: int) -
         "higher_is_better": True, "scaling": "strong",
         "config": {"workload": "BASELINE config 5: batched serving step, %d observations sharded over %d GPU(s)"
                                % (observations, world),
-                   "model": "12 x Qwen3 decoder (2048, GQA 16/2x128, SwiGLU 11008) over 848 tokens -> 256 "
-                            "cognition tokens -> 1536 -> TransformerMemory (2 layers, 8 x 256 tokens) -> "
+                   "model": "12 x Qwen3 decoder (2048, GQA 16/2x128, SwiGLU 11008) over 848 prompt + 256 "
+                            "cognition tokens, video-token compression before layer 4 (1104 -> 511 tokens) "
+                            "-> 256 cognition tokens -> 1536 -> TransformerMemory (2 layers, 8 x 256 tokens) -> "
                             "config-2 MSAT decoder (VL 256 + 256, 4 Euler steps)",
                    "global_batch": observations, "seq_len": T,
                    "parallelism": f"data parallel x{world} (observations sharded, no collective)",

@@ -534,6 +534,17 @@ typedef struct {
    * deepstack_rows token rows listed in rldx_llm_weights.deepstack_row_index.  0: none. */
   int deepstack_layers;
   int deepstack_rows;
+  /* Video-token compression (LayerWrapper with internal_projection = compress_layer,
+   * rldx/model/modules/backbone/layer_wrapper.py:73-113; the reference inference engine's static
+   * form, graph_safe_qwen3vl_text_model.py:26-59 and 142-175): before layer compress_layer the
+   * token rows [compress_begin, compress_end) of every sequence are replaced by one row, their
+   * mean (bf16 sum over the rows, then bf16 division by their count), and the layers from there
+   * on run on tokens - (compress_end - compress_begin) + 1 tokens with the RoPE rows
+   * [0, compress_begin], [compress_end, tokens).  compress_end <= compress_begin: none (a
+   * zero-filled tail).  deepstack_layers must not exceed compress_layer. */
+  int compress_layer;
+  int compress_begin;
+  int compress_end;
 } rldx_llm_config;
 
 typedef struct {
@@ -560,8 +571,11 @@ typedef struct {
 
 int rldx_llm_create(const rldx_llm_config* cfg, const rldx_llm_weights* w, rldx_llm** out);
 int rldx_llm_destroy(rldx_llm* h);
-/* hidden_in / hidden_out: [batch, tokens, hidden] bf16 device pointers; asynchronous on stream. */
+/* hidden_in: [batch, tokens, hidden], hidden_out: [batch, rldx_llm_out_tokens(h), hidden] bf16
+ * device (or pinned host) pointers; asynchronous on stream. */
 int rldx_llm_prefill(rldx_llm* h, const void* hidden_in, void* hidden_out, void* stream);
+/* tokens per sequence of the prefill's output: tokens, or the compressed count */
+int rldx_llm_out_tokens(const rldx_llm* h);
 /* kernel launches of one prefill (graph nodes when captured) */
 int rldx_llm_launch_count(const rldx_llm* h);
 

@@ -12,6 +12,11 @@ loads with strict=True:
   Qwen3VLTextAttention      :404-490  per-head q/k RMSNorm before RoPE; sdpa with GQA, causal
   Qwen3VLTextMLP            :493-506  down(silu(gate(x)) * up(x)), no biases
   Qwen3VLTextDecoderLayer   :509-560  pre-norm residual blocks
+and the video-token compression of the VTC backbone, rldx/model/modules/backbone/layer_wrapper.py
+(LayerWrapper, wrapped around every text layer with internal_projection=4 by modeling_vtc.py:158-164):
+  get_removing_indices      :25-51    first / last (or num_views-th last) image-start marker
+  forward                   :73-113   before layer `internal_projection`, the rows [begin, end)
+                                      become one mean row; RoPE rows follow (:201-240)
 The attention call is transformers' sdpa_attention_forward for a causal prefill without a mask:
 F.scaled_dot_product_attention(q, k, v, scale=head_dim**-0.5, is_causal=True, enable_gqa=True).
 Pinned against golden vectors of the reference's own layers: tests/golden/make_golden_llm.py.
@@ -122,12 +127,16 @@ class TextStack(nn.Module):
 
     @torch.no_grad()
     def forward(self, h, cos, sin, final_norm: bool = True, return_hidden: bool = False,
-                deepstack=None, deepstack_rows=None):
+                deepstack=None, deepstack_rows=None, compress=None):
         """deepstack: per-layer visual features [n, D] added, after layer i < len(deepstack), to
         the token rows `deepstack_rows` of every sequence (Qwen3VLTextModel._deepstack_process,
-        modeling_qwen3_vl.py:1086-1113: hidden[mask] = hidden[mask] + embeds, one rounding)."""
+        modeling_qwen3_vl.py:1086-1113: hidden[mask] = hidden[mask] + embeds, one rounding).
+        compress: (layer, begin, end) -- video-token compression before that layer (see
+        compress_sequence); the returned hidden states are shorter from that layer on."""
         hidden = []
         for i, layer in enumerate(self.layers):
+            if compress is not None and i == compress[0] and compress[2] > compress[1]:
+                h, cos, sin = compress_sequence(h, cos, sin, compress[1], compress[2])
             h = layer(h, cos, sin)
             if deepstack is not None and i < len(deepstack):
                 h = h.clone()
@@ -156,3 +165,42 @@ def init_weights(module: nn.Module, seed: int, std: float = 0.02) -> nn.Module:
             else:
                 p.copy_((torch.randn(p.shape, generator=g) * std).to(p.dtype))
     return module
+
+
+def find_compress_rows(input_ids: torch.Tensor, img_pattern=(151652,), num_views=None):
+    """(begin, end) token rows of the compressed region of each sequence: begin = the first
+    occurrence of `img_pattern` (the image-start marker), end = the last occurrence, or the
+    num_views-th last when image-wise encoding keeps the newest frame's views
+    (LayerWrapper.get_removing_indices, layer_wrapper.py:25-51).  Returns two lists."""
+    n = len(img_pattern)
+    pat = torch.tensor(list(img_pattern), dtype=input_ids.dtype)
+    begins, ends = [], []
+    for row in input_ids:
+        hits = [t for t in range(row.numel() - n + 1) if torch.equal(row[t:t + n], pat)]
+        if not hits:
+            raise ValueError("no image-start marker in the sequence")
+        begins.append(hits[0])
+        ends.append(hits[-num_views] if num_views is not None else hits[-1])
+    return begins, ends
+
+
+def compress_sequence(h, cos, sin, begin: int, end: int):
+    """Video-token compression (LayerWrapper.forward, layer_wrapper.py:73-113, 201-240): the rows
+    [begin, end) of every sequence -- the old frames' tokens -- are replaced by one row, their mean,
+    placed at `begin`; the rows before and after are kept in order.  The mean is the tensor-dtype
+    sum over the sequence axis of the rows weighted 1 (dropped) / 0 (kept), then divided by the
+    number of dropped rows, each result rounded to the tensor dtype.  The RoPE rows follow the
+    tokens: the mean row takes row `begin`'s cos / sin.  begin, end are shared by the batch (the
+    reference inference engine's static indices, graph_safe_qwen3vl_text_model.py:26-59)."""
+    T = h.shape[1]
+    weight = torch.zeros(T, dtype=h.dtype)
+    weight[begin:end] = 1
+    total = (h * weight[None, :, None]).sum(dim=1)
+    count = torch.full((h.shape[0], 1), end - begin, dtype=torch.int64)
+    mean = (total / count).unsqueeze(1)
+    h = torch.cat([h[:, :begin], mean, h[:, end:]], dim=1)
+
+    def rows(t):
+        return torch.cat([t[:, :begin], t[:, begin:begin + 1], t[:, end:]], dim=1)
+
+    return h, rows(cos), rows(sin)

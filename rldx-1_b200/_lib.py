@@ -140,7 +140,8 @@ class LlmConfig(C.Structure):
                 ("kv_heads", C.c_int), ("head_dim", C.c_int), ("ffn", C.c_int), ("layers", C.c_int),
                 ("rms_eps", C.c_float), ("final_norm", C.c_int), ("use_graph", C.c_int),
                 ("no_qk_norm", C.c_int), ("norm_weight_first", C.c_int), ("causal_block", C.c_int),
-                ("deepstack_layers", C.c_int), ("deepstack_rows", C.c_int)]
+                ("deepstack_layers", C.c_int), ("deepstack_rows", C.c_int), ("compress_layer", C.c_int),
+                ("compress_begin", C.c_int), ("compress_end", C.c_int)]
 
 
 class LlmLayerWeights(C.Structure):
@@ -178,6 +179,7 @@ SIGNATURES = {
     "rldx_llm_destroy": (C.c_int, [vp]),
     "rldx_llm_prefill": (C.c_int, [vp, vp, vp, vp]),
     "rldx_llm_launch_count": (C.c_int, [vp]),
+    "rldx_llm_out_tokens": (C.c_int, [vp]),
     "rldx_llm_set_deepstack": (C.c_int, [vp, vp, vp]),
     "rldx_qkv_prep": (C.c_int, [C.POINTER(QkvSegment), C.c_int, C.c_int, C.c_int, C.c_int, C.c_int,
                                 C.c_float, vp, vp, vp, vp]),

@@ -178,6 +178,11 @@ cudaError_t launch_elementwise(const __nv_bfloat16* x, __nv_bfloat16* y, long lo
 
 // kmask [B, L]: VL keys (t < nvl) from vl [B, nvl], then nsa visible keys, then the physics
 // keys from p [B] (nonzero = visible)
+// Video-token compression: [B, T, D] -> [B, T - (end - begin) + 1, D], rows [begin, end) of
+// every sequence replaced by their mean (bf16 sum, then bf16 division by the row count).
+cudaError_t launch_compress_rows(const __nv_bfloat16* x, __nv_bfloat16* y, int B, int T, int D, int begin, int end,
+                                 cudaStream_t stream);
+
 cudaError_t launch_key_mask(uint8_t* kmask, const uint8_t* vl, const uint8_t* p, int B, int L, int nvl,
                             int nsa, cudaStream_t stream);
 

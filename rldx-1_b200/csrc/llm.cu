@@ -16,12 +16,19 @@
 //   g   = silu(n @ Wg^T) * (n @ Wu^T)                 gemm_bf16_kernel (SwiGLU epilogue on
 //                                                    [32 gate | 32 up] interleaved rows)
 //   h   = h + g @ Wd^T                                gemm_bf16_kernel (residual epilogue)
-// and an optional final RMSNorm.  Every bf16 rounding follows the eager module: each linear
+// and an optional final RMSNorm.  With video-token compression (the VTC backbone's LayerWrapper,
+// rldx/model/modules/backbone/layer_wrapper.py:73-113, run with static rows as the reference
+// inference engine does, graph_safe_qwen3vl_text_model.py:142-175) one compress_rows_kernel
+// before layer compress_layer replaces the rows [begin, end) of every sequence with their mean,
+// and the layers from there on run on the shorter sequence with the matching RoPE rows (front,
+// row begin, back).  Every bf16 rounding follows the eager module: each linear
 // rounds once, the residual adds round, RMSNorm casts before its weight, RoPE rounds each
 // product and the sum, silu rounds before the product.
 //
 // Layout: token-major activations [B*T, width]; q [B, Hq, T, 128], k [B, Hkv, T, 128] and
-// V^T [B, Hkv, 128, Tp] (Tp = T rounded up to 8) for the attention kernel.
+// V^T [B, Hkv, 128, Tp] (Tp = T rounded up to 8) for the attention kernel.  A compressed stack
+// has a second set of hidden / q / k / V^T buffers and RoPE tables for its T2 tokens; the
+// token-major scratch (norm output, qkv, attention output, SwiGLU hidden) is shared.
 #include "host_util.h"
 
 using namespace rldx;
@@ -35,10 +42,17 @@ struct rldx_llm {
     bf16 *in_norm, *qkv, *qn, *kn, *o, *post_norm, *w12, *down;
   };
   std::vector<LayerW> lw;
-  bf16 *final_norm = nullptr, *cos = nullptr, *sin = nullptr;
-  bf16 *h = nullptr, *n = nullptr, *qkv = nullptr, *q = nullptr, *k = nullptr, *vt = nullptr, *a = nullptr,
-       *g = nullptr;
-  bf16* out = nullptr;  // result of the last op (n after the final norm, else h)
+  bf16* final_norm = nullptr;
+  // one sequence length of the stack: all layers, or the layers before / after compression
+  struct Seq {
+    int T = 0, Tp = 0, M = 0;
+    bf16 *h = nullptr, *q = nullptr, *k = nullptr, *vt = nullptr, *cos = nullptr, *sin = nullptr;
+  };
+  Seq pre, post;  // post == pre without compression
+  bool compress = false;
+  bf16 *h = nullptr, *n = nullptr, *qkv = nullptr, *a = nullptr, *g = nullptr;
+  bf16* out = nullptr;  // result of the last op (n after the final norm, else the last hidden)
+  int out_rows = 0;     // B * tokens of the output
   int ds_layers = 0, ds_rows = 0;
   int* ds_index = nullptr;  // [ds_rows] token rows
   bf16* ds_feat = nullptr;  // [ds_layers][B][ds_rows][D]
@@ -99,7 +113,7 @@ struct rldx_llm {
     ws_need = std::max(ws_need, need);
     ops.push_back([gp](cudaStream_t st, bool p) { return launch_gemm(gp, st, p); });
   }
-  void push_rmsnorm(const bf16* x, const bf16* w, bf16* outp) {
+  void push_rmsnorm(const bf16* x, const bf16* w, bf16* outp, int M) {
     ResLnParams p;
     std::memset(&p, 0, sizeof(p));
     p.seg[0].x = x;
@@ -138,6 +152,14 @@ struct rldx_llm {
     if (c.deepstack_layers < 0 || c.deepstack_layers > c.layers || c.deepstack_rows < 0 ||
         (c.deepstack_layers > 0) != (c.deepstack_rows > 0))
       throw Fail(RLDX_ERR_ARG, "llm_create: deepstack_layers in [0, layers] and deepstack_rows > 0 together");
+    compress = c.compress_end > c.compress_begin;
+    if (compress) {
+      if (c.compress_begin < 0 || c.compress_end > c.tokens || c.compress_layer < 0 || c.compress_layer >= c.layers)
+        throw Fail(RLDX_ERR_ARG, "llm_create: compression needs 0 <= compress_begin < compress_end <= tokens and "
+                                 "0 <= compress_layer < layers");
+      if (c.deepstack_layers > c.compress_layer)
+        throw Fail(RLDX_ERR_UNSUPPORTED, "llm_create: deepstack layers must come before the compression layer");
+    }
     if (c.deepstack_layers > 0) {
       if (!w.deepstack_row_index) throw Fail(RLDX_ERR_ARG, "llm_create: missing deepstack_row_index");
       for (int j = 0; j < c.deepstack_rows; ++j)
@@ -186,15 +208,29 @@ struct rldx_llm {
          "deepstack rows");
       ds_feat = alloc<bf16>(static_cast<size_t>(ds_layers) * B * ds_rows * D);  // zero until set
     }
-    cos = copy_in(w.rope_cos, static_cast<size_t>(T) * hd, "rope cos");
-    sin = copy_in(w.rope_sin, static_cast<size_t>(T) * hd, "rope sin");
-
-    h = alloc<bf16>(static_cast<size_t>(M) * D);
+    pre = make_seq(T);
+    pre.cos = copy_in(w.rope_cos, static_cast<size_t>(T) * hd, "rope cos");
+    pre.sin = copy_in(w.rope_sin, static_cast<size_t>(T) * hd, "rope sin");
+    post = pre;
+    if (compress) {  // RoPE rows of the compressed sequence: [0, begin), begin, [end, T)
+      const int b0 = c.compress_begin, e0 = c.compress_end;
+      post = make_seq(T - (e0 - b0) + 1);
+      post.cos = alloc<bf16>(static_cast<size_t>(post.T) * hd);
+      post.sin = alloc<bf16>(static_cast<size_t>(post.T) * hd);
+      const size_t row = static_cast<size_t>(hd) * 2;
+      for (int t = 0; t < 2; ++t) {
+        bf16* dst = t ? post.sin : post.cos;
+        const bf16* src = t ? pre.sin : pre.cos;
+        ck(cudaMemcpyAsync(dst, src, (b0 + 1) * row, cudaMemcpyDeviceToDevice, stream), "rope rows");
+        if (e0 < T)
+          ck(cudaMemcpyAsync(reinterpret_cast<char*>(dst) + (b0 + 1) * row, reinterpret_cast<const char*>(src) + e0 * row,
+                             static_cast<size_t>(T - e0) * row, cudaMemcpyDeviceToDevice, stream),
+             "rope rows");
+      }
+    }
+    h = pre.h;
     n = alloc<bf16>(static_cast<size_t>(M) * D);
     qkv = alloc<bf16>(static_cast<size_t>(M) * NQKV);
-    q = alloc<bf16>(static_cast<size_t>(B) * Hq * T * phd);  // zero-filled: padded dims stay zero
-    k = alloc<bf16>(static_cast<size_t>(B) * Hkv * T * phd);
-    vt = alloc<bf16>(static_cast<size_t>(B) * Hkv * phd * Tp);
     a = alloc<bf16>(static_cast<size_t>(M) * qd);
     g = alloc<bf16>(static_cast<size_t>(M) * Fp);
 
@@ -233,6 +269,19 @@ struct rldx_llm {
     }
   }
 
+  // hidden / q / k / V^T buffers of a sequence of T_ tokens (zero-filled: padded head dims stay zero)
+  Seq make_seq(int T_) {
+    Seq s_;
+    s_.T = T_;
+    s_.Tp = (T_ + 7) / 8 * 8;
+    s_.M = B * T_;
+    s_.h = alloc<bf16>(static_cast<size_t>(s_.M) * D);
+    s_.q = alloc<bf16>(static_cast<size_t>(B) * Hq * T_ * phd);
+    s_.k = alloc<bf16>(static_cast<size_t>(B) * Hkv * T_ * phd);
+    s_.vt = alloc<bf16>(static_cast<size_t>(B) * Hkv * phd * s_.Tp);
+    return s_;
+  }
+
   void push_status(int which) {
     unsigned int* slot = status.dev + which;
     ops.push_back([slot](cudaStream_t st, bool) { return launch_status_take(slot, st); });
@@ -241,9 +290,20 @@ struct rldx_llm {
   void plan() {
     const int qd = Hq * hd;
     push_status(0);  // a code left by earlier work -> slot 0; the call starts from a clean word
+    const Seq* last = &pre;
     for (int li = 0; li < c.layers; ++li) {
       const LayerW& l = lw[li];
-      push_rmsnorm(h, l.in_norm, n);
+      if (compress && li == c.compress_layer) {
+        const bf16* x = pre.h;
+        bf16* y = post.h;
+        const int b_ = B, t_ = T, d_ = D, b0 = c.compress_begin, e0 = c.compress_end;
+        ops.push_back([=](cudaStream_t st, bool) { return launch_compress_rows(x, y, b_, t_, d_, b0, e0, st); });
+      }
+      const Seq& sq = (compress && li >= c.compress_layer) ? post : pre;
+      last = &sq;
+      const int M = sq.M, T = sq.T, Tp = sq.Tp;
+      bf16 *h = sq.h, *q = sq.q, *k = sq.k, *vt = sq.vt;
+      push_rmsnorm(h, l.in_norm, n, M);
       push_gemm(rldx_msat::lin(n, D, l.qkv, nullptr, M, NQKV, D, qkv, NQKV));
       {
         QkNormRopeParams p;
@@ -254,8 +314,8 @@ struct rldx_llm {
         p.k = k;
         p.wq = l.qn;
         p.wk = l.kn;
-        p.cos = cos;
-        p.sin = sin;
+        p.cos = sq.cos;
+        p.sin = sq.sin;
         p.nrows = static_cast<unsigned>(M * (Hq + Hkv));
         p.heads = static_cast<unsigned>(Hq + Hkv);
         p.Hq = static_cast<unsigned>(Hq);
@@ -303,7 +363,7 @@ struct rldx_llm {
         d.ld_add = D;
         push_gemm(d);
       }
-      push_rmsnorm(h, l.post_norm, n);
+      push_rmsnorm(h, l.post_norm, n, M);
       {
         rldx_gemm_desc d = rldx_msat::lin(n, D, l.w12, nullptr, M, 2 * Fp, D, g, Fp);
         d.epilogue = RLDX_EPI_SWIGLU;
@@ -323,9 +383,10 @@ struct rldx_llm {
         ops.push_back([=](cudaStream_t st, bool) { return launch_rows_add(hp, idx, r_, f, b_, t_, d_, st); });
       }
     }
-    out = h;
+    out = last->h;
+    out_rows = last->M;
     if (c.final_norm) {
-      push_rmsnorm(h, final_norm, n);
+      push_rmsnorm(last->h, final_norm, n, last->M);
       out = n;
     }
     push_status(1);  // a code raised during the call -> slot 1
@@ -383,7 +444,8 @@ int rldx_llm_prefill(rldx_llm* h, const void* hidden_in, void* hidden_out, void*
       ck(cudaGraphLaunch(h->exec, st), "graph launch");
     else
       h->run_ops(st);
-    ck(cudaMemcpyAsync(hidden_out, h->out, bytes, cudaMemcpyDefault, st), "hidden out");
+    ck(cudaMemcpyAsync(hidden_out, h->out, static_cast<size_t>(h->out_rows) * h->D * 2, cudaMemcpyDefault, st),
+       "hidden out");
     ck(cudaEventRecord(h->status.done, st), "status event");
   });
 }
@@ -395,6 +457,8 @@ int rldx_llm_status(rldx_llm* h, int wait, unsigned int* code) {
 }
 
 int rldx_llm_launch_count(const rldx_llm* h) { return h ? static_cast<int>(h->ops.size()) : 0; }
+
+int rldx_llm_out_tokens(const rldx_llm* h) { return h ? h->post.T : 0; }
 
 int rldx_llm_set_deepstack(rldx_llm* h, const void* features, void* stream) {
   if (!h || !features) return set_error(RLDX_ERR_ARG, "llm_set_deepstack: null argument");

@@ -93,6 +93,81 @@ cudaError_t launch_rows_add(__nv_bfloat16* x, const int* rows, int nrows, const 
   return cudaGetLastError();
 }
 
+// Video-token compression of B sequences [B, T, D] -> [B, T2, D], T2 = T - (end - begin) + 1:
+// the rows [begin, end) become one row, their mean, at `begin`; the rows before and after are
+// copied in order.  Blocks [0, mean_blocks) each own 64 columns of one sequence's mean row:
+// 8 column groups x 32 row lanes sum the dropped rows in fp32 (lane l takes rows begin + l,
+// begin + l + 32, ...), the lane partials are added in lane order through shared memory (a fixed
+// order, so the result does not depend on scheduling), the sum is rounded to bf16, divided by the
+// row count and rounded again (the module's bf16 sum followed by a bf16 true division).  The
+// other blocks copy the kept rows, 16 bytes per thread.
+__global__ void __launch_bounds__(256) compress_rows_kernel(const __nv_bfloat16* __restrict__ x,
+                                                            __nv_bfloat16* __restrict__ y, int B, int T, int D,
+                                                            int begin, int end, int mean_blocks) {
+  const int T2 = T - (end - begin) + 1;
+  if (static_cast<int>(blockIdx.x) < mean_blocks) {
+    __shared__ float part[32][65];
+    const int per_seq = D / 64;
+    const int b = blockIdx.x / per_seq, c0 = (blockIdx.x % per_seq) * 64;
+    const int grp = threadIdx.x & 7, lane = threadIdx.x >> 3;
+    float acc[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) acc[k] = 0.f;
+    const __nv_bfloat16* base = x + static_cast<long long>(b) * T * D + c0 + grp * 8;
+#pragma unroll 4
+    for (int r = begin + lane; r < end; r += 32) {
+      const uint4 v = *reinterpret_cast<const uint4*>(base + static_cast<long long>(r) * D);
+      const __nv_bfloat162* hv = reinterpret_cast<const __nv_bfloat162*>(&v);
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const float2 f = __bfloat1622float2(hv[k]);
+        acc[2 * k] += f.x;
+        acc[2 * k + 1] += f.y;
+      }
+    }
+#pragma unroll
+    for (int k = 0; k < 8; ++k) part[lane][grp * 8 + k] = acc[k];
+    __syncthreads();
+    if (threadIdx.x < 64) {
+      float sum = 0.f;
+      for (int l = 0; l < 32; ++l) sum += part[l][threadIdx.x];
+      const float rounded = __bfloat162float(__float2bfloat16_rn(sum));
+      const float mean = __fdiv_rn(rounded, static_cast<float>(end - begin));
+      y[(static_cast<long long>(b) * T2 + begin) * D + c0 + threadIdx.x] = __float2bfloat16_rn(mean);
+    }
+    return;
+  }
+  const int kept = T2 - 1;
+  if (kept <= 0) return;
+  const int nv = D / 8;
+  const long long total = static_cast<long long>(B) * kept * nv;
+  const long long stride = static_cast<long long>(gridDim.x - mean_blocks) * blockDim.x;
+  for (long long i = static_cast<long long>(blockIdx.x - mean_blocks) * blockDim.x + threadIdx.x; i < total;
+       i += stride) {
+    const int v = static_cast<int>(i % nv);
+    const long long br = i / nv;
+    const int j = static_cast<int>(br % kept);
+    const int b = static_cast<int>(br / kept);
+    const int r2 = j < begin ? j : j + 1;                  // output row (the mean row is skipped)
+    const int r = r2 < begin ? r2 : r2 - begin - 1 + end;  // source row
+    reinterpret_cast<uint4*>(y + (static_cast<long long>(b) * T2 + r2) * D)[v] =
+        reinterpret_cast<const uint4*>(x + (static_cast<long long>(b) * T + r) * D)[v];
+  }
+}
+
+cudaError_t launch_compress_rows(const __nv_bfloat16* x, __nv_bfloat16* y, int B, int T, int D, int begin, int end,
+                                 cudaStream_t stream) {
+  if (B <= 0 || D % 64 || begin < 0 || end <= begin || end > T) return cudaErrorInvalidValue;
+  const long long mean_blocks = static_cast<long long>(B) * (D / 64);
+  const long long kept = static_cast<long long>(B) * (T - (end - begin)) * (D / 8);
+  long long copy_blocks = (kept + 255) / 256;
+  if (copy_blocks > 4 * 148) copy_blocks = 4 * 148;
+  if (mean_blocks + copy_blocks > (1LL << 31) - 1) return cudaErrorInvalidValue;
+  compress_rows_kernel<<<static_cast<unsigned>(mean_blocks + copy_blocks), 256, 0, stream>>>(
+      x, y, B, T, D, begin, end, static_cast<int>(mean_blocks));
+  return cudaGetLastError();
+}
+
 // Key mask of the joint sequence [VL | SA | P] of every observation: VL keys from the backbone
 // mask, action / state / time keys visible, physics keys from the observation's physics mask.
 __global__ void key_mask_kernel(uint8_t* __restrict__ kmask, const uint8_t* __restrict__ vl,

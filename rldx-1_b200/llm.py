@@ -20,6 +20,16 @@ custom_llm_chain.py:137-161) are added after layer i to those rows of every sequ
 eager path's single bf16 rounding (Qwen3VLTextModel._deepstack_process,
 modeling_qwen3_vl.py:1102-1113); the rows and the number of deepstack layers are bound on the
 first call.
+
+Video-token compression (the VTC backbone wraps every text layer in LayerWrapper with
+internal_projection=4, rldx/model/modules/backbone/modeling_vtc.py:158-164) runs inside the same
+graph: `compress_info` (the dict of the reference's _find_compress_info,
+rldx/inference/backbone/llm/model/graph_safe_qwen3vl_text_model.py:26-59, which
+find_compress_info below computes from the prompt's input_ids) makes the chain replace the old
+frames' token rows [static_begin, static_end) with their mean before layer compress_layer_idx;
+the output then has static_out_len tokens.  Where the reference engine runs a pre-compression
+chain, a torch compress step and a post-compression chain (custom_backbone_chain.py:177-214),
+this is one chain and one graph.
 """
 
 from __future__ import annotations
@@ -41,6 +51,51 @@ def _raw_layer(layer: nn.Module) -> nn.Module:
     return layer
 
 
+def find_compress_rows(input_ids: torch.Tensor, img_pattern=(151652,), num_views=None):
+    """Static (begin, end) of the compressed region, the rows LayerWrapper.get_removing_indices
+    finds (layer_wrapper.py:25-51): begin = the first occurrence of `img_pattern` (the image-start
+    marker), end = its last occurrence, or the num_views-th last with image-wise encoding.  The
+    reference engine takes sequence 0's rows for the whole batch; here every sequence must give
+    the same rows (a batch whose prompts differ would be compressed wrongly), else ValueError."""
+    ids = input_ids.detach().to("cpu", torch.int64)
+    if ids.dim() == 1:
+        ids = ids[None]
+    pat = torch.as_tensor(list(img_pattern), dtype=torch.int64)
+    n = pat.numel()
+    if ids.shape[1] < n:
+        raise ValueError("input_ids shorter than the image pattern")
+    hit = torch.ones(ids.shape[0], ids.shape[1] - n + 1, dtype=torch.bool)
+    for j in range(n):
+        hit &= ids[:, j: ids.shape[1] - n + 1 + j] == pat[j]
+    rows = set()
+    for b in range(ids.shape[0]):
+        pos = torch.nonzero(hit[b]).flatten().tolist()
+        if not pos:
+            raise ValueError(f"sequence {b} has no image-start marker {list(img_pattern)}")
+        if num_views is not None and int(num_views) > len(pos):
+            raise ValueError(f"sequence {b} has {len(pos)} markers, fewer than num_views={num_views}")
+        rows.add((pos[0], pos[-int(num_views)] if num_views is not None else pos[-1]))
+    if len(rows) != 1:
+        raise ValueError(f"the sequences of the batch compress different rows: {sorted(rows)}")
+    return rows.pop()
+
+
+def find_compress_info(layers, input_ids: torch.Tensor, n_cog_tokens: int = 0, num_views=None):
+    """The reference's _find_compress_info (graph_safe_qwen3vl_text_model.py:26-59): the first
+    LayerWrapper whose layer_idx equals its internal_projection compresses; returns
+    {"compress_layer_idx", "static_begin", "static_end", "static_out_len"}, or None when no layer
+    compresses or begin >= end (one frame: LayerWrapper's compress_mask is false)."""
+    for idx, layer in enumerate(layers):
+        if hasattr(layer, "layer") and hasattr(layer, "internal_projection") and \
+                layer.layer_idx == layer.internal_projection:
+            b, e = find_compress_rows(input_ids, getattr(layer, "img_pattern", (151652,)), num_views)
+            if b >= e:
+                return None
+            L = int(input_ids.shape[-1]) + int(n_cog_tokens)
+            return {"compress_layer_idx": idx, "static_begin": b, "static_end": e, "static_out_len": b + 1 + (L - e)}
+    return None
+
+
 def unsigned_sin(signed_sin: torch.Tensor) -> torch.Tensor:
     half = signed_sin.shape[-1] // 2
     sin = signed_sin.clone()
@@ -50,12 +105,23 @@ def unsigned_sin(signed_sin: torch.Tensor) -> torch.Tensor:
 
 class B200LLMChain(nn.Module):
     """norm_weight_first / causal_block select the memory module's variant (see
-    B200MemoryChain); a layer without q_norm / k_norm runs without the per-head QK RMSNorm."""
+    B200MemoryChain); a layer without q_norm / k_norm runs without the per-head QK RMSNorm.
+    compress_info: video-token compression (find_compress_info's dict); pos_cos / signed_sin are
+    then the tables of the uncompressed sequence."""
 
     def __init__(self, layers, norm: nn.Module, pos_cos: torch.Tensor, signed_sin: torch.Tensor,
                  apply_final_norm: bool = True, *, device=None, use_graph: bool = True,
-                 norm_weight_first: bool = False, causal_block: int = 1):
+                 norm_weight_first: bool = False, causal_block: int = 1, compress_info: Optional[dict] = None):
         super().__init__()
+        self.compress_info = dict(compress_info) if compress_info else None
+        if self.compress_info is not None:
+            ci = self.compress_info
+            M = pos_cos.shape[0]
+            b, e, li = int(ci["static_begin"]), int(ci["static_end"]), int(ci["compress_layer_idx"])
+            if not (0 <= b < e <= M and 0 <= li < len(layers)):
+                raise ValueError(f"compress_info {ci} does not fit {len(layers)} layers over {M} tokens")
+            if "static_out_len" in ci and int(ci["static_out_len"]) != M - (e - b) + 1:
+                raise ValueError(f"compress_info static_out_len {ci['static_out_len']} != {M - (e - b) + 1}")
         self.layers = [_raw_layer(layer) for layer in layers]
         if not self.layers:
             raise ValueError("B200LLMChain needs at least one decoder layer")
@@ -103,6 +169,10 @@ class B200LLMChain(nn.Module):
                         no_qk_norm=0 if self.qk_norm else 1, norm_weight_first=1 if self.norm_weight_first else 0,
                         causal_block=self.causal_block, deepstack_layers=deepstack_layers if nrows else 0,
                         deepstack_rows=nrows)
+        if self.compress_info is not None:
+            cfg.compress_layer = int(self.compress_info["compress_layer_idx"])
+            cfg.compress_begin = int(self.compress_info["static_begin"])
+            cfg.compress_end = int(self.compress_info["static_end"])
         arr = (LlmLayerWeights * len(self.layers))()
         for i, layer in enumerate(self.layers):
             a, m = layer.self_attn, layer.mlp
@@ -128,6 +198,15 @@ class B200LLMChain(nn.Module):
         self._handle = handle
         self._batch = batch
         self._ds = (deepstack_layers, tuple(deepstack_rows.tolist())) if nrows else None
+
+    @property
+    def out_tokens(self) -> int:
+        """Tokens per sequence of the output (the compressed count with compress_info)."""
+        if self._handle:
+            return int(_lib.load().rldx_llm_out_tokens(self._handle))
+        M = self.cos.shape[0]
+        ci = self.compress_info
+        return M - (int(ci["static_end"]) - int(ci["static_begin"])) + 1 if ci else M
 
     @property
     def launches_per_call(self) -> int:
@@ -166,7 +245,7 @@ class B200LLMChain(nn.Module):
         x = hidden_states
         if x.device != self.device or x.dtype != torch.bfloat16 or not x.is_contiguous():
             x = x.to(device=self.device, dtype=torch.bfloat16).contiguous()
-        out = torch.empty_like(x)
+        out = torch.empty(B, self.out_tokens, D, dtype=torch.bfloat16, device=self.device)
         stream = torch.cuda.current_stream(self.device)
         if ds is not None:
             L, rows = ds

@@ -11,7 +11,14 @@ oracle has the same parameter names, so the same seed gives the same weights) an
 per-layer hidden states and the final-norm output.  The RoPE tables come from the reference's
 own rotary embedding with 3-D (mRoPE) position ids of an image grid followed by text.
 
-Usage:  python tests/golden/make_golden_llm.py [--deepstack-only]
+The video-token-compression fixtures (llm_vtc_*.pt) wrap six such layers in the reference's own
+LayerWrapper (rldx/model/modules/backbone/layer_wrapper.py, internal_projection=4 as
+modeling_vtc.py:158-164 wires it) and run them through the text model's layer loop
+(modeling_qwen3_vl.py:1062-1080: each wrapper returns the layer output and the kwargs it
+compressed, which the loop carries to the next layer).  They also record the wrapper's
+get_removing_indices on a few marker layouts.
+
+Usage:  python tests/golden/make_golden_llm.py [--deepstack-only | --vtc-only]
 """
 
 from __future__ import annotations
@@ -142,14 +149,114 @@ def fixture_deepstack(mod, dtype, batch):
             "hidden": hidden, "out": out}
 
 
+VTC_LAYERS = 6
+VISION_START, VISION_END, IMAGE_PAD = 151652, 151653, 151655
+
+
+def vtc_ids(frames: int, views: int = 1, patches: int = 16, prefix: int = 4, total: int = T) -> torch.Tensor:
+    """Prompt ids: `prefix` text ids, then per frame and view an image-start marker, `patches`
+    image ids and an image-end marker, then text up to `total` ids."""
+    ids = list(range(1000, 1000 + prefix))
+    for _ in range(frames * views):
+        ids += [VISION_START] + [IMAGE_PAD] * patches + [VISION_END]
+    ids += list(range(2000, 2000 + total - len(ids)))
+    return torch.tensor(ids[:total], dtype=torch.long)
+
+
+def vtc_positions(ids: torch.Tensor, batch: int) -> torch.Tensor:
+    """[3, B, T] mRoPE ids for the layout of vtc_ids: text and markers advance all three ids,
+    each 4 x 4 image block shares its temporal id and spreads height / width over the grid."""
+    pos = torch.zeros(3, ids.numel(), dtype=torch.long)
+    p, t = 0, 0
+    while t < ids.numel():
+        if ids[t] == IMAGE_PAD:
+            n = 0
+            while t + n < ids.numel() and ids[t + n] == IMAGE_PAD:
+                pos[0, t + n] = p
+                pos[1, t + n] = p + n // 4
+                pos[2, t + n] = p + n % 4
+                n += 1
+            t += n
+            p += 4
+        else:
+            pos[:, t] = p
+            p += 1
+            t += 1
+    return pos[:, None, :].expand(3, batch, ids.numel()).contiguous()
+
+
+def fixture_vtc(mod, wrapper_mod, dtype, batch):
+    """Six layers wrapped in the reference LayerWrapper (compression before layer 4) over three
+    frames of 16 image tokens each: the first two frames (rows [4, 40)) become one mean token."""
+    import copy
+
+    global CFG
+    saved = CFG
+    CFG = copy.replace(saved, layers=VTC_LAYERS) if hasattr(copy, "replace") else oq.Qwen3Config(
+        **{**vars(saved), "layers": VTC_LAYERS})
+    try:
+        stack, rotary = reference_stack(mod)
+    finally:
+        cfg_vtc, CFG = CFG, saved
+    oq.init_weights(stack, seed=2025)
+    stack = stack.to(dtype).eval()
+    wrapped = [wrapper_mod.LayerWrapper(layer, layer_idx=i, internal_projection=4, img_pattern=[VISION_START],
+                                        motion_token=1) for i, layer in enumerate(stack.layers)]
+    ids = vtc_ids(frames=3)[None].expand(batch, T).contiguous()
+    g = torch.Generator().manual_seed(9)
+    h0 = torch.randn(batch, T, cfg_vtc.hidden, generator=g).to(dtype)
+    position_ids = vtc_positions(ids[0], batch)
+    with torch.no_grad():
+        cos, sin = rotary(h0, position_ids)
+        kw = {"attention_mask": None, "position_ids": position_ids[0], "past_key_values": None,
+              "cache_position": torch.arange(T), "position_embeddings": (cos, sin)}
+        hidden = []
+        h = h0
+        for layer in wrapped:  # the text model's loop, modeling_qwen3_vl.py:1062-1080
+            out = layer(h, ids, **kw)
+            h = out[0]
+            for key in ("attention_mask", "position_ids", "past_key_values", "cache_position",
+                        "position_embeddings"):
+                if key in out[1]:
+                    kw[key] = out[1][key]
+            hidden.append(h.clone())
+        out = stack.norm(h)
+        begin, end = wrapped[4].get_removing_indices(h0, ids)
+    return {"config": vars(cfg_vtc), "seed": 2025, "dtype": str(dtype), "batch": batch,
+            "inputs": {"hidden": h0, "cos": cos, "sin": sin, "input_ids": ids},
+            "compress": (4, int(begin[0, 0]), int(end[0, 0])), "hidden": hidden, "out": out}
+
+
+def vtc_index_cases(wrapper_mod):
+    """The wrapper's (begin, end) on marker layouts: several frames, one frame (begin == end: no
+    compression), and image-wise encoding with 2 and 3 views per frame (end = the num_views-th
+    last marker)."""
+    layer = wrapper_mod.LayerWrapper(nn.Identity(), layer_idx=4, internal_projection=4,
+                                     img_pattern=[VISION_START], motion_token=1)
+    cases = []
+    for frames, views, num_views in ((3, 1, None), (1, 1, None), (4, 1, None), (2, 2, 2), (3, 3, 3), (2, 2, None)):
+        ids = vtc_ids(frames, views, patches=6, prefix=3, total=3 + frames * views * 8 + 5)[None]
+        b, e = layer.get_removing_indices(torch.zeros(1, ids.shape[1], 1), ids, num_views=
+                                          [num_views] if num_views is not None else None)
+        cases.append({"input_ids": ids, "num_views": num_views, "begin": int(b[0, 0]), "end": int(e[0, 0])})
+    return cases
+
+
 def main():
     mod = import_reference()
     only_ds = "--deepstack-only" in sys.argv
+    only_vtc = "--vtc-only" in sys.argv
+    wrapper_mod = importlib.import_module("rldx.model.modules.backbone.layer_wrapper")
     for dtype, dn in ((torch.float32, "fp32"), (torch.bfloat16, "bf16")):
         for batch in (1, 2):
-            if not only_ds:
+            if not only_ds and not only_vtc:
                 torch.save(fixture(mod, dtype, batch), HERE / f"llm_b{batch}_{dn}.pt")
-            torch.save(fixture_deepstack(mod, dtype, batch), HERE / f"llm_ds_b{batch}_{dn}.pt")
+            if not only_vtc:
+                torch.save(fixture_deepstack(mod, dtype, batch), HERE / f"llm_ds_b{batch}_{dn}.pt")
+            fx = fixture_vtc(mod, wrapper_mod, dtype, batch)
+            if batch == 1:
+                fx["index_cases"] = vtc_index_cases(wrapper_mod)
+            torch.save(fx, HERE / f"llm_vtc_b{batch}_{dn}.pt")
     for f in sorted(HERE.glob("llm_*.pt")):
         print(f.name, f.stat().st_size)
 

@@ -38,7 +38,7 @@ def test_struct_layouts_match_header():
     assert C.sizeof(_lib.BlockWeights) == 3 * (4 * 16 + 16)
     assert C.sizeof(_lib.SingleBlockWeights) == 2 * (3 * 16 + 16)
     assert C.sizeof(_lib.QkvSegment) == 64
-    assert C.sizeof(_lib.LlmConfig) == 16 * 4 and C.sizeof(_lib.LlmLayerWeights) == 11 * 8
+    assert C.sizeof(_lib.LlmConfig) == 19 * 4 and C.sizeof(_lib.LlmLayerWeights) == 11 * 8
     assert C.sizeof(_lib.LlmWeights) == 5 * 8
     assert C.sizeof(_lib.AttentionDesc) == 3 * 8 + 8 * 4 + 8 + 3 * 8 + 3 * 4 + 3 * 4 + 3 * 4 + 4
     assert C.sizeof(_lib.ResLnSegment) == 6 * 8 + 2 * 4 + 8 + 8
@@ -58,3 +58,4 @@ def test_null_arguments_are_rejected_without_a_device(lib):
     assert lib.rldx_msat_block_end(None, 0, 0, C.byref(n)) == _lib.RLDX_ERR_ARG
     assert lib.rldx_msat_run_partial(None, None, 0, None) == _lib.RLDX_ERR_ARG
     assert lib.rldx_get_wait_limit(None) == _lib.RLDX_ERR_ARG
+    assert lib.rldx_llm_out_tokens(None) == 0 and lib.rldx_llm_launch_count(None) == 0

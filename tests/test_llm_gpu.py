@@ -173,3 +173,75 @@ def test_memory_cache_over_consecutive_calls(cuda, concat):
         check_close(out, ref, f"step {step}")
     dev_cache.reset_memory()
     assert int(dev_cache._cached_cog.abs().sum().item()) == 0
+
+
+@pytest.mark.parametrize("batch", [1, 2])
+def test_llm_video_token_compression_matches_reference_golden(cuda, batch):
+    """Six layers wrapped in the reference's LayerWrapper (compression before layer 4 of the rows
+    of the two old frames, tests/golden/make_golden_llm.py): one chain, one graph, 100 tokens in,
+    65 out; the compression info comes from the prompt's input_ids as the reference engine
+    derives it.  Eager launch list == graph."""
+    from rldx_b200.llm import find_compress_info
+
+    fx = torch.load(GOLD / f"llm_vtc_b{batch}_bf16.pt", weights_only=False)
+    cfg = oq.Qwen3Config(**fx["config"])
+    stack = oq.init_weights(oq.TextStack(cfg), seed=fx["seed"]).to(BF)
+    inp = fx["inputs"]
+    wrapped = [torch.nn.Module() for _ in stack.layers]
+    for i, (w, layer) in enumerate(zip(wrapped, stack.layers)):
+        w.layer, w.layer_idx, w.internal_projection, w.img_pattern = layer, i, 4, [151652]
+    ci = find_compress_info(wrapped, inp["input_ids"])
+    assert (ci["compress_layer_idx"], ci["static_begin"], ci["static_end"]) == fx["compress"]
+    cos, ssin = inp["cos"][0].to(cuda), signed(inp["sin"][0]).to(cuda)
+    chain = B200LLMChain(wrapped, stack.norm, cos, ssin, compress_info=ci)
+    out = chain(inp["hidden"].to(cuda))
+    torch.cuda.synchronize()
+    assert out.shape == fx["out"].shape and chain.out_tokens == 65
+    check_close(out, fx["out"], "final norm after compression")
+    eager = B200LLMChain(wrapped, stack.norm, cos, ssin, compress_info=ci, use_graph=False)
+    assert torch.equal(eager(inp["hidden"].to(cuda)), out)
+    last = B200LLMChain(wrapped, stack.norm, cos, ssin, compress_info=ci, apply_final_norm=False)
+    h = last(inp["hidden"].to(cuda))
+    torch.cuda.synchronize()
+    check_close(h, fx["hidden"][-1], "last hidden after compression")
+    assert chain.device_status() == 0
+
+
+@pytest.mark.parametrize("layer,begin,end", [(0, 3, 40), (1, 0, 100), (1, 10, 100), (2, 50, 51)])
+def test_llm_compression_edges_against_oracle(cuda, layer, begin, end):
+    """Compression before the first layer, of the whole sequence, up to the last row, and of a
+    single row (the mean of one row is the row), against the pinned oracle."""
+    fx = torch.load(GOLD / "llm_b2_bf16.pt", weights_only=False)
+    cfg = oq.Qwen3Config(**fx["config"])
+    stack = oq.init_weights(oq.TextStack(cfg), seed=fx["seed"]).to(BF)
+    inp = fx["inputs"]
+    ref = stack(inp["hidden"], inp["cos"], inp["sin"], compress=(layer, begin, end))
+    chain = B200LLMChain(stack.layers, stack.norm, inp["cos"][0].to(cuda), signed(inp["sin"][0]).to(cuda),
+                         compress_info={"compress_layer_idx": layer, "static_begin": begin, "static_end": end})
+    out = chain(inp["hidden"].to(cuda))
+    torch.cuda.synchronize()
+    assert out.shape == ref.shape
+    check_close(out, ref, f"compress {layer} [{begin}, {end})")
+
+
+def test_llm_config5_compression_against_oracle(cuda):
+    """Config-5 decoder dims with the VTC layout of the bench: 4 frames x (marker + 196 patches +
+    marker) after 8 text ids, 48 text ids and 256 cognition tokens (1104 tokens); the first three
+    frames are compressed before layer 1 of 2 (511 tokens after)."""
+    from rldx_b200.llm import find_compress_rows
+
+    cfg = oq.Qwen3Config(hidden=2048, q_heads=16, kv_heads=2, head_dim=128, ffn=11008, layers=2)
+    stack = oq.init_weights(oq.TextStack(cfg), seed=6).to(BF)
+    ids = torch.tensor(list(range(8)) + ([151652] + [151655] * 196 + [151653]) * 4 + list(range(48)))
+    begin, end = find_compress_rows(ids)
+    assert (begin, end) == (8, 8 + 3 * 198)
+    T = ids.numel() + 256
+    cos, sin = oq.rope_tables(cfg, torch.arange(T), dtype=BF)
+    x = torch.randn(1, T, cfg.hidden, generator=torch.Generator().manual_seed(4)).to(BF)
+    ref = stack(x, cos[None], sin[None], compress=(1, begin, end))
+    chain = B200LLMChain(stack.layers, stack.norm, cos.to(cuda), signed(sin).to(cuda),
+                         compress_info={"compress_layer_idx": 1, "static_begin": begin, "static_end": end})
+    out = chain(x.to(cuda))
+    torch.cuda.synchronize()
+    assert out.shape == (1, 511, cfg.hidden)
+    check_close(out, ref, "config-5 compression")

@@ -58,3 +58,32 @@ def test_oracle_deepstack_matches_reference(name):
             assert torch.equal(got, exp), (got.float() - exp.float()).abs().max()
         else:
             torch.testing.assert_close(got, exp, rtol=1e-5, atol=1e-5)
+
+
+@pytest.mark.parametrize("name", [f"llm_vtc_b{b}_{dt}.pt" for b in (1, 2) for dt in ("fp32", "bf16")])
+def test_oracle_video_token_compression_matches_reference(name):
+    """Six layers with the reference's LayerWrapper (compression before layer 4): the rows of the
+    two old frames become one mean token, the RoPE rows follow, layers 4 and 5 run on 65 tokens."""
+    fx = torch.load(GOLD / name, weights_only=False)
+    cfg = oq.Qwen3Config(**fx["config"])
+    dtype = torch.bfloat16 if "bf16" in name else torch.float32
+    stack = oq.init_weights(oq.TextStack(cfg), seed=fx["seed"]).to(dtype)
+    inp = fx["inputs"]
+    begins, ends = oq.find_compress_rows(inp["input_ids"])
+    assert (begins[0], ends[0]) == fx["compress"][1:]
+    out, hidden = stack(inp["hidden"], inp["cos"], inp["sin"], return_hidden=True, compress=fx["compress"])
+    assert [tuple(h.shape) for h in hidden] == [tuple(h.shape) for h in fx["hidden"]]
+    for got, exp in list(zip(hidden, fx["hidden"])) + [(out, fx["out"])]:
+        if dtype == torch.bfloat16:
+            assert torch.equal(got, exp), (got.float() - exp.float()).abs().max()
+        else:
+            torch.testing.assert_close(got, exp, rtol=1e-5, atol=1e-5)
+
+
+def test_compress_rows_match_reference_marker_search():
+    """find_compress_rows against the wrapper's get_removing_indices on the recorded layouts
+    (several frames, one frame, image-wise encoding with 2 and 3 views)."""
+    fx = torch.load(GOLD / "llm_vtc_b1_fp32.pt", weights_only=False)
+    for case in fx["index_cases"]:
+        b, e = oq.find_compress_rows(case["input_ids"], num_views=case["num_views"])
+        assert (b[0], e[0]) == (case["begin"], case["end"]), case
