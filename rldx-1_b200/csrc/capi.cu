@@ -174,6 +174,12 @@ constexpr double kChunkNs = 20.0;
 constexpr double kUnitNs = 1500.0;
 constexpr double kTmaOpNs = 210.0;        // one TMA box occupies the SM's copy engine >= ~400 cycles
 constexpr double kTmaBytesPerNs = 175.0;  // ... and streams ~92 bytes per cycle beyond ~36 KB
+// A K-split unit also pays for its tile's arrival count and the epilogue warps' barrier rounds,
+// and the last one waits for the partials of its tile before its epilogue can start: ~1 us
+// beyond the partials' traffic (B200: the config-2 output projection runs 15.6 us on 64-column
+// tiles without splits, 18.2 us on 128-column tiles split in two, which the model without this
+// term ranked the other way round).
+constexpr double kSplitNs = 1000.0;
 constexpr int kMinSplitChunks = 4;
 constexpr int kMaxSplit = 8;
 constexpr size_t kCounterBytes = ((kMaxUnits * 4 + 255) / 256) * 256;
@@ -211,7 +217,7 @@ double unit_ns(const ProbShape& s, int bn, int chunks, int nsplit) {
   const int ksub = std::max(1, std::min(ksub_for(s, bn), chunks));
   double t = ((chunks + ksub - 1) / ksub) * slot_ns(s, bn, ksub);
   t += kUnitNs + bn * epi_ns_per_col(s.epi);
-  if (nsplit > 1) t += s.live_rows * bn * 4.0 * 2.0 / kFillBytesPerNs;
+  if (nsplit > 1) t += s.live_rows * bn * 4.0 * 2.0 / kFillBytesPerNs + kSplitNs;
   return t;
 }
 
@@ -256,6 +262,11 @@ void choose_tiles_uncached(const ProbShape* sh, const int* fixed_bn, int n, int 
                            bool can_split, int* best_bn, int* best_split) {
   double best_mk = 1e300;
   int cand[kMaxProblems][3], ncand[kMaxProblems];
+  // 64-column tiles for multi-tile problems only when 128-column tiles leave SMs idle: there
+  // they fill the SMs without K splits; elsewhere they only multiply the A re-reads
+  long long tiles128 = 0;
+  for (int i = 0; i < n; ++i) tiles128 += static_cast<long long>(sh[i].tiles_m) * ((sh[i].N + 127) / 128);
+  const bool narrow = tiles128 < nsm;
   for (int i = 0; i < n; ++i) {
     if (fixed_bn[i]) {
       cand[i][0] = fixed_bn[i];
@@ -266,7 +277,7 @@ void choose_tiles_uncached(const ProbShape* sh, const int* fixed_bn, int n, int 
     int k = 0;
     for (int bn : {64, 128, 256}) {
       if (bn > nmax) continue;
-      if (sh[i].tiles_m >= 2 && bn == 64 && nmax > 64) continue;  // A re-reads: keep tiles wide
+      if (sh[i].tiles_m >= 2 && bn == 64 && nmax > 64 && !narrow) continue;  // A re-reads: keep tiles wide
       cand[i][k++] = bn;
     }
     ncand[i] = k;

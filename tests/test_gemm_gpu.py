@@ -213,10 +213,11 @@ def _block_like(cuda, seed, hidden=4096):
     return keep, cases
 
 
-@pytest.mark.parametrize("hidden", [1536, 4096])
+@pytest.mark.parametrize("hidden", [3072, 4096])
 def test_split_k_workspace_matches_reference_and_is_deterministic(cuda, hidden):
     """Grouped long-K GEMM (w3-like, residual epilogue) through the K-split path: close to the
-    fp32 reference, bit-identical across calls, counters back at zero."""
+    fp32 reference, bit-identical across calls, counters back at zero.  (At K = 1536 the planner
+    runs these shapes on 64-column tiles without splits: see the next test.)"""
     keep, cases = _block_like(cuda, 21 + hidden, hidden)
     outs = [torch.empty(x.shape[0], 1536, dtype=BF, device=cuda) for x, *_ in cases]
     descs = [ops.gemm_desc(x, w, o, b, add=res) for (x, w, b, res), o in zip(cases, outs)]
@@ -235,6 +236,25 @@ def test_split_k_workspace_matches_reference_and_is_deterministic(cuda, hidden):
         ref = r(ref_finish(x.float() @ w.float().t(), b, _lib.BIAS_FUSED, 0) + res.float())
         close(o, ref)
     assert int(ws[:COUNTER_BYTES].count_nonzero()) == 0
+    assert ops.device_error() == 0
+
+
+def test_narrow_launch_prefers_unsplit_64_column_tiles(cuda):
+    """The output-projection shape (K = N = 1536 over [VL 512 | SA 18 | P 32]) has 72 tiles of
+    128 columns for 148 SMs: the planner fills the SMs with 64-column tiles instead of K splits
+    (measured faster on B200), and the result matches the fp32 reference."""
+    keep, cases = _block_like(cuda, 77, 1536)
+    outs = [torch.empty(x.shape[0], 1536, dtype=BF, device=cuda) for x, *_ in cases]
+    descs = [ops.gemm_desc(x, w, o, b, add=res) for (x, w, b, res), o in zip(cases, outs)]
+    plan = ops.gemm_plan(descs)
+    if plan["ctas"] >= 144:  # the part has the full SM count the plan is tuned for
+        assert plan["tile_n"] == 64 and plan["splits"] == 1, plan
+    assert ops.gemm_workspace_size(descs) == 0
+    ops.gemm(descs)
+    torch.cuda.synchronize()
+    for (x, w, b, res), o in zip(cases, outs):
+        ref = r(ref_finish(x.float() @ w.float().t(), b, _lib.BIAS_FUSED, 0) + res.float())
+        close(o, ref)
     assert ops.device_error() == 0
 
 

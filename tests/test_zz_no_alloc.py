@@ -26,13 +26,14 @@ def _static(descs):
 
 
 def _problems(cuda, seed):
-    """Three width-1536 projections (rows 512 / 18 / 32) with a residual add: the planner splits
-    them along K and needs less workspace than the static scratch holds."""
+    """A w3-like projection of the 18 action-stream rows (K = 4096 -> 1536) with a residual add:
+    its few output tiles leave most SMs idle, so the planner splits it along K, and any split
+    plan of one 18-row problem needs less workspace than the static scratch holds."""
     g = torch.Generator(device=cuda).manual_seed(seed)
     keep, descs, outs = [], [], []
-    for M in (512, 18, 32):
-        x = torch.randn(M, 1536, device=cuda, generator=g).to(BF)
-        w = (torch.randn(1536, 1536, device=cuda, generator=g) * 0.03).to(BF)
+    for M in (18,):
+        x = torch.randn(M, 4096, device=cuda, generator=g).to(BF)
+        w = (torch.randn(1536, 4096, device=cuda, generator=g) * 0.03).to(BF)
         b = (torch.randn(1536, device=cuda, generator=g) * 0.1).to(BF)
         res = torch.randn(M, 1536, device=cuda, generator=g).to(BF)
         out = torch.empty(M, 1536, dtype=BF, device=cuda)
