@@ -90,3 +90,74 @@ class Heartbeat:
             if now - last > self.timeout_s:
                 dead.append(r)
         return dead
+
+
+class ReplicaPool:
+    """One serving endpoint over several GPUs of one process: a replica of the action head per
+    device, each device's contiguous share of a batch of independent observations (shard_bounds)
+    copied in, run through its chain's captured graph and copied back on that device's own
+    stream, so one host thread keeps every GPU busy at once and no device reads another's memory.
+
+        pool = ReplicaPool(lambda dev: B200ExpandedActionHeadChain(gs, dev), ["cuda:0", "cuda:1"])
+        actions = pool(vl_embs=..., state=..., embodiment_id=..., init_noise=..., ...)  # CPU tensor
+
+    The keyword arguments are the chain's forward() arguments, batch-major tensors on the host
+    (pinned memory lets the copies overlap) or on any device; actions come back as one CPU tensor
+    in the input order.  A replica binds its shard's shapes on the first call, so later batches
+    must split the same way (the chain raises on shape drift).  The reference serves one GPU per
+    process and batches inside it (rldx/model/core/rldx.py:1072-1082)."""
+
+    def __init__(self, make_chain: Callable, devices: Sequence):
+        if not devices:
+            raise ValueError("ReplicaPool needs at least one device")
+        self.devices = [torch.device(d) for d in devices]
+        self.chains = [make_chain(d) for d in self.devices]
+        self.streams = []
+        for d in self.devices:
+            with torch.cuda.device(d):
+                self.streams.append(torch.cuda.Stream(d))
+        self._host_out = None
+
+    def __len__(self) -> int:
+        return len(self.chains)
+
+    def __call__(self, **observations) -> torch.Tensor:
+        batch = {k: v for k, v in observations.items() if isinstance(v, torch.Tensor)}
+        n = {v.shape[0] for v in batch.values()}
+        if len(n) != 1:
+            raise ValueError(f"observation tensors disagree on the batch size: {sorted(n)}")
+        n = n.pop()
+        world = len(self.chains)
+        outs, spans = [], []
+        for r, (chain, dev, stream) in enumerate(zip(self.chains, self.devices, self.streams)):
+            s, e = shard_bounds(n, world, r)
+            spans.append((s, e))
+            if e == s:
+                outs.append(None)
+                continue
+            with torch.cuda.device(dev), torch.cuda.stream(stream):
+                args = {k: (v[s:e].to(dev, non_blocking=True) if k in batch else v)
+                        for k, v in observations.items()}
+                outs.append(chain(**args))
+        for o in outs:
+            if o is not None:
+                shape = (n,) + tuple(o.shape[1:])
+                break
+        else:
+            raise ValueError("empty batch")
+        if self._host_out is None or tuple(self._host_out.shape) != shape:
+            self._host_out = torch.empty(shape, dtype=torch.bfloat16).pin_memory()
+        for o, (s, e), dev, stream in zip(outs, spans, self.devices, self.streams):
+            if o is not None:
+                with torch.cuda.device(dev), torch.cuda.stream(stream):
+                    self._host_out[s:e].copy_(o, non_blocking=True)
+        for o, stream in zip(outs, self.streams):
+            if o is not None:
+                stream.synchronize()
+        for chain in self.chains:
+            code = chain.device_status(wait=False) if hasattr(chain, "device_status") else 0
+            if code:
+                from ._lib import RLDX_ERR_DEVICE, RldxError
+
+                raise RldxError(RLDX_ERR_DEVICE, f"device error 0x{code:x} recorded by a replica")
+        return self._host_out.clone()
