@@ -108,7 +108,9 @@ def max_over_ranks(x: float, world: int, device) -> float:
 
 
 class ClockSampler:
-    """nvidia-smi clocks / throttle reasons sampled every 100 ms during the timed region."""
+    """nvidia-smi clocks / throttle reasons sampled every 100 ms during the timed region.  Entering
+    waits (up to 5 s) for nvidia-smi's first line, so that a short timed region is sampled from
+    its start; only the samples that arrive inside the region are kept."""
 
     QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
@@ -118,6 +120,7 @@ class ClockSampler:
         self.gpu = gpu_index
         self.proc = None
         self.lines = []
+        self.start = 0
 
     def __enter__(self):
         try:
@@ -127,8 +130,12 @@ class ClockSampler:
                 stderr=subprocess.DEVNULL, text=True)
             self.t = threading.Thread(target=self._read, daemon=True)
             self.t.start()
+            t0 = time.time()
+            while not self.lines and time.time() - t0 < 5.0 and self.proc.poll() is None:
+                time.sleep(0.01)
         except OSError:
             self.proc = None
+        self.start = len(self.lines)  # samples from here on fall inside the timed region
         return self
 
     def _read(self):
@@ -146,7 +153,7 @@ class ClockSampler:
     def summary(self):
         sm, smax, reasons = [], None, set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for ln in self.lines:
+        for ln in self.lines[self.start:]:
             f = [x.strip() for x in ln.split(",")]
             if len(f) < 9:
                 continue
