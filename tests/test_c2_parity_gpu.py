@@ -74,7 +74,8 @@ def fp32_actions(head16, args16, cfg):
     tables = dict(rope.named_buffers())  # complex tables must not go through .to(bf16) again
     h32 = head16.float()
     try:
-        return om.denoise(h32, *[a.float() if a.is_floating_point() else a for a in args16], cfg.num_steps)
+        return om.denoise(h32, *[a.float() if a is not None and a.is_floating_point() else a for a in args16],
+                          cfg.num_steps)
     finally:
         head16.to(BF)  # back to the bf16 module (exact: the weights are bf16 values)
         for name, t in tables.items():
@@ -175,3 +176,29 @@ def test_full_rotation_rope_through_the_chain(cuda):
         head_c = fast_init(om.ActionHead(cfg), seed=3, cuda=cuda).to(BF)
         out_c = B200ExpandedActionHeadChain(head_c, cuda)(*d).cpu()
         assert not torch.equal(out_c, out)
+
+
+@pytest.mark.parametrize("addons", [False, True])
+def test_released_heads_at_full_size(cuda, addons):
+    """The reference's released heads at their real size (rldx/configs/model/rldx.py:81-112, the
+    `bench.py --workload production / production_addons` shapes): 4 double blocks with a 4096-wide
+    VL stream, then 8 single blocks; without add-ons (64 VL tokens, standard path,
+    vl_proj_to_sa) and with them (80 VL tokens, the physics stream, expanded blocks).  Actions
+    against the oracle's bf16 and fp32 control steps with the same criterion as config 2."""
+    from rldx_b200.chain import B200ActionHeadChain
+
+    cfg = om.MsatHeadConfig(n_vl=80 if addons else 64, depth=4, depth_single=8, vl_dim=4096,
+                            use_physics=addons, action_dim=64, state_dim=64, max_seq_len=512,
+                            physics_hist=16 if addons else 0, physics_fut=16 if addons else 0)
+    assert cfg.vl_mlp_hidden == 10922 and cfg.single_expanded == 6144
+    head = fast_init(om.ActionHead(cfg), seed=11, cuda=cuda).to(BF)
+    inp = om.make_inputs(cfg, batch=1, seed=13, emb_ids=[5])
+    names = ("vl", "state", "embodiment_id", "init_noise") + (("physics_hist", "physics_noise") if addons else ())
+    args = [inp[k].to(BF) if inp[k].is_floating_point() else inp[k] for k in names]
+    full = args + ([] if addons else [None, None])
+    ref16 = om.denoise(head, *full, cfg.num_steps)
+    d = [a.to(cuda) for a in args]
+    chain = (B200ExpandedActionHeadChain if addons else B200ActionHeadChain)(head, cuda)
+    out = chain(*d).cpu()
+    assert chain.device_status() == 0
+    assert_actions_close(out, ref16, fp32_actions(head, full, cfg))
