@@ -69,6 +69,8 @@ def parse_args():
     p.add_argument("--no-batched", action="store_true",
                    help="config-2 line without the `batched` (config 5) object")
     p.add_argument("--batched-steps", type=int, default=5, help="timed steps of the `batched` object")
+    p.add_argument("--no-block", action="store_true",
+                   help="config-2 line without the `block` (config 1 on the GPU, batch 1) object")
     return p.parse_args()
 
 
@@ -121,6 +123,7 @@ class ClockSampler:
         self.proc = None
         self.lines = []
         self.start = 0
+        self.after = False  # the only sample came right after the region
 
     def __enter__(self):
         try:
@@ -143,6 +146,12 @@ class ClockSampler:
             self.lines.append(line.strip())
 
     def __exit__(self, *a):
+        if self.proc and len(self.lines) == self.start:
+            # a region shorter than the sampling period: the next sample, taken right after it
+            t0 = time.time()
+            while len(self.lines) == self.start and time.time() - t0 < 0.5 and self.proc.poll() is None:
+                time.sleep(0.01)
+            self.after = len(self.lines) > self.start
         if self.proc:
             self.proc.terminate()
             try:
@@ -165,8 +174,11 @@ class ClockSampler:
             for nm, v in zip(names, f[5:9]):
                 if v.lower() == "active":
                     reasons.add(nm)
-        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": smax,
-                "reasons": sorted(reasons), "samples": len(sm)}
+        out = {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": smax,
+               "reasons": sorted(reasons), "samples": len(sm)}
+        if self.after:
+            out["sampled"] = "right after the timed region (shorter than the 100 ms sampling period)"
+        return out
 
 
 def measured_peaks():
@@ -358,31 +370,40 @@ def cpu_baseline_c1(budget_s: float, steps: int = 20):
 
 
 def run_c1(args, rank, world, local):
+    """BASELINE config 1 as the line's own workload (see c1_measure)."""
+    line = c1_measure(rank, world, local, args.batch, args.steps, args.warmup)
+    if rank != 0:
+        return
+    if world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline_c1(args.cpu_sample_s)
+    print(json.dumps(line), flush=True)
+
+
+def c1_measure(rank, world, local, B: int, steps: int, warmup: int) -> dict:
     """BASELINE config 1 on the GPU: one ExpandedDoubleStreamBlock (cognition 256, action 16,
     physics 16, hidden 1024, 16 x 64 heads, SwiGLU 2816) in bf16 through
-    B200ExpandedDoubleStreamBlock (11 launches replayed as one CUDA graph), `--batch`
-    independent sequences per GPU; seeded N(0, 0.02) weights."""
+    B200ExpandedDoubleStreamBlock (11 launches replayed as one CUDA graph), B independent
+    sequences per GPU; seeded N(0, 0.02) weights.  Returns the whole-job line (max over ranks)."""
     import rldx_b200  # noqa: F401
     from rldx_b200.block import B200ExpandedDoubleStreamBlock
     from rldx_b200.microbench import c1_block_module
 
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
-    B = args.batch
     gpu = B200ExpandedDoubleStreamBlock(c1_block_module(0), dev, use_graph=True)
     act, cog, phys, pe = c1_inputs(B, seed=11 + rank)
     d_in = [t.to(dev, torch.bfloat16) for t in (act, cog, phys)]
     gpu(*d_in, pe.to(dev))
     flush = torch.empty(2 * L2_BYTES // 4, dtype=torch.int32, device=dev)
-    for _ in range(args.warmup):
+    for _ in range(warmup):
         gpu.replay()
     torch.cuda.synchronize()
-    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
     barrier(world)
     torch.cuda.synchronize()
     with ClockSampler(local) as clocks:
-        for i in range(args.steps):
+        for i in range(steps):
             flush.fill_(i)  # the block's 75 MB of weights would otherwise stay in L2
             starts[i].record()
             gpu.replay()
@@ -396,7 +417,7 @@ def run_c1(args, rank, world, local):
     pe_d = pe.to(dev)
     e_ms = []
     barrier(world)
-    for i in range(args.steps):
+    for i in range(steps):
         flush.fill_(i)
         torch.cuda.synchronize()
         s_, e_ = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -411,30 +432,27 @@ def run_c1(args, rank, world, local):
     e_total = max_over_ranks(sum(e_ms), world, dev)
     flops = (2 * 288 * (1024 * 3072 + 1024 * 1024 + 1024 * 5632 + 2816 * 1024) + 4.0 * 288 * 288 * 1024) * B
     _, tc_peak, peak_kind = measured_peaks()
-    step_s = total_ms / args.steps * 1e-3
-    if rank != 0:
-        return
-    line = {
+    step_s = total_ms / steps * 1e-3
+    launches = gpu.launches * steps
+    del gpu
+    return {
         "metric": "blocks_per_s", "value": world / step_s, "unit": "blocks/s (batch of %d sequences each)" % B,
-        "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": total_ms / args.steps,
+        "n_gpus": world, "steps": steps, "warmup": warmup, "ms_per_step": total_ms / steps,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic (seeded N(0, 0.02) weights, N(0, 1) streams with the config-1 shapes)",
         "config": {"workload": "BASELINE config 1 on the GPU: one 3-stream ExpandedDoubleStreamBlock",
                    "model": "cognition 256 / action 16 / physics 16 tokens, hidden 1024, 16x64 heads, SwiGLU 2816",
                    "global_batch": B * world, "seq_len": 288, "parallelism": f"replicas x{world}",
                    "l2": "flushed between timed steps (256 MB write)"},
-        "e2e": {"value": world / (e_total / args.steps * 1e-3), "unit": "blocks/s",
+        "e2e": {"value": world / (e_total / steps * 1e-3), "unit": "blocks/s",
                 "h2d_bytes_per_step": sum(t.numel() * 2 for t in h_in) * world,
                 "d2h_bytes_per_step": sum(t.numel() * 2 for t in h_out) * world},
-        "gpu_launches": gpu.launches * args.steps,
+        "gpu_launches": launches,
         "roofline": {"bound": "tensor", "kernel": "whole block (batch 1 is launch-bound: 11 dependent launches)",
                      "achieved": flops / step_s / 1e12, "peak": tc_peak, "unit": "TFLOP/s",
                      "frac": flops / step_s / 1e12 / tc_peak, "peak_source": peak_kind, "traffic": None},
         "clocks": clocks.summary(),
     }
-    if world == 1 and not args.no_cpu_baseline:
-        line["cpu_baseline"] = cpu_baseline_c1(args.cpu_sample_s)
-    print(json.dumps(line), flush=True)
 
 
 def run_reference(args):
@@ -600,6 +618,9 @@ def run_b200(args, rank, world, local):
         del chain
         torch.cuda.empty_cache()
         batched = c5_measure(rank, world, local, args.observations, args.batched_steps, max(3, min(args.warmup, 3)))
+    block = None
+    if not args.no_block and args.workload == "c2":
+        block = c1_measure(rank, world, local, 1, 1000, max(3, min(args.warmup, 3)))
 
     if rank != 0:
         return
@@ -644,6 +665,8 @@ def run_b200(args, rank, world, local):
     line["clocks"] = clocks.summary()
     if batched is not None:
         line["batched"] = batched
+    if block is not None:
+        line["block"] = block
     if world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(args.cpu_sample_s, workload=args.workload)
     print(json.dumps(line), flush=True)
