@@ -55,7 +55,7 @@ struct AttnShape {
   static constexpr int kCols = 64 / kW;  // keys of a tile per softmax thread
   static constexpr uint32_t kOCol = 128 * kG;
   static constexpr uint32_t kTmemCols = (kG == 1) ? 256 : 512;
-  static constexpr int kBars = 1 + 2 * kKStages + 2 * kVStages + 13 * kG + 1;  // + drain
+  static constexpr int kBars = 1 + 2 * kKStages + 2 * kVStages + 14 * kG + 1;  // + drain
   static constexpr int kXchFloats = kG * (2 + 1) * kW * 128;  // per-tile maxima (2 buffers), sums
   static constexpr size_t kSmem = 1024 + static_cast<size_t>(kG) * kQBytes +
                                   static_cast<size_t>(kKStages) * kKTileBytes +
@@ -87,19 +87,19 @@ __global__ void __launch_bounds__(AttnShape<kHD, kG, kW>::kThreads, 1)
   uint64_t* k_empty = k_full + kKS;
   uint64_t* v_full = k_empty + kKS;
   uint64_t* v_empty = v_full + kVS;
-  // per group: s_full[2], s_empty[2], p_full[2], p_empty[2], o_done (one phase per PV MMA),
-  // o_final (one phase: the group's last PV MMA landed), xch[2] (the column warpgroups' row
-  // maxima of a tile are in shared memory), l_xch (their row sums are)
+  // per group: s_full[2], s_empty[2], p_full[2], p_empty[2], o_done[2] (PV_j commits to
+  // o_done[j & 1]), o_final (one phase: the group's last PV MMA landed), xch[2] (the column
+  // warpgroups' row maxima of a tile are in shared memory), l_xch (their row sums are)
   uint64_t* gbar = v_empty + kVS;
-  auto s_full = [&](int g) { return gbar + 13 * g; };
-  auto s_empty = [&](int g) { return gbar + 13 * g + 2; };
-  auto p_full = [&](int g) { return gbar + 13 * g + 4; };
-  auto p_empty = [&](int g) { return gbar + 13 * g + 6; };
-  auto o_done = [&](int g) { return gbar + 13 * g + 8; };
-  auto o_final = [&](int g) { return gbar + 13 * g + 9; };
-  auto xch = [&](int g) { return gbar + 13 * g + 10; };
-  auto l_xch = [&](int g) { return gbar + 13 * g + 12; };
-  uint64_t* drain = gbar + 13 * kG;  // failure path: the issued MMAs have landed
+  auto s_full = [&](int g) { return gbar + 14 * g; };
+  auto s_empty = [&](int g) { return gbar + 14 * g + 2; };
+  auto p_full = [&](int g) { return gbar + 14 * g + 4; };
+  auto p_empty = [&](int g) { return gbar + 14 * g + 6; };
+  auto o_done = [&](int g) { return gbar + 14 * g + 8; };
+  auto o_final = [&](int g) { return gbar + 14 * g + 10; };
+  auto xch = [&](int g) { return gbar + 14 * g + 11; };
+  auto l_xch = [&](int g) { return gbar + 14 * g + 13; };
+  uint64_t* drain = gbar + 14 * kG;  // failure path: the issued MMAs have landed
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   // exchange floats: group g, buffer sb, warpgroup w, row r at xf[((g * 3 + sb) * kW + w) * 128 + r]
   // (sb = 2: the final row sums)
@@ -138,8 +138,8 @@ __global__ void __launch_bounds__(AttnShape<kHD, kG, kW>::kThreads, 1)
         mbar_init(&p_full(g)[i], 4 * kW);
         mbar_init(&p_empty(g)[i], 1);
         mbar_init(&xch(g)[i], 4 * kW);
+        mbar_init(&o_done(g)[i], 1);
       }
-      mbar_init(o_done(g), 1);
       mbar_init(o_final(g), 1);
       mbar_init(l_xch(g), 4 * kW);
     }
@@ -168,9 +168,9 @@ __global__ void __launch_bounds__(AttnShape<kHD, kG, kW>::kThreads, 1)
 #pragma unroll
         for (int c = 0; c < Sh::kChunks; ++c)
           tma_load_3d(sQ + g * kQBytes + c * Sh::kQChunk, &P.tq, q_full, c * 64, q0 + 128 * g, bh, pol);
-      // K(i) and V(i - 1) per step: K leads by one tile (S_{j+1} is issued before PV_j)
+      // K(i) and V(i - 2) per step: K leads by two tiles (S_{j+2} is issued before PV_j)
       bool ok = true;
-      for (int i = 0; ok && i <= nkv; ++i) {
+      for (int i = 0; ok && i <= nkv + 1; ++i) {
         if (i < nkv) {
           const int s = i % kKS;
           if (!mbar_wait(&k_empty[s], (static_cast<uint32_t>(i / kKS) & 1u) ^ 1u, kErrAttnTimeout + 1)) {
@@ -182,8 +182,8 @@ __global__ void __launch_bounds__(AttnShape<kHD, kG, kW>::kThreads, 1)
           for (int c = 0; c < Sh::kChunks; ++c)
             tma_load_3d(sK + s * kKTileBytes + c * Sh::kKChunk, &P.tk, &k_full[s], c * 64, i * 64, bh_kv, pol);
         }
-        if (i >= 1) {
-          const int j = i - 1;
+        if (i >= 2 && i - 2 < nkv) {
+          const int j = i - 2;
           const int s = j % kVS;
           if (!mbar_wait(&v_empty[s], (static_cast<uint32_t>(j / kVS) & 1u) ^ 1u, kErrAttnTimeout + 1)) {
             ok = false;
@@ -221,10 +221,14 @@ __global__ void __launch_bounds__(AttnShape<kHD, kG, kW>::kThreads, 1)
         umma_commit(&k_empty[s]);
         return true;
       };
+      // S runs two key tiles ahead of PV: S_{j+2} goes to the S buffer that softmax j has just
+      // read into registers, before PV_j (which waits for P_j), so the scores of the next tile
+      // are ready when its softmax turn comes
       if (ok) ok = issue_s(0);
+      if (ok && nkv > 1) ok = issue_s(1);
       for (int j = 0; ok && j < nkv; ++j) {
-        if (j + 1 < nkv) {
-          ok = issue_s(j + 1);
+        if (j + 2 < nkv) {
+          ok = issue_s(j + 2);
           if (!ok) break;
         }
         const int pb = j & 1;
@@ -245,7 +249,7 @@ __global__ void __launch_bounds__(AttnShape<kHD, kG, kW>::kThreads, 1)
           for (int k = 0; k < 4; ++k)
             umma_f16(tmem + Sh::kOCol + g * kHD, umma_desc_sw128(p_addr + 32 * k),
                      umma_desc_sw128(v_addr + 32 * k), idesc_pv, (j | k) != 0 ? 1u : 0u);
-          umma_commit(o_done(g));
+          umma_commit(&o_done(g)[pb]);
           umma_commit(&p_empty(g)[pb]);
           if (j == nkv - 1) umma_commit(o_final(g));
         }
@@ -346,9 +350,10 @@ __global__ void __launch_bounds__(AttnShape<kHD, kG, kW>::kThreads, 1)
         l_run *= alpha;
       }
       if (wsub == 0 && j > 0 && __any_sync(0xffffffffu, grow)) {
-        // O holds PV_0..PV_{j-1}: wait for the last one, scale the rows that moved (S_j was
-        // issued after PV_{j-2}, so o_done is at most one phase behind here)
-        ok = mbar_wait(o_done(g), static_cast<uint32_t>(j - 1) & 1u, kErrAttnTimeout + 3);
+        // O holds PV_0..PV_{j-1}: wait for the last one, scale the rows that moved.  S_j was
+        // issued after PV_{j-3}, whose commit went to the same barrier as PV_{j-1}'s; S_j has
+        // landed, so PV_{j-3} has too and the parity wait for PV_{j-1} is unambiguous
+        ok = mbar_wait(&o_done(g)[(j - 1) & 1], static_cast<uint32_t>((j - 1) >> 1) & 1u, kErrAttnTimeout + 3);
         if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
         tc_fence_after();
 #pragma unroll
