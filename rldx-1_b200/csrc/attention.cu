@@ -14,8 +14,8 @@
 //
 // One CTA = one or two 128-query tiles of one (head, batch element).  Q, K come as [B*H, L, d] and V as
 // V^T [B*H, d, Lp] (written by the QKV GEMM epilogue), so every tcgen05 operand is K-major:
-//   S_j  = Q K_j^T          (M=128, N=64 keys, K=d dims)    -> TMEM, double buffered
-//   O   += P_j V_j          (M=128, N=d dims, K=64 keys)    -> one TMEM accumulator
+//   S_j  = Q K_j^T          (M=128, N=kBN keys, K=d dims)   -> TMEM
+//   O   += P_j V_j          (M=128, N=d dims, K=kBN keys)   -> one TMEM accumulator
 // Q and K tiles are held as d/64 chunks of 64 dims (one 128-byte swizzle atom per row each).
 // Each softmax warpgroup (four warps) owns one query tile, one row per thread, so row max / sum
 // need no shuffles.
@@ -28,33 +28,44 @@
 
 namespace rldx {
 
-constexpr int kPBytes = 128 * 128;
 constexpr float kRescaleLog2 = 8.0f;  // lazy-rescale threshold (log2 units)
 
 // kG query tiles of 128 rows per CTA share every K / V tile: kG = 1 for latency (more CTAs),
 // kG = 2 for throughput (two softmax warpgroups keep the special-function and ALU pipes busy
 // while the tensor core works on the other tile, and K / V are read once per 256 queries).
-// kW softmax warpgroups per query tile split each 64-key tile's columns (kW = 2: 32 keys per
+// kW softmax warpgroups per query tile split each key tile's columns (kW = 2: half the keys per
 // thread); their row maxima meet through shared memory once per tile and their row sums at
 // the end, so the exponentials of one tile take half as long (the short-sequence, batch-1 case
 // is bound by that chain).
-// TMEM columns: S of group g, buffer b at (2g + b) * 64; O of group g at kG * 128 + g * d.
+// Key tile width kBN: the variants that run one CTA per SM (head_dim 128 with one query tile,
+// head_dim 64 with the column split) take 128 keys per tile, so the S MMAs have N = 128 (an
+// M = 128 MMA takes as long at N = 64 as at N = 128) and the softmax chain's fixed costs per tile
+// (waits, TMEM load latency, barrier round trips) cover twice the keys.  Their softmax reads S
+// into registers at the start of a tile, so one S buffer suffices (S_{j+1} is issued once
+// softmax j has read S_j).  The other variants keep 64-key tiles and two S buffers.  K and V^T
+// tiles of 128 keys arrive as two 64-key boxes each (the tensor maps' boxes stay 64 rows / keys).
+// TMEM columns: S of group g, buffer b at (kNS g + b) kBN; O of group g at kG kNS kBN + g d.
 template <int kHD, int kG, int kW = 1>
 struct AttnShape {
+  static constexpr int kBN = (kG == 1 && (kW == 2 || kHD == 128)) ? 128 : 64;  // keys per tile
+  static constexpr int kNS = (kBN == 128) ? 1 : 2;   // S buffers per query tile
   static constexpr int kChunks = kHD / 64;           // 64-dim chunks of a Q / K row
   static constexpr int kQBytes = 128 * kHD * 2;      // 128 queries
   static constexpr int kQChunk = 128 * 128;          // one 64-dim chunk of a Q tile
-  static constexpr int kKTileBytes = 64 * kHD * 2;   // 64 keys
-  static constexpr int kKChunk = 64 * 128;           // one 64-dim chunk of a K tile
-  static constexpr int kVTileBytes = kHD * 64 * 2;   // V^T: d rows x 64 keys
+  static constexpr int kKTileBytes = kBN * kHD * 2;  // kBN keys
+  static constexpr int kKChunk = kBN * 128;          // one 64-dim chunk of a K tile
+  static constexpr int kVTileBytes = kHD * kBN * 2;  // V^T: d rows x kBN keys
+  static constexpr int kVChunk = kHD * 128;          // one 64-key chunk of a V^T tile
+  static constexpr int kPBytes = 128 * kBN * 2;      // P: 128 rows x kBN keys, 64-key chunks
+  static constexpr int kPChunk = 128 * 128;
   // separate K and V rings: K(j) is free once the S MMAs of tile j are done, V(j) once its PV
   // MMAs are, so the K loads run ahead of the PV work
-  static constexpr int kKStages = 3;
-  static constexpr int kVStages = (kHD == 128 && kG == 2) ? 2 : 3;
+  static constexpr int kKStages = (kHD == 128 && kBN == 128) ? 2 : 3;
+  static constexpr int kVStages = (kHD == 128) ? 2 : 3;
   static constexpr int kThreads = 64 + 128 * kG * kW;
-  static constexpr int kCols = 64 / kW;  // keys of a tile per softmax thread
-  static constexpr uint32_t kOCol = 128 * kG;
-  static constexpr uint32_t kTmemCols = (kG == 1) ? 256 : 512;
+  static constexpr int kCols = kBN / kW;  // keys of a tile per softmax thread
+  static constexpr uint32_t kOCol = kG * kNS * kBN;
+  static constexpr uint32_t kTmemCols = (kOCol + kG * kHD <= 256) ? 256 : 512;
   static constexpr int kBars = 1 + 2 * kKStages + 2 * kVStages + 14 * kG + 1;  // + drain
   static constexpr int kXchFloats = kG * (2 + 1) * kW * 128;  // per-tile maxima (2 buffers), sums
   static constexpr size_t kSmem = 1024 + static_cast<size_t>(kG) * kQBytes +
@@ -62,6 +73,8 @@ struct AttnShape {
                                   static_cast<size_t>(kVStages) * kVTileBytes +
                                   static_cast<size_t>(kG) * 2 * kPBytes + 8 * kBars + 16 +
                                   4 * static_cast<size_t>(kXchFloats);
+  static_assert(kSmem <= 232448, "shared memory of one CTA");
+  static_assert(kOCol + kG * kHD <= 512, "TMEM columns");
 };
 
 template <int kHD, int kG, int kW>
@@ -72,6 +85,9 @@ __global__ void __launch_bounds__(AttnShape<kHD, kG, kW>::kThreads, 1)
   constexpr int kQBytes = Sh::kQBytes;
   constexpr int kKTileBytes = Sh::kKTileBytes;
   constexpr int kVTileBytes = Sh::kVTileBytes;
+  constexpr int kPBytes = Sh::kPBytes;
+  constexpr int kBN = Sh::kBN;
+  constexpr int kNS = Sh::kNS;
   constexpr int kKS = Sh::kKStages;
   constexpr int kVS = Sh::kVStages;
   extern __shared__ uint8_t smem_raw[];
@@ -80,7 +96,7 @@ __global__ void __launch_bounds__(AttnShape<kHD, kG, kW>::kThreads, 1)
   uint8_t* sQ = smem;                               // kG Q tiles
   uint8_t* sK = sQ + kG * kQBytes;                  // kKS K tiles
   uint8_t* sV = sK + kKS * kKTileBytes;             // kVS V^T tiles
-  uint8_t* sP = sV + kVS * kVTileBytes;             // kG x 2 x 16 KB
+  uint8_t* sP = sV + kVS * kVTileBytes;             // kG x 2 P tiles
   uint64_t* bars = reinterpret_cast<uint64_t*>(sP + kG * 2 * kPBytes);
   uint64_t* q_full = bars;
   uint64_t* k_full = bars + 1;
@@ -116,7 +132,8 @@ __global__ void __launch_bounds__(AttnShape<kHD, kG, kW>::kThreads, 1)
   // keys j < (i / cb + 1) * cb for row i (cb = 1: j <= i)
   const int cb = P.causal_block > 1 ? P.causal_block : 1;
   const int last_row = min(L, q0 + 128 * kG) - 1;
-  const int nkv = P.causal ? min((L + 63) / 64, (min(L, (last_row / cb + 1) * cb) - 1) / 64 + 1) : (L + 63) / 64;
+  const int nkv = P.causal ? min((L + kBN - 1) / kBN, (min(L, (last_row / cb + 1) * cb) - 1) / kBN + 1)
+                           : (L + kBN - 1) / kBN;
   const int ng = (kG == 2 && q0 + 128 < L) ? 2 : 1;  // query tiles with rows inside L
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -168,29 +185,34 @@ __global__ void __launch_bounds__(AttnShape<kHD, kG, kW>::kThreads, 1)
 #pragma unroll
         for (int c = 0; c < Sh::kChunks; ++c)
           tma_load_3d(sQ + g * kQBytes + c * Sh::kQChunk, &P.tq, q_full, c * 64, q0 + 128 * g, bh, pol);
-      // K(i) and V(i - 2) per step: K leads by two tiles (S_{j+2} is issued before PV_j)
+      // K(i) and V(i - kNS) per step: K leads by kNS tiles (S_{j+kNS} is issued before PV_j)
       bool ok = true;
-      for (int i = 0; ok && i <= nkv + 1; ++i) {
+      for (int i = 0; ok && i < nkv + kNS; ++i) {
         if (i < nkv) {
           const int s = i % kKS;
           if (!mbar_wait(&k_empty[s], (static_cast<uint32_t>(i / kKS) & 1u) ^ 1u, kErrAttnTimeout + 1)) {
             ok = false;
             break;
           }
-          mbar_arrive_expect_tx(&k_full[s], kKTileBytes);
+          mbar_arrive_expect_tx(&k_full[s], kKTileBytes);  // keys past L arrive zero-filled
 #pragma unroll
-          for (int c = 0; c < Sh::kChunks; ++c)
-            tma_load_3d(sK + s * kKTileBytes + c * Sh::kKChunk, &P.tk, &k_full[s], c * 64, i * 64, bh_kv, pol);
+          for (int hb = 0; hb < kBN / 64; ++hb)
+#pragma unroll
+            for (int c = 0; c < Sh::kChunks; ++c)
+              tma_load_3d(sK + s * kKTileBytes + c * Sh::kKChunk + hb * 64 * 128, &P.tk, &k_full[s], c * 64,
+                          i * kBN + hb * 64, bh_kv, pol);
         }
-        if (i >= 2 && i - 2 < nkv) {
-          const int j = i - 2;
+        if (i >= kNS && i - kNS < nkv) {
+          const int j = i - kNS;
           const int s = j % kVS;
           if (!mbar_wait(&v_empty[s], (static_cast<uint32_t>(j / kVS) & 1u) ^ 1u, kErrAttnTimeout + 1)) {
             ok = false;
             break;
           }
           mbar_arrive_expect_tx(&v_full[s], kVTileBytes);
-          tma_load_3d(sV + s * kVTileBytes, &P.tv, &v_full[s], j * 64, 0, bh_kv, pol);
+#pragma unroll
+          for (int hb = 0; hb < kBN / 64; ++hb)
+            tma_load_3d(sV + s * kVTileBytes + hb * Sh::kVChunk, &P.tv, &v_full[s], j * kBN + hb * 64, 0, bh_kv, pol);
         }
       }
       if (!ok) settle_issued_copies();  // loads already issued land before the CTA exits
@@ -198,37 +220,36 @@ __global__ void __launch_bounds__(AttnShape<kHD, kG, kW>::kThreads, 1)
   } else if (warp == 1) {
     // ---------------- MMA issuer ----------------
     if (lane == 0) {
-      const uint32_t idesc = umma_idesc_bf16(128, 64);
+      const uint32_t idesc = umma_idesc_bf16(128, kBN);
       const uint32_t idesc_pv = umma_idesc_bf16(128, kHD);
       bool ok = mbar_wait(q_full, 0, kErrAttnTimeout + 2);
       auto issue_s = [&](int j) -> bool {
         const int s = j % kKS;
-        const int sb = j & 1;
+        const int sb = j % kNS;
         if (!mbar_wait(&k_full[s], static_cast<uint32_t>(j / kKS) & 1u, kErrAttnTimeout + 2))
           return false;
         const uint32_t k_addr = smem_u32(sK + s * kKTileBytes);
         for (int g = 0; g < ng; ++g) {
-          if (!mbar_wait(&s_empty(g)[sb], (static_cast<uint32_t>(j >> 1) & 1u) ^ 1u, kErrAttnTimeout + 2))
+          if (!mbar_wait(&s_empty(g)[sb], (static_cast<uint32_t>(j / kNS) & 1u) ^ 1u, kErrAttnTimeout + 2))
             return false;
           tc_fence_after();
           const uint32_t q_addr = smem_u32(sQ + g * kQBytes);
 #pragma unroll
           for (int k = 0; k < 4 * Sh::kChunks; ++k)
-            umma_f16(tmem + (2 * g + sb) * 64, umma_desc_sw128(q_addr + (k >> 2) * Sh::kQChunk + 32 * (k & 3)),
+            umma_f16(tmem + (kNS * g + sb) * kBN, umma_desc_sw128(q_addr + (k >> 2) * Sh::kQChunk + 32 * (k & 3)),
                      umma_desc_sw128(k_addr + (k >> 2) * Sh::kKChunk + 32 * (k & 3)), idesc, k != 0 ? 1u : 0u);
           umma_commit(&s_full(g)[sb]);
         }
         umma_commit(&k_empty[s]);
         return true;
       };
-      // S runs two key tiles ahead of PV: S_{j+2} goes to the S buffer that softmax j has just
+      // S runs kNS key tiles ahead of PV: S_{j+kNS} goes to the S buffer that softmax j has just
       // read into registers, before PV_j (which waits for P_j), so the scores of the next tile
       // are ready when its softmax turn comes
-      if (ok) ok = issue_s(0);
-      if (ok && nkv > 1) ok = issue_s(1);
+      for (int t = 0; ok && t < kNS && t < nkv; ++t) ok = issue_s(t);
       for (int j = 0; ok && j < nkv; ++j) {
-        if (j + 2 < nkv) {
-          ok = issue_s(j + 2);
+        if (j + kNS < nkv) {
+          ok = issue_s(j + kNS);
           if (!ok) break;
         }
         const int pb = j & 1;
@@ -246,9 +267,9 @@ __global__ void __launch_bounds__(AttnShape<kHD, kG, kW>::kThreads, 1)
           tc_fence_after();
           const uint32_t p_addr = smem_u32(sP + (2 * g + pb) * kPBytes);
 #pragma unroll
-          for (int k = 0; k < 4; ++k)
-            umma_f16(tmem + Sh::kOCol + g * kHD, umma_desc_sw128(p_addr + 32 * k),
-                     umma_desc_sw128(v_addr + 32 * k), idesc_pv, (j | k) != 0 ? 1u : 0u);
+          for (int k = 0; k < kBN / 16; ++k)  // 16 keys per MMA; 64-key chunks of P and V^T
+            umma_f16(tmem + Sh::kOCol + g * kHD, umma_desc_sw128(p_addr + (k >> 2) * Sh::kPChunk + 32 * (k & 3)),
+                     umma_desc_sw128(v_addr + (k >> 2) * Sh::kVChunk + 32 * (k & 3)), idesc_pv, (j | k) != 0 ? 1u : 0u);
           umma_commit(&o_done(g)[pb]);
           umma_commit(&p_empty(g)[pb]);
           if (j == nkv - 1) umma_commit(o_final(g));
@@ -279,33 +300,35 @@ __global__ void __launch_bounds__(AttnShape<kHD, kG, kW>::kThreads, 1)
     bool ok = g < ng;
 
     for (int j = 0; ok && j < nkv; ++j) {
-      const int sb = j & 1;
+      const int sb = j & 1;  // P buffer and exchange buffer of this tile
       const uint32_t ph = static_cast<uint32_t>(j >> 1) & 1u;
+      const int ssb = j % kNS;  // S buffer
       // every exit is warp-uniform: the warp-collective TMEM loads / stores and the vote below
       // need all 32 lanes
-      ok = mbar_wait(&s_full(g)[sb], ph, kErrAttnTimeout + 3);
+      ok = mbar_wait(&s_full(g)[ssb], static_cast<uint32_t>(j / kNS) & 1u, kErrAttnTimeout + 3);
       if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
       tc_fence_after();
       float sv[kCols];
 #pragma unroll
       for (int h = 0; h < kCols / 32; ++h)
-        tmem_ld32(tmem + lane_off + (2 * g + sb) * 64 + c0 + 32 * h, *reinterpret_cast<float(*)[32]>(&sv[32 * h]));
+        tmem_ld32(tmem + lane_off + (kNS * g + ssb) * kBN + c0 + 32 * h,
+                  *reinterpret_cast<float(*)[32]>(&sv[32 * h]));
       tmem_wait_ld();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&s_empty(g)[sb]);
+      if (lane == 0) mbar_arrive(&s_empty(g)[ssb]);
 
       // mask, row max of the raw scores (four independent chains; the scale is positive, so it
       // is applied to the max and folded into the exponent's fma).  Tiles wholly inside the
       // sequence without a key mask skip the masking; the key mask, when there is one, is read
-      // as 64 bytes once per tile, so the per-element work stays branch-free.
-      const int kbase = j * 64;
+      // as kBN bytes once per tile, so the per-element work stays branch-free.
+      const int kbase = j * kBN;
       // keys of this thread's columns visible to this row: inside the sequence and, when causal,
       // <= the row
       const int nvis = (P.causal ? min(L, (qrow / cb + 1) * cb) - kbase : L - kbase) - c0;
       float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
       // a tile below the diagonal for every row of the group needs no mask (warp-uniform test)
-      const bool full_tile = L - kbase >= 64 && (!P.causal || kbase + 63 < ((q0 + 128 * g) / cb + 1) * cb);
+      const bool full_tile = L - kbase >= kBN && (!P.causal || kbase + kBN - 1 < ((q0 + 128 * g) / cb + 1) * cb);
       if (kmask == nullptr && full_tile) {
 #pragma unroll
         for (int c = 0; c < kCols; ++c) mx4[c & 3] = fmaxf(mx4[c & 3], sv[c]);
@@ -316,7 +339,7 @@ __global__ void __launch_bounds__(AttnShape<kHD, kG, kW>::kThreads, 1)
           mx4[c & 3] = fmaxf(mx4[c & 3], sv[c]);
         }
       } else {
-        uint32_t mbits[2] = {0u, 0u};  // bit c: key kbase + c0 + c visible
+        uint32_t mbits[kCols / 32] = {};  // bit c: key kbase + c0 + c visible
 #pragma unroll 1
         for (int c = 0; c < kCols; ++c)
           if (c < nvis && kmask[kbase + c0 + c] != 0) mbits[c >> 5] |= 1u << (c & 31);
@@ -351,8 +374,9 @@ __global__ void __launch_bounds__(AttnShape<kHD, kG, kW>::kThreads, 1)
       }
       if (wsub == 0 && j > 0 && __any_sync(0xffffffffu, grow)) {
         // O holds PV_0..PV_{j-1}: wait for the last one, scale the rows that moved.  S_j was
-        // issued after PV_{j-3}, whose commit went to the same barrier as PV_{j-1}'s; S_j has
-        // landed, so PV_{j-3} has too and the parity wait for PV_{j-1} is unambiguous
+        // issued after PV_{j-kNS-1} (so after PV_{j-3}), whose commit went to the same barrier as
+        // PV_{j-1}'s when kNS = 2; S_j has landed, so PV_{j-3} has too and the parity wait for
+        // PV_{j-1} is unambiguous
         ok = mbar_wait(&o_done(g)[(j - 1) & 1], static_cast<uint32_t>((j - 1) >> 1) & 1u, kErrAttnTimeout + 3);
         if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
         tc_fence_after();
@@ -385,7 +409,8 @@ __global__ void __launch_bounds__(AttnShape<kHD, kG, kW>::kThreads, 1)
       }
       l_run += (ps01.x + ps01.y) + (ps23.x + ps23.y);
 
-      // P_j -> shared memory (K-major, 128-byte swizzle: chunk c of row r at (c ^ (r & 7)) * 16)
+      // P_j -> shared memory: 64-key chunks of [128 rows x 128 bytes], K-major, 128-byte swizzle
+      // (16-byte group c of row r at (c ^ (r & 7)) * 16)
       ok = mbar_wait(&p_empty(g)[sb], ph ^ 1u, kErrAttnTimeout + 3);
       if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
       uint8_t* prow = sP + (2 * g + sb) * kPBytes + r * 128;
@@ -396,8 +421,8 @@ __global__ void __launch_bounds__(AttnShape<kHD, kG, kW>::kThreads, 1)
         u.y = pack_bf16x2(sv[8 * cc + 2], sv[8 * cc + 3]);
         u.z = pack_bf16x2(sv[8 * cc + 4], sv[8 * cc + 5]);
         u.w = pack_bf16x2(sv[8 * cc + 6], sv[8 * cc + 7]);
-        const int chunk = c0 / 8 + cc;
-        *reinterpret_cast<uint4*>(prow + ((chunk ^ (r & 7)) << 4)) = u;
+        const int grp = c0 / 8 + cc;  // 8-key group within the tile
+        *reinterpret_cast<uint4*>(prow + (grp >> 3) * Sh::kPChunk + (((grp & 7) ^ (r & 7)) << 4)) = u;
       }
       fence_proxy_async_smem();
       tc_fence_before();
@@ -494,7 +519,8 @@ cudaError_t launch_variant(const AttnParams& p, cudaStream_t stream, bool pdl) {
 }  // namespace
 
 size_t attention_smem_bytes(int head_dim) {
-  return head_dim == 128 ? AttnShape<128, 2>::kSmem : std::max(AttnShape<64, 2>::kSmem, AttnShape<64, 1, 2>::kSmem);
+  return head_dim == 128 ? std::max(AttnShape<128, 1>::kSmem, AttnShape<128, 2>::kSmem)
+                         : std::max(AttnShape<64, 1>::kSmem, std::max(AttnShape<64, 2>::kSmem, AttnShape<64, 1, 2>::kSmem));
 }
 
 cudaError_t attention_prepare_device() {
