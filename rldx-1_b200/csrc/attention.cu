@@ -30,6 +30,35 @@ namespace rldx {
 
 constexpr float kRescaleLog2 = 8.0f;  // lazy-rescale threshold (log2 units)
 
+// Of every four exponent pairs of a tile, this many are computed on the FMA pipe
+// (exp2_fma_x2) and the rest by the special-function unit (16 results per cycle per SM: 1024
+// cycles for a 128 x 128 tile).  Measured on the config-4 sweep: one in four +1.5-2.4 %, two
+// in four no gain, three in four slower (the polynomial's instructions then cost more issue
+// slots than the special-function unit saves).
+#ifndef RLDX_ATTN_EXP_FMA
+#define RLDX_ATTN_EXP_FMA 1
+#endif
+constexpr int kExpFmaPairs = RLDX_ATTN_EXP_FMA;
+
+// 2^x for two values on the FMA pipe: n = round(x) through the 1.5 * 2^23 shift (exact for
+// |x| < 2^22), 2^(x - n) by a degree-4 polynomial fitted to 2^f on [-1/2, 1/2] (weighted least
+// squares on Chebyshev nodes, relative error below 3e-6 in fp32 evaluation), then n added to
+// the exponent field; arguments below -126 (and -inf) give 0.
+__device__ __forceinline__ float2 exp2_fma_x2(float2 x) {
+  const float2 t = add_f32x2(x, make_float2(12582912.0f, 12582912.0f));
+  const float2 n = add_f32x2(t, make_float2(-12582912.0f, -12582912.0f));
+  const float2 f = fma_f32x2(n, make_float2(-1.0f, -1.0f), x);
+  float2 p = make_float2(0.009570094756782055f, 0.009570094756782055f);
+  p = fma_f32x2(p, f, make_float2(0.05591786280274391f, 0.05591786280274391f));
+  p = fma_f32x2(p, f, make_float2(0.240247443318367f, 0.240247443318367f));
+  p = fma_f32x2(p, f, make_float2(0.6931217908859253f, 0.6931217908859253f));
+  p = fma_f32x2(p, f, make_float2(0.9999992847442627f, 0.9999992847442627f));
+  // the low bits of t hold n; shifted by 23 they add n to the exponent field of p
+  const float ex = __int_as_float(__float_as_int(p.x) + (__float_as_int(t.x) << 23));
+  const float ey = __int_as_float(__float_as_int(p.y) + (__float_as_int(t.y) << 23));
+  return make_float2(x.x >= -126.0f ? ex : 0.0f, x.y >= -126.0f ? ey : 0.0f);
+}
+
 // kG query tiles of 128 rows per CTA share every K / V tile: kG = 1 for latency (more CTAs),
 // kG = 2 for throughput (two softmax warpgroups keep the special-function and ALU pipes busy
 // while the tensor core works on the other tile, and K / V are read once per 256 queries).
@@ -398,8 +427,14 @@ __global__ void __launch_bounds__(AttnShape<kHD, kG, kW>::kThreads, 1)
 #pragma unroll
       for (int c = 0; c < kCols; c += 2) {
         const float2 t = fma_f32x2(make_float2(sv[c], sv[c + 1]), sc2, nm2);
-        sv[c] = ex2_approx(t.x);
-        sv[c + 1] = ex2_approx(t.y);
+        if (((c >> 1) & 3) < kExpFmaPairs) {
+          const float2 e = exp2_fma_x2(t);
+          sv[c] = e.x;
+          sv[c + 1] = e.y;
+        } else {
+          sv[c] = ex2_approx(t.x);
+          sv[c + 1] = ex2_approx(t.y);
+        }
       }
       float2 ps01 = make_float2(0.0f, 0.0f), ps23 = make_float2(0.0f, 0.0f);
 #pragma unroll
