@@ -85,16 +85,21 @@ struct AttnShape {
   static constexpr int kKChunk = kBN * 128;          // one 64-dim chunk of a K tile
   static constexpr int kVTileBytes = kHD * kBN * 2;  // V^T: d rows x kBN keys
   static constexpr int kVChunk = kHD * 128;          // one 64-key chunk of a V^T tile
-  static constexpr int kPBytes = 128 * kBN * 2;      // P: 128 rows x kBN keys, 64-key chunks
+  // P of the 128-key variants lives in TMEM (the PV MMA reads its A operand from there: no
+  // shared-memory round trip, no proxy fence); the others keep P in shared memory
+  static constexpr bool kPT = (kBN == 128);
+  static constexpr int kPBytes = kPT ? 0 : 128 * kBN * 2;  // smem P: 128 rows x kBN keys, 64-key chunks
   static constexpr int kPChunk = 128 * 128;
+  static constexpr int kPCols = kPT ? kBN / 2 : 0;         // TMEM columns of one P buffer (bf16 pairs)
   // separate K and V rings: K(j) is free once the S MMAs of tile j are done, V(j) once its PV
   // MMAs are, so the K loads run ahead of the PV work
-  static constexpr int kKStages = (kHD == 128 && kBN == 128) ? 2 : 3;
-  static constexpr int kVStages = (kHD == 128) ? 2 : 3;
+  static constexpr int kKStages = 3;
+  static constexpr int kVStages = (kHD == 128 && kG == 2) ? 2 : 3;
   static constexpr int kThreads = 64 + 128 * kG * kW;
   static constexpr int kCols = kBN / kW;  // keys of a tile per softmax thread
   static constexpr uint32_t kOCol = kG * kNS * kBN;
-  static constexpr uint32_t kTmemCols = (kOCol + kG * kHD <= 256) ? 256 : 512;
+  static constexpr uint32_t kPCol = kOCol + kG * kHD;  // P buffers (2 per group) when kPT
+  static constexpr uint32_t kTmemCols = (kPCol + 2 * kG * kPCols <= 256) ? 256 : 512;
   static constexpr int kBars = 1 + 2 * kKStages + 2 * kVStages + 14 * kG + 1;  // + drain
   static constexpr int kXchFloats = kG * (2 + 1) * kW * 128;  // per-tile maxima (2 buffers), sums
   static constexpr size_t kSmem = 1024 + static_cast<size_t>(kG) * kQBytes +
@@ -103,7 +108,7 @@ struct AttnShape {
                                   static_cast<size_t>(kG) * 2 * kPBytes + 8 * kBars + 16 +
                                   4 * static_cast<size_t>(kXchFloats);
   static_assert(kSmem <= 232448, "shared memory of one CTA");
-  static_assert(kOCol + kG * kHD <= 512, "TMEM columns");
+  static_assert(kPCol + 2 * kG * kPCols <= 512, "TMEM columns");
 };
 
 template <int kHD, int kG, int kW>
@@ -294,11 +299,21 @@ __global__ void __launch_bounds__(AttnShape<kHD, kG, kW>::kThreads, 1)
             break;
           }
           tc_fence_after();
-          const uint32_t p_addr = smem_u32(sP + (2 * g + pb) * kPBytes);
+          if constexpr (Sh::kPT) {  // P from TMEM: 16 keys = 8 columns per MMA
+            const uint32_t p_tmem = tmem + Sh::kPCol + static_cast<uint32_t>((2 * g + pb) * Sh::kPCols);
 #pragma unroll
-          for (int k = 0; k < kBN / 16; ++k)  // 16 keys per MMA; 64-key chunks of P and V^T
-            umma_f16(tmem + Sh::kOCol + g * kHD, umma_desc_sw128(p_addr + (k >> 2) * Sh::kPChunk + 32 * (k & 3)),
-                     umma_desc_sw128(v_addr + (k >> 2) * Sh::kVChunk + 32 * (k & 3)), idesc_pv, (j | k) != 0 ? 1u : 0u);
+            for (int k = 0; k < kBN / 16; ++k)
+              umma_f16_ts(tmem + Sh::kOCol + g * kHD, p_tmem + 8 * k,
+                          umma_desc_sw128(v_addr + (k >> 2) * Sh::kVChunk + 32 * (k & 3)), idesc_pv,
+                          (j | k) != 0 ? 1u : 0u);
+          } else {
+            const uint32_t p_addr = smem_u32(sP + (2 * g + pb) * kPBytes);
+#pragma unroll
+            for (int k = 0; k < kBN / 16; ++k)  // 16 keys per MMA; 64-key chunks of P and V^T
+              umma_f16(tmem + Sh::kOCol + g * kHD, umma_desc_sw128(p_addr + (k >> 2) * Sh::kPChunk + 32 * (k & 3)),
+                       umma_desc_sw128(v_addr + (k >> 2) * Sh::kVChunk + 32 * (k & 3)), idesc_pv,
+                       (j | k) != 0 ? 1u : 0u);
+          }
           umma_commit(&o_done(g)[pb]);
           umma_commit(&p_empty(g)[pb]);
           if (j == nkv - 1) umma_commit(o_final(g));
@@ -448,18 +463,30 @@ __global__ void __launch_bounds__(AttnShape<kHD, kG, kW>::kThreads, 1)
       // (16-byte group c of row r at (c ^ (r & 7)) * 16)
       ok = mbar_wait(&p_empty(g)[sb], ph ^ 1u, kErrAttnTimeout + 3);
       if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
-      uint8_t* prow = sP + (2 * g + sb) * kPBytes + r * 128;
+      if constexpr (Sh::kPT) {  // P -> TMEM: column c of this row's share holds keys 2c, 2c + 1
+        const uint32_t pcol = tmem + lane_off + Sh::kPCol + static_cast<uint32_t>((2 * g + sb) * Sh::kPCols + c0 / 2);
 #pragma unroll
-      for (int cc = 0; cc < kCols / 8; ++cc) {
-        uint4 u;
-        u.x = pack_bf16x2(sv[8 * cc + 0], sv[8 * cc + 1]);
-        u.y = pack_bf16x2(sv[8 * cc + 2], sv[8 * cc + 3]);
-        u.z = pack_bf16x2(sv[8 * cc + 4], sv[8 * cc + 5]);
-        u.w = pack_bf16x2(sv[8 * cc + 6], sv[8 * cc + 7]);
-        const int grp = c0 / 8 + cc;  // 8-key group within the tile
-        *reinterpret_cast<uint4*>(prow + (grp >> 3) * Sh::kPChunk + (((grp & 7) ^ (r & 7)) << 4)) = u;
+        for (int h = 0; h < kCols / 64; ++h) {
+          float pk[32];
+#pragma unroll
+          for (int i = 0; i < 32; ++i) pk[i] = __uint_as_float(pack_bf16x2(sv[64 * h + 2 * i], sv[64 * h + 2 * i + 1]));
+          tmem_st32(pcol + 32 * h, pk);
+        }
+        tmem_wait_st();
+      } else {
+        uint8_t* prow = sP + (2 * g + sb) * kPBytes + r * 128;
+#pragma unroll
+        for (int cc = 0; cc < kCols / 8; ++cc) {
+          uint4 u;
+          u.x = pack_bf16x2(sv[8 * cc + 0], sv[8 * cc + 1]);
+          u.y = pack_bf16x2(sv[8 * cc + 2], sv[8 * cc + 3]);
+          u.z = pack_bf16x2(sv[8 * cc + 4], sv[8 * cc + 5]);
+          u.w = pack_bf16x2(sv[8 * cc + 6], sv[8 * cc + 7]);
+          const int grp = c0 / 8 + cc;  // 8-key group within the tile
+          *reinterpret_cast<uint4*>(prow + (grp >> 3) * Sh::kPChunk + (((grp & 7) ^ (r & 7)) << 4)) = u;
+        }
+        fence_proxy_async_smem();
       }
-      fence_proxy_async_smem();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&p_full(g)[sb]);
