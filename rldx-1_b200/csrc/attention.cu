@@ -19,7 +19,8 @@
 // Q and K tiles are held as d/64 chunks of 64 dims (one 128-byte swizzle atom per row each).
 // Each softmax warpgroup (four warps) owns one query tile, one row per thread, so row max / sum
 // need no shuffles.
-// P_j goes to shared memory in the 128-byte-swizzled K-major layout the PV MMA reads.  The
+// P_j goes to TMEM as bf16 pairs (the PV MMA takes its A operand from tensor memory), or, for
+// head_dim 128 with two query tiles, to shared memory in the 128-byte-swizzled K-major layout.  The
 // running max is rescaled lazily: exponentials use a reference max that only moves when a
 // row's max grows by more than 2^8 (P then stays <= 256, exact in the final O / l); only then
 // is that row of O read from TMEM, scaled and written back, after the previous PV MMA landed.
@@ -85,9 +86,10 @@ struct AttnShape {
   static constexpr int kKChunk = kBN * 128;          // one 64-dim chunk of a K tile
   static constexpr int kVTileBytes = kHD * kBN * 2;  // V^T: d rows x kBN keys
   static constexpr int kVChunk = kHD * 128;          // one 64-key chunk of a V^T tile
-  // P of the 128-key variants lives in TMEM (the PV MMA reads its A operand from there: no
-  // shared-memory round trip, no proxy fence); the others keep P in shared memory
-  static constexpr bool kPT = (kBN == 128);
+  // P lives in TMEM (the PV MMA reads its A operand from there: no shared-memory round trip, no
+  // proxy fence) wherever two P buffers fit beside S and O: every variant but head_dim 128 with
+  // two query tiles, which keeps P in shared memory
+  static constexpr bool kPT = !(kHD == 128 && kG == 2);
   static constexpr int kPBytes = kPT ? 0 : 128 * kBN * 2;  // smem P: 128 rows x kBN keys, 64-key chunks
   static constexpr int kPChunk = 128 * 128;
   static constexpr int kPCols = kPT ? kBN / 2 : 0;         // TMEM columns of one P buffer (bf16 pairs)
