@@ -64,9 +64,9 @@ __device__ __forceinline__ float2 exp2_fma_x2(float2 x) {
 // kG = 2 for throughput (two softmax warpgroups keep the special-function and ALU pipes busy
 // while the tensor core works on the other tile, and K / V are read once per 256 queries).
 // kW softmax warpgroups per query tile split each key tile's columns (kW = 2: half the keys per
-// thread); their row maxima meet through shared memory once per tile and their row sums at
-// the end, so the exponentials of one tile take half as long (the short-sequence, batch-1 case
-// is bound by that chain).
+// thread), so the exponentials of one tile take half as long (the short-sequence, batch-1 case
+// is bound by that chain).  Each keeps its own reference max, row sum and O accumulator over
+// its keys; the row maxima and sums meet through shared memory once, after the last tile.
 // Key tile width kBN: the variants that run one CTA per SM (head_dim 128 with one query tile,
 // head_dim 64 with the column split) take 128 keys per tile, so the S MMAs have N = 128 (an
 // M = 128 MMA takes as long at N = 64 as at N = 128) and the softmax chain's fixed costs per tile
@@ -100,7 +100,9 @@ struct AttnShape {
   static constexpr int kThreads = 64 + 128 * kG * kW;
   static constexpr int kCols = kBN / kW;  // keys of a tile per softmax thread
   static constexpr uint32_t kOCol = kG * kNS * kBN;
-  static constexpr uint32_t kPCol = kOCol + kG * kHD;  // P buffers (2 per group) when kPT
+  // one O accumulator per column warpgroup: each keeps its own reference max, row sum and O over
+  // its share of the keys, merged once at the end (no exchange of row maxima per tile)
+  static constexpr uint32_t kPCol = kOCol + kG * kW * kHD;  // P buffers (2 per group) when kPT
   static constexpr uint32_t kTmemCols = (kPCol + 2 * kG * kPCols <= 256) ? 256 : 512;
   static constexpr int kBars = 1 + 2 * kKStages + 2 * kVStages + 14 * kG + 1;  // + drain
   static constexpr int kXchFloats = kG * (2 + 1) * kW * 128;  // per-tile maxima (2 buffers), sums
@@ -111,6 +113,7 @@ struct AttnShape {
                                   4 * static_cast<size_t>(kXchFloats);
   static_assert(kSmem <= 232448, "shared memory of one CTA");
   static_assert(kPCol + 2 * kG * kPCols <= 512, "TMEM columns");
+  static_assert(kW == 1 || kPT, "column split: P in TMEM");
 };
 
 template <int kHD, int kG, int kW>
@@ -304,10 +307,13 @@ __global__ void __launch_bounds__(AttnShape<kHD, kG, kW>::kThreads, 1)
           if constexpr (Sh::kPT) {  // P from TMEM: 16 keys = 8 columns per MMA
             const uint32_t p_tmem = tmem + Sh::kPCol + static_cast<uint32_t>((2 * g + pb) * Sh::kPCols);
 #pragma unroll
-            for (int k = 0; k < kBN / 16; ++k)
-              umma_f16_ts(tmem + Sh::kOCol + g * kHD, p_tmem + 8 * k,
+            for (int k = 0; k < kBN / 16; ++k) {
+              constexpr int kPerW = kBN / 16 / kW;  // MMAs over one column warpgroup's keys
+              const int w = k / kPerW;
+              umma_f16_ts(tmem + Sh::kOCol + (g * kW + w) * kHD, p_tmem + 8 * k,
                           umma_desc_sw128(v_addr + (k >> 2) * Sh::kVChunk + 32 * (k & 3)), idesc_pv,
-                          (j | k) != 0 ? 1u : 0u);
+                          (j > 0 || k % kPerW != 0) ? 1u : 0u);
+            }
           } else {
             const uint32_t p_addr = smem_u32(sP + (2 * g + pb) * kPBytes);
 #pragma unroll
@@ -338,7 +344,7 @@ __global__ void __launch_bounds__(AttnShape<kHD, kG, kW>::kThreads, 1)
     const int r = quad * 32 + lane;
     const int qrow = q0 + 128 * g + r;
     const uint32_t lane_off = static_cast<uint32_t>(quad * 32) << 16;
-    const uint32_t o_col = Sh::kOCol + g * kHD;
+    const uint32_t o_col = Sh::kOCol + (g * kW + wsub) * kHD;  // this warpgroup's O
     const unsigned char* kmask = P.key_mask ? P.key_mask + static_cast<size_t>(b) * L : nullptr;
     const float scale = P.scale_log2;
     float m_ref = -INFINITY;  // reference max of the exponentials (log2 units)
@@ -395,19 +401,9 @@ __global__ void __launch_bounds__(AttnShape<kHD, kG, kW>::kThreads, 1)
           mx4[c & 3] = fmaxf(mx4[c & 3], sv[c]);
         }
       }
+      // the maximum over this warpgroup's keys only: each column warpgroup keeps its own
+      // reference max, row sum and O accumulator, merged after the last tile
       float mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3]));
-      if constexpr (kW > 1) {
-        // the row's maximum over the whole tile: every column warpgroup publishes its part and
-        // reads the others' (buffer sb is rewritten two tiles later, after every warpgroup has
-        // published tile j + 1, i.e. read tile j)
-        xf[((g * 3 + sb) * kW + wsub) * 128 + r] = mx;
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&xch(g)[sb]);
-        ok = mbar_wait(&xch(g)[sb], ph, kErrAttnTimeout + 3);
-        if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
-#pragma unroll
-        for (int w = 0; w < kW; ++w) mx = fmaxf(mx, xf[((g * 3 + sb) * kW + w) * 128 + r]);
-      }
       mx *= scale;
 
       // lazy rescale of O and l when this row's max outgrows the reference by 2^8
@@ -418,7 +414,7 @@ __global__ void __launch_bounds__(AttnShape<kHD, kG, kW>::kThreads, 1)
         m_ref = mx;
         l_run *= alpha;
       }
-      if (wsub == 0 && j > 0 && __any_sync(0xffffffffu, grow)) {
+      if (j > 0 && __any_sync(0xffffffffu, grow)) {
         // O holds PV_0..PV_{j-1}: wait for the last one, scale the rows that moved.  S_j was
         // issued after PV_{j-kNS-1} (so after PV_{j-3}), whose commit went to the same barrier as
         // PV_{j-1}'s when kNS = 2; S_j has landed, so PV_{j-3} has too and the parity wait for
@@ -498,17 +494,28 @@ __global__ void __launch_bounds__(AttnShape<kHD, kG, kW>::kThreads, 1)
     // o_done may be anywhere from two phases behind to complete, which a parity wait on it
     // cannot tell apart.
     if (ok && nkv > 0) ok = mbar_wait(o_final(g), 0u, kErrAttnTimeout + 3);
+    // merge of the column warpgroups: O = sum_w O_w 2^(m_w - m) / sum_w l_w 2^(m_w - m) with m
+    // the largest reference max (a warpgroup that saw no visible key contributes nothing)
+    float wscale[kW];
+    wscale[0] = 1.0f;
     if constexpr (kW > 1) {
-      // the row sum over all keys: each column warpgroup's part, published once at the end
       if (__all_sync(0xffffffffu, ok) && nkv > 0) {
+        xf[((g * 3 + 0) * kW + wsub) * 128 + r] = m_ref;
         xf[((g * 3 + 2) * kW + wsub) * 128 + r] = l_run;
         __syncwarp();
         if (lane == 0) mbar_arrive(l_xch(g));
         ok = mbar_wait(l_xch(g), 0u, kErrAttnTimeout + 3);
         if (__all_sync(0xffffffffu, ok)) {
+          float m = -INFINITY;
+#pragma unroll
+          for (int w = 0; w < kW; ++w) m = fmaxf(m, xf[((g * 3 + 0) * kW + w) * 128 + r]);
           l_run = 0.0f;
 #pragma unroll
-          for (int w = 0; w < kW; ++w) l_run += xf[((g * 3 + 2) * kW + w) * 128 + r];
+          for (int w = 0; w < kW; ++w) {
+            const float mw = xf[((g * 3 + 0) * kW + w) * 128 + r];
+            wscale[w] = (mw == -INFINITY) ? 0.0f : ex2_approx(mw - m);
+            l_run += xf[((g * 3 + 2) * kW + w) * 128 + r] * wscale[w];
+          }
         }
       }
     }
@@ -529,11 +536,25 @@ __global__ void __launch_bounds__(AttnShape<kHD, kG, kW>::kThreads, 1)
 #pragma unroll
       for (int half = 0; half < kHD / 64; ++half) {  // 64 output dims at a time
         float o[kODims];
-        const uint32_t ocol = o_col + 64 * half + wsub * kODims;
+        const uint32_t ocol = Sh::kOCol + g * kW * kHD + 64 * half + wsub * kODims;
 #pragma unroll
         for (int h = 0; h < kODims / 32; ++h)
           tmem_ld32(tmem + lane_off + ocol + 32 * h, *reinterpret_cast<float(*)[32]>(&o[32 * h]));
         tmem_wait_ld();
+        if constexpr (kW > 1) {
+#pragma unroll
+          for (int c = 0; c < kODims; ++c) o[c] *= wscale[0];
+#pragma unroll
+          for (int w = 1; w < kW; ++w) {
+            float o2[kODims];
+#pragma unroll
+            for (int h = 0; h < kODims / 32; ++h)
+              tmem_ld32(tmem + lane_off + ocol + w * kHD + 32 * h, *reinterpret_cast<float(*)[32]>(&o2[32 * h]));
+            tmem_wait_ld();
+#pragma unroll
+            for (int c = 0; c < kODims; ++c) o[c] = fmaf(o2[c], wscale[w], o[c]);
+          }
+        }
         if (qrow < L) {
 #pragma unroll
           for (int cc0 = 0; cc0 < kODims / 8; ++cc0) {
