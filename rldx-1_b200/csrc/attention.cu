@@ -143,8 +143,9 @@ __global__ void __launch_bounds__(AttnShape<kHD, kG, kW>::kThreads, 1)
   uint64_t* v_full = k_empty + kKS;
   uint64_t* v_empty = v_full + kVS;
   // per group: s_full[2], s_empty[2], p_full[2], p_empty[2], o_done[2] (PV_j commits to
-  // o_done[j & 1]), o_final (one phase: the group's last PV MMA landed), xch[2] (the column
-  // warpgroups' row maxima of a tile are in shared memory), l_xch (their row sums are)
+  // o_done[j & 1]), o_final (one phase: the group's last PV MMA landed), xch[2] (initialised
+  // but no longer waited on: the column warpgroups keep their own row maxima), l_xch (their
+  // reference maxima and row sums are in shared memory, once, after the last tile)
   uint64_t* gbar = v_empty + kVS;
   auto s_full = [&](int g) { return gbar + 14 * g; };
   auto s_empty = [&](int g) { return gbar + 14 * g + 2; };
